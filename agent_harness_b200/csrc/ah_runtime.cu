@@ -1,0 +1,110 @@
+// ah_runtime.cu — status/error plumbing, device facts and the host-slice
+// staging used by the ah_host_* drop-in entries.
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "ah_common.cuh"
+
+namespace ah {
+
+static thread_local char t_last_error[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int* device_error_word() {
+  static std::mutex mu;
+  static std::vector<int*> words;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)words.size() <= dev) words.resize(dev + 1, nullptr);
+  if (!words[dev]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess || cudaMemset(p, 0, sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    words[dev] = p;
+  }
+  return words[dev];
+}
+
+int sm_count() {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+}  // namespace ah
+
+using namespace ah;
+
+extern "C" {
+
+const char* ah_strerror(int status) {
+  switch (status) {
+    case AH_OK: return "ok";
+    case AH_EINVAL: return "invalid argument";
+    case AH_ENOMEM: return "out of memory";
+    case AH_ECUDA: return "CUDA error";
+    case AH_ENCCL: return "NCCL error";
+    case AH_ETIMEOUT: return "device-side wait timed out";
+    case AH_EUNSUPPORTED: return "unsupported";
+    default: return "unknown status";
+  }
+}
+
+const char* ah_last_error(void) { return t_last_error; }
+
+int ah_version(void) { return 1; }
+
+int ah_device_init(int device) {
+  AH_CUDA_TRY(cudaSetDevice(device));
+  AH_CUDA_TRY(cudaFree(nullptr));  // establish the primary context
+  (void)sm_count();
+  if (!device_error_word()) return fail(AH_ENOMEM, "device_init: error word allocation failed");
+  return AH_OK;
+}
+
+int ah_check_device_error(void* stream) {
+  int* w = device_error_word();
+  if (!w) return fail(AH_ENOMEM, "check_device_error: error word unavailable");
+  int v = 0;
+  AH_CUDA_TRY(cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream)));
+  AH_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
+  if (v != 0) {
+    AH_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
+    return fail(AH_ETIMEOUT, "a bounded device-side wait gave up (code 0x%x)", v);
+  }
+  return AH_OK;
+}
+
+int64_t ah_packed_bytes(int64_t n) { return n < 0 ? 0 : (n + 1) / 2; }
+int64_t ah_n_groups(int64_t n, int64_t gs) { return (n < 0 || gs <= 0) ? 0 : (n + gs - 1) / gs; }
+int64_t ah_quantized_bytes(int64_t n, int64_t gs) { return ah_n_groups(n, gs) * 4 + ah_packed_bytes(n); }
+
+}  // extern "C"

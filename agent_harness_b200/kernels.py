@@ -1,0 +1,188 @@
+"""Device-tensor front-end of the C ABI (torch CUDA tensors in, tensors out).
+
+torch supplies device memory and streams only; every computation below is one
+of the library's sm_100a kernels.  All calls run on torch's current stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import AhError, call, lib
+
+DTYPE_F32, DTYPE_F16, DTYPE_Q4_0, DTYPE_Q8_0, DTYPE_Q6_K, DTYPE_BF16 = 0, 1, 2, 8, 13, 30
+GROUP_SIZE = 32
+
+
+def _stream(dev: torch.device | None = None):
+    return C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _ptr(t: torch.Tensor):
+    if not t.is_cuda:
+        raise AhError(-1, "expected a CUDA tensor")
+    if not t.is_contiguous():
+        raise AhError(-1, "expected a contiguous tensor")
+    return C.c_void_p(t.data_ptr())
+
+
+def _as_u8(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dtype == torch.uint8 else t.contiguous().view(torch.uint8)
+
+
+# --- conversions ---------------------------------------------------------------
+
+def f16_to_f32(src: torch.Tensor) -> torch.Tensor:
+    """formats/gguf.rs:93-120 semantics over f16 bit patterns (int16/uint16/float16)."""
+    out = torch.empty(src.numel(), dtype=torch.float32, device=src.device)
+    call("ah_f16_to_f32", _ptr(src), _ptr(out), src.numel(), _stream(src.device))
+    return out
+
+
+def bf16_to_f32(src: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(src.numel(), dtype=torch.float32, device=src.device)
+    call("ah_bf16_to_f32", _ptr(src), _ptr(out), src.numel(), _stream(src.device))
+    return out
+
+
+def f32_to_f16(src: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(src.numel(), dtype=torch.int16, device=src.device)
+    call("ah_f32_to_f16", _ptr(src), _ptr(out), src.numel(), _stream(src.device))
+    return out
+
+
+# --- dequantisation --------------------------------------------------------------
+
+def dequant_q8_0(blocks: torch.Tensor, n: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    out = out if out is not None else torch.empty(n, dtype=torch.float32, device=blocks.device)
+    call("ah_dequant_q8_0_f32", _ptr(blocks), _ptr(out), n, _stream(blocks.device))
+    return out
+
+
+def dequant_q4_0(blocks: torch.Tensor, n: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    out = out if out is not None else torch.empty(n, dtype=torch.float32, device=blocks.device)
+    call("ah_dequant_q4_0_f32", _ptr(blocks), _ptr(out), n, _stream(blocks.device))
+    return out
+
+
+def dequant_layer(scales: torch.Tensor, packed: torch.Tensor, n: int, group_size: int = GROUP_SIZE) -> torch.Tensor:
+    out = torch.empty(n, dtype=torch.float32, device=packed.device)
+    call("ah_dequant_layer", _ptr(scales), _ptr(packed), _ptr(out), n, group_size, _stream(packed.device))
+    return out
+
+
+def dequantize_to_f32(raw: torch.Tensor, dtype: int, element_count: int) -> torch.Tensor:
+    raw = _as_u8(raw)
+    cap = max(element_count, raw.numel() // 2, 1)
+    out = torch.empty(cap, dtype=torch.float32, device=raw.device)
+    n_out = C.c_int64(0)
+    call("ah_dequantize_to_f32", _ptr(raw), raw.numel(), dtype, element_count, _ptr(out), C.byref(n_out),
+         _stream(raw.device))
+    return out[: n_out.value]
+
+
+# --- quantisers ---------------------------------------------------------------------
+
+def quantize_q4(w: torch.Tensor, group_size: int = GROUP_SIZE):
+    n = w.numel()
+    gs = max(group_size, 1)
+    scales = torch.empty((n + gs - 1) // gs, dtype=torch.float32, device=w.device)
+    packed = torch.empty((n + 1) // 2, dtype=torch.uint8, device=w.device)
+    call("ah_quantize_q4", _ptr(w), n, group_size, _ptr(scales), _ptr(packed), _stream(w.device))
+    return scales, packed
+
+
+def quantize_q8_0(w: torch.Tensor) -> torch.Tensor:
+    n = w.numel()
+    blocks = torch.empty(((n + 31) // 32) * 34, dtype=torch.uint8, device=w.device)
+    call("ah_quantize_q8_0", _ptr(w), n, _ptr(blocks), _stream(w.device))
+    return blocks
+
+
+def quantize_q4_0(w: torch.Tensor) -> torch.Tensor:
+    n = w.numel()
+    blocks = torch.empty(((n + 31) // 32) * 18, dtype=torch.uint8, device=w.device)
+    call("ah_quantize_q4_0", _ptr(w), n, _ptr(blocks), _stream(w.device))
+    return blocks
+
+
+# --- synthetic inputs ------------------------------------------------------------------
+
+def fill_normal(n: int, mean: float, std: float, seed: int, device="cuda", index_offset: int = 0) -> torch.Tensor:
+    out = torch.empty(n, dtype=torch.float32, device=device)
+    call("ah_fill_normal", _ptr(out), n, mean, std, seed, index_offset, _stream(out.device))
+    return out
+
+
+def synth_q4_0(rows: int, cols: int, std: float, seed: int, device="cuda", row0: int = 0, col0: int = 0,
+               full_cols: int | None = None) -> torch.Tensor:
+    full_cols = cols if full_cols is None else full_cols
+    blocks = torch.empty(rows * (cols // 32) * 18, dtype=torch.uint8, device=device)
+    call("ah_synth_q4_0", _ptr(blocks), row0, rows, col0, cols, full_cols, std, seed, _stream(blocks.device))
+    return blocks
+
+
+def synth_f16(n: int, mean: float, std: float, seed: int, device="cuda", index_offset: int = 0) -> torch.Tensor:
+    out = torch.empty(n, dtype=torch.int16, device=device)
+    call("ah_synth_f16", _ptr(out), n, mean, std, seed, index_offset, _stream(out.device))
+    return out
+
+
+# --- fused GEMV ----------------------------------------------------------------------------
+
+class Q4Weight:
+    """A device-resident quantised matrix in the GEMV's tiled layout."""
+
+    def __init__(self, handle: C.c_void_p, rows: int, cols: int, device: torch.device):
+        self._h = handle
+        self.rows, self.cols, self.device = rows, cols, device
+
+    @classmethod
+    def from_q4_0(cls, blocks: torch.Tensor, rows: int, cols: int) -> "Q4Weight":
+        h = C.c_void_p()
+        call("ah_q4w_from_q4_0", _ptr(blocks), rows, cols, C.byref(h), _stream(blocks.device))
+        return cls(h, rows, cols, blocks.device)
+
+    @classmethod
+    def from_engine(cls, scales: torch.Tensor, packed: torch.Tensor, rows: int, cols: int) -> "Q4Weight":
+        h = C.c_void_p()
+        call("ah_q4w_from_engine", _ptr(scales), _ptr(packed), rows, cols, C.byref(h), _stream(packed.device))
+        return cls(h, rows, cols, packed.device)
+
+    @property
+    def handle(self) -> C.c_void_p:
+        return self._h
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(lib().ah_q4w_weight_bytes(self._h))
+
+    def gemv(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y[b] = W @ x[b] for x of shape [cols] or [batch, cols] (batch <= 16)."""
+        squeeze = x.dim() == 1
+        xb = x.reshape(-1, self.cols)
+        batch = xb.shape[0]
+        if out is None:
+            out = torch.empty(batch, self.rows, dtype=torch.float32, device=x.device)
+        call("ah_q4w_gemv", self._h, _ptr(xb), _ptr(out), batch, _stream(x.device))
+        return out.reshape(self.rows) if squeeze else out
+
+    def close(self):
+        if self._h:
+            lib().ah_q4w_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def gemv_4bit_into(out: torch.Tensor, scales: torch.Tensor, packed: torch.Tensor, x: torch.Tensor, rows: int,
+                   cols: int, group_size: int = GROUP_SIZE) -> torch.Tensor:
+    """inference/math.rs:255-295 on device tensors in the engine's own storage."""
+    call("ah_gemv_4bit_into", _ptr(out), _ptr(scales), _ptr(packed), _ptr(x) if x.numel() else None, rows, cols,
+         group_size, _stream(out.device))
+    return out

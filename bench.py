@@ -1,0 +1,386 @@
+"""Benchmark of the quantized-weight hot path on B200.
+
+Headline (`value`): fused Q4_0 dequant+GEMV, batch-1 decode shape 4096x4096
+(W ~ N(0,0.02) seed 2, x ~ N(0,1) seed 3), in HBM GB/s of algorithmic bytes
+(W blocks 9,437,184 B + x 16,384 B + y 16,384 B per GEMV).  One step = one
+sweep of batch-1 GEMVs over a rotating set of 64 distinct weight copies
+(606 MB, > 4x L2), so every GEMV streams its weights from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--quick]
+
+Under torchrun each rank runs the same per-GPU work on its own GPU (replicas:
+the 4096x4096 GEMV does not shard) and rank 0 prints one JSON line with the
+whole-job value over the max-over-ranks device time.  `--impl reference`
+times the reference's own CPU implementation (its AVX-512 gemv_4bit_into,
+restated in C) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fused Q4 GEMV & dequant HBM GB/s (% of 8 TB/s); 8B-shape decode tokens/s"
+ROWS = COLS = 4096
+N_COPIES = 64
+GEMV_BYTES = ROWS * (COLS // 32) * 18 + COLS * 4 + ROWS * 4  # 9,469,952
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+# dram__bytes_read.sum + dram__bytes_write.sum per GEMV launch, from the ncu
+# capture summarised in profiles/gemv_q4_0_4096x4096.md (None until captured).
+NCU_TRAFFIC_PER_LAUNCH = None
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the reference's own algorithm, restated in C under oracle/)
+# ---------------------------------------------------------------------------
+
+def cpu_gemv_setup(n_copies: int):
+    """Engine-format copies of the benchmark weight (same values as the Q4_0
+    blocks: f32 scale = f16 d, identical nibbles), for the reference's
+    gemv_4bit_into (f32 scales, linear nibbles)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal(ROWS * COLS) * 0.02).astype(np.float32)
+    blocks = O.quantize_q4_0(w).reshape(-1, 18)
+    scales = blocks[:, :2].copy().view(np.float16).astype(np.float32).ravel()
+    packed = np.ascontiguousarray(blocks[:, 2:]).ravel()
+    x = np.random.default_rng(3).standard_normal(COLS).astype(np.float32)
+    copies = [(scales.copy(), packed.copy()) for _ in range(n_copies)]
+    return O, copies, x
+
+
+def cpu_threads():
+    return max(1, min(os.cpu_count() or 1, 32))  # inference/math.rs:275 caps at 32
+
+
+def time_cpu_gemv(seconds: float = 8.0, n_copies: int = 32):
+    O, copies, x = cpu_gemv_setup(n_copies)
+    out = np.empty(ROWS, np.float32)
+    nt = cpu_threads()
+    for s, p in copies[:2]:
+        O.avx_gemv_4bit_into(out, s, p, x, ROWS, COLS, nt)
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        s, p = copies[n % n_copies]
+        O.avx_gemv_4bit_into(out, s, p, x, ROWS, COLS, nt)
+        n += 1
+        if n % n_copies == 0 and time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    # single-thread scalar worker, as benches/dequant_bench.rs also times
+    t1 = time.perf_counter()
+    s, p = copies[0]
+    O.lib().or_gemv_4bit_worker_scalar(out, s, p, x, 0, ROWS, COLS, 32)
+    dt1 = time.perf_counter() - t1
+    return {"value": n * GEMV_BYTES / dt / 1e9, "unit": "GB/s", "cores": nt, "kind": "port",
+            "sample": f"{n} AVX-512 gemv_4bit_into calls (math.rs:255-380 restated) over {n_copies} rotating "
+                      f"4096x4096 copies, {dt:.1f} s; GB/s counts the same {GEMV_BYTES} algorithmic bytes per GEMV",
+            "scalar_1thread_gbs": GEMV_BYTES / dt1 / 1e9}
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    O, copies, x = cpu_gemv_setup(N_COPIES if args.steps >= N_COPIES else max(2, args.steps))
+    nc = len(copies)
+    out = np.empty(ROWS, np.float32)
+    nt = cpu_threads()
+    for i in range(args.warmup):
+        s, p = copies[i % nc]
+        O.avx_gemv_4bit_into(out, s, p, x, ROWS, COLS, nt)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        s, p = copies[i % nc]
+        O.avx_gemv_4bit_into(out, s, p, x, ROWS, COLS, nt)
+    dt = time.perf_counter() - t0
+    v = args.steps * GEMV_BYTES / dt / 1e9
+    line = {"metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "Q4_0 fused dequant+GEMV 4096x4096 batch 1 (one GEMV per step on CPU)",
+                       "rows": ROWS, "cols": COLS, "batch": 1, "rotating_copies": nc},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": nt, "kind": "port",
+                             "sample": f"{args.steps} AVX-512 gemv_4bit_into calls (inference/math.rs:255-380 "
+                                       f"restated in C, thread spawn per call as in the reference)"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+
+def run_gpu(args):
+    import torch
+    rank, world, local = dist_env()
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    from agent_harness_b200 import _lib
+    from agent_harness_b200 import kernels as K
+    _lib.check(_lib.lib().ah_device_init(dev.index))
+
+    # --- inputs (resident in HBM before timing) ---
+    blocks = K.synth_q4_0(ROWS, COLS, 0.02, 2, device=dev)
+    Ws = [K.Q4Weight.from_q4_0(blocks, ROWS, COLS) for _ in range(N_COPIES)]
+    del blocks
+    x = K.fill_normal(COLS, 0.0, 1.0, 3, device=dev)
+    y = torch.empty(ROWS, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def sweep():
+        for W in Ws:
+            W.gemv(x, out=y)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            sweep()
+    torch.cuda.synchronize()
+    # capture `chunk` steps per graph (the weights do not change between steps)
+    chunk = next(c for c in (16, 10, 8, 5, 4, 2, 1) if args.steps % c == 0)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(chunk):
+            sweep()
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps // chunk):
+            g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    launches = args.steps * N_COPIES
+    per_launch_s = ms / 1e3 / launches
+    value = world * launches * GEMV_BYTES / (ms / 1e3) / 1e9
+    achieved = GEMV_BYTES / per_launch_s / 1e9
+    peak, peak_kind = peaks()
+
+    # correctness spot check of the timed kernel's output (cheap, outside timing)
+    ok = bool(torch.isfinite(y).all().item())
+
+    # --- end to end through the public API: host x in, host y out, per GEMV ---
+    x_host = torch.empty(COLS, dtype=torch.float32).pin_memory()
+    x_host.copy_(x.cpu())
+    y_host = torch.empty(ROWS, dtype=torch.float32).pin_memory()
+    xd = torch.empty_like(x)
+    e2e_steps = max(1, min(args.steps, 200))
+    with torch.cuda.stream(stream):
+        for W in Ws[:4]:
+            xd.copy_(x_host, non_blocking=True)
+            W.gemv(xd, out=y)
+            y_host.copy_(y, non_blocking=True)
+            stream.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            for W in Ws:
+                xd.copy_(x_host, non_blocking=True)
+                W.gemv(xd, out=y)
+                y_host.copy_(y, non_blocking=True)
+                stream.synchronize()
+        e2e_dt = time.perf_counter() - t0
+    e2e_val = world * e2e_steps * N_COPIES * GEMV_BYTES / e2e_dt / 1e9
+    if world > 1:
+        t = torch.tensor([e2e_dt], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_val = world * e2e_steps * N_COPIES * GEMV_BYTES / float(t.item()) / 1e9
+
+    extra = {}
+    if rank == 0 and not args.quick:
+        extra = secondary_measurements(K, dev, stream, peak)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = time_cpu_gemv(seconds=args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_0 x f32 (f16-split tensor-core, f32 accumulate)",
+            "data": "synthetic (seeded counter-based N(0,1) generator; weights N(0,0.02) seed 2, x seed 3)",
+            "config": {"workload": "Q4_0 fused dequant+GEMV 4096x4096 batch 1", "rows": ROWS, "cols": COLS,
+                       "batch": 1, "rotating_copies": N_COPIES, "gemvs_per_step": N_COPIES,
+                       "l2": "inputs larger than L2: each step streams 64 distinct weight copies (606 MB)",
+                       "bytes_per_gemv": GEMV_BYTES, "graph_steps_per_replay": chunk,
+                       "parallelism": f"replicas x{world}"},
+            "pct_of_8tbs": round(100.0 * achieved / NOMINAL_HBM_GBS, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "kernel": "k_gemv_q4<1,false,0,0,8>", "bytes_per_launch": GEMV_BYTES,
+                         "avg_launch_us": round(per_launch_s * 1e6, 4)},
+            "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": N_COPIES * COLS * 4,
+                    "d2h_bytes_per_step": N_COPIES * ROWS * 4,
+                    "path": "kernels.Q4Weight.gemv per GEMV: pinned x H2D, GEMV, y D2H, stream sync; weights "
+                            "resident from load"},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "output_finite": ok,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baseline"]["value"] = round(cpu["value"], 3)
+            line["cpu_scalar_1thread_gbs"] = round(cpu["scalar_1thread_gbs"], 3)
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    for W in Ws:
+        W.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def secondary_measurements(K, dev, stream, peak):
+    """Config-1 dequant and f16->f32 throughput (each launch > L2)."""
+    import torch
+    out = {}
+    n = 4096 * 11008
+    w = K.fill_normal(n, 0.0, 0.02, 0, device=dev)
+    q8 = K.quantize_q8_0(w)
+    del w
+    f = torch.empty(n, dtype=torch.float32, device=dev)
+    h = K.f32_to_f16(K.fill_normal(n, 0.0, 1.0, 1, device=dev))
+    for name, fn, nbytes in (("dequant_q8_0", lambda: K.dequant_q8_0(q8, n, out=f), q8.numel() + 4 * n),
+                             ("f16_to_f32", lambda: K.f16_to_f32(h), 2 * n + 4 * n)):
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            iters = 20
+            e0.record(stream)
+            for _ in range(iters):
+                fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        s = e0.elapsed_time(e1) / 1e3 / iters
+        gbs = nbytes / s / 1e9
+        out[name] = {"gbs": round(gbs, 2), "pct_of_8tbs": round(100 * gbs / NOMINAL_HBM_GBS, 2),
+                     "frac_of_measured_peak": round(gbs / peak, 4), "bytes_per_call": nbytes,
+                     "us_per_call": round(s * 1e6, 2), "shape": "4096x11008"}
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--quick", action="store_true", help="headline only")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

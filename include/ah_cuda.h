@@ -1,0 +1,171 @@
+/*
+ * ah_cuda.h — C ABI of agent_harness_b200, the B200 (sm_100a) implementation of
+ * agent_harness's quantized-weight hot path.
+ *
+ * Every entry point returns an int status (AH_OK = 0, negative on error) and
+ * never aborts; ah_last_error() returns the calling thread's last message.
+ * Pointers named *_dev are device pointers; `stream` is a cudaStream_t passed
+ * as void* (NULL = legacy default stream).  Device-pointer entries are
+ * asynchronous on `stream`.  Entries named ah_host_* take HOST slices exactly as
+ * the reference's Rust functions do, and are synchronous (upload, compute,
+ * download).  "Reference:" lines cite the agent_harness function each entry
+ * replaces (paths relative to the agent_harness source tree).
+ */
+#ifndef AH_CUDA_H
+#define AH_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AH_API __attribute__((visibility("default")))
+#else
+#define AH_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define AH_OK 0
+#define AH_EINVAL (-1)       /* bad shape, size, alignment or argument        */
+#define AH_ENOMEM (-2)       /* device or pinned allocation failed            */
+#define AH_ECUDA (-3)        /* a CUDA runtime call failed                    */
+#define AH_ENCCL (-4)        /* an NCCL call failed                           */
+#define AH_ETIMEOUT (-5)     /* a bounded device-side wait gave up            */
+#define AH_EUNSUPPORTED (-6) /* valid request this build does not implement   */
+
+/* GGML dtype codes accepted by ah_dequantize_to_f32 (formats/gguf.rs:57-74). */
+#define AH_DTYPE_F32 0u
+#define AH_DTYPE_F16 1u
+#define AH_DTYPE_Q4_0 2u
+#define AH_DTYPE_Q8_0 8u
+#define AH_DTYPE_Q6_K 13u
+#define AH_DTYPE_BF16 30u
+
+/* Bytes per 32-element block (types/dtype.rs:69-83). */
+#define AH_Q4_0_BLOCK_BYTES 18
+#define AH_Q8_0_BLOCK_BYTES 34
+#define AH_GROUP_SIZE 32 /* models/quantization.rs:365 GROUP_SIZE */
+
+/* ---- runtime --------------------------------------------------------------- */
+AH_API const char* ah_strerror(int status);
+AH_API const char* ah_last_error(void);
+AH_API int ah_version(void);
+/* Makes `device` current for the calling thread and caches its properties. */
+AH_API int ah_device_init(int device);
+/* Reads and clears the device-side error word that bounded waits set
+ * (AH_ETIMEOUT when a wait gave up since the last call). */
+AH_API int ah_check_device_error(void* stream);
+
+/* ---- sizes (models/quantization.rs:423-435) -------------------------------- */
+AH_API int64_t ah_packed_bytes(int64_t n_elements);
+AH_API int64_t ah_n_groups(int64_t n_elements, int64_t group_size);
+AH_API int64_t ah_quantized_bytes(int64_t n_elements, int64_t group_size);
+
+/* ---- conversions (device pointers) ------------------------------------------ */
+/* Reference: formats/gguf.rs:93-120 f16_to_f32 (IEEE; NaN -> +-0x7FC00000);
+ * also the defined semantics of models/avx512_kernel.rs:212-232 f16_bytes_to_f32. */
+AH_API int ah_f16_to_f32(const uint16_t* src_dev, float* dst_dev, int64_t n, void* stream);
+/* Reference: formats/gguf.rs:124-126 bf16_to_f32; avx512_kernel.rs:236-255. */
+AH_API int ah_bf16_to_f32(const uint16_t* src_dev, float* dst_dev, int64_t n, void* stream);
+/* No reference counterpart (the reference never narrows): IEEE RNE f32 -> f16. */
+AH_API int ah_f32_to_f16(const float* src_dev, uint16_t* dst_dev, int64_t n, void* stream);
+
+/* ---- block dequantisation (device pointers; bit-exact incl. NaN bits) -------- */
+/* Reference: formats/gguf.rs:460-479 (Q8_0 branch of dequantize_to_f32).
+ * `blocks_dev` holds ceil(n/32) 34-byte blocks {u16 d; i8 qs[32]}. */
+AH_API int ah_dequant_q8_0_f32(const void* blocks_dev, float* out_dev, int64_t n, void* stream);
+/* Reference: formats/gguf.rs:480-502 (Q4_0 branch); 18-byte blocks
+ * {u16 d; u8 qs[16]}, byte i = element 2i (low nibble), 2i+1 (high nibble). */
+AH_API int ah_dequant_q4_0_f32(const void* blocks_dev, float* out_dev, int64_t n, void* stream);
+/* Reference: models/quantization.rs:439-454 dequant_layer (scalar semantics,
+ * :444-452): out[i] = (nib(i) - 8) * scales[i / group_size]. */
+AH_API int ah_dequant_layer(const float* scales_dev, const uint8_t* packed_dev, float* out_dev, int64_t n,
+                     int64_t group_size, void* stream);
+/* Reference: formats/gguf.rs:434-535 GGUFFile::dequantize_to_f32 — dispatch on
+ * the GGML dtype code.  *n_out receives the element count the reference's Vec
+ * would hold (F32/F16/BF16: raw_bytes / elem size; Q8_0: limited by raw_bytes;
+ * unknown dtype: n zeros).  A truncated Q4_0 block (where the reference panics)
+ * returns AH_EINVAL.  Q6_K follows the reference's approximate branch. */
+AH_API int ah_dequantize_to_f32(const void* raw_dev, int64_t raw_bytes, uint32_t dtype, int64_t element_count,
+                         float* out_dev, int64_t* n_out, void* stream);
+
+/* ---- quantisers (device pointers) -------------------------------------------- */
+/* Reference: models/quantization.rs:369-404 quantize (and inference/math.rs:223-253):
+ * per group scale = absmax/7 (f32), q = clamp(round(w/scale),-8,7)+8, low nibble =
+ * even index.  scales_dev: ceil(n/gs) floats; packed_dev: ceil(n/2) bytes. */
+AH_API int ah_quantize_q4(const float* w_dev, int64_t n, int64_t group_size, float* scales_dev, uint8_t* packed_dev,
+                   void* stream);
+/* No reference quantiser exists for these block formats (their dequant is
+ * formats/gguf.rs:459-502): d = f16(absmax/127), q = clamp(round(w/d),-127,127). */
+AH_API int ah_quantize_q8_0(const float* w_dev, int64_t n, void* blocks_dev, void* stream);
+/* d = f16(absmax/8), q = clamp(round(w/d)+8, 0, 15), reference nibble order. */
+AH_API int ah_quantize_q4_0(const float* w_dev, int64_t n, void* blocks_dev, void* stream);
+
+/* ---- synthetic data (no reference counterpart: seeded benchmark inputs) -------- */
+/* out[i] = mean + std * N(0,1) from a counter-based generator keyed by (seed, i + index_offset). */
+AH_API int ah_fill_normal(float* out_dev, int64_t n, float mean, float std, uint64_t seed, int64_t index_offset,
+                   void* stream);
+/* Rows [row0, row0+rows) and columns [col0, col0+cols) of a logical matrix with
+ * `full_cols` columns drawn as ah_fill_normal(seed) in row-major order, quantised
+ * straight to Q4_0 blocks (cols % 32 == 0, col0 % 32 == 0). */
+AH_API int ah_synth_q4_0(void* blocks_dev, int64_t row0, int64_t rows, int64_t col0, int64_t cols, int64_t full_cols,
+                  float std, uint64_t seed, void* stream);
+/* Same for f16 values mean + std*N(0,1) (embeddings, norm weights). */
+AH_API int ah_synth_f16(uint16_t* out_dev, int64_t n, float mean, float std, uint64_t seed, int64_t index_offset,
+                 void* stream);
+
+/* ---- fused Q4 GEMV ------------------------------------------------------------ */
+/* Opaque device-resident quantised weight in the GEMV's tiled layout (rows
+ * padded to 16, columns to 64; nibbles and scales in separate planes). */
+typedef struct AhQ4Weight AhQ4Weight;
+
+/* Reference: inference/mod.rs:184-314 decompress_all_parallel's per-tensor
+ * quantise + store step — here an upload-and-repack of an already-quantised
+ * tensor into device memory owned by the handle.  Source pointers are DEVICE
+ * pointers in the reference formats. */
+AH_API int ah_q4w_from_q4_0(const void* blocks_dev, int64_t rows, int64_t cols, AhQ4Weight** out, void* stream);
+AH_API int ah_q4w_from_engine(const float* scales_dev, const uint8_t* packed_dev, int64_t rows, int64_t cols,
+                       AhQ4Weight** out, void* stream);
+AH_API int ah_q4w_destroy(AhQ4Weight* w);
+AH_API int ah_q4w_shape(const AhQ4Weight* w, int64_t* rows, int64_t* cols);
+/* Bytes the algorithm must read per GEMV (nibbles + scales, unpadded). */
+AH_API int64_t ah_q4w_weight_bytes(const AhQ4Weight* w);
+
+/* Reference: inference/math.rs:255-295 gemv_4bit_into (batch 1) and its
+ * token-by-token use in inference/mod.rs:411-538, batched to `batch` <= 16
+ * tokens: y[b][r] = sum_j W[r][j] * x[b][j], f32 accumulate, dequantised
+ * weights never written to memory.  x_dev: [batch][cols] f32, y_dev: [batch][rows]. */
+AH_API int ah_q4w_gemv(const AhQ4Weight* w, const float* x_dev, float* y_dev, int batch, void* stream);
+
+/* Reference: inference/math.rs:255-295 gemv_4bit_into on the engine format as
+ * stored (f32 scales [rows][ceil(cols/gs)], linear nibbles), device pointers, any
+ * group size; empty input -> zero output (math.rs:264-267). */
+AH_API int ah_gemv_4bit_into(float* out_dev, const float* scales_dev, const uint8_t* packed_dev, const float* x_dev,
+                      int64_t rows, int64_t cols, int64_t group_size, void* stream);
+/* Reference: inference/math.rs:205-214 matvec_4bit_into (square). */
+AH_API int ah_matvec_4bit_into(float* out_dev, const float* scales_dev, const uint8_t* packed_dev, const float* x_dev,
+                        int64_t dim, int64_t group_size, void* stream);
+
+/* ---- host-slice drop-ins (synchronous; reference signatures) ---------------------- */
+/* Reference: inference/math.rs:255-295 gemv_4bit_into(out, scales, packed, x, rows, cols, gs). */
+AH_API int ah_host_gemv_4bit_into(float* out, const float* scales, const uint8_t* packed, const float* x, size_t rows,
+                           size_t cols, size_t group_size);
+/* Reference: models/quantization.rs:439-454 dequant_layer(scales, packed, result, gs). */
+AH_API int ah_host_dequant_layer(const float* scales, const uint8_t* packed, float* result, size_t n, size_t group_size);
+/* Reference: models/quantization.rs:369-404 quantize(weights, gs) -> (scales, packed). */
+AH_API int ah_host_quantize(const float* weights, size_t n, size_t group_size, float* scales, uint8_t* packed);
+/* Reference: models/avx512_kernel.rs:212-232 f16_bytes_to_f32 (defined semantics). */
+AH_API int ah_host_f16_bytes_to_f32(const uint8_t* src, size_t n_bytes, float* out);
+/* Reference: models/avx512_kernel.rs:236-255 bf16_bytes_to_f32. */
+AH_API int ah_host_bf16_bytes_to_f32(const uint8_t* src, size_t n_bytes, float* out);
+/* Reference: formats/gguf.rs:434-535 GGUFFile::dequantize_to_f32(raw, dtype, n). */
+AH_API int ah_host_dequantize_to_f32(const uint8_t* raw, size_t raw_bytes, uint32_t dtype, size_t element_count,
+                              float* out, size_t* n_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AH_CUDA_H */

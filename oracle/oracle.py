@@ -1,0 +1,260 @@
+"""ctypes front-end for the CPU oracle (oracle/ah_oracle*.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline legs, always as the checker or the timed CPU baseline
+of the reference's own algorithm, never as a product code path.  Every
+function forwards to the C restatement, which cites the reference's file:line.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libah_oracle.so")
+_lib = None
+
+f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+i64 = C.c_int64
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (system gcc, no FP contraction)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        L.or_f16_to_f32.argtypes = [C.c_uint16]; L.or_f16_to_f32.restype = C.c_float
+        L.or_bf16_to_f32.argtypes = [C.c_uint16]; L.or_bf16_to_f32.restype = C.c_float
+        L.or_f16_to_f32_scalar_asis.argtypes = [C.c_uint16]; L.or_f16_to_f32_scalar_asis.restype = C.c_float
+        L.or_f32_to_f16.argtypes = [C.c_float]; L.or_f32_to_f16.restype = C.c_uint16
+        L.or_f16_array_to_f32.argtypes = [u16p, f32p, i64]
+        L.or_bf16_array_to_f32.argtypes = [u16p, f32p, i64]
+        L.or_f32_array_to_f16.argtypes = [f32p, u16p, i64]
+        L.or_dequantize_to_f32.argtypes = [u8p, i64, C.c_uint32, i64, f32p]; L.or_dequantize_to_f32.restype = i64
+        L.or_packed_bytes.argtypes = [i64]; L.or_packed_bytes.restype = i64
+        L.or_n_groups.argtypes = [i64, i64]; L.or_n_groups.restype = i64
+        L.or_quantized_bytes.argtypes = [i64, i64]; L.or_quantized_bytes.restype = i64
+        L.or_quantize_q4.argtypes = [f32p, i64, i64, f32p, u8p]
+        L.or_dequant_weight.argtypes = [f32p, u8p, i64, i64]; L.or_dequant_weight.restype = C.c_float
+        L.or_dequant_layer.argtypes = [f32p, u8p, f32p, i64, i64]
+        L.or_quantize_q8_0.argtypes = [f32p, i64, u8p]
+        L.or_quantize_q4_0.argtypes = [f32p, i64, u8p]
+        L.or_gemv_4bit_worker_scalar.argtypes = [f32p, f32p, u8p, f32p, i64, i64, i64, i64]
+        L.or_gemv_4bit_into.argtypes = [f32p, f32p, u8p, f32p, i64, i64, i64]
+        L.or_gemv_q4_0.argtypes = [f32p, u8p, f32p, i64, i64]
+        L.or_gemm_q4_0.argtypes = [f32p, u8p, f32p, i64, i64, i64]
+        L.or_gemv_f32.argtypes = [f32p, f32p, f32p, i64, i64]
+        L.or_rms_norm_into.argtypes = [f32p, f32p, f32p, i64, C.c_float]
+        L.or_sigmoid.argtypes = [C.c_float]; L.or_sigmoid.restype = C.c_float
+        L.or_silu.argtypes = [C.c_float]; L.or_silu.restype = C.c_float
+        L.or_softmax.argtypes = [f32p, i64]
+        L.or_rope_multi.argtypes = [f32p, i64, i64, np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS"), C.c_float]
+        L.or_argmax.argtypes = [f32p, i64]; L.or_argmax.restype = C.c_uint32
+        L.or_swiglu_4bit_into.argtypes = [f32p, f32p, f32p, u8p, f32p, u8p, f32p, u8p, i64, i64, i64, f32p, f32p, f32p]
+        L.or_model_forward.argtypes = [C.c_void_p, C.c_int32, i64, f32p]; L.or_model_forward.restype = C.c_int
+        # AVX-512 as-is restatements (timing only)
+        L.or_avx_gemv_4bit_into.argtypes = [f32p, f32p, u8p, f32p, i64, i64, i64, C.c_int]
+        L.or_avx_gemv_4bit_worker.argtypes = [f32p, f32p, u8p, f32p, i64, i64, i64]
+        L.or_avx_gemm_rows.argtypes = [f32p, f32p, u8p, f32p, i64, i64, i64, C.c_int]
+        L.or_avx_dequant_layer.argtypes = [f32p, u8p, f32p, i64]
+        L.or_avx_f16_bytes_to_f32.argtypes = [u8p, i64, f32p]; L.or_avx_f16_bytes_to_f32.restype = i64
+        L.or_avx_bf16_bytes_to_f32.argtypes = [u8p, i64, f32p]; L.or_avx_bf16_bytes_to_f32.restype = i64
+        _lib = L
+    return _lib
+
+
+def _c(a, dt):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+# --- conversions -----------------------------------------------------------
+
+def f16_to_f32(bits: np.ndarray) -> np.ndarray:
+    bits = _c(bits, np.uint16)
+    out = np.empty(bits.shape, np.float32)
+    lib().or_f16_array_to_f32(bits.ravel(), out.ravel(), bits.size)
+    return out
+
+
+def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
+    bits = _c(bits, np.uint16)
+    out = np.empty(bits.shape, np.float32)
+    lib().or_bf16_array_to_f32(bits.ravel(), out.ravel(), bits.size)
+    return out
+
+
+def f32_to_f16(x: np.ndarray) -> np.ndarray:
+    x = _c(x, np.float32)
+    out = np.empty(x.shape, np.uint16)
+    lib().or_f32_array_to_f16(x.ravel(), out.ravel(), x.size)
+    return out
+
+
+def dequantize_to_f32(raw: np.ndarray, dtype: int, element_count: int) -> np.ndarray | None:
+    """GGUFFile::dequantize_to_f32 semantics; None where the reference panics."""
+    raw = _c(raw, np.uint8).ravel()
+    cap = max(element_count, raw.size // 2 + 1, 1)
+    out = np.empty(cap, np.float32)
+    k = lib().or_dequantize_to_f32(raw if raw.size else np.zeros(1, np.uint8), raw.size, dtype, element_count, out)
+    if k < 0:
+        return None
+    return out[:k].copy()
+
+
+# --- engine INT4 format ----------------------------------------------------
+
+def quantize_q4(w: np.ndarray, group_size: int = 32):
+    w = _c(w, np.float32).ravel()
+    n = w.size
+    gs = max(group_size, 1)
+    scales = np.empty((n + gs - 1) // gs, np.float32)
+    packed = np.empty((n + 1) // 2, np.uint8)
+    lib().or_quantize_q4(w if n else np.zeros(1, np.float32), n, group_size,
+                         scales if scales.size else np.zeros(1, np.float32),
+                         packed if packed.size else np.zeros(1, np.uint8))
+    return scales, packed
+
+
+def dequant_layer(scales, packed, n, group_size=32):
+    out = np.empty(n, np.float32)
+    lib().or_dequant_layer(_c(scales, np.float32), _c(packed, np.uint8), out, n, group_size)
+    return out
+
+
+def quantize_q8_0(w: np.ndarray) -> np.ndarray:
+    w = _c(w, np.float32).ravel()
+    blocks = np.empty(((w.size + 31) // 32) * 34, np.uint8)
+    lib().or_quantize_q8_0(w, w.size, blocks)
+    return blocks
+
+
+def quantize_q4_0(w: np.ndarray) -> np.ndarray:
+    w = _c(w, np.float32).ravel()
+    blocks = np.empty(((w.size + 31) // 32) * 18, np.uint8)
+    lib().or_quantize_q4_0(w, w.size, blocks)
+    return blocks
+
+
+# --- GEMV / GEMM -----------------------------------------------------------
+
+def gemv_4bit_into(scales, packed, x, rows, cols, group_size=32) -> np.ndarray:
+    out = np.zeros(rows, np.float32)
+    x = _c(x, np.float32)
+    lib().or_gemv_4bit_into(out, _c(scales, np.float32), _c(packed, np.uint8),
+                            x if x.size else np.zeros(1, np.float32), rows, cols, group_size)
+    return out
+
+
+def gemv_q4_0(blocks, x, rows, cols) -> np.ndarray:
+    out = np.empty(rows, np.float32)
+    lib().or_gemv_q4_0(out, _c(blocks, np.uint8), _c(x, np.float32), rows, cols)
+    return out
+
+
+def gemm_q4_0(blocks, a, n) -> np.ndarray:
+    a = _c(a, np.float32)
+    m, k = a.shape
+    out = np.empty((m, n), np.float32)
+    lib().or_gemm_q4_0(out, _c(blocks, np.uint8), a, m, n, k)
+    return out
+
+
+def rms_norm(x, w, eps):
+    x = _c(x, np.float32)
+    out = np.empty_like(x)
+    lib().or_rms_norm_into(out, x, _c(w, np.float32), x.size, eps)
+    return out
+
+
+def rope_head(x, pos, freq_base, sections=None):
+    x = _c(x, np.float32).copy()
+    if sections is None:
+        sections = np.array([x.size // 2, 0, 0, 0], np.int32)
+    lib().or_rope_multi(x, x.size, pos, _c(sections, np.int32), freq_base)
+    return x
+
+
+def argmax(logits) -> int:
+    logits = _c(logits, np.float32)
+    return int(lib().or_argmax(logits, logits.size))
+
+
+def silu(v: float) -> float:
+    return float(lib().or_silu(v))
+
+
+# --- decoder ----------------------------------------------------------------
+
+class _OrModel(C.Structure):
+    _fields_ = [
+        ("n_layer", i64), ("n_embd", i64), ("n_ff", i64), ("n_head", i64), ("n_head_kv", i64),
+        ("head_dim", i64), ("vocab", i64), ("max_seq", i64),
+        ("rope_base", C.c_float), ("eps", C.c_float),
+        ("tok_embd", C.c_void_p), ("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("out_norm", C.c_void_p),
+        ("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
+        ("wg", C.c_void_p), ("wu", C.c_void_p), ("wd", C.c_void_p),
+        ("lm_head", C.c_void_p), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p),
+    ]
+
+
+class OracleModel:
+    """Host-side decoder oracle over Q4_0 blocks (inference/mod.rs:333-545).
+
+    `weights` is a dict with numpy arrays: tok_embd/attn_norm/ffn_norm/out_norm
+    (uint16 f16 bits) and per-layer lists wq..wd plus lm_head (uint8 Q4_0 blocks).
+    """
+
+    def __init__(self, cfg: dict, weights: dict, max_seq: int):
+        self.cfg = cfg
+        self._keep = []
+        L = cfg["n_layer"]
+
+        def ptr(a):
+            a = np.ascontiguousarray(a)
+            self._keep.append(a)
+            return a.ctypes.data
+
+        def ptrs(lst):
+            arr = (C.c_void_p * L)(*[ptr(a) for a in lst])
+            self._keep.append(arr)
+            return C.cast(arr, C.c_void_p).value
+
+        hd = cfg["head_dim"]
+        self.k_cache = np.zeros((L, cfg["n_head_kv"], max_seq, hd), np.uint16)
+        self.v_cache = np.zeros_like(self.k_cache)
+        self.m = _OrModel(L, cfg["n_embd"], cfg["n_ff"], cfg["n_head"], cfg["n_head_kv"], hd, cfg["vocab"], max_seq,
+                          cfg["rope_base"], cfg["eps"],
+                          ptr(weights["tok_embd"]), ptr(weights["attn_norm"]), ptr(weights["ffn_norm"]),
+                          ptr(weights["out_norm"]),
+                          ptrs(weights["wq"]), ptrs(weights["wk"]), ptrs(weights["wv"]), ptrs(weights["wo"]),
+                          ptrs(weights["wg"]), ptrs(weights["wu"]), ptrs(weights["wd"]),
+                          ptr(weights["lm_head"]), self.k_cache.ctypes.data, self.v_cache.ctypes.data)
+
+    def forward(self, token: int, pos: int) -> np.ndarray:
+        logits = np.empty(self.cfg["vocab"], np.float32)
+        rc = lib().or_model_forward(C.addressof(self.m), token, pos, logits)
+        if rc != 0:
+            raise ValueError("oracle forward rejected token/pos")
+        return logits
+
+
+# --- AVX-512 as-is (timing) -------------------------------------------------
+
+def avx_gemv_4bit_into(out, scales, packed, x, rows, cols, nthreads):
+    lib().or_avx_gemv_4bit_into(out, scales, packed, x, rows, cols, 32, nthreads)
+
+
+def avx_f16_bytes_to_f32(src_u8, out):
+    return lib().or_avx_f16_bytes_to_f32(src_u8, src_u8.size, out)
