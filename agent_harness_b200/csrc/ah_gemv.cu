@@ -250,11 +250,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
   uint8_t* xs = smem;
   float* red = reinterpret_cast<float*>(smem + (size_t)2 * B * plane);  // [warps][16][B]
   float* fin = red + kGemvWarps * 16 * B;                               // [16][B]
-  float* tok_down = fin + 16 * B;                                       // 2^-s per token
-  float* tok_up = tok_down + kGemvMaxBatch;                             // 2^s
-  float* tok_inv = tok_up + kGemvMaxBatch;                              // RMSNorm 1/rms
-  float* wred = tok_inv + kGemvMaxBatch;                                // [warps][2*BM]
-  int* flag = reinterpret_cast<int*>(wred + kGemvWarps * 2 * BM);
+  float* tok_inv = fin + 16 * B;                                        // RMSNorm 1/rms per token
+  float* exps = tok_inv + kGemvMaxBatch;                                // [B][kbc] 2^-s per block
+  float* wred = exps + B * kbc;                                         // [warps][BM]
+  int* flag = reinterpret_cast<int*>(wred + kGemvWarps * BM);
 
   const int64_t npairs = pe - pb;
   const int64_t per_warp = (npairs + kGemvWarps - 1) / kGemvWarps;
@@ -274,74 +273,97 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
     }
   pdl_wait();
 
-  // ---- prologue: per-token statistics ------------------------------------
+  // ---- prologue ------------------------------------------------------------
   const int64_t K = a.w.cols;
   const int64_t k0 = pb * 64, k1 = min(pe * 64, K);
-  {
-    float ss[BM], am[BM];
-#pragma unroll
-    for (int b = 0; b < BM; ++b) { ss[b] = 0.0f; am[b] = 0.0f; }
-    if (PRO == kProRmsNorm) {
-      for (int64_t k = tid; k < K; k += kGemvThreads) {
-        const float nw = __half2float(__ushort_as_half(a.norm_w[k]));
-        const bool in = k >= k0 && k < k1;
-#pragma unroll
-        for (int b = 0; b < BM; ++b)
-          if (b < B) {
-            const float v = a.x[b * a.x_stride + k];
-            ss[b] = fmaf(v, v, ss[b]);
-            if (in) am[b] = fmaxf(am[b], fabsf(v * nw));
-          }
-      }
-    } else {
-      for (int64_t k = k0 + tid; k < k1; k += kGemvThreads)
-#pragma unroll
-        for (int b = 0; b < BM; ++b)
-          if (b < B) am[b] = fmaxf(am[b], fabsf(a.x[b * a.x_stride + k]));
-    }
+  if (PRO == kProRmsNorm) {
+    // RMSNorm statistics (inference/math.rs:53-63) from the producer's
+    // per-tile partial sums of squares of x.
+    float ss[BM];
 #pragma unroll
     for (int b = 0; b < BM; ++b) {
+      ss[b] = 0.0f;
+      if (b < B)
+        for (int i = tid; i < a.n_ss_in; i += kGemvThreads) ss[b] += a.ss_in[b * a.n_ss_in + i];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        ss[b] += __shfl_xor_sync(0xFFFFFFFFu, ss[b], o);
-        am[b] = fmaxf(am[b], __shfl_xor_sync(0xFFFFFFFFu, am[b], o));
-      }
+      for (int o = 16; o > 0; o >>= 1) ss[b] += __shfl_xor_sync(0xFFFFFFFFu, ss[b], o);
     }
     if (lane == 0)
 #pragma unroll
-      for (int b = 0; b < BM; ++b) { wred[warp * 2 * BM + b] = ss[b]; wred[warp * 2 * BM + BM + b] = am[b]; }
+      for (int b = 0; b < BM; ++b) wred[warp * BM + b] = ss[b];
     __syncthreads();
     if (tid < B) {
-      float s_tot = 0.0f, m = 0.0f;
-      for (int w = 0; w < kGemvWarps; ++w) { s_tot += wred[w * 2 * BM + tid]; m = fmaxf(m, wred[w * 2 * BM + BM + tid]); }
-      float inv = 1.0f;
-      if (PRO == kProRmsNorm) inv = __fdiv_rn(1.0f, sqrtf(__fdiv_rn(s_tot, (float)K) + a.eps));
-      m *= inv;
-      int s = 0;
-      if (m > 0.0f && m <= 3.0e38f) s = min(max(14 - ilogbf(m), -120), 120);
-      tok_inv[tid] = inv;
-      tok_up[tid] = ldexpf(1.0f, s);
-      tok_down[tid] = ldexpf(1.0f, -s);
+      float s_tot = 0.0f;
+      for (int w = 0; w < kGemvWarps; ++w) s_tot += wred[w * BM + tid];
+      tok_inv[tid] = __fdiv_rn(1.0f, sqrtf(__fdiv_rn(s_tot, (float)K) + a.eps));
     }
     __syncthreads();
   }
-  // ---- split x (scaled by 2^s) into f16 hi/lo planes ------------------------
+  // ---- split x into f16 hi/lo planes, one power-of-two scale per (token, block) --
+  // Eight threads share a 32-column block; each loads 4 values (one 16-byte
+  // load), four blocks per thread are in flight per round.
   {
-    const int span = kbc * 32;
-    for (int idx = tid; idx < B * span; idx += kGemvThreads) {
-      const int b = idx / span, kk = idx - b * span;
-      const int64_t k = k0 + kk;
-      float v = 0.0f;
-      if (k < k1) {
-        v = a.x[b * a.x_stride + k];
-        if (PRO == kProRmsNorm) v = (v * tok_inv[b]) * __half2float(__ushort_as_half(a.norm_w[k]));
+    constexpr int UNR = 4;
+    const int tasks = B * kbc;
+    const int rounds = (tasks + 32 * UNR - 1) / (32 * UNR);
+    const int sub = tid & 7;
+    const bool vec_ok = ((a.x_stride & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0);
+    for (int r = 0; r < rounds; ++r) {
+      float4 v[UNR];
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int task = (r * UNR + u) * 32 + (tid >> 3);
+        v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (task < tasks) {
+          const int b = task / kbc, kb = task - b * kbc;
+          const int64_t k = k0 + (int64_t)kb * 32 + sub * 4;
+          const float* xr = a.x + b * a.x_stride;
+          if (vec_ok && k + 3 < k1) {
+            v[u] = __ldg(reinterpret_cast<const float4*>(xr + k));
+          } else {
+            if (k < k1) v[u].x = xr[k];
+            if (k + 1 < k1) v[u].y = xr[k + 1];
+            if (k + 2 < k1) v[u].z = xr[k + 2];
+            if (k + 3 < k1) v[u].w = xr[k + 3];
+          }
+        }
       }
-      v *= tok_up[b];
-      const __half hi = __float2half_rn(v);
-      const __half lo = __float2half_rn(v - __half2float(hi));
-      const int pos = xs_pos(kk);
-      reinterpret_cast<__half*>(xs + (2 * b) * plane)[pos] = hi;
-      reinterpret_cast<__half*>(xs + (2 * b + 1) * plane)[pos] = lo;
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int task = (r * UNR + u) * 32 + (tid >> 3);
+        const bool live = task < tasks;
+        const int b = live ? task / kbc : 0;
+        const int kb = live ? task - b * kbc : 0;
+        const int64_t k = k0 + (int64_t)kb * 32 + sub * 4;
+        float xv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+        if (PRO == kProRmsNorm && live) {
+          const float inv = tok_inv[b];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (k + i < k1) xv[i] = (xv[i] * inv) * __half2float(__ushort_as_half(a.norm_w[k + i]));
+        }
+        float m = fmaxf(fmaxf(fabsf(xv[0]), fabsf(xv[1])), fmaxf(fabsf(xv[2]), fabsf(xv[3])));
+        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
+        // scale so the block max lands in [2^14, 2^15): hi+lo then carry ~22 bits
+        const int eb = (int)((__float_as_uint(m) >> 23) & 0xFFu);
+        const int sc = (m == 0.0f) ? 0 : min(max(14 - (eb - 127), -120), 120);
+        const float up = __uint_as_float((uint32_t)(127 + sc) << 23);
+        if (live) {
+          __half* ph = reinterpret_cast<__half*>(xs + (2 * b) * plane);
+          __half* pl = reinterpret_cast<__half*>(xs + (2 * b + 1) * plane);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float sv = xv[i] * up;
+            const __half hi = __float2half_rn(sv);
+            const int pos = xs_pos(kb * 32 + sub * 4 + i);
+            ph[pos] = hi;
+            pl[pos] = __float2half_rn(sv - __half2float(hi));
+          }
+          if (sub == 0) exps[b * kbc + kb] = __uint_as_float((uint32_t)(127 - sc) << 23);
+        }
+      }
     }
   }
   __syncthreads();
@@ -375,13 +397,16 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
             const int col = 8 * j + g;
             uint4 bf = make_uint4(0u, 0u, 0u, 0u);
             if (col < 2 * B) bf = *reinterpret_cast<const uint4*>(xs + col * plane + (kb_rel + blk) * 64 + t * 16);
+            const int tok = 4 * j + t;  // this lane's accumulator columns 2t, 2t+1 = token tok (hi, lo)
+            const float ex = tok < B ? exps[tok * kbc + kb_rel + blk] : 0.0f;
             float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             mma16816(acc, a0, c0, a1, c1, bf.x, bf.y, acc);
             mma16816(acc, a2, c2, a3, c3, bf.z, bf.w, acc);
-            tot[j][0] = fmaf(dg, acc[0], tot[j][0]);
-            tot[j][1] = fmaf(dg, acc[1], tot[j][1]);
-            tot[j][2] = fmaf(dg8, acc[2], tot[j][2]);
-            tot[j][3] = fmaf(dg8, acc[3], tot[j][3]);
+            const float de = dg * ex, d8e = dg8 * ex;
+            tot[j][0] = fmaf(de, acc[0], tot[j][0]);
+            tot[j][1] = fmaf(de, acc[1], tot[j][1]);
+            tot[j][2] = fmaf(d8e, acc[2], tot[j][2]);
+            tot[j][3] = fmaf(d8e, acc[3], tot[j][3]);
           }
         }
       }
@@ -404,7 +429,6 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
     const int r = i / B, b = i - r * B;
     float v = 0.0f;
     for (int w = 0; w < kGemvWarps; ++w) v += red[(w * 16 + r) * B + b];
-    v *= tok_down[b];
     if (a.ksplit == 1) fin[i] = v;
     else a.partial[((int64_t)ky * rows_pad + rt * 16 + r) * B + b] = v;
   }
@@ -435,10 +459,22 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
     for (int i = tid; i < 16 * B; i += kGemvThreads) {
       const int r = i / B, b = i - r * B;
       const int64_t R = rt * 16 + r;
+      float h = 0.0f;
       if (R < a.w.rows) {
         float* dst = a.y + b * a.y_stride + R;
-        if (EPI == kEpiAdd) *dst = *dst + fin[i];
-        else *dst = fin[i];
+        h = (EPI == kEpiAdd) ? *dst + fin[i] : fin[i];  // residual: hidden[i] += out[i]
+        *dst = h;
+      }
+      if (a.ss_out) fin[i] = h;
+    }
+    if (a.ss_out) {
+      // per-tile partial sum of squares of the new values, for the next
+      // kernel's RMSNorm prologue
+      __syncthreads();
+      if (tid < B) {
+        float s2 = 0.0f;
+        for (int r = 0; r < 16; ++r) s2 = fmaf(fin[r * B + tid], fin[r * B + tid], s2);
+        a.ss_out[tid * a.w.r16 + rt] = s2;
       }
     }
   }
@@ -471,8 +507,8 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch) {
   p.ksplit = (int)((w.kp + ppc - 1) / ppc);
   p.pairs_per_chunk = (w.kp + p.ksplit - 1) / p.ksplit;
   const int64_t plane = 2 * p.pairs_per_chunk * 64 + 64;
-  p.smem = (size_t)2 * batch * plane + (size_t)(kGemvWarps * 16 * batch + 16 * batch + 3 * kGemvMaxBatch) * 4 +
-           (size_t)kGemvWarps * 2 * (4 * p.nt) * 4 + 16;
+  p.smem = (size_t)2 * batch * plane + (size_t)(kGemvWarps * 16 * batch + 16 * batch + kGemvMaxBatch) * 4 +
+           (size_t)batch * (2 * p.pairs_per_chunk) * 4 + (size_t)kGemvWarps * (4 * p.nt) * 4 + 16;
   return p;
 }
 
@@ -511,7 +547,8 @@ void gemv_workspace_free(GemvWorkspace& ws) {
 
 int gemv_launch(GemvArgs a, int pro, int epi, GemvWorkspace& ws, cudaStream_t st, bool pdl) {
   AH_REQUIRE(a.batch >= 1 && a.batch <= kGemvMaxBatch, "gemv: batch must be 1..16");
-  AH_REQUIRE(pro != kProRmsNorm || a.norm_w != nullptr, "gemv: RMSNorm prologue needs a norm weight");
+  AH_REQUIRE(pro != kProRmsNorm || (a.norm_w != nullptr && a.ss_in != nullptr && a.n_ss_in > 0),
+             "gemv: RMSNorm prologue needs a norm weight and the producer's partial sums of squares");
   AH_REQUIRE(epi != kEpiSwiglu || a.w.rows % 16 == 0, "gemv: SwiGLU epilogue needs interleaved rows %% 16 == 0");
   const GemvPlan plan = gemv_plan(a.w, a.batch);
   if (plan.ksplit > 1) {

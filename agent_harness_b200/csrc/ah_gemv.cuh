@@ -13,11 +13,12 @@
 // Scales sit in their own plane, 8 entries per (rt,kp): entry g holds
 // {d(2kp,g), d(2kp,g+8), d(2kp+1,g), d(2kp+1,g+8)} as f16 (Q4_0) or f32 (engine).
 //
-// The activation x is scaled by 2^s (per token, so its max |x| lands in
-// [2^14, 2^15)) and split into two f16 planes hi + lo that together carry ~22
-// significant bits; the tensor core then forms sum_j (q_j-8) * x_j with f32
-// accumulation over each 32-element block, and the block scale d (times 2^-s)
-// is applied in f32.  Dequantised weights never leave registers.
+// The activation x is scaled by 2^s per (token, 32-column block) so that the
+// block's max |x| lands in [2^14, 2^15), and split into two f16 planes hi + lo
+// that together carry ~22 significant bits; the tensor core then forms
+// sum_j (q_j-8) * x_j with f32 accumulation over each 32-element block, and
+// the block scale d (times 2^-s) is applied in f32.  Dequantised weights never
+// leave registers.
 #pragma once
 
 #include "ah_common.cuh"
@@ -48,9 +49,15 @@ struct GemvArgs {
   float* y;                // [batch][y_stride] f32
   int64_t y_stride;
   int batch;
-  // prologue: RMSNorm of x with f16 weight, eps (inference/math.rs:53-63)
+  // prologue: RMSNorm of x with f16 weight, eps (inference/math.rs:53-63);
+  // ss_in holds the producer's partial sums of squares of x, [batch][n_ss_in]
   const uint16_t* norm_w;
   float eps;
+  const float* ss_in;
+  int n_ss_in;
+  // epilogue: optional per-16-row-tile partial sums of squares of the values
+  // written, [batch][r16] (feeds the next kernel's RMSNorm prologue)
+  float* ss_out;
   // k-split: each CTA covers pairs [ky*pairs_per_chunk, ...) of its tile row
   int64_t pairs_per_chunk;
   int ksplit;
@@ -110,7 +117,7 @@ __device__ __forceinline__ void unpack_word(uint32_t w, uint32_t& p0, uint32_t& 
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1, const float (&c)[4]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%11,%12,%13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
