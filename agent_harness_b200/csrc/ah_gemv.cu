@@ -21,7 +21,6 @@ struct AhQ4Weight {
   int64_t weight_bytes = 0;
   void* nib_alloc = nullptr;
   void* scale_alloc = nullptr;
-  GemvWorkspace ws;  // lazily sized k-split workspace for ah_q4w_gemv
   std::mutex mu;
 };
 
@@ -91,7 +90,7 @@ __global__ void __launch_bounds__(kThreads) k_repack(uint4* __restrict__ nib, vo
       }
 #pragma unroll
       for (int pp = 0; pp < 8; ++pp) {
-        const int e = 2 * t + 8 * (pp & 3) + (pp >> 2);
+        const int e = 2 * t + (pp >> 2) + 16 * (pp & 1) + 8 * ((pp >> 1) & 1);
         uint32_t q = 8;  // padding: weight (8-8)*d = 0
         if (live_row && b * 32 + e < cols) {
           if (kEngine) {
@@ -196,7 +195,6 @@ const Q4Tiled& q4w_tiled(const AhQ4Weight* w) { return w->t; }
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr int kXsBudget = 96 * 1024;  // shared memory for the split-x planes
 
 template <bool kF32>
 struct ScaleT;
@@ -225,14 +223,71 @@ __device__ __forceinline__ float silu_ref(float x) {  // inference/math.rs:83-95
   return x * sg;
 }
 
-// Position of chunk-relative column kk inside an x plane (halves): the 8
-// values lane t needs for one 32-column block are contiguous (one LDS.128).
-__device__ __forceinline__ int xs_pos(int kk) {
-  const int e = kk & 31;
-  return (kk >> 5) * 32 + ((e >> 1) & 3) * 8 + 2 * ((e >> 3) & 3) + (e & 1);
+// ---------------------------------------------------------------------------
+// The fused GEMV.  A thread-block cluster of kGemvCluster CTAs covers one row
+// group of kGemvWarps 16-row tiles (128 rows) over the full K; cluster CTA c
+// takes K-chunk c (ppc = ceil(kp/8) block pairs).  Each CTA splits its own chunk
+// of x into shared memory and its warp w multiplies row tile w against it, so
+// the main loop reads only local shared memory; weights stream HBM ->
+// registers, prefetched before the kernel waits on its predecessor.  The chunk
+// partials of row tile r meet in cluster CTA r, which sums them over DSMEM in
+// chunk order (deterministic; no global scratch, fences or atomics) and runs the
+// epilogue.
+// ---------------------------------------------------------------------------
+template <bool kF32>
+__device__ __forceinline__ void load_pairs(uint4 (&w)[kGemvU], typename ScaleT<kF32>::V (&sv)[kGemvU],
+                                           const uint4* nibp, const typename ScaleT<kF32>::V* sclp, int p, int np) {
+#pragma unroll
+  for (int u = 0; u < kGemvU; ++u)
+    if (p + u < np) {
+      w[u] = ldg_stream_v4(nibp + (p + u) * 32);
+      sv[u] = ScaleT<kF32>::load(sclp + (p + u) * 8);
+    }
 }
 
-template <int NT, bool kF32, int PRO, int EPI, int U>
+template <int NT, bool kF32>
+__device__ __forceinline__ void mma_pairs(float (&tot)[NT][4], const uint4 (&w)[kGemvU],
+                                          const typename ScaleT<kF32>::V (&sv)[kGemvU], int p, int np, int B,
+                                          int g, int t, const uint8_t* xs, const float4* blk_info, int plane,
+                                          int kbc) {
+#pragma unroll
+  for (int u = 0; u < kGemvU; ++u) {
+    if (p + u < np) {
+#pragma unroll
+      for (int blk = 0; blk < 2; ++blk) {
+        // nibbles -> exact f16 subnormals n*2^-24 (k-step 0) and n*2^-20 (k-step 1)
+        const uint32_t w0 = blk ? w[u].z : w[u].x;  // row g
+        const uint32_t w8 = blk ? w[u].w : w[u].y;  // row g+8
+        const uint32_t w0s = w0 >> 8, w8s = w8 >> 8;
+        const uint32_t s0a0 = w0 & 0x000F000Fu, s0a1 = w8 & 0x000F000Fu;
+        const uint32_t s0a2 = w0s & 0x000F000Fu, s0a3 = w8s & 0x000F000Fu;
+        const uint32_t s1a0 = w0 & 0x00F000F0u, s1a1 = w8 & 0x00F000F0u;
+        const uint32_t s1a2 = w0s & 0x00F000F0u, s1a3 = w8s & 0x00F000F0u;
+        float dg, dg8;
+        ScaleT<kF32>::get(sv[u], blk, dg, dg8);
+        const int kb = 2 * (p + u) + blk;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const int col = 8 * j + g;
+          uint4 bf = make_uint4(0u, 0u, 0u, 0u);
+          if (col < 2 * B) bf = *reinterpret_cast<const uint4*>(xs + col * plane + kb * 64 + t * 16);
+          const int tok = 4 * j + t;  // accumulator columns 2t, 2t+1 = token tok (hi, lo)
+          const float4 bi = tok < B ? blk_info[tok * kbc + kb] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          float acc[4] = {bi.y, bi.z, bi.y, bi.z};  // -8 * sum(x) start value, rows g and g+8
+          mma16816(acc, s0a0, s0a1, s0a2, s0a3, bf.x, bf.y, acc);
+          mma16816(acc, s1a0, s1a1, s1a2, s1a3, bf.z, bf.w, acc);
+          const float de = dg * bi.x, d8e = dg8 * bi.x;
+          tot[j][0] = fmaf(de, acc[0], tot[j][0]);
+          tot[j][1] = fmaf(de, acc[1], tot[j][1]);
+          tot[j][2] = fmaf(d8e, acc[2], tot[j][2]);
+          tot[j][3] = fmaf(d8e, acc[3], tot[j][3]);
+        }
+      }
+    }
+  }
+}
+
+template <int NT, bool kF32, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
   constexpr int BM = 4 * NT;  // tokens this instantiation can hold
   using SV = typename ScaleT<kF32>::V;
@@ -240,45 +295,40 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int B = a.batch;
-  const int64_t rt = blockIdx.x;
-  const int ky = blockIdx.y;
+  const int crank = (int)cluster_ctarank();  // = K-chunk
+  const int64_t rg = blockIdx.x / kGemvCluster;
+  const int64_t rt = rg * kGemvWarps + warp;  // this warp's row tile
+  const bool warp_live = rt < a.w.r16;
   const int64_t KP = a.w.kp;
-  const int64_t pb = (int64_t)ky * a.pairs_per_chunk;
-  const int64_t pe = min(pb + a.pairs_per_chunk, KP);
-  const int kbc = (int)(2 * a.pairs_per_chunk);
+  const int ppc = (int)a.pairs_per_chunk;
+  const int kbc = 2 * ppc;          // blocks per chunk
   const int plane = kbc * 64 + 64;  // bytes per x plane (64 B pad staggers banks)
-  uint8_t* xs = smem;
-  float* red = reinterpret_cast<float*>(smem + (size_t)2 * B * plane);  // [warps][16][B]
-  float* fin = red + kGemvWarps * 16 * B;                               // [16][B]
-  float* tok_inv = fin + 16 * B;                                        // RMSNorm 1/rms per token
-  float* exps = tok_inv + kGemvMaxBatch;                                // [B][kbc] 2^-s per block
-  float* wred = exps + B * kbc;                                         // [warps][BM]
-  int* flag = reinterpret_cast<int*>(wred + kGemvWarps * BM);
+  uint8_t* xs = smem;                                                           // [2B][plane]
+  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc]
+  float* part = reinterpret_cast<float*>(blk_info + B * kbc);                   // [warps][16][B]
+  float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
+  float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
 
-  const int64_t npairs = pe - pb;
-  const int64_t per_warp = (npairs + kGemvWarps - 1) / kGemvWarps;
-  const int64_t wp0 = pb + warp * per_warp;
-  const int64_t wp1 = min(wp0 + per_warp, pe);
-  const uint4* nibp = a.w.nib + rt * KP * 32 + lane;
-  const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + rt * KP * 8 + g;
-
-  // Weights do not depend on the previous kernel: start streaming them now.
-  uint4 wv[U];
-  SV sv[U];
-#pragma unroll
-  for (int u = 0; u < U; ++u)
-    if (wp0 + u < wp1) {
-      wv[u] = ldg_stream_v4(nibp + (wp0 + u) * 32);
-      sv[u] = ScaleT<kF32>::load(sclp + (wp0 + u) * 8);
-    }
+  // Weights do not depend on the previous kernel: start streaming them now
+  // (two batches of kGemvU pairs in flight per lane).
+  const int64_t p0 = (int64_t)crank * ppc;
+  const int np = (int)max((int64_t)0, min(p0 + ppc, KP) - p0);
+  const uint4* nibp = a.w.nib + (rt * KP + p0) * 32 + lane;
+  const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + (rt * KP + p0) * 8 + g;
+  uint4 wa[kGemvU], wb[kGemvU];
+  SV sa[kGemvU], sb[kGemvU];
+  if (warp_live) {
+    load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
+    load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+  }
+  // A grid resident in one wave lets the next kernel launch now, so its weight
+  // prefetch overlaps this kernel; larger grids trigger after the main loop.
+  if (a.early_trigger) pdl_launch_dependents();
   pdl_wait();
 
-  // ---- prologue ------------------------------------------------------------
+  // ---- prologue: RMSNorm statistics from the producer's partial sums ----------
   const int64_t K = a.w.cols;
-  const int64_t k0 = pb * 64, k1 = min(pe * 64, K);
   if (PRO == kProRmsNorm) {
-    // RMSNorm statistics (inference/math.rs:53-63) from the producer's
-    // per-tile partial sums of squares of x.
     float ss[BM];
 #pragma unroll
     for (int b = 0; b < BM; ++b) {
@@ -295,20 +345,29 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
     if (tid < B) {
       float s_tot = 0.0f;
       for (int w = 0; w < kGemvWarps; ++w) s_tot += wred[w * BM + tid];
-      tok_inv[tid] = __fdiv_rn(1.0f, sqrtf(__fdiv_rn(s_tot, (float)K) + a.eps));
+      tok_inv[tid] = __fdiv_rn(1.0f, sqrtf(__fdiv_rn(s_tot, (float)K) + a.eps));  // inference/math.rs:59
     }
     __syncthreads();
   }
-  // ---- split x into f16 hi/lo planes, one power-of-two scale per (token, block) --
-  // Eight threads share a 32-column block; each loads 4 values (one 16-byte
-  // load), four blocks per thread are in flight per round.
+  // ---- split this CTA's K-chunk of x into f16 hi/lo planes ------------------------
+  // Eight threads share a (token, 32-column block) task; each loads 4 values.
+  // Per block this also records {2^(24-s), -8*2^-24*sum(hi), -8*2^-24*sum(lo)}:
+  // the exponent that undoes the power-of-two scaling and the accumulator start
+  // value that applies the -8 nibble offset inside the tensor core.
   {
-    constexpr int UNR = 4;
+    const int64_t k0 = p0 * 64, k1 = min(k0 + (int64_t)ppc * 64, K);
+    constexpr int UNR = 2;
     const int tasks = B * kbc;
     const int rounds = (tasks + 32 * UNR - 1) / (32 * UNR);
     const int sub = tid & 7;
+    const int e0 = sub * 4;                  // this thread's first column in the block
+    const int stp = e0 >> 4, reg = (e0 & 15) >> 3;
+    const int tA = ((e0 & 15) >> 1) & 3;     // fragment owner of values 0,1 (values 2,3: tA+1)
+    const int halfA = tA * 4 + stp * 2 + reg;  // half2 index of values 0,1 within the block
+    const float pre = stp ? 0.0625f : 1.0f;  // k-step-1 columns meet A values 16x larger
     const bool vec_ok = ((a.x_stride & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0);
     for (int r = 0; r < rounds; ++r) {
+      if ((r * UNR) * 32 + warp * 4 >= tasks) break;  // warp-uniform: nothing left for this warp
       float4 v[UNR];
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
@@ -316,7 +375,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
         v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (task < tasks) {
           const int b = task / kbc, kb = task - b * kbc;
-          const int64_t k = k0 + (int64_t)kb * 32 + sub * 4;
+          const int64_t k = k0 + (int64_t)kb * 32 + e0;
           const float* xr = a.x + b * a.x_stride;
           if (vec_ok && k + 3 < k1) {
             v[u] = __ldg(reinterpret_cast<const float4*>(xr + k));
@@ -330,13 +389,13 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
       }
 #pragma unroll
       for (int u = 0; u < UNR; ++u) {
+        if ((r * UNR + u) * 32 + warp * 4 >= tasks) break;  // warp-uniform
         const int task = (r * UNR + u) * 32 + (tid >> 3);
-        const bool live = task < tasks;
-        const int b = live ? task / kbc : 0;
-        const int kb = live ? task - b * kbc : 0;
-        const int64_t k = k0 + (int64_t)kb * 32 + sub * 4;
+        const bool tl = task < tasks;
+        const int b = tl ? task / kbc : 0, kb = tl ? task - b * kbc : 0;
+        const int64_t k = k0 + (int64_t)kb * 32 + e0;
         float xv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-        if (PRO == kProRmsNorm && live) {
+        if (PRO == kProRmsNorm && tl) {
           const float inv = tok_inv[b];
 #pragma unroll
           for (int i = 0; i < 4; ++i)
@@ -348,152 +407,128 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
         m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
         // scale so the block max lands in [2^14, 2^15): hi+lo then carry ~22 bits
         const int eb = (int)((__float_as_uint(m) >> 23) & 0xFFu);
-        const int sc = (m == 0.0f) ? 0 : min(max(14 - (eb - 127), -120), 120);
-        const float up = __uint_as_float((uint32_t)(127 + sc) << 23);
-        if (live) {
-          __half* ph = reinterpret_cast<__half*>(xs + (2 * b) * plane);
-          __half* pl = reinterpret_cast<__half*>(xs + (2 * b + 1) * plane);
+        const int sc = (m == 0.0f) ? 0 : min(max(14 - (eb - 127), -100), 100);
+        const float up = __uint_as_float((uint32_t)(127 + sc) << 23) * pre;
+        const float2 s01 = make_float2(xv[0] * up, xv[1] * up), s23 = make_float2(xv[2] * up, xv[3] * up);
+        const __half2 h01 = __float22half2_rn(s01), h23 = __float22half2_rn(s23);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        const __half2 l01 = __float22half2_rn(make_float2(s01.x - f01.x, s01.y - f01.y));
+        const __half2 l23 = __float22half2_rn(make_float2(s23.x - f23.x, s23.y - f23.y));
+        const float2 g01 = __half22float2(l01), g23 = __half22float2(l23);
+        // threads 4..7 hold the k-step-1 columns, stored /16: their sums count 16x
+        const float wsum = stp ? 16.0f : 1.0f;
+        float shi = ((f01.x + f01.y) + (f23.x + f23.y)) * wsum;
+        float slo = ((g01.x + g01.y) + (g23.x + g23.y)) * wsum;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float sv = xv[i] * up;
-            const __half hi = __float2half_rn(sv);
-            const int pos = xs_pos(kb * 32 + sub * 4 + i);
-            ph[pos] = hi;
-            pl[pos] = __float2half_rn(sv - __half2float(hi));
+        for (int o = 1; o < 8; o <<= 1) {
+          shi += __shfl_xor_sync(0xFFFFFFFFu, shi, o);
+          slo += __shfl_xor_sync(0xFFFFFFFFu, slo, o);
+        }
+        if (tl) {
+          __half2* ph = reinterpret_cast<__half2*>(xs + (2 * b) * plane) + kb * 16 + halfA;
+          __half2* pl = reinterpret_cast<__half2*>(xs + (2 * b + 1) * plane) + kb * 16 + halfA;
+          ph[0] = h01;
+          ph[4] = h23;
+          pl[0] = l01;
+          pl[4] = l23;
+          if (sub == 0) {
+            const float c = -8.0f * 5.9604644775390625e-8f;  // -8 * 2^-24
+            blk_info[b * kbc + kb] = make_float4(__uint_as_float((uint32_t)(127 + 24 - sc) << 23), c * shi, c * slo,
+                                                 0.0f);
           }
-          if (sub == 0) exps[b * kbc + kb] = __uint_as_float((uint32_t)(127 - sc) << 23);
         }
       }
     }
   }
   __syncthreads();
 
-  // ---- main loop: stream weights, unpack to f16 fragments, mma -----------------
+  // ---- main loop: row tile `warp` x this CTA's K-chunk, all local -----------------
   float tot[NT][4];
 #pragma unroll
   for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
-  for (int64_t p = wp0; p < wp1; p += U) {
-    if (p != wp0) {
-#pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (p + u < wp1) {
-          wv[u] = ldg_stream_v4(nibp + (p + u) * 32);
-          sv[u] = ScaleT<kF32>::load(sclp + (p + u) * 8);
-        }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      if (p + u < wp1) {
-        const int kb_rel = (int)(2 * (p + u - pb));
-#pragma unroll
-        for (int blk = 0; blk < 2; ++blk) {
-          uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
-          unpack_word(blk ? wv[u].z : wv[u].x, a0, a1, a2, a3);  // row g
-          unpack_word(blk ? wv[u].w : wv[u].y, c0, c1, c2, c3);  // row g+8
-          float dg, dg8;
-          ScaleT<kF32>::get(sv[u], blk, dg, dg8);
-#pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            const int col = 8 * j + g;
-            uint4 bf = make_uint4(0u, 0u, 0u, 0u);
-            if (col < 2 * B) bf = *reinterpret_cast<const uint4*>(xs + col * plane + (kb_rel + blk) * 64 + t * 16);
-            const int tok = 4 * j + t;  // this lane's accumulator columns 2t, 2t+1 = token tok (hi, lo)
-            const float ex = tok < B ? exps[tok * kbc + kb_rel + blk] : 0.0f;
-            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            mma16816(acc, a0, c0, a1, c1, bf.x, bf.y, acc);
-            mma16816(acc, a2, c2, a3, c3, bf.z, bf.w, acc);
-            const float de = dg * ex, d8e = dg8 * ex;
-            tot[j][0] = fmaf(de, acc[0], tot[j][0]);
-            tot[j][1] = fmaf(de, acc[1], tot[j][1]);
-            tot[j][2] = fmaf(d8e, acc[2], tot[j][2]);
-            tot[j][3] = fmaf(d8e, acc[3], tot[j][3]);
-          }
-        }
-      }
+  if (warp_live) {
+    for (int p = 0; p < np; p += 2 * kGemvU) {
+      mma_pairs<NT, kF32>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc);
+      if (p + 2 * kGemvU < np) load_pairs<kF32>(wa, sa, nibp, sclp, p + 2 * kGemvU, np);
+      mma_pairs<NT, kF32>(tot, wb, sb, p + kGemvU, np, B, g, t, xs, blk_info, plane, kbc);
+      if (p + 3 * kGemvU < np) load_pairs<kF32>(wb, sb, nibp, sclp, p + 3 * kGemvU, np);
     }
   }
-  pdl_launch_dependents();
+  if (!a.early_trigger) pdl_launch_dependents();
 
-  // ---- epilogue: columns -> tokens, warps -> tile, chunks -> row ------------------
+  // ---- chunk partials -> cluster CTA `warp` over DSMEM ----------------------------
 #pragma unroll
   for (int j = 0; j < NT; ++j) {
-    const int b = 4 * j + t;
+    const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
     if (b < B) {
-      red[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
-      red[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
+      part[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
+      part[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
     }
   }
-  __syncthreads();
-  const int64_t rows_pad = a.w.r16 * 16;
-  for (int i = tid; i < 16 * B; i += kGemvThreads) {
-    const int r = i / B, b = i - r * B;
-    float v = 0.0f;
-    for (int w = 0; w < kGemvWarps; ++w) v += red[(w * 16 + r) * B + b];
-    if (a.ksplit == 1) fin[i] = v;
-    else a.partial[((int64_t)ky * rows_pad + rt * 16 + r) * B + b] = v;
-  }
-  if (a.ksplit > 1) {
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) *flag = (atomicAdd(&a.counters[rt], 1) == a.ksplit - 1);
-    __syncthreads();
-    if (!*flag) return;
-    __threadfence();
+  cluster_arrive();
+  cluster_wait();  // every CTA's partials are visible cluster-wide
+  const int64_t my_rt = rg * kGemvWarps + crank;  // the row tile this CTA finalises
+  const bool fin_live = my_rt < a.w.r16;
+  float* fin = wred;  // [16][B]
+  if (fin_live) {
+    // partial of chunk c for row tile `crank` sits at part[crank] in cluster CTA c
+    const uint32_t local = smem_u32(part + crank * 16 * B);
     for (int i = tid; i < 16 * B; i += kGemvThreads) {
-      const int r = i / B, b = i - r * B;
       float v = 0.0f;
-      for (int c = 0; c < a.ksplit; ++c) v += __ldcg(&a.partial[((int64_t)c * rows_pad + rt * 16 + r) * B + b]);
+#pragma unroll
+      for (int c = 0; c < kGemvCluster; ++c) v += ld_dsmem_f32(mapa_shared(local + i * 4, (uint32_t)c));
       fin[i] = v;
     }
-    if (tid == 0) a.counters[rt] = 0;
   }
+  cluster_arrive();  // this CTA's DSMEM reads are done
   __syncthreads();
-  if (EPI == kEpiSwiglu) {
-    // rows g < 8 of the tile are gate rows 8rt+g, rows g+8 the matching up rows.
-    for (int i = tid; i < 8 * B; i += kGemvThreads) {
-      const int r = i / B, b = i - r * B;
-      const int64_t o = rt * 8 + r;
-      if (o < a.w.rows / 2) a.y[b * a.y_stride + o] = silu_ref(fin[r * B + b]) * fin[(r + 8) * B + b];
-    }
-  } else {
-    for (int i = tid; i < 16 * B; i += kGemvThreads) {
-      const int r = i / B, b = i - r * B;
-      const int64_t R = rt * 16 + r;
-      float h = 0.0f;
-      if (R < a.w.rows) {
-        float* dst = a.y + b * a.y_stride + R;
-        h = (EPI == kEpiAdd) ? *dst + fin[i] : fin[i];  // residual: hidden[i] += out[i]
-        *dst = h;
+  if (fin_live) {
+    if (EPI == kEpiSwiglu) {
+      // tile rows r < 8 are gate rows 8rt+r, rows r+8 the matching up rows
+      for (int i = tid; i < 8 * B; i += kGemvThreads) {
+        const int r = i / B, b = i - r * B;
+        const int64_t o = my_rt * 8 + r;
+        if (o < a.w.rows / 2) a.y[b * a.y_stride + o] = silu_ref(fin[r * B + b]) * fin[(r + 8) * B + b];
       }
-      if (a.ss_out) fin[i] = h;
-    }
-    if (a.ss_out) {
-      // per-tile partial sum of squares of the new values, for the next
-      // kernel's RMSNorm prologue
-      __syncthreads();
-      if (tid < B) {
-        float s2 = 0.0f;
-        for (int r = 0; r < 16; ++r) s2 = fmaf(fin[r * B + tid], fin[r * B + tid], s2);
-        a.ss_out[tid * a.w.r16 + rt] = s2;
+    } else {
+      for (int i = tid; i < 16 * B; i += kGemvThreads) {
+        const int r = i / B, b = i - r * B;
+        const int64_t R = my_rt * 16 + r;
+        float h = 0.0f;
+        if (R < a.w.rows) {
+          float* d = a.y + b * a.y_stride + R;
+          h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
+          *d = h;
+        }
+        fin[i] = h;
+      }
+      if (a.ss_out) {
+        // per-tile partial sum of squares of the values written (next RMSNorm)
+        __syncthreads();
+        if (tid < B) {
+          float q = 0.0f;
+          for (int r = 0; r < 16; ++r) q = fmaf(fin[r * B + tid], fin[r * B + tid], q);
+          a.ss_out[tid * a.w.r16 + my_rt] = q;
+        }
       }
     }
   }
+  cluster_wait();  // no CTA leaves while another may still read its shared memory
 }
 
 using GemvKernel = void (*)(const GemvArgs);
 
 template <int NT>
 GemvKernel pick_kernel(bool f32s, int pro, int epi) {
-  constexpr int U = NT == 1 ? 8 : 4;
-  if (f32s) return (pro == kProPlain && epi == kEpiStore) ? k_gemv_q4<NT, true, kProPlain, kEpiStore, U> : nullptr;
+  if (f32s) return (pro == kProPlain && epi == kEpiStore) ? k_gemv_q4<NT, true, kProPlain, kEpiStore> : nullptr;
   if (pro == kProPlain) {
-    if (epi == kEpiStore) return k_gemv_q4<NT, false, kProPlain, kEpiStore, U>;
-    if (epi == kEpiAdd) return k_gemv_q4<NT, false, kProPlain, kEpiAdd, U>;
-    return k_gemv_q4<NT, false, kProPlain, kEpiSwiglu, U>;
+    if (epi == kEpiStore) return k_gemv_q4<NT, false, kProPlain, kEpiStore>;
+    if (epi == kEpiAdd) return k_gemv_q4<NT, false, kProPlain, kEpiAdd>;
+    return k_gemv_q4<NT, false, kProPlain, kEpiSwiglu>;
   }
-  if (epi == kEpiStore) return k_gemv_q4<NT, false, kProRmsNorm, kEpiStore, U>;
-  if (epi == kEpiAdd) return k_gemv_q4<NT, false, kProRmsNorm, kEpiAdd, U>;
-  return k_gemv_q4<NT, false, kProRmsNorm, kEpiSwiglu, U>;
+  if (epi == kEpiStore) return k_gemv_q4<NT, false, kProRmsNorm, kEpiStore>;
+  if (epi == kEpiAdd) return k_gemv_q4<NT, false, kProRmsNorm, kEpiAdd>;
+  return k_gemv_q4<NT, false, kProRmsNorm, kEpiSwiglu>;
 }
 
 }  // namespace
@@ -501,69 +536,26 @@ GemvKernel pick_kernel(bool f32s, int pro, int epi) {
 GemvPlan gemv_plan(const Q4Tiled& w, int batch) {
   GemvPlan p{};
   p.nt = (batch + 3) / 4;
-  int64_t max_kbc = ((int64_t)kXsBudget / (2 * batch) - 64) / 64;
-  int64_t ppc = std::max<int64_t>(1, max_kbc / 2);
-  ppc = std::min<int64_t>(ppc, w.kp);
-  p.ksplit = (int)((w.kp + ppc - 1) / ppc);
-  p.pairs_per_chunk = (w.kp + p.ksplit - 1) / p.ksplit;
-  const int64_t plane = 2 * p.pairs_per_chunk * 64 + 64;
-  p.smem = (size_t)2 * batch * plane + (size_t)(kGemvWarps * 16 * batch + 16 * batch + kGemvMaxBatch) * 4 +
-           (size_t)batch * (2 * p.pairs_per_chunk) * 4 + (size_t)kGemvWarps * (4 * p.nt) * 4 + 16;
+  p.pairs_per_chunk = (w.kp + kGemvCluster - 1) / kGemvCluster;  // one K-chunk per cluster CTA
+  p.ksplit = 1;
+  const int64_t kbc = 2 * p.pairs_per_chunk;
+  const int64_t plane = kbc * 64 + 64;
+  p.smem = (size_t)2 * batch * plane + (size_t)batch * kbc * 16 + (size_t)kGemvWarps * 16 * batch * 4 +
+           (size_t)kGemvMaxBatch * 4 + (size_t)kGemvWarps * (4 * p.nt) * 4 + (size_t)16 * batch * 4 + 16;
   return p;
 }
 
-int gemv_workspace_reserve(GemvWorkspace& ws, const Q4Tiled& w, const GemvPlan& plan, int batch) {
-  if (plan.ksplit <= 1) return AH_OK;
-  const size_t need = (size_t)plan.ksplit * w.r16 * 16 * batch;
-  if (ws.partial_floats < need) {
-    if (ws.partial) cudaFree(ws.partial);
-    ws.partial = nullptr;
-    ws.partial_floats = 0;
-    if (cudaMalloc(&ws.partial, need * sizeof(float)) != cudaSuccess) {
-      cudaGetLastError();
-      return fail(AH_ENOMEM, "gemv workspace: cudaMalloc of %zu floats failed", need);
-    }
-    ws.partial_floats = need;
-  }
-  if (ws.n_counters < w.r16) {
-    if (ws.counters) cudaFree(ws.counters);
-    ws.counters = nullptr;
-    ws.n_counters = 0;
-    if (cudaMalloc(&ws.counters, (size_t)w.r16 * sizeof(int)) != cudaSuccess) {
-      cudaGetLastError();
-      return fail(AH_ENOMEM, "gemv workspace: counter allocation failed");
-    }
-    AH_CUDA_TRY(cudaMemset(ws.counters, 0, (size_t)w.r16 * sizeof(int)));
-    ws.n_counters = w.r16;
-  }
-  return AH_OK;
-}
-
-void gemv_workspace_free(GemvWorkspace& ws) {
-  if (ws.partial) cudaFree(ws.partial);
-  if (ws.counters) cudaFree(ws.counters);
-  ws = GemvWorkspace{};
-}
-
-int gemv_launch(GemvArgs a, int pro, int epi, GemvWorkspace& ws, cudaStream_t st, bool pdl) {
+int gemv_launch(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   AH_REQUIRE(a.batch >= 1 && a.batch <= kGemvMaxBatch, "gemv: batch must be 1..16");
   AH_REQUIRE(pro != kProRmsNorm || (a.norm_w != nullptr && a.ss_in != nullptr && a.n_ss_in > 0),
              "gemv: RMSNorm prologue needs a norm weight and the producer's partial sums of squares");
+  AH_REQUIRE(a.x != nullptr && a.y != nullptr, "gemv: null activation or output");
   AH_REQUIRE(epi != kEpiSwiglu || a.w.rows % 16 == 0, "gemv: SwiGLU epilogue needs interleaved rows %% 16 == 0");
   const GemvPlan plan = gemv_plan(a.w, a.batch);
-  if (plan.ksplit > 1) {
-    if (ws.partial_floats < (size_t)plan.ksplit * a.w.r16 * 16 * a.batch || ws.n_counters < a.w.r16) {
-      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-      cudaStreamIsCapturing(st, &cs);
-      AH_REQUIRE(cs == cudaStreamCaptureStatusNone, "gemv: k-split workspace must be reserved before graph capture");
-      int rc = gemv_workspace_reserve(ws, a.w, plan, a.batch);
-      if (rc) return rc;
-    }
-  }
+  if (plan.smem > (size_t)kGemvSmemLimit)
+    return fail(AH_EUNSUPPORTED, "gemv: batch %d x %lld columns needs %zu B of shared memory per CTA (limit %d)",
+                a.batch, (long long)a.w.cols, plan.smem, kGemvSmemLimit);
   a.pairs_per_chunk = plan.pairs_per_chunk;
-  a.ksplit = plan.ksplit;
-  a.partial = ws.partial;
-  a.counters = ws.counters;
   GemvKernel kern = nullptr;
   switch (plan.nt) {
     case 1: kern = pick_kernel<1>(a.w.f32_scales, pro, epi); break;
@@ -593,16 +585,39 @@ int gemv_launch(GemvArgs a, int pro, int epi, GemvWorkspace& ws, cudaStream_t st
       done.push_back({{dev, (void*)kern}, plan.smem});
     }
   }
+  const int64_t n_clusters = (a.w.r16 + kGemvWarps - 1) / kGemvWarps;  // row groups
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)a.w.r16, (unsigned)plan.ksplit, 1);
+  cfg.gridDim = dim3((unsigned)(n_clusters * kGemvCluster), 1, 1);
   cfg.blockDim = dim3(kGemvThreads, 1, 1);
   cfg.dynamicSmemBytes = plan.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kGemvCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
+  {
+    static std::mutex mu;
+    static std::vector<std::pair<std::pair<int, void*>, std::pair<size_t, int>>> occ;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int max_clusters = -1;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto& e : occ)
+      if (e.first.first == dev && e.first.second == (void*)kern && e.second.first == plan.smem)
+        max_clusters = e.second.second;
+    if (max_clusters < 0) {
+      cudaLaunchConfig_t q = cfg;
+      q.numAttrs = 1;  // occupancy query: cluster shape only
+      AH_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_clusters, kern, &q));
+      occ.push_back({{dev, (void*)kern}, {plan.smem, max_clusters}});
+    }
+    a.early_trigger = n_clusters <= max_clusters ? 1 : 0;
+  }
   AH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
   return AH_OK;
 }
@@ -670,7 +685,6 @@ int ah_q4w_destroy(AhQ4Weight* w) {
   cudaSetDevice(w->device);
   cudaFree(w->nib_alloc);
   cudaFree(w->scale_alloc);
-  gemv_workspace_free(w->ws);
   cudaSetDevice(cur);
   delete w;
   return AH_OK;
@@ -685,10 +699,9 @@ int ah_q4w_shape(const AhQ4Weight* w, int64_t* rows, int64_t* cols) {
 
 int64_t ah_q4w_weight_bytes(const AhQ4Weight* w) { return w ? w->weight_bytes : 0; }
 
-int ah_q4w_gemv(const AhQ4Weight* wc, const float* x, float* y, int batch, void* stream) {
-  AH_REQUIRE(wc && x && y, "q4w_gemv: null argument");
+int ah_q4w_gemv(const AhQ4Weight* w, const float* x, float* y, int batch, void* stream) {
+  AH_REQUIRE(w && x && y, "q4w_gemv: null argument");
   AH_REQUIRE(batch >= 1 && batch <= kGemvMaxBatch, "q4w_gemv: batch must be 1..16");
-  AhQ4Weight* w = const_cast<AhQ4Weight*>(wc);
   GemvArgs a{};
   a.w = w->t;
   a.x = x;
@@ -696,8 +709,7 @@ int ah_q4w_gemv(const AhQ4Weight* wc, const float* x, float* y, int batch, void*
   a.y = y;
   a.y_stride = w->t.rows;
   a.batch = batch;
-  std::lock_guard<std::mutex> lk(w->mu);
-  return gemv_launch(a, kProPlain, kEpiStore, w->ws, as_stream(stream), true);
+  return gemv_launch(a, kProPlain, kEpiStore, as_stream(stream), true);
 }
 
 int ah_gemv_4bit_into(float* out, const float* scales, const uint8_t* packed, const float* x, int64_t rows,

@@ -258,7 +258,7 @@ def run_gpu(args):
         ms = float(t.item())
     launches = args.steps * N_COPIES
     per_launch_s = ms / 1e3 / launches
-    value = world * launches * GEMV_BYTES / (ms / 1e3) / 1e9
+    value = world * args.steps * N_COPIES * GEMV_BYTES / (ms / 1e3) / 1e9
     achieved = GEMV_BYTES / per_launch_s / 1e9
     peak, peak_kind = peaks()
 
@@ -313,7 +313,7 @@ def run_gpu(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": NCU_TRAFFIC_PER_LAUNCH,
-                         "kernel": "k_gemv_q4<1,false,0,0,8>", "bytes_per_launch": GEMV_BYTES,
+                         "kernel": "k_gemv_q4<1,false,0,0>", "bytes_per_launch": GEMV_BYTES,
                          "avg_launch_us": round(per_launch_s * 1e6, 4)},
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": N_COPIES * COLS * 4,
                     "d2h_bytes_per_step": N_COPIES * ROWS * 4,

@@ -137,7 +137,8 @@ AH_API int64_t ah_q4w_weight_bytes(const AhQ4Weight* w);
 /* Reference: inference/math.rs:255-295 gemv_4bit_into (batch 1) and its
  * token-by-token use in inference/mod.rs:411-538, batched to `batch` <= 16
  * tokens: y[b][r] = sum_j W[r][j] * x[b][j], f32 accumulate, dequantised
- * weights never written to memory.  x_dev: [batch][cols] f32, y_dev: [batch][rows]. */
+ * weights never written to memory.  x_dev: [batch][cols] f32, y_dev: [batch][rows].
+ */
 AH_API int ah_q4w_gemv(const AhQ4Weight* w, const float* x_dev, float* y_dev, int batch, void* stream);
 
 /* Reference: inference/math.rs:255-295 gemv_4bit_into on the engine format as

@@ -56,9 +56,9 @@ def test_ragged_shapes(cuda, oracle, rows, cols):
     assert relerr(y, ref) <= TOL
 
 
-def test_ksplit_large_batch_and_k(cuda, oracle):
-    # batch 16 at K = 14336 exceeds one CTA's x planes -> cross-CTA k-split with
-    # the arrival-counter reduction; run twice to check the counters reset.
+def test_large_batch_and_k(cuda, oracle):
+    # batch 16 at K = 14336: 28 block pairs per cluster CTA (register ping-pong
+    # over several batches); run twice (no state carried between calls).
     from agent_harness_b200 import kernels as K
     rows, cols, batch = 256, 14336, 16
     blocks, W = _q4_0_weight(K, rows, cols, 77, cuda)
