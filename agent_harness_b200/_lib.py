@@ -52,6 +52,16 @@ SIGNATURES = {
     "ah_q4w_gemv": (i32, [vp, vp, vp, i32, vp]),
     "ah_gemv_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, i64, vp]),
     "ah_matvec_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, vp]),
+    "ah_model_create": (i32, [vp, C.POINTER(vp)]),
+    "ah_model_destroy": (i32, [vp]),
+    "ah_model_load_tensor": (i32, [vp, i32, i32, vp, vp]),
+    "ah_model_init_random": (i32, [vp, u64, f32, f32, f32]),
+    "ah_model_tensor_seed": (u64, [u64, i32, i32]),
+    "ah_model_generate": (i32, [vp, vp, i32, i32, i32, vp, vp]),
+    "ah_model_reset": (i32, [vp, i32, vp]),
+    "ah_model_forward": (i32, [vp, vp, vp, vp]),
+    "ah_model_decode": (i32, [vp, i32, vp, vp]),
+    "ah_model_position": (i32, [vp, C.POINTER(i32)]),
     "ah_host_gemv_4bit_into": (i32, [vp, vp, vp, vp, sz, sz, sz]),
     "ah_host_dequant_layer": (i32, [vp, vp, vp, sz, sz]),
     "ah_host_quantize": (i32, [vp, sz, sz, vp, vp]),

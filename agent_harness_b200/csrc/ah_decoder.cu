@@ -1,0 +1,824 @@
+// ah_decoder.cu — the Llama-shaped decoder step (inference/mod.rs:333-545)
+// built from the fused GEMV plus three small kernels, replayed as CUDA graphs.
+//
+// One step for `batch` sequences at a shared position `pos` (device scalar):
+//   embed      hidden = f16->f32(token_embd[token]); partial sums of squares
+//   per layer  qkv   = Wqkv . RMSNorm(hidden)        (GEMV, RMSNorm prologue)
+//              attn  = GQA attention over the f16 KV cache, RoPE on q/k and
+//                      the KV append fused in (k_attention)
+//              hidden += Wo . attn                    (GEMV, residual epilogue)
+//              act   = silu(Wg . n) * (Wu . n), n = RMSNorm(hidden)
+//                                                     (GEMV, SwiGLU epilogue)
+//              hidden += Wd . act                     (GEMV, residual epilogue)
+//   head       logits = Wlm . RMSNorm(hidden); next = argmax(logits)
+//   advance    pos += 1 (and, while prefilling, the next prompt token)
+// RMSNorm statistics travel as per-16-row partial sums of squares written by
+// the kernel that produced `hidden` (embed or a residual epilogue).
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "ah_gemv_impl.cuh"
+
+using namespace ah;
+
+namespace ah {
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kAttnSplits = 64;     // context splits per (sequence, kv head)
+constexpr int kAttnMaxChunk = 128;  // positions per split staged in shared memory
+constexpr int kArgmaxChunks = 64;
+
+struct AttnArgs {
+  const float* qkv;       // [B][dq + 2*dkv]
+  uint16_t* kc;           // [B][L][nkv][max_seq][hd]
+  uint16_t* vc;
+  const float2* rope;     // [max_seq][hd/2] (cos, sin)
+  const int* pos;         // device scalar: position of this step's token
+  float* part;            // [B][nkv][S][G][hd] partial sums, then [B][nkv][S][G][2] (max, sum)
+  int* cnt;               // [B][nkv]
+  float* out;             // [B][dq]
+  int* err;               // device error word (bounded waits)
+  int layer, n_layer, n_head, n_kv, hd, max_seq;
+  float scale;
+};
+
+inline size_t attn_smem_bytes(int G, int hd) {
+  return (size_t)2 * kAttnMaxChunk * hd * 2 +                       // K, V rows (f16)
+         sizeof(float) * ((size_t)G * hd + 2 * hd + (size_t)G * kAttnMaxChunk + 2 * G) + 16;
+}
+
+// grid (n_kv, kAttnSplits, B).  CTA (h, s, b) handles the G = n_head/n_kv query
+// heads of kv head h over context split s: its K and V rows arrive in shared
+// memory with two bulk (TMA) copies, the scores, softmax pieces and weighted V
+// are computed there, and the last CTA of (b, h) combines the splits.  Split 0
+// also appends this step's k (after RoPE) and v to the cache.  Follows
+// inference/mod.rs:469-502 with per-head RoPE (attention.rs:126-139).
+__global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t smraw[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
+  const int hd = a.hd, G = a.n_head / a.n_kv, half = hd / 2;
+  const int dq = a.n_head * hd, dkv = a.n_kv * hd;
+  uint16_t* Ks = reinterpret_cast<uint16_t*>(smraw);     // [chunk][hd]
+  uint16_t* Vs = Ks + kAttnMaxChunk * hd;                  // [chunk][hd]
+  float* q = reinterpret_cast<float*>(Vs + kAttnMaxChunk * hd);  // [G][hd] rotated queries
+  float* knew = q + G * hd;            // [hd] this step's k (rotated, f16-rounded)
+  float* vnew = knew + hd;             // [hd]
+  float* sc = vnew + hd;               // [G][kAttnMaxChunk] scores, then weights
+  float* red = sc + G * kAttnMaxChunk; // [G][2]
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int last;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int pos = *a.pos;
+  const int n_ctx = pos + 1;
+  // splits in use: at least 64 positions each (short contexts need few)
+  const int n_split = min(kAttnSplits, (n_ctx + 63) / 64);
+  if (s >= n_split) return;
+  const int chunk = (n_ctx + n_split - 1) / n_split;
+  const int p0 = min(s * chunk, n_ctx), p1 = min(p0 + chunk, n_ctx);
+  const int n = p1 - p0;
+  const int ncache = max(0, min(p1, pos) - p0);  // rows already in the cache
+  const size_t head_off = ((((size_t)b * a.n_layer + a.layer) * a.n_kv + h) * a.max_seq) * hd;
+  uint16_t* kh = a.kc + head_off;
+  uint16_t* vh = a.vc + head_off;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bar, (uint32_t)(2 * ncache * hd * 2));
+    if (ncache > 0) {
+      bulk_g2s(Ks, kh + (size_t)p0 * hd, (uint32_t)(ncache * hd * 2), &bar);
+      bulk_g2s(Vs, vh + (size_t)p0 * hd, (uint32_t)(ncache * hd * 2), &bar);
+    }
+  }
+  const float* row = a.qkv + (size_t)b * (dq + 2 * dkv);
+  const float2* cs = a.rope + (size_t)pos * half;
+  // RoPE on adjacent pairs (2i, 2i+1), theta_i = pos * base^(-i/half) (math.rs:119-151)
+  for (int i = tid; i < G * half; i += kAttnThreads) {
+    const int g = i / half, k = i - g * half;
+    const float x0 = row[(h * G + g) * hd + 2 * k], x1 = row[(h * G + g) * hd + 2 * k + 1];
+    const float2 c = cs[k];
+    q[g * hd + 2 * k] = x0 * c.x - x1 * c.y;
+    q[g * hd + 2 * k + 1] = x0 * c.y + x1 * c.x;
+  }
+  for (int k = tid; k < half; k += kAttnThreads) {
+    const float x0 = row[dq + h * hd + 2 * k], x1 = row[dq + h * hd + 2 * k + 1];
+    const float2 c = cs[k];
+    // the cache holds f16 (the decode configs' f16 KV); use the rounded values
+    knew[2 * k] = __half2float(__float2half_rn(x0 * c.x - x1 * c.y));
+    knew[2 * k + 1] = __half2float(__float2half_rn(x0 * c.y + x1 * c.x));
+  }
+  for (int d = tid; d < hd; d += kAttnThreads) vnew[d] = __half2float(__float2half_rn(row[dq + dkv + h * hd + d]));
+  __syncthreads();  // q/knew/vnew ready, barrier initialised
+  if (s == 0)
+    for (int d = tid; d < hd; d += kAttnThreads) {
+      kh[(size_t)pos * hd + d] = __half_as_ushort(__float2half_rn(knew[d]));
+      vh[(size_t)pos * hd + d] = __half_as_ushort(__float2half_rn(vnew[d]));
+    }
+  const bool ok = mbar_wait_bounded(&bar, 0, a.err, 0x401);
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) mbar_wait_bounded(&bar, 0, a.err, 0x402);  // let copies in flight land
+    return;
+  }
+  if (pos >= p0 && pos < p1)  // this step's row comes from registers, not the cache
+    for (int d = tid; d < hd; d += kAttnThreads) {
+      Ks[(pos - p0) * hd + d] = __half_as_ushort(__float2half_rn(knew[d]));
+      Vs[(pos - p0) * hd + d] = __half_as_ushort(__float2half_rn(vnew[d]));
+    }
+  __syncthreads();
+  // scores: one warp per position, lanes over head dims (hd = 32 * per_lane)
+  const int per_lane = hd / 32;
+  for (int i = warp; i < n; i += kAttnThreads / 32) {
+    float kv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const uint16_t* kr = Ks + i * hd + lane * per_lane;
+    for (int e = 0; e < per_lane; ++e) kv[e] = __half2float(__ushort_as_half(kr[e]));
+    for (int g = 0; g < G; ++g) {
+      float dot = 0.0f;
+      for (int e = 0; e < per_lane; ++e) dot = fmaf(q[g * hd + lane * per_lane + e], kv[e], dot);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
+      if (lane == 0) sc[g * kAttnMaxChunk + i] = dot * a.scale;
+    }
+  }
+  __syncthreads();
+  // softmax pieces per head: m = max, weights exp(s - m), l = sum
+  for (int g = warp; g < G; g += kAttnThreads / 32) {
+    float m = -INFINITY;
+    for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[g * kAttnMaxChunk + i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    float l = 0.0f;
+    for (int i = lane; i < n; i += 32) {
+      const float e = expf(sc[g * kAttnMaxChunk + i] - m);
+      sc[g * kAttnMaxChunk + i] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xFFFFFFFFu, l, o);
+    if (lane == 0) {
+      red[g * 2] = m;
+      red[g * 2 + 1] = l;
+    }
+  }
+  __syncthreads();
+  // weighted V: thread per head dim
+  const size_t bh = (size_t)b * a.n_kv + h;
+  float* pacc = a.part + ((bh * kAttnSplits + s) * G) * hd;                                   // [G][hd]
+  float* pml = a.part + (size_t)gridDim.z * a.n_kv * kAttnSplits * G * hd + (bh * kAttnSplits + s) * G * 2;
+  for (int d = tid; d < hd; d += kAttnThreads) {
+    float acc[8];
+    for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+    for (int i = 0; i < n; ++i) {
+      const float v = __half2float(__ushort_as_half(Vs[i * hd + d]));
+      for (int g = 0; g < G; ++g) acc[g] = fmaf(sc[g * kAttnMaxChunk + i], v, acc[g]);
+    }
+    for (int g = 0; g < G; ++g) pacc[g * hd + d] = acc[g];
+  }
+  if (tid < G) {
+    pml[tid * 2] = n > 0 ? red[tid * 2] : -INFINITY;
+    pml[tid * 2 + 1] = n > 0 ? red[tid * 2 + 1] : 0.0f;
+  }
+  // the last split to finish combines (deterministic split order)
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    last = atomicAdd(&a.cnt[bh], 1) == n_split - 1;
+    if (last) __threadfence();
+  }
+  __syncthreads();
+  if (!last) return;
+  const float* acc_base = a.part + (bh * kAttnSplits * G) * hd;
+  const float* ml_base = a.part + (size_t)gridDim.z * a.n_kv * kAttnSplits * G * hd + bh * kAttnSplits * G * 2;
+  // reuse sc: [G][S] split weights exp(m_s - M); red[g] = 1/L
+  float* fm = sc;
+  static_assert(kAttnMaxChunk >= kAttnSplits, "combine weights must fit in the score buffer");
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int t = 0; t < n_split; ++t) M = fmaxf(M, __ldcg(ml_base + (t * G + tid) * 2));
+    float L = 0.0f;
+    for (int t = 0; t < n_split; ++t) {
+      const float mt = __ldcg(ml_base + (t * G + tid) * 2);
+      const float f = (mt == -INFINITY) ? 0.0f : expf(mt - M);
+      fm[tid * kAttnSplits + t] = f;
+      L = fmaf(__ldcg(ml_base + (t * G + tid) * 2 + 1), f, L);
+    }
+    red[tid] = 1.0f / L;
+  }
+  __syncthreads();
+  for (int i4 = tid; i4 < G * hd / 4; i4 += kAttnThreads) {  // four consecutive head dims per thread
+    const int g = (i4 * 4) / hd;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+    for (int t = 0; t < n_split; ++t) {
+      const float f = fm[g * kAttnSplits + t];
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(acc_base + (size_t)t * G * hd) + i4);
+      acc.x = fmaf(v.x, f, acc.x);
+      acc.y = fmaf(v.y, f, acc.y);
+      acc.z = fmaf(v.z, f, acc.z);
+      acc.w = fmaf(v.w, f, acc.w);
+    }
+    const float inv = red[g];
+    float* o = a.out + (size_t)b * dq + (size_t)h * G * hd + i4 * 4;  // mod.rs:492-500
+    o[0] = acc.x * inv;
+    o[1] = acc.y * inv;
+    o[2] = acc.z * inv;
+    o[3] = acc.w * inv;
+  }
+  if (tid == 0) a.cnt[bh] = 0;
+}
+
+// hidden = f16 -> f32 (token_embd[token]) (mod.rs:392-397); ss partials per 16.
+// grid ((d + 255) / 256, B); d is a multiple of 16.
+__global__ void __launch_bounds__(256) k_embed(const uint16_t* __restrict__ emb, const int* __restrict__ tok,
+                                               float* __restrict__ hidden, float* __restrict__ ss, int d, int vocab) {
+  const int b = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool live = i < d;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = tok[b];
+  const int tv = (t >= 0 && t < vocab) ? t : 0;
+  const float v = live ? f16_bits_to_f32(emb[(size_t)tv * d + i]) : 0.0f;
+  if (live) hidden[(size_t)b * d + i] = v;
+  float q = v * v;
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
+  if (live && (i & 15) == 0) ss[(size_t)b * (d / 16) + i / 16] = q;
+}
+
+// Greedy next token per sequence (sampling.rs:4-14: the first strict maximum;
+// NaN never wins; all -inf or NaN gives 0).  grid (kArgmaxChunks, B).
+__global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits, int vocab, float* pv, int* pi,
+                                                int* cnt, int* tok, int* tok_log, const int* pos, int batch) {
+  const int b = blockIdx.y, c = blockIdx.x, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int chunk = (vocab + kArgmaxChunks - 1) / kArgmaxChunks;
+  const int i0 = c * chunk, i1 = min(i0 + chunk, vocab);
+  float bv = -INFINITY;
+  int bi = INT_MAX;
+  for (int i = i0 + tid; i < i1; i += 256) {
+    const float v = logits[(size_t)b * vocab + i];
+    if (v > bv) { bv = v; bi = i; }
+  }
+  __shared__ float sv[256];
+  __shared__ int si[256];
+  sv[tid] = bv;
+  si[tid] = bi;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (tid < o) {
+      const float v2 = sv[tid + o];
+      const int i2 = si[tid + o];
+      if (v2 > sv[tid] || (v2 == sv[tid] && i2 < si[tid])) { sv[tid] = v2; si[tid] = i2; }
+    }
+    __syncthreads();
+  }
+  __shared__ int last;
+  if (tid == 0) {
+    pv[b * kArgmaxChunks + c] = sv[0];
+    pi[b * kArgmaxChunks + c] = si[0];
+    __threadfence();
+    last = atomicAdd(&cnt[b], 1) == kArgmaxChunks - 1;
+    if (last) __threadfence();
+  }
+  __syncthreads();
+  if (!last || tid != 0) return;
+  float best = -INFINITY;
+  int besti = INT_MAX;
+  for (int k = 0; k < kArgmaxChunks; ++k) {
+    const float v = __ldcg(pv + b * kArgmaxChunks + k);
+    const int i = __ldcg(pi + b * kArgmaxChunks + k);
+    if (v > best || (v == best && i < besti)) { best = v; besti = i; }
+  }
+  const int next = (besti == INT_MAX) ? 0 : besti;
+  tok[b] = next;
+  tok_log[(size_t)(*pos) * batch + b] = next;
+  cnt[b] = 0;
+}
+
+// pos += 1; while prefilling, also load the next prompt token.
+__global__ void k_advance(int* pos, int* tok, const int* prompt, int n_prompt, int batch) {
+  pdl_wait();
+  const int p = *pos + 1;
+  if (threadIdx.x < batch && prompt != nullptr && p < n_prompt) tok[threadIdx.x] = prompt[threadIdx.x * n_prompt + p];
+  __syncthreads();
+  if (threadIdx.x == 0) *pos = p;
+}
+
+__global__ void k_rope_table(float2* t, int max_seq, int half, float base) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= max_seq * half) return;
+  const int p = i / half, k = i - p * half;
+  const float theta = (float)p * powf(base, -((float)k) / ((float)half));  // math.rs:139
+  float sn, cs;
+  sincosf(theta, &sn, &cs);
+  t[i] = make_float2(cs, sn);
+}
+
+template <typename... Args>
+int launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  AH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, args...));
+  return AH_OK;
+}
+
+}  // namespace
+}  // namespace ah
+
+// ---------------------------------------------------------------------------
+// Model object
+// ---------------------------------------------------------------------------
+struct AhModel {
+  AhModelConfig c{};
+  int device = 0;
+  int dq = 0, dkv = 0;
+  std::vector<AhQ4Weight*> wqkv, wo, wgu, wd;
+  AhQ4Weight* lm = nullptr;
+  std::vector<void*> pend[5];  // q, k, v, gate, up Q4_0 blocks awaiting fusion
+  uint16_t *tok_embd = nullptr, *attn_norm = nullptr, *ffn_norm = nullptr, *out_norm = nullptr;
+  uint16_t *kc = nullptr, *vc = nullptr;
+  float2* rope = nullptr;
+  float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr, *ss = nullptr;
+  float* att_part = nullptr;
+  int* att_cnt = nullptr;
+  float* am_v = nullptr;
+  int* am_i = nullptr;
+  int* am_cnt = nullptr;
+  int* d_pos = nullptr;
+  int* d_tok = nullptr;
+  int* d_prompt = nullptr;
+  int* tok_log = nullptr;  // [max_seq][max_batch]
+  int* err = nullptr;      // device error word
+  int batch = 1;
+  int pos = 0;
+  int n_prompt_dev = 0;
+  bool ready_checked = false;
+  cudaGraphExec_t g_step[2] = {nullptr, nullptr};  // [0] prefill step, [1] full step
+  int g_batch[2] = {0, 0};
+  const int* g_prompt[2] = {nullptr, nullptr};
+  int g_nprompt[2] = {0, 0};
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+int dalloc(AhModel* m, void** p, size_t bytes) {
+  if (cudaMalloc(p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    *p = nullptr;
+    return fail(AH_ENOMEM, "model: cudaMalloc of %zu bytes failed", bytes);
+  }
+  m->allocs.push_back(*p);
+  return AH_OK;
+}
+
+#define AH_TRY(expr)              \
+  do {                            \
+    int _rc = (expr);             \
+    if (_rc != AH_OK) return _rc; \
+  } while (0)
+
+int model_ready(AhModel* m) {
+  const int L = m->c.n_layer;
+  for (int l = 0; l < L; ++l)
+    if (!m->wqkv[l] || !m->wo[l] || !m->wgu[l] || !m->wd[l])
+      return fail(AH_EINVAL, "model: layer %d is missing projection weights", l);
+  if (!m->lm) return fail(AH_EINVAL, "model: output.weight not loaded");
+  return AH_OK;
+}
+
+GemvArgs gemv_args(const AhQ4Weight* w, const float* x, int64_t xs, float* y, int64_t ys, int batch) {
+  GemvArgs a{};
+  a.w = q4w_tiled(w);
+  a.x = x;
+  a.x_stride = xs;
+  a.y = y;
+  a.y_stride = ys;
+  a.batch = batch;
+  return a;
+}
+
+// Enqueues one decoder step (all layers; with_head adds LM head + argmax).
+int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cudaStream_t st) {
+  const AhModelConfig& c = m->c;
+  const int B = m->batch, d = c.n_embd;
+  AH_TRY(launch_pdl(k_embed, dim3((d + 255) / 256, B), dim3(256), 0, st, (const uint16_t*)m->tok_embd,
+                    (const int*)m->d_tok, m->hidden, m->ss, d, c.vocab_size));
+  const size_t attn_smem = attn_smem_bytes(c.n_head / c.n_head_kv, c.head_dim);
+  for (int l = 0; l < c.n_layer; ++l) {
+    GemvArgs q = gemv_args(m->wqkv[l], m->hidden, d, m->qkv, m->dq + 2 * m->dkv, B);
+    q.norm_w = m->attn_norm + (size_t)l * d;
+    q.eps = c.rms_eps;
+    q.ss_in = m->ss;
+    q.n_ss_in = d / 16;
+    AH_TRY(gemv_launch(q, kProRmsNorm, kEpiStore, st, true));
+    AttnArgs at{};
+    at.qkv = m->qkv;
+    at.kc = m->kc;
+    at.vc = m->vc;
+    at.rope = m->rope;
+    at.pos = m->d_pos;
+    at.part = m->att_part;
+    at.cnt = m->att_cnt;
+    at.out = m->attn;
+    at.layer = l;
+    at.n_layer = c.n_layer;
+    at.n_head = c.n_head;
+    at.n_kv = c.n_head_kv;
+    at.hd = c.head_dim;
+    at.max_seq = c.max_seq;
+    at.scale = 1.0f / sqrtf((float)c.head_dim);  // mod.rs:478
+    at.err = m->err;
+    AH_TRY(launch_pdl(k_attention, dim3(c.n_head_kv, kAttnSplits, B), dim3(kAttnThreads), attn_smem, st, at));
+    GemvArgs o = gemv_args(m->wo[l], m->attn, m->dq, m->hidden, d, B);
+    o.ss_out = m->ss;
+    AH_TRY(gemv_launch(o, kProPlain, kEpiAdd, st, true));
+    GemvArgs gu = gemv_args(m->wgu[l], m->hidden, d, m->act, c.n_ff, B);
+    gu.norm_w = m->ffn_norm + (size_t)l * d;
+    gu.eps = c.rms_eps;
+    gu.ss_in = m->ss;
+    gu.n_ss_in = d / 16;
+    AH_TRY(gemv_launch(gu, kProRmsNorm, kEpiSwiglu, st, true));
+    GemvArgs dn = gemv_args(m->wd[l], m->act, c.n_ff, m->hidden, d, B);
+    dn.ss_out = m->ss;
+    AH_TRY(gemv_launch(dn, kProPlain, kEpiAdd, st, true));
+  }
+  if (with_head) {
+    GemvArgs h = gemv_args(m->lm, m->hidden, d, m->logits, c.vocab_size, B);
+    h.norm_w = m->out_norm;
+    h.eps = c.rms_eps;
+    h.ss_in = m->ss;
+    h.n_ss_in = d / 16;
+    AH_TRY(gemv_launch(h, kProRmsNorm, kEpiStore, st, true));
+    AH_TRY(launch_pdl(k_argmax, dim3(kArgmaxChunks, B), dim3(256), 0, st, (const float*)m->logits, c.vocab_size,
+                      m->am_v, m->am_i, m->am_cnt, m->d_tok, m->tok_log, (const int*)m->d_pos, B));
+  }
+  AH_TRY(launch_pdl(k_advance, dim3(1), dim3(32), 0, st, m->d_pos, m->d_tok, prompt, n_prompt, B));
+  return AH_OK;
+}
+
+// Kernel attributes and occupancy are resolved before a capture starts.
+int prepare_step(AhModel* m) {
+  const AhModelConfig& c = m->c;
+  const int B = m->batch;
+  AH_TRY(gemv_prepare(q4w_tiled(m->lm), B, kProRmsNorm, kEpiStore));
+  AH_TRY(gemv_prepare(q4w_tiled(m->wqkv[0]), B, kProRmsNorm, kEpiStore));
+  AH_TRY(gemv_prepare(q4w_tiled(m->wo[0]), B, kProPlain, kEpiAdd));
+  AH_TRY(gemv_prepare(q4w_tiled(m->wgu[0]), B, kProRmsNorm, kEpiSwiglu));
+  AH_TRY(gemv_prepare(q4w_tiled(m->wd[0]), B, kProPlain, kEpiAdd));
+  const size_t attn_smem = attn_smem_bytes(c.n_head / c.n_head_kv, c.head_dim);
+  AH_CUDA_TRY(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem));
+  return AH_OK;
+}
+
+int run_step_graph(AhModel* m, int which, const int* prompt, int n_prompt, cudaStream_t st) {
+  if (!m->g_step[which] || m->g_batch[which] != m->batch || m->g_prompt[which] != prompt ||
+      m->g_nprompt[which] != n_prompt) {
+    AH_TRY(prepare_step(m));
+    if (m->g_step[which]) cudaGraphExecDestroy(m->g_step[which]);
+    m->g_step[which] = nullptr;
+    cudaStream_t cap;
+    AH_CUDA_TRY(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
+    cudaGraph_t g = nullptr;
+    AH_CUDA_TRY(cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_step(m, which == 1, prompt, n_prompt, cap);
+    cudaError_t e = cudaStreamEndCapture(cap, &g);
+    cudaStreamDestroy(cap);
+    if (rc != AH_OK) {
+      if (g) cudaGraphDestroy(g);
+      return rc;
+    }
+    if (e != cudaSuccess) return fail(AH_ECUDA, "model: step capture failed: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&m->g_step[which], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail(AH_ECUDA, "model: step graph instantiate: %s", cudaGetErrorString(e));
+    m->g_batch[which] = m->batch;
+    m->g_prompt[which] = prompt;
+    m->g_nprompt[which] = n_prompt;
+  }
+  AH_CUDA_TRY(cudaGraphLaunch(m->g_step[which], st));
+  m->pos += 1;
+  return AH_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+uint64_t ah_model_tensor_seed(uint64_t seed, int kind, int layer) {
+  return splitmix64(splitmix64(seed + 0x1000003ull * (uint64_t)(kind + 1)) + (uint64_t)layer);
+}
+
+int ah_model_create(const AhModelConfig* cfg, AhModel** out) {
+  AH_REQUIRE(cfg && out, "model_create: null argument");
+  *out = nullptr;
+  const AhModelConfig& c = *cfg;
+  AH_REQUIRE(c.n_layer > 0 && c.n_embd > 0 && c.n_ff > 0 && c.n_head > 0 && c.n_head_kv > 0 && c.head_dim > 0 &&
+                 c.vocab_size > 0 && c.max_seq > 0 && c.max_batch >= 1 && c.max_batch <= kGemvMaxBatch,
+             "model_create: non-positive dimension or batch outside 1..16");
+  AH_REQUIRE(c.n_embd % 64 == 0 && c.n_ff % 64 == 0 && (c.n_head * c.head_dim) % 64 == 0,
+             "model_create: n_embd, n_ff and n_head*head_dim must be multiples of 64");
+  AH_REQUIRE(c.n_head % c.n_head_kv == 0 && c.n_head / c.n_head_kv <= 8, "model_create: GQA group must divide, <= 8");
+  AH_REQUIRE(c.head_dim % 32 == 0 && c.head_dim <= 128, "model_create: head_dim must be 32, 64, 96 or 128");
+  AH_REQUIRE(c.max_seq <= kAttnSplits * kAttnMaxChunk, "model_create: max_seq above %d", kAttnSplits * kAttnMaxChunk);
+  AhModel* m = new (std::nothrow) AhModel();
+  if (!m) return fail(AH_ENOMEM, "model_create: host allocation");
+  m->c = c;
+  cudaGetDevice(&m->device);
+  m->dq = c.n_head * c.head_dim;
+  m->dkv = c.n_head_kv * c.head_dim;
+  const int L = c.n_layer, B = c.max_batch, d = c.n_embd;
+  m->wqkv.assign(L, nullptr);
+  m->wo.assign(L, nullptr);
+  m->wgu.assign(L, nullptr);
+  m->wd.assign(L, nullptr);
+  for (auto& p : m->pend) p.assign(L, nullptr);
+  int rc = AH_OK;
+  auto A = [&](void** p, size_t bytes) {
+    if (rc == AH_OK) rc = dalloc(m, p, bytes);
+  };
+  A((void**)&m->tok_embd, (size_t)c.vocab_size * d * 2);
+  A((void**)&m->attn_norm, (size_t)L * d * 2);
+  A((void**)&m->ffn_norm, (size_t)L * d * 2);
+  A((void**)&m->out_norm, (size_t)d * 2);
+  const size_t kv = (size_t)B * L * c.n_head_kv * c.max_seq * c.head_dim * 2;
+  A((void**)&m->kc, kv);
+  A((void**)&m->vc, kv);
+  A((void**)&m->rope, (size_t)c.max_seq * (c.head_dim / 2) * sizeof(float2));
+  A((void**)&m->hidden, (size_t)B * d * 4);
+  A((void**)&m->qkv, (size_t)B * (m->dq + 2 * m->dkv) * 4);
+  A((void**)&m->attn, (size_t)B * m->dq * 4);
+  A((void**)&m->act, (size_t)B * c.n_ff * 4);
+  A((void**)&m->logits, (size_t)B * c.vocab_size * 4);
+  A((void**)&m->ss, (size_t)B * (d / 16) * 4);
+  const int G = c.n_head / c.n_head_kv;
+  A((void**)&m->att_part, (size_t)B * c.n_head_kv * kAttnSplits * G * (c.head_dim + 2) * 4 + 16);
+  A((void**)&m->att_cnt, (size_t)B * c.n_head_kv * 4);
+  A((void**)&m->am_v, (size_t)B * kArgmaxChunks * 4);
+  A((void**)&m->am_i, (size_t)B * kArgmaxChunks * 4);
+  A((void**)&m->am_cnt, (size_t)B * 4);
+  A((void**)&m->d_pos, 16);
+  A((void**)&m->d_tok, (size_t)B * 4);
+  A((void**)&m->tok_log, (size_t)c.max_seq * B * 4);
+  if (rc == AH_OK) {
+    m->err = device_error_word();
+    if (!m->err) rc = fail(AH_ENOMEM, "model_create: device error word");
+  }
+  if (rc != AH_OK) {
+    ah_model_destroy(m);
+    return rc;
+  }
+  cudaMemset(m->att_cnt, 0, (size_t)B * c.n_head_kv * 4);
+  cudaMemset(m->am_cnt, 0, (size_t)B * 4);
+  cudaMemset(m->kc, 0, kv);
+  cudaMemset(m->vc, 0, kv);
+  cudaMemset(m->d_pos, 0, 16);
+  cudaMemset(m->d_tok, 0, (size_t)B * 4);
+  const int n = c.max_seq * (c.head_dim / 2);
+  k_rope_table<<<(n + 255) / 256, 256>>>(m->rope, c.max_seq, c.head_dim / 2, c.rope_freq_base);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    ah_model_destroy(m);
+    return fail(AH_ECUDA, "model_create: %s", cudaGetErrorString(e));
+  }
+  *out = m;
+  return AH_OK;
+}
+
+int ah_model_destroy(AhModel* m) {
+  if (!m) return AH_OK;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(m->device);
+  for (auto& g : m->g_step)
+    if (g) cudaGraphExecDestroy(g);
+  for (auto* w : m->wqkv) ah_q4w_destroy(w);
+  for (auto* w : m->wo) ah_q4w_destroy(w);
+  for (auto* w : m->wgu) ah_q4w_destroy(w);
+  for (auto* w : m->wd) ah_q4w_destroy(w);
+  ah_q4w_destroy(m->lm);
+  for (auto& v : m->pend)
+    for (void* p : v)
+      if (p) cudaFree(p);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->d_prompt) cudaFree(m->d_prompt);
+  cudaSetDevice(cur);
+  delete m;
+  return AH_OK;
+}
+
+int ah_model_load_tensor(AhModel* m, int kind, int layer, const void* data, void* stream) {
+  AH_REQUIRE(m && data, "model_load_tensor: null argument");
+  const AhModelConfig& c = m->c;
+  const int d = c.n_embd;
+  cudaStream_t st = as_stream(stream);
+  const bool per_layer = !(kind == AH_T_TOK_EMBD || kind == AH_T_OUT_NORM || kind == AH_T_LM_HEAD);
+  AH_REQUIRE(!per_layer || (layer >= 0 && layer < c.n_layer), "model_load_tensor: layer %d out of range", layer);
+  auto q4_bytes = [](int64_t rows, int64_t cols) { return (size_t)rows * (cols / 32) * 18; };
+  switch (kind) {
+    case AH_T_TOK_EMBD:
+      AH_CUDA_TRY(cudaMemcpyAsync(m->tok_embd, data, (size_t)c.vocab_size * d * 2, cudaMemcpyDeviceToDevice, st));
+      return AH_OK;
+    case AH_T_ATTN_NORM:
+      AH_CUDA_TRY(cudaMemcpyAsync(m->attn_norm + (size_t)layer * d, data, (size_t)d * 2, cudaMemcpyDeviceToDevice, st));
+      return AH_OK;
+    case AH_T_FFN_NORM:
+      AH_CUDA_TRY(cudaMemcpyAsync(m->ffn_norm + (size_t)layer * d, data, (size_t)d * 2, cudaMemcpyDeviceToDevice, st));
+      return AH_OK;
+    case AH_T_OUT_NORM:
+      AH_CUDA_TRY(cudaMemcpyAsync(m->out_norm, data, (size_t)d * 2, cudaMemcpyDeviceToDevice, st));
+      return AH_OK;
+    case AH_T_WO:
+      if (m->wo[layer]) ah_q4w_destroy(m->wo[layer]);
+      m->wo[layer] = nullptr;
+      return ah_q4w_from_q4_0(data, d, m->dq, &m->wo[layer], stream);
+    case AH_T_WDOWN:
+      if (m->wd[layer]) ah_q4w_destroy(m->wd[layer]);
+      m->wd[layer] = nullptr;
+      return ah_q4w_from_q4_0(data, d, c.n_ff, &m->wd[layer], stream);
+    case AH_T_LM_HEAD:
+      if (m->lm) ah_q4w_destroy(m->lm);
+      m->lm = nullptr;
+      return ah_q4w_from_q4_0(data, c.vocab_size, d, &m->lm, stream);
+    case AH_T_WQ: case AH_T_WK: case AH_T_WV: case AH_T_WGATE: case AH_T_WUP: {
+      const int slot = kind == AH_T_WQ ? 0 : kind == AH_T_WK ? 1 : kind == AH_T_WV ? 2 : kind == AH_T_WGATE ? 3 : 4;
+      const int64_t rows = slot == 0 ? m->dq : slot <= 2 ? m->dkv : c.n_ff;
+      const size_t bytes = q4_bytes(rows, d);
+      void*& p = m->pend[slot][layer];
+      if (!p && cudaMalloc(&p, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        p = nullptr;
+        return fail(AH_ENOMEM, "model_load_tensor: staging of %zu bytes", bytes);
+      }
+      AH_CUDA_TRY(cudaMemcpyAsync(p, data, bytes, cudaMemcpyDeviceToDevice, st));
+      if (slot <= 2 && m->pend[0][layer] && m->pend[1][layer] && m->pend[2][layer]) {
+        const void* srcs[3] = {m->pend[0][layer], m->pend[1][layer], m->pend[2][layer]};
+        const int64_t rws[3] = {m->dq, m->dkv, m->dkv};
+        if (m->wqkv[layer]) ah_q4w_destroy(m->wqkv[layer]);
+        m->wqkv[layer] = nullptr;
+        AH_TRY(q4w_create_q4_0_multi(srcs, rws, 3, 0, d, &m->wqkv[layer], st));
+        AH_CUDA_TRY(cudaStreamSynchronize(st));
+        for (int k = 0; k < 3; ++k) {
+          cudaFree(m->pend[k][layer]);
+          m->pend[k][layer] = nullptr;
+        }
+      }
+      if (slot >= 3 && m->pend[3][layer] && m->pend[4][layer]) {
+        const void* srcs[2] = {m->pend[3][layer], m->pend[4][layer]};
+        const int64_t rws[2] = {c.n_ff, c.n_ff};
+        if (m->wgu[layer]) ah_q4w_destroy(m->wgu[layer]);
+        m->wgu[layer] = nullptr;
+        AH_TRY(q4w_create_q4_0_multi(srcs, rws, 2, 1, d, &m->wgu[layer], st));
+        AH_CUDA_TRY(cudaStreamSynchronize(st));
+        for (int k = 3; k < 5; ++k) {
+          cudaFree(m->pend[k][layer]);
+          m->pend[k][layer] = nullptr;
+        }
+      }
+      return AH_OK;
+    }
+    default:
+      return fail(AH_EINVAL, "model_load_tensor: unknown kind %d", kind);
+  }
+}
+
+int ah_model_init_random(AhModel* m, uint64_t seed, float w_std, float emb_std, float norm_std) {
+  AH_REQUIRE(m, "model_init_random: null model");
+  const AhModelConfig& c = m->c;
+  const int d = c.n_embd;
+  cudaStream_t st = nullptr;
+  AH_TRY(ah_synth_f16(m->tok_embd, (int64_t)c.vocab_size * d, 0.0f, emb_std, ah_model_tensor_seed(seed, AH_T_TOK_EMBD, 0),
+                      0, st));
+  AH_TRY(ah_synth_f16(m->out_norm, d, 1.0f, norm_std, ah_model_tensor_seed(seed, AH_T_OUT_NORM, 0), 0, st));
+  const int64_t max_rows = std::max<int64_t>({(int64_t)m->dq, (int64_t)c.n_ff, (int64_t)d});
+  const int64_t max_cols = std::max<int64_t>({(int64_t)m->dq, (int64_t)c.n_ff, (int64_t)d});
+  void* tmp = nullptr;
+  const size_t tmp_bytes = (size_t)std::max<int64_t>(max_rows * (d / 32), (int64_t)d * (max_cols / 32)) * 18;
+  if (cudaMalloc(&tmp, tmp_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(AH_ENOMEM, "model_init_random: staging of %zu bytes", tmp_bytes);
+  }
+  struct Spec { int kind; int64_t rows, cols; };
+  const Spec specs[7] = {{AH_T_WQ, m->dq, d},      {AH_T_WK, m->dkv, d},   {AH_T_WV, m->dkv, d},
+                         {AH_T_WO, d, m->dq},      {AH_T_WGATE, c.n_ff, d}, {AH_T_WUP, c.n_ff, d},
+                         {AH_T_WDOWN, d, c.n_ff}};
+  int rc = AH_OK;
+  for (int l = 0; l < c.n_layer && rc == AH_OK; ++l) {
+    rc = ah_synth_f16(m->attn_norm + (size_t)l * d, d, 1.0f, norm_std, ah_model_tensor_seed(seed, AH_T_ATTN_NORM, l),
+                      0, st);
+    if (rc == AH_OK)
+      rc = ah_synth_f16(m->ffn_norm + (size_t)l * d, d, 1.0f, norm_std, ah_model_tensor_seed(seed, AH_T_FFN_NORM, l),
+                        0, st);
+    for (const Spec& s : specs) {
+      if (rc != AH_OK) break;
+      rc = ah_synth_q4_0(tmp, 0, s.rows, 0, s.cols, s.cols, w_std, ah_model_tensor_seed(seed, s.kind, l), st);
+      if (rc == AH_OK) rc = ah_model_load_tensor(m, s.kind, l, tmp, st);
+    }
+  }
+  if (rc == AH_OK) {
+    // the LM head is the largest tensor: generate it in its own buffer
+    void* lmb = nullptr;
+    if (cudaMalloc(&lmb, (size_t)c.vocab_size * (d / 32) * 18) != cudaSuccess) {
+      cudaGetLastError();
+      rc = fail(AH_ENOMEM, "model_init_random: output.weight staging");
+    } else {
+      rc = ah_synth_q4_0(lmb, 0, c.vocab_size, 0, d, d, w_std, ah_model_tensor_seed(seed, AH_T_LM_HEAD, 0), st);
+      if (rc == AH_OK) rc = ah_model_load_tensor(m, AH_T_LM_HEAD, 0, lmb, st);
+      cudaStreamSynchronize(st);
+      cudaFree(lmb);
+    }
+  }
+  cudaStreamSynchronize(st);
+  cudaFree(tmp);
+  return rc;
+}
+
+int ah_model_reset(AhModel* m, int batch, void* stream) {
+  AH_REQUIRE(m && batch >= 1 && batch <= m->c.max_batch, "model_reset: batch must be 1..max_batch");
+  AH_TRY(model_ready(m));
+  cudaStream_t st = as_stream(stream);
+  m->batch = batch;
+  m->pos = 0;
+  AH_CUDA_TRY(cudaMemsetAsync(m->d_pos, 0, 4, st));
+  return AH_OK;
+}
+
+int ah_model_position(const AhModel* m, int* pos) {
+  AH_REQUIRE(m && pos, "model_position: null argument");
+  *pos = m->pos;
+  return AH_OK;
+}
+
+int ah_model_forward(AhModel* m, const int32_t* tokens, float* logits, void* stream) {
+  AH_REQUIRE(m && tokens, "model_forward: null argument");
+  AH_REQUIRE(m->pos < m->c.max_seq, "model_forward: KV cache full (max_seq %d)", m->c.max_seq);
+  cudaStream_t st = as_stream(stream);
+  AH_CUDA_TRY(cudaMemcpyAsync(m->d_tok, tokens, (size_t)m->batch * 4, cudaMemcpyDeviceToDevice, st));
+  AH_TRY(run_step_graph(m, 1, nullptr, 0, st));
+  if (logits)
+    AH_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)m->batch * m->c.vocab_size * 4, cudaMemcpyDeviceToDevice,
+                                st));
+  return AH_OK;
+}
+
+int ah_model_decode(AhModel* m, int n, int32_t* out, void* stream) {
+  AH_REQUIRE(m && n >= 0, "model_decode: bad arguments");
+  AH_REQUIRE(m->pos >= 1, "model_decode: feed at least one token first");
+  AH_REQUIRE(m->pos + n <= m->c.max_seq + 1, "model_decode: would exceed max_seq");
+  cudaStream_t st = as_stream(stream);
+  // token i of the output is the argmax taken after position pos-1+i
+  const int first = m->pos - 1;
+  for (int i = 0; i < n; ++i) {
+    if (i > 0) AH_TRY(run_step_graph(m, 1, nullptr, 0, st));
+  }
+  if (out && n > 0)
+    AH_CUDA_TRY(cudaMemcpyAsync(out, m->tok_log + (size_t)first * m->batch, (size_t)n * m->batch * 4,
+                                cudaMemcpyDeviceToDevice, st));
+  return AH_OK;
+}
+
+int ah_model_generate(AhModel* m, const int32_t* prompt, int batch, int n_prompt, int n_new, int32_t* out,
+                      void* stream) {
+  AH_REQUIRE(m && prompt && n_prompt >= 1 && n_new >= 0, "model_generate: bad arguments");
+  AH_REQUIRE(n_prompt + n_new - 1 <= m->c.max_seq, "model_generate: prompt + new tokens exceed max_seq");
+  cudaStream_t st = as_stream(stream);
+  AH_TRY(ah_model_reset(m, batch, stream));
+  if (m->d_prompt) cudaFree(m->d_prompt);
+  m->d_prompt = nullptr;
+  if (cudaMalloc(&m->d_prompt, (size_t)batch * n_prompt * 4) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(AH_ENOMEM, "model_generate: prompt buffer");
+  }
+  AH_CUDA_TRY(cudaMemcpyAsync(m->d_prompt, prompt, (size_t)batch * n_prompt * 4, cudaMemcpyHostToDevice, st));
+  // first prompt token of every sequence
+  std::vector<int32_t> first(batch);
+  for (int b = 0; b < batch; ++b) first[b] = prompt[(size_t)b * n_prompt];
+  AH_CUDA_TRY(cudaMemcpyAsync(m->d_tok, first.data(), (size_t)batch * 4, cudaMemcpyHostToDevice, st));
+  AH_CUDA_TRY(cudaStreamSynchronize(st));
+  for (int p = 0; p + 1 < n_prompt; ++p) AH_TRY(run_step_graph(m, 0, m->d_prompt, n_prompt, st));
+  if (n_new == 0) return AH_OK;
+  AH_TRY(run_step_graph(m, 1, nullptr, 0, st));  // last prompt token: logits -> first new token
+  for (int i = 1; i < n_new; ++i) AH_TRY(run_step_graph(m, 1, nullptr, 0, st));
+  if (out)
+    AH_CUDA_TRY(cudaMemcpyAsync(out, m->tok_log + (size_t)(n_prompt - 1) * batch, (size_t)n_new * batch * 4,
+                                cudaMemcpyDeviceToHost, st));
+  AH_CUDA_TRY(cudaStreamSynchronize(st));
+  return AH_OK;
+}
+
+}  // extern "C"

@@ -224,15 +224,16 @@ __device__ __forceinline__ float silu_ref(float x) {  // inference/math.rs:83-95
 }
 
 // ---------------------------------------------------------------------------
-// The fused GEMV.  A thread-block cluster of kGemvCluster CTAs covers one row
-// group of kGemvWarps 16-row tiles (128 rows) over the full K; cluster CTA c
-// takes K-chunk c (ppc = ceil(kp/8) block pairs).  Each CTA splits its own chunk
-// of x into shared memory and its warp w multiplies row tile w against it, so
-// the main loop reads only local shared memory; weights stream HBM ->
-// registers, prefetched before the kernel waits on its predecessor.  The chunk
-// partials of row tile r meet in cluster CTA r, which sums them over DSMEM in
-// chunk order (deterministic; no global scratch, fences or atomics) and runs the
-// epilogue.
+// The fused GEMV.  A thread-block cluster of kGemvCluster CTAs walks row groups
+// of kGemvWarps 16-row tiles (128 rows) over the full K; cluster CTA c takes
+// K-chunk c (ppc = ceil(kp/8) block pairs).  Each CTA splits its chunk of x
+// into shared memory once, and for every row group its warp w multiplies row
+// tile w against it, so the main loop reads only local shared memory; weights
+// stream HBM -> registers, and the next row group's are in flight while the
+// current one is reduced.  The chunk partials of row tile r meet in cluster CTA
+// r, which sums them over DSMEM in chunk order (deterministic; no global
+// scratch, fences or atomics) and runs the epilogue.  The grid holds at most
+// as many clusters as are resident at once (persistent).
 // ---------------------------------------------------------------------------
 template <bool kF32>
 __device__ __forceinline__ void load_pairs(uint4 (&w)[kGemvU], typename ScaleT<kF32>::V (&sv)[kGemvU],
@@ -249,7 +250,7 @@ template <int NT, bool kF32>
 __device__ __forceinline__ void mma_pairs(float (&tot)[NT][4], const uint4 (&w)[kGemvU],
                                           const typename ScaleT<kF32>::V (&sv)[kGemvU], int p, int np, int B,
                                           int g, int t, const uint8_t* xs, const float4* blk_info, int plane,
-                                          int kbc) {
+                                          int kbc, int kb0) {
 #pragma unroll
   for (int u = 0; u < kGemvU; ++u) {
     if (p + u < np) {
@@ -265,7 +266,7 @@ __device__ __forceinline__ void mma_pairs(float (&tot)[NT][4], const uint4 (&w)[
         const uint32_t s1a2 = w0s & 0x00F000F0u, s1a3 = w8s & 0x00F000F0u;
         float dg, dg8;
         ScaleT<kF32>::get(sv[u], blk, dg, dg8);
-        const int kb = 2 * (p + u) + blk;
+        const int kb = kb0 + 2 * (p + u) + blk;
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
           const int col = 8 * j + g;
@@ -287,46 +288,12 @@ __device__ __forceinline__ void mma_pairs(float (&tot)[NT][4], const uint4 (&w)[
   }
 }
 
-template <int NT, bool kF32, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
-  constexpr int BM = 4 * NT;  // tokens this instantiation can hold
-  using SV = typename ScaleT<kF32>::V;
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t = lane & 3;
+// RMSNorm statistics (inference/math.rs:53-63): 1/rms per token from the
+// producer's partial sums of squares of x.
+template <int BM, int PRO>
+__device__ __forceinline__ void rms_stats(const GemvArgs& a, float* wred, float* tok_inv, int tid, int lane,
+                                          int warp) {
   const int B = a.batch;
-  const int crank = (int)cluster_ctarank();  // = K-chunk
-  const int64_t rg = blockIdx.x / kGemvCluster;
-  const int64_t rt = rg * kGemvWarps + warp;  // this warp's row tile
-  const bool warp_live = rt < a.w.r16;
-  const int64_t KP = a.w.kp;
-  const int ppc = (int)a.pairs_per_chunk;
-  const int kbc = 2 * ppc;          // blocks per chunk
-  const int plane = kbc * 64 + 64;  // bytes per x plane (64 B pad staggers banks)
-  uint8_t* xs = smem;                                                           // [2B][plane]
-  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc]
-  float* part = reinterpret_cast<float*>(blk_info + B * kbc);                   // [warps][16][B]
-  float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
-  float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
-
-  // Weights do not depend on the previous kernel: start streaming them now
-  // (two batches of kGemvU pairs in flight per lane).
-  const int64_t p0 = (int64_t)crank * ppc;
-  const int np = (int)max((int64_t)0, min(p0 + ppc, KP) - p0);
-  const uint4* nibp = a.w.nib + (rt * KP + p0) * 32 + lane;
-  const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + (rt * KP + p0) * 8 + g;
-  uint4 wa[kGemvU], wb[kGemvU];
-  SV sa[kGemvU], sb[kGemvU];
-  if (warp_live) {
-    load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
-    load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
-  }
-  // A grid resident in one wave lets the next kernel launch now, so its weight
-  // prefetch overlaps this kernel; larger grids trigger after the main loop.
-  if (a.early_trigger) pdl_launch_dependents();
-  pdl_wait();
-
-  // ---- prologue: RMSNorm statistics from the producer's partial sums ----------
   const int64_t K = a.w.cols;
   if (PRO == kProRmsNorm) {
     float ss[BM];
@@ -349,13 +316,18 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
     }
     __syncthreads();
   }
-  // ---- split this CTA's K-chunk of x into f16 hi/lo planes ------------------------
-  // Eight threads share a (token, 32-column block) task; each loads 4 values.
-  // Per block this also records {2^(24-s), -8*2^-24*sum(hi), -8*2^-24*sum(lo)}:
-  // the exponent that undoes the power-of-two scaling and the accumulator start
-  // value that applies the -8 nibble offset inside the tensor core.
+}
+
+// Splits columns [k0, k1) of x (block-relative 0 .. kbc*32) into f16 hi/lo
+// planes.  Eight threads share a (token, 32-column block) task; each loads 4
+// values.  Per block this also records {2^(24-s), -8*2^-24*sum(hi),
+// -8*2^-24*sum(lo)}: the exponent that undoes the power-of-two scaling and the
+// accumulator start value that applies the -8 nibble offset inside the tensor core.
+template <int PRO>
+__device__ __forceinline__ void split_x(const GemvArgs& a, uint8_t* xs, float4* blk_info, int plane, int kbc,
+                                        int64_t k0, int64_t k1, const float* tok_inv, int tid, int warp) {
+  const int B = a.batch;
   {
-    const int64_t k0 = p0 * 64, k1 = min(k0 + (int64_t)ppc * 64, K);
     constexpr int UNR = 2;
     const int tasks = B * kbc;
     const int rounds = (tasks + 32 * UNR - 1) / (32 * UNR);
@@ -440,60 +412,231 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
       }
     }
   }
+}
+
+template <int NT, bool kF32, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
+  constexpr int BM = 4 * NT;  // tokens this instantiation can hold
+  using SV = typename ScaleT<kF32>::V;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int B = a.batch;
+  const int crank = (int)cluster_ctarank();  // = K-chunk
+  const int64_t n_rg = (a.w.r16 + kGemvWarps - 1) / kGemvWarps;
+  const int64_t n_cl = gridDim.x / kGemvCluster;
+  int64_t rg = blockIdx.x / kGemvCluster;
+  int64_t rt = rg * kGemvWarps + warp;  // this warp's row tile
+  bool warp_live = rt < a.w.r16;
+  const int64_t KP = a.w.kp;
+  const int ppc = (int)a.pairs_per_chunk;
+  const int kbc = 2 * ppc;          // blocks per chunk
+  const int plane = kbc * 64 + 64;  // bytes per x plane (64 B pad staggers banks)
+  uint8_t* xs = smem;                                                           // [2B][plane]
+  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc]
+  float* part = reinterpret_cast<float*>(blk_info + B * kbc);                   // [warps][16][B]
+  float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
+  float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
+
+  // Weights do not depend on the previous kernel: start streaming them now
+  // (two batches of kGemvU pairs in flight per lane).
+  const int64_t p0 = (int64_t)crank * ppc;
+  const int np = (int)max((int64_t)0, min(p0 + ppc, KP) - p0);
+  const uint4* nibp = a.w.nib + (rt * KP + p0) * 32 + lane;
+  const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + (rt * KP + p0) * 8 + g;
+  const int64_t tile_nib = KP * 32 * kGemvWarps * n_cl;  // uint4 stride to the next row group of this CTA
+  const int64_t tile_scl = KP * 8 * kGemvWarps * n_cl;
+  uint4 wa[kGemvU], wb[kGemvU];
+  SV sa[kGemvU], sb[kGemvU];
+  if (warp_live) {
+    load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
+    load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+  }
+  // A grid resident in one wave lets the next kernel launch now, so its weight
+  // prefetch overlaps this kernel; larger grids trigger after the main loop.
+  if (a.early_trigger) pdl_launch_dependents();
+  pdl_wait();
+
+  const int64_t K = a.w.cols;
+  rms_stats<BM, PRO>(a, wred, tok_inv, tid, lane, warp);
+  split_x<PRO>(a, xs, blk_info, plane, kbc, p0 * 64, min(p0 * 64 + (int64_t)ppc * 64, K), tok_inv, tid, warp);
   __syncthreads();
 
-  // ---- main loop: row tile `warp` x this CTA's K-chunk, all local -----------------
-  float tot[NT][4];
+  // ---- row groups: main loop (local), DSMEM reduction, epilogue ------------------
+  for (; rg < n_rg; rg += n_cl) {
+    float tot[NT][4];
 #pragma unroll
-  for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
-  if (warp_live) {
+    for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
+    if (warp_live) {
+      for (int p = 0; p < np; p += 2 * kGemvU) {
+        mma_pairs<NT, kF32>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, 0);
+        if (p + 2 * kGemvU < np) load_pairs<kF32>(wa, sa, nibp, sclp, p + 2 * kGemvU, np);
+        mma_pairs<NT, kF32>(tot, wb, sb, p + kGemvU, np, B, g, t, xs, blk_info, plane, kbc, 0);
+        if (p + 3 * kGemvU < np) load_pairs<kF32>(wb, sb, nibp, sclp, p + 3 * kGemvU, np);
+      }
+    }
+    // prefetch the next row group's first two batches while this one is reduced
+    const int64_t rg_next = rg + n_cl;
+    const int64_t rt_next = rg_next * kGemvWarps + warp;
+    const bool next_live = rg_next < n_rg && rt_next < a.w.r16;
+    nibp += tile_nib;
+    sclp += tile_scl;
+    if (next_live) {
+      load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
+      load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+    }
+    if (rg_next >= n_rg && !a.early_trigger) pdl_launch_dependents();
+
+    // chunk partials -> cluster CTA `warp` over DSMEM
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
+      if (b < B) {
+        part[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
+        part[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
+      }
+    }
+    cluster_arrive();
+    cluster_wait();  // every CTA's partials are visible cluster-wide
+    const int64_t my_rt = rg * kGemvWarps + crank;  // the row tile this CTA finalises
+    const bool fin_live = my_rt < a.w.r16;
+    float* fin = wred;  // [16][B]
+    if (fin_live) {
+      // partial of chunk c for row tile `crank` sits at part[crank] in cluster CTA c
+      const uint32_t local = smem_u32(part + crank * 16 * B);
+      for (int i = tid; i < 16 * B; i += kGemvThreads) {
+        float v = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kGemvCluster; ++c) v += ld_dsmem_f32(mapa_shared(local + i * 4, (uint32_t)c));
+        fin[i] = v;
+      }
+    }
+    cluster_arrive();  // this CTA's DSMEM reads are done
+    __syncthreads();
+    if (fin_live) {
+      if (EPI == kEpiSwiglu) {
+        // tile rows r < 8 are gate rows 8rt+r, rows r+8 the matching up rows
+        for (int i = tid; i < 8 * B; i += kGemvThreads) {
+          const int r = i / B, b = i - r * B;
+          const int64_t o = my_rt * 8 + r;
+          if (o < a.w.rows / 2) a.y[b * a.y_stride + o] = silu_ref(fin[r * B + b]) * fin[(r + 8) * B + b];
+        }
+      } else {
+        for (int i = tid; i < 16 * B; i += kGemvThreads) {
+          const int r = i / B, b = i - r * B;
+          const int64_t R = my_rt * 16 + r;
+          float h = 0.0f;
+          if (R < a.w.rows) {
+            float* d = a.y + b * a.y_stride + R;
+            h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
+            *d = h;
+          }
+          fin[i] = h;
+        }
+        if (a.ss_out) {
+          // per-tile partial sum of squares of the values written (next RMSNorm)
+          __syncthreads();
+          if (tid < B) {
+            float q = 0.0f;
+            for (int r = 0; r < 16; ++r) q = fmaf(fin[r * B + tid], fin[r * B + tid], q);
+            a.ss_out[tid * a.w.r16 + my_rt] = q;
+          }
+        }
+      }
+    }
+    cluster_wait();  // every CTA has read the partials: they may be overwritten (or the CTA may leave)
+    __syncthreads();
+    rt = rt_next;
+    warp_live = next_live;
+  }
+}
+
+// Persistent full-K CTAs for GEMVs with many row tiles (FFN gate/up, the
+// fused QKV, the LM head): each CTA splits all of x into shared memory once,
+// then walks row tiles rt = blockIdx.x, +gridDim.x, ...; its eight warps take
+// the eight K-chunks of the tile and meet in local shared memory, so a tile
+// costs one CTA barrier instead of a cluster exchange.  The next tile's weights
+// are in flight while the current one is reduced.
+template <int NT, bool kF32, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) k_gemv_q4_rows(const GemvArgs a) {
+  constexpr int BM = 4 * NT;
+  using SV = typename ScaleT<kF32>::V;
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int B = a.batch;
+  const int64_t KP = a.w.kp, r16 = a.w.r16;
+  const int ppc = (int)a.pairs_per_chunk;  // pairs per warp = ceil(kp / 8)
+  const int kbc = 2 * (int)KP;             // the whole K
+  const int plane = kbc * 64 + 64;
+  uint8_t* xs = smem;                                                           // [2B][plane]
+  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc]
+  float* part = reinterpret_cast<float*>(blk_info + B * kbc);                   // [warps][16][B]
+  float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
+  float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
+  int64_t rt = blockIdx.x;
+  const int64_t p0 = (int64_t)warp * ppc;
+  const int np = (int)max((int64_t)0, min(p0 + ppc, KP) - p0);
+  const uint4* nibp = a.w.nib + (rt * KP + p0) * 32 + lane;
+  const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + (rt * KP + p0) * 8 + g;
+  const int64_t tile_nib = KP * 32 * gridDim.x, tile_scl = KP * 8 * gridDim.x;
+  uint4 wa[kGemvU], wb[kGemvU];
+  SV sa[kGemvU], sb[kGemvU];
+  if (rt < r16) {
+    load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
+    load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+  }
+  if (a.early_trigger) pdl_launch_dependents();
+  pdl_wait();
+  rms_stats<BM, PRO>(a, wred, tok_inv, tid, lane, warp);
+  split_x<PRO>(a, xs, blk_info, plane, kbc, 0, a.w.cols, tok_inv, tid, warp);
+  __syncthreads();
+  float* fin = wred;  // [16][B]
+  for (; rt < r16; rt += gridDim.x) {
+    float tot[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
     for (int p = 0; p < np; p += 2 * kGemvU) {
-      mma_pairs<NT, kF32>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc);
+      mma_pairs<NT, kF32>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
       if (p + 2 * kGemvU < np) load_pairs<kF32>(wa, sa, nibp, sclp, p + 2 * kGemvU, np);
-      mma_pairs<NT, kF32>(tot, wb, sb, p + kGemvU, np, B, g, t, xs, blk_info, plane, kbc);
+      mma_pairs<NT, kF32>(tot, wb, sb, p + kGemvU, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
       if (p + 3 * kGemvU < np) load_pairs<kF32>(wb, sb, nibp, sclp, p + 3 * kGemvU, np);
     }
-  }
-  if (!a.early_trigger) pdl_launch_dependents();
-
-  // ---- chunk partials -> cluster CTA `warp` over DSMEM ----------------------------
-#pragma unroll
-  for (int j = 0; j < NT; ++j) {
-    const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
-    if (b < B) {
-      part[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
-      part[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
+    const bool has_next = rt + gridDim.x < r16;
+    nibp += tile_nib;
+    sclp += tile_scl;
+    if (has_next) {
+      load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
+      load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+    } else if (!a.early_trigger) {
+      pdl_launch_dependents();
     }
-  }
-  cluster_arrive();
-  cluster_wait();  // every CTA's partials are visible cluster-wide
-  const int64_t my_rt = rg * kGemvWarps + crank;  // the row tile this CTA finalises
-  const bool fin_live = my_rt < a.w.r16;
-  float* fin = wred;  // [16][B]
-  if (fin_live) {
-    // partial of chunk c for row tile `crank` sits at part[crank] in cluster CTA c
-    const uint32_t local = smem_u32(part + crank * 16 * B);
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
+      if (b < B) {
+        part[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
+        part[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
+      }
+    }
+    __syncthreads();
     for (int i = tid; i < 16 * B; i += kGemvThreads) {
       float v = 0.0f;
 #pragma unroll
-      for (int c = 0; c < kGemvCluster; ++c) v += ld_dsmem_f32(mapa_shared(local + i * 4, (uint32_t)c));
+      for (int w = 0; w < kGemvWarps; ++w) v += part[w * 16 * B + i];  // K-chunk order
       fin[i] = v;
     }
-  }
-  cluster_arrive();  // this CTA's DSMEM reads are done
-  __syncthreads();
-  if (fin_live) {
+    __syncthreads();
     if (EPI == kEpiSwiglu) {
-      // tile rows r < 8 are gate rows 8rt+r, rows r+8 the matching up rows
       for (int i = tid; i < 8 * B; i += kGemvThreads) {
         const int r = i / B, b = i - r * B;
-        const int64_t o = my_rt * 8 + r;
+        const int64_t o = rt * 8 + r;
         if (o < a.w.rows / 2) a.y[b * a.y_stride + o] = silu_ref(fin[r * B + b]) * fin[(r + 8) * B + b];
       }
     } else {
       for (int i = tid; i < 16 * B; i += kGemvThreads) {
         const int r = i / B, b = i - r * B;
-        const int64_t R = my_rt * 16 + r;
+        const int64_t R = rt * 16 + r;
         float h = 0.0f;
         if (R < a.w.rows) {
           float* d = a.y + b * a.y_stride + R;
@@ -503,46 +646,151 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
         fin[i] = h;
       }
       if (a.ss_out) {
-        // per-tile partial sum of squares of the values written (next RMSNorm)
         __syncthreads();
         if (tid < B) {
           float q = 0.0f;
           for (int r = 0; r < 16; ++r) q = fmaf(fin[r * B + tid], fin[r * B + tid], q);
-          a.ss_out[tid * a.w.r16 + my_rt] = q;
+          a.ss_out[tid * a.w.r16 + rt] = q;
         }
       }
     }
   }
-  cluster_wait();  // no CTA leaves while another may still read its shared memory
 }
 
 using GemvKernel = void (*)(const GemvArgs);
+#define AH_TRY_GEMV(expr)         \
+  do {                            \
+    int _rc = (expr);             \
+    if (_rc != AH_OK) return _rc; \
+  } while (0)
 
-template <int NT>
+template <int NT, bool kRows>
 GemvKernel pick_kernel(bool f32s, int pro, int epi) {
-  if (f32s) return (pro == kProPlain && epi == kEpiStore) ? k_gemv_q4<NT, true, kProPlain, kEpiStore> : nullptr;
+#define AH_K(F, P, E) (kRows ? k_gemv_q4_rows<NT, F, P, E> : k_gemv_q4<NT, F, P, E>)
+  if (f32s) return (pro == kProPlain && epi == kEpiStore) ? AH_K(true, kProPlain, kEpiStore) : nullptr;
   if (pro == kProPlain) {
-    if (epi == kEpiStore) return k_gemv_q4<NT, false, kProPlain, kEpiStore>;
-    if (epi == kEpiAdd) return k_gemv_q4<NT, false, kProPlain, kEpiAdd>;
-    return k_gemv_q4<NT, false, kProPlain, kEpiSwiglu>;
+    if (epi == kEpiStore) return AH_K(false, kProPlain, kEpiStore);
+    if (epi == kEpiAdd) return AH_K(false, kProPlain, kEpiAdd);
+    return AH_K(false, kProPlain, kEpiSwiglu);
   }
-  if (epi == kEpiStore) return k_gemv_q4<NT, false, kProRmsNorm, kEpiStore>;
-  if (epi == kEpiAdd) return k_gemv_q4<NT, false, kProRmsNorm, kEpiAdd>;
-  return k_gemv_q4<NT, false, kProRmsNorm, kEpiSwiglu>;
+  if (epi == kEpiStore) return AH_K(false, kProRmsNorm, kEpiStore);
+  if (epi == kEpiAdd) return AH_K(false, kProRmsNorm, kEpiAdd);
+  return AH_K(false, kProRmsNorm, kEpiSwiglu);
+#undef AH_K
 }
 
 }  // namespace
 
-GemvPlan gemv_plan(const Q4Tiled& w, int batch) {
+GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
   GemvPlan p{};
   p.nt = (batch + 3) / 4;
-  p.pairs_per_chunk = (w.kp + kGemvCluster - 1) / kGemvCluster;  // one K-chunk per cluster CTA
+  p.rows_mode = rows_mode;
+  p.pairs_per_chunk = (w.kp + kGemvCluster - 1) / kGemvCluster;  // one K-chunk per warp (rows) or cluster CTA
   p.ksplit = 1;
-  const int64_t kbc = 2 * p.pairs_per_chunk;
+  const int64_t kbc = rows_mode ? 2 * w.kp : 2 * p.pairs_per_chunk;
   const int64_t plane = kbc * 64 + 64;
   p.smem = (size_t)2 * batch * plane + (size_t)batch * kbc * 16 + (size_t)kGemvWarps * 16 * batch * 4 +
            (size_t)kGemvMaxBatch * 4 + (size_t)kGemvWarps * (4 * p.nt) * 4 + (size_t)16 * batch * 4 + 16;
   return p;
+}
+
+GemvPlan gemv_plan(const Q4Tiled& w, int batch) { return gemv_plan(w, batch, false); }
+
+namespace {
+GemvKernel select_kernel(const GemvPlan& plan, bool f32s, int pro, int epi) {
+  if (plan.rows_mode) {
+    switch (plan.nt) {
+      case 1: return pick_kernel<1, true>(f32s, pro, epi);
+      case 2: return pick_kernel<2, true>(f32s, pro, epi);
+      case 3: return pick_kernel<3, true>(f32s, pro, epi);
+      default: return pick_kernel<4, true>(f32s, pro, epi);
+    }
+  }
+  switch (plan.nt) {
+    case 1: return pick_kernel<1, false>(f32s, pro, epi);
+    case 2: return pick_kernel<2, false>(f32s, pro, epi);
+    case 3: return pick_kernel<3, false>(f32s, pro, epi);
+    default: return pick_kernel<4, false>(f32s, pro, epi);
+  }
+}
+
+// Per (device, kernel, smem): raises the dynamic shared-memory cap once and
+// caches how many clusters (cluster mode) or CTAs (rows mode) fit in one wave.
+int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
+  static std::mutex mu;
+  struct Entry { int dev; void* k; size_t smem; int cap; };
+  static std::vector<Entry> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  for (auto& e : cache)
+    if (e.dev == dev && e.k == (void*)kern && e.smem == plan.smem) {
+      *capacity = e.cap;
+      return AH_OK;
+    }
+  AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem));
+  int n = 0;
+  if (plan.rows_mode) {
+    AH_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, plan.smem));
+    n *= sm_count();
+  } else {
+    cudaLaunchConfig_t q{};
+    q.gridDim = dim3(kGemvCluster, 1, 1);
+    q.blockDim = dim3(kGemvThreads, 1, 1);
+    q.dynamicSmemBytes = plan.smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kGemvCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    q.attrs = attr;
+    q.numAttrs = 1;
+    AH_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &q));
+  }
+  cache.push_back({dev, (void*)kern, plan.smem, n});
+  *capacity = n;
+  return AH_OK;
+}
+
+// Cluster mode for GEMVs whose row groups fit in one wave (one pass each);
+// rows mode for many-tile GEMVs whose full-K split fits comfortably in shared
+// memory (it is then amortised over several tiles per CTA).
+int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, GemvKernel* kern, int* cap) {
+  GemvPlan pc = gemv_plan(w, batch, false);
+  if (pc.smem > (size_t)kGemvSmemLimit)
+    return fail(AH_EUNSUPPORTED, "gemv: batch %d x %lld columns needs %zu B of shared memory per CTA (limit %d)",
+                batch, (long long)w.cols, pc.smem, kGemvSmemLimit);
+  GemvKernel kc = select_kernel(pc, w.f32_scales, pro, epi);
+  if (!kc) return fail(AH_EUNSUPPORTED, "gemv: engine-format weights support only the plain GEMV");
+  int ccap = 0;
+  AH_TRY_GEMV(kernel_setup(kc, pc, &ccap));
+  const int64_t n_rg = (w.r16 + kGemvWarps - 1) / kGemvWarps;
+  GemvPlan pr = gemv_plan(w, batch, true);
+  if (n_rg > ccap && pr.smem <= (size_t)kGemvRowsSmem) {
+    GemvKernel kr = select_kernel(pr, w.f32_scales, pro, epi);
+    int rcap = 0;
+    AH_TRY_GEMV(kernel_setup(kr, pr, &rcap));
+    if (rcap > 0) {
+      *plan = pr;
+      *kern = kr;
+      *cap = rcap;
+      return AH_OK;
+    }
+  }
+  AH_REQUIRE(ccap > 0, "gemv: no cluster of this kernel fits on the device");
+  *plan = pc;
+  *kern = kc;
+  *cap = ccap;
+  return AH_OK;
+}
+}  // namespace
+
+int gemv_prepare(const Q4Tiled& w, int batch, int pro, int epi) {
+  AH_REQUIRE(batch >= 1 && batch <= kGemvMaxBatch, "gemv: batch must be 1..16");
+  GemvPlan plan;
+  GemvKernel kern;
+  int cap;
+  return choose_plan(w, batch, pro, epi, &plan, &kern, &cap);
 }
 
 int gemv_launch(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
@@ -551,73 +799,37 @@ int gemv_launch(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
              "gemv: RMSNorm prologue needs a norm weight and the producer's partial sums of squares");
   AH_REQUIRE(a.x != nullptr && a.y != nullptr, "gemv: null activation or output");
   AH_REQUIRE(epi != kEpiSwiglu || a.w.rows % 16 == 0, "gemv: SwiGLU epilogue needs interleaved rows %% 16 == 0");
-  const GemvPlan plan = gemv_plan(a.w, a.batch);
-  if (plan.smem > (size_t)kGemvSmemLimit)
-    return fail(AH_EUNSUPPORTED, "gemv: batch %d x %lld columns needs %zu B of shared memory per CTA (limit %d)",
-                a.batch, (long long)a.w.cols, plan.smem, kGemvSmemLimit);
+  GemvPlan plan;
+  GemvKernel kern;
+  int cap = 0;
+  AH_TRY_GEMV(choose_plan(a.w, a.batch, pro, epi, &plan, &kern, &cap));
   a.pairs_per_chunk = plan.pairs_per_chunk;
-  GemvKernel kern = nullptr;
-  switch (plan.nt) {
-    case 1: kern = pick_kernel<1>(a.w.f32_scales, pro, epi); break;
-    case 2: kern = pick_kernel<2>(a.w.f32_scales, pro, epi); break;
-    case 3: kern = pick_kernel<3>(a.w.f32_scales, pro, epi); break;
-    default: kern = pick_kernel<4>(a.w.f32_scales, pro, epi); break;
-  }
-  if (!kern) return fail(AH_EUNSUPPORTED, "gemv: engine-format weights support only the plain GEMV");
-  {
-    // Raise the kernel's dynamic shared-memory cap once per (device, kernel, size).
-    static std::mutex mu;
-    static std::vector<std::pair<std::pair<int, void*>, size_t>> done;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> lk(mu);
-    bool found = false;
-    for (auto& e : done)
-      if (e.first.first == dev && e.first.second == (void*)kern) {
-        found = true;
-        if (e.second < plan.smem) {
-          AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem));
-          e.second = plan.smem;
-        }
-      }
-    if (!found) {
-      AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem));
-      done.push_back({{dev, (void*)kern}, plan.smem});
-    }
-  }
-  const int64_t n_clusters = (a.w.r16 + kGemvWarps - 1) / kGemvWarps;  // row groups
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((unsigned)(n_clusters * kGemvCluster), 1, 1);
   cfg.blockDim = dim3(kGemvThreads, 1, 1);
   cfg.dynamicSmemBytes = plan.smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kGemvCluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  {
-    static std::mutex mu;
-    static std::vector<std::pair<std::pair<int, void*>, std::pair<size_t, int>>> occ;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int max_clusters = -1;
-    std::lock_guard<std::mutex> lk(mu);
-    for (auto& e : occ)
-      if (e.first.first == dev && e.first.second == (void*)kern && e.second.first == plan.smem)
-        max_clusters = e.second.second;
-    if (max_clusters < 0) {
-      cudaLaunchConfig_t q = cfg;
-      q.numAttrs = 1;  // occupancy query: cluster shape only
-      AH_CUDA_TRY(cudaOccupancyMaxActiveClusters(&max_clusters, kern, &q));
-      occ.push_back({{dev, (void*)kern}, {plan.smem, max_clusters}});
-    }
-    a.early_trigger = n_clusters <= max_clusters ? 1 : 0;
+  int na = 0;
+  if (plan.rows_mode) {
+    const int64_t n = std::min<int64_t>(a.w.r16, cap);
+    a.early_trigger = a.w.r16 <= cap ? 1 : 0;
+    cfg.gridDim = dim3((unsigned)n, 1, 1);
+  } else {
+    const int64_t n_rg = (a.w.r16 + kGemvWarps - 1) / kGemvWarps;  // row groups
+    const int64_t n_clusters = std::min<int64_t>(n_rg, cap);
+    a.early_trigger = n_rg <= cap ? 1 : 0;
+    cfg.gridDim = dim3((unsigned)(n_clusters * kGemvCluster), 1, 1);
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = kGemvCluster;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
   }
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  ++na;
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
   AH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
   return AH_OK;
 }

@@ -36,6 +36,7 @@ constexpr int kGemvMaxBatch = 16;
 constexpr int kGemvCluster = kGemvWarps;  // CTAs per cluster = K-chunks = warps per CTA
 constexpr int kGemvU = 4;                 // block pairs per register batch (two batches in flight)
 constexpr int kGemvSmemLimit = 200 * 1024;
+constexpr int kGemvRowsSmem = 96 * 1024;   // rows mode only while two CTAs fit per SM
 
 struct Q4Tiled {
   const uint4* nib;    // [r16][kp][32]

@@ -11,15 +11,20 @@ namespace ah {
 struct GemvPlan {
   int nt;                   // n8 tensor-core column tiles (4 tokens each)
   int64_t pairs_per_chunk;  // 64-column block pairs per K-chunk (cluster CTA)
-  int ksplit;               // always 1: the cluster covers the full K
+  int ksplit;               // always 1: a launch covers the full K
   size_t smem;              // dynamic shared memory bytes
+  bool rows_mode;           // persistent full-K CTAs instead of clusters
 };
 
 GemvPlan gemv_plan(const Q4Tiled& w, int batch);
+GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode);
 // Launches the fused GEMV with the given prologue/epilogue; `pdl` enables
 // programmatic dependent launch (weights are prefetched before the kernel waits
 // for its predecessor's output).
 int gemv_launch(GemvArgs a, int prologue, int epilogue, cudaStream_t st, bool pdl);
+// Resolves the kernel's shared-memory attribute and occupancy for (w, batch,
+// prologue, epilogue) without launching, so a later launch can be captured.
+int gemv_prepare(const Q4Tiled& w, int batch, int prologue, int epilogue);
 
 const Q4Tiled& q4w_tiled(const AhQ4Weight* w);
 int q4w_create_q4_0_multi(const void* const* srcs, const int64_t* src_rows, int nsrc, int mode, int64_t cols,

@@ -1,0 +1,119 @@
+"""Llama-shaped decoder on the C ABI (ah_model_*): the B200 counterpart of
+agent_harness's InferenceEngine (inference/mod.rs) for Q4_0 weights."""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ._lib import call, lib
+
+# tensor kinds (include/ah_cuda.h)
+TOK_EMBD, ATTN_NORM, FFN_NORM, OUT_NORM, WQ, WK, WV, WO, WGATE, WUP, WDOWN, LM_HEAD = range(12)
+
+
+class _Cfg(C.Structure):
+    _fields_ = [("n_layer", C.c_int32), ("n_embd", C.c_int32), ("n_ff", C.c_int32), ("n_head", C.c_int32),
+                ("n_head_kv", C.c_int32), ("head_dim", C.c_int32), ("vocab_size", C.c_int32),
+                ("max_seq", C.c_int32), ("max_batch", C.c_int32), ("rope_freq_base", C.c_float),
+                ("rms_eps", C.c_float)]
+
+
+@dataclass
+class ModelConfig:
+    """inference/config.rs:6-58 (the fields the decoder uses)."""
+    n_layer: int
+    n_embd: int
+    n_ff: int
+    n_head: int
+    n_head_kv: int
+    head_dim: int
+    vocab_size: int
+    max_seq: int = 4096
+    max_batch: int = 1
+    rope_freq_base: float = 500000.0
+    rms_eps: float = 1e-5
+
+    def to_c(self) -> _Cfg:
+        return _Cfg(self.n_layer, self.n_embd, self.n_ff, self.n_head, self.n_head_kv, self.head_dim,
+                    self.vocab_size, self.max_seq, self.max_batch, self.rope_freq_base, self.rms_eps)
+
+    def shapes(self) -> dict:
+        dq, dkv = self.n_head * self.head_dim, self.n_head_kv * self.head_dim
+        return {WQ: (dq, self.n_embd), WK: (dkv, self.n_embd), WV: (dkv, self.n_embd), WO: (self.n_embd, dq),
+                WGATE: (self.n_ff, self.n_embd), WUP: (self.n_ff, self.n_embd), WDOWN: (self.n_embd, self.n_ff),
+                LM_HEAD: (self.vocab_size, self.n_embd)}
+
+
+LLAMA_8B = ModelConfig(n_layer=32, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128,
+                       vocab_size=128256, max_seq=2304, max_batch=1, rope_freq_base=500000.0, rms_eps=1e-5)
+LLAMA_70B = ModelConfig(n_layer=80, n_embd=8192, n_ff=28672, n_head=64, n_head_kv=8, head_dim=128,
+                        vocab_size=128256, max_seq=2176, max_batch=16, rope_freq_base=500000.0, rms_eps=1e-5)
+
+
+def tensor_seed(seed: int, kind: int, layer: int) -> int:
+    return int(lib().ah_model_tensor_seed(C.c_uint64(seed), kind, layer))
+
+
+class Model:
+    def __init__(self, cfg: ModelConfig, device="cuda"):
+        self.cfg = cfg
+        dev = torch.device(device)
+        self.device = torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
+        torch.cuda.set_device(self.device)
+        self._h = C.c_void_p()
+        c = cfg.to_c()
+        call("ah_model_create", C.byref(c), C.byref(self._h))
+
+    def _stream(self):
+        return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def init_random(self, seed: int, w_std=0.02, emb_std=1.0, norm_std=0.02):
+        call("ah_model_init_random", self._h, C.c_uint64(seed), w_std, emb_std, norm_std)
+        torch.cuda.synchronize(self.device)
+
+    def load_tensor(self, kind: int, layer: int, data: torch.Tensor):
+        call("ah_model_load_tensor", self._h, kind, layer, C.c_void_p(data.data_ptr()), self._stream())
+
+    def reset(self, batch: int = 1):
+        call("ah_model_reset", self._h, batch, self._stream())
+
+    def forward(self, tokens) -> torch.Tensor:
+        """One forward() per sequence; returns logits [batch][vocab]."""
+        t = torch.as_tensor(np.asarray(tokens, np.int32)).to(self.device)
+        out = torch.empty(t.numel(), self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+        call("ah_model_forward", self._h, C.c_void_p(t.data_ptr()), C.c_void_p(out.data_ptr()), self._stream())
+        return out
+
+    def decode(self, n: int, batch: int) -> torch.Tensor:
+        out = torch.empty(n, batch, dtype=torch.int32, device=self.device)
+        call("ah_model_decode", self._h, n, C.c_void_p(out.data_ptr()), self._stream())
+        return out
+
+    def generate(self, prompt: np.ndarray, n_new: int) -> np.ndarray:
+        """Greedy generate for prompt [batch][n_prompt]; returns [n_new][batch]."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        batch, n_prompt = p.shape
+        out = np.zeros((n_new, batch), np.int32)
+        call("ah_model_generate", self._h, p.ctypes.data_as(C.c_void_p), batch, n_prompt, n_new,
+             out.ctypes.data_as(C.c_void_p), self._stream())
+        return out
+
+    @property
+    def position(self) -> int:
+        v = C.c_int(0)
+        call("ah_model_position", self._h, C.byref(v))
+        return v.value
+
+    def close(self):
+        if self._h:
+            lib().ah_model_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -291,9 +291,19 @@ def run_gpu(args):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_val = world * e2e_steps * N_COPIES * GEMV_BYTES / float(t.item()) / 1e9
 
+    for W in Ws:
+        W.close()
+    Ws = []
     extra = {}
     if rank == 0 and not args.quick:
         extra = secondary_measurements(K, dev, stream, peak)
+    if not args.quick and not args.no_decode:
+        dec = decode_8b(dev, args.decode_prompt, args.decode_new)
+        if world > 1:
+            t = torch.tensor([dec["ms_per_token"]], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            dec["tokens_per_s_all_replicas"] = round(world * 1e3 / float(t.item()), 2)
+        extra["decode_8b"] = dec
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = time_cpu_gemv(seconds=args.cpu_seconds)
@@ -337,6 +347,45 @@ def run_gpu(args):
     return 0
 
 
+DECODE_PROMPT, DECODE_NEW = 2048, 256
+DECODE_BYTES_PER_TOKEN_WEIGHTS = 4221370368  # all Q4_0 projections + LM head of the 8B shape
+
+
+def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW):
+    """8B-shape greedy decode, batch 1: 32 layers, d 4096, FFN 14336, 32/8 heads
+    x 128, vocab 128256, theta 5e5; Q4_0 projections N(0,0.02) seed 6, f16
+    embeddings/norms, f16 KV; prompt of uniform token ids (seed 7)."""
+    import torch
+    from agent_harness_b200.model import LLAMA_8B, Model
+    cfg = LLAMA_8B
+    cfg.max_seq = n_prompt + n_new + 8
+    m = Model(cfg, device=dev)
+    m.init_random(6, w_std=0.02, emb_std=1.0, norm_std=0.02)
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab_size, (1, n_prompt)).astype(np.int32)
+    t0 = time.perf_counter()
+    first = m.generate(prompt, 1)  # token-by-token prefill (inference/mod.rs:550) + first token
+    prefill_s = time.perf_counter() - t0
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    toks = m.decode(n_new + 1, 1)  # n_new full decode steps after the first token
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    tk = toks.cpu().numpy().ravel()
+    # replay check: the same prompt decodes to the same tokens
+    again = m.generate(prompt[:, :64], 8)
+    again2 = m.generate(prompt[:, :64], 8)
+    m.close()
+    per_tok = ms / 1e3 / n_new
+    return {"tokens_per_s": round(n_new / (ms / 1e3), 2), "ms_per_token": round(per_tok * 1e3, 4),
+            "prefill_tokens_per_s_token_by_token": round((n_prompt - 1) / prefill_s, 1),
+            "weight_gbs": round(DECODE_BYTES_PER_TOKEN_WEIGHTS / per_tok / 1e9, 1),
+            "n_prompt": n_prompt, "n_new": n_new, "first_tokens": [int(first[0, 0])] + [int(v) for v in tk[1:6]],
+            "deterministic": bool(np.array_equal(again, again2)),
+            "note": "decode steps replayed as one CUDA graph each (5 fused kernels per layer + head + argmax)"}
+
+
 def secondary_measurements(K, dev, stream, peak):
     """Config-1 dequant and f16->f32 throughput (each launch > L2)."""
     import torch
@@ -374,11 +423,24 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode"],
+                    help="decode: only the 8B decode measurement (for profiling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
+    ap.add_argument("--decode-prompt", type=int, default=DECODE_PROMPT)
+    ap.add_argument("--decode-new", type=int, default=DECODE_NEW)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "decode":
+        import torch
+        torch.cuda.set_device(0)
+        from agent_harness_b200 import _lib
+        _lib.check(_lib.lib().ah_device_init(0))
+        print(json.dumps({"workload": "decode_8b", **decode_8b(torch.device("cuda", 0), args.decode_prompt,
+                                                               args.decode_new)}), flush=True)
+        return 0
     return run_gpu(args)
 
 

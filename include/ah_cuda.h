@@ -150,6 +150,64 @@ AH_API int ah_gemv_4bit_into(float* out_dev, const float* scales_dev, const uint
 AH_API int ah_matvec_4bit_into(float* out_dev, const float* scales_dev, const uint8_t* packed_dev, const float* x_dev,
                         int64_t dim, int64_t group_size, void* stream);
 
+/* ---- Llama-shaped decoder ----------------------------------------------------------- */
+/* Reference: inference/config.rs:6-58 ModelConfig (the fields the decoder uses;
+ * rope sections default to [head_dim/2, 0, 0, 0] as config.rs:170-172 does). */
+typedef struct {
+  int32_t n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, vocab_size;
+  int32_t max_seq;    /* KV-cache capacity per sequence (inference/kv_cache.rs:24 uses 4096) */
+  int32_t max_batch;  /* sequences decoded together, 1..16 */
+  float rope_freq_base, rms_eps;
+} AhModelConfig;
+
+typedef struct AhModel AhModel;
+
+/* Tensor kinds for ah_model_load_tensor (GGUF names in inference/mod.rs:392-538). */
+#define AH_T_TOK_EMBD 0   /* token_embd.weight   f16 [vocab][n_embd]             */
+#define AH_T_ATTN_NORM 1  /* blk.L.attn_norm     f16 [n_embd]                    */
+#define AH_T_FFN_NORM 2   /* blk.L.ffn_norm      f16 [n_embd]                    */
+#define AH_T_OUT_NORM 3   /* output_norm.weight  f16 [n_embd]                    */
+#define AH_T_WQ 4         /* blk.L.attn_q        Q4_0 [n_head*head_dim][n_embd]  */
+#define AH_T_WK 5         /* blk.L.attn_k        Q4_0 [n_head_kv*head_dim][n_embd] */
+#define AH_T_WV 6         /* blk.L.attn_v        Q4_0 [n_head_kv*head_dim][n_embd] */
+#define AH_T_WO 7         /* blk.L.attn_output   Q4_0 [n_embd][n_head*head_dim]  */
+#define AH_T_WGATE 8      /* blk.L.ffn_gate      Q4_0 [n_ff][n_embd]             */
+#define AH_T_WUP 9        /* blk.L.ffn_up        Q4_0 [n_ff][n_embd]             */
+#define AH_T_WDOWN 10     /* blk.L.ffn_down      Q4_0 [n_embd][n_ff]             */
+#define AH_T_LM_HEAD 11   /* output.weight       Q4_0 [vocab][n_embd]            */
+
+/* Reference: inference/mod.rs:70-331 InferenceEngine::open_with_progress's
+ * device side: allocates the weight arena, f16 KV cache [batch][layer][kv_head]
+ * [max_seq][head_dim] and activations on the current device. */
+AH_API int ah_model_create(const AhModelConfig* cfg, AhModel** out);
+AH_API int ah_model_destroy(AhModel* m);
+/* Loads one tensor from device memory (f16 bits or Q4_0 blocks, per kind);
+ * Q4_0 projections are repacked into the GEMV layout (q|k|v fused, gate/up
+ * interleaved).  Layer is ignored for the model-level kinds. */
+AH_API int ah_model_load_tensor(AhModel* m, int kind, int layer, const void* data_dev, void* stream);
+/* Seeded synthetic weights (no reference counterpart): every projection Q4_0 of
+ * N(0, w_std), embeddings f16 N(0, emb_std), norm weights f16 1 + N(0, norm_std);
+ * tensor t of layer l draws from seed ah_model_tensor_seed(seed, kind, l). */
+AH_API int ah_model_init_random(AhModel* m, uint64_t seed, float w_std, float emb_std, float norm_std);
+AH_API uint64_t ah_model_tensor_seed(uint64_t seed, int kind, int layer);
+/* Reference: inference/mod.rs:547-562 generate with temperature 0 (greedy,
+ * sampling.rs:4-14 argmax), for `batch` sequences in lock step.  `prompt` is
+ * [batch][n_prompt] host int32; prefill runs forward() token by token as the
+ * reference does (mod.rs:550), then `n_new` greedy steps write their tokens to
+ * `out_tokens` [n_new][batch] (host).  Resets the KV cache. */
+AH_API int ah_model_generate(AhModel* m, const int32_t* prompt, int batch, int n_prompt, int n_new,
+                             int32_t* out_tokens, void* stream);
+/* Lower-level stepping (same semantics): reset, feed one token per sequence
+ * (forward(), inference/mod.rs:333-545) and read the logits [batch][vocab]. */
+AH_API int ah_model_reset(AhModel* m, int batch, void* stream);
+AH_API int ah_model_forward(AhModel* m, const int32_t* tokens_dev, float* logits_dev, void* stream);
+/* Runs `n` greedy decode steps from the current state as one CUDA graph per
+ * step (captured on first use); the first step consumes the argmax of the
+ * last forward's logits.  Tokens land in out_tokens_dev [n][batch]. */
+AH_API int ah_model_decode(AhModel* m, int n, int32_t* out_tokens_dev, void* stream);
+/* Current position (tokens consumed per sequence). */
+AH_API int ah_model_position(const AhModel* m, int* pos);
+
 /* ---- host-slice drop-ins (synchronous; reference signatures) ---------------------- */
 /* Reference: inference/math.rs:255-295 gemv_4bit_into(out, scales, packed, x, rows, cols, gs). */
 AH_API int ah_host_gemv_4bit_into(float* out, const float* scales, const uint8_t* packed, const float* x, size_t rows,

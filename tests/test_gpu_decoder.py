@@ -1,0 +1,111 @@
+"""GPU parity: the decoder step (inference/mod.rs:333-545 with per-head RoPE,
+f16 KV) against the oracle decoder on identical seeded weights.  Logits agree
+to 1e-3 normwise (max|d| / max|ref|) per step; greedy tokens match exactly."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def relerr(y, ref):
+    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def oracle_weights(cfg, seed, dev, w_std=0.02, emb_std=1.0, norm_std=0.02):
+    """Regenerates every tensor with the same device synthesizers the model uses."""
+    from agent_harness_b200 import kernels as K
+    from agent_harness_b200 import model as M
+    d, L = cfg.n_embd, cfg.n_layer
+
+    def f16(n, mean, std, kind, layer):
+        return K.synth_f16(n, mean, std, M.tensor_seed(seed, kind, layer), device=dev).cpu().numpy().view(np.uint16)
+
+    W = {"tok_embd": f16(cfg.vocab_size * d, 0.0, emb_std, M.TOK_EMBD, 0),
+         "out_norm": f16(d, 1.0, norm_std, M.OUT_NORM, 0),
+         "attn_norm": np.concatenate([f16(d, 1.0, norm_std, M.ATTN_NORM, l) for l in range(L)]),
+         "ffn_norm": np.concatenate([f16(d, 1.0, norm_std, M.FFN_NORM, l) for l in range(L)])}
+    shapes = cfg.shapes()
+    names = {M.WQ: "wq", M.WK: "wk", M.WV: "wv", M.WO: "wo", M.WGATE: "wg", M.WUP: "wu", M.WDOWN: "wd"}
+    for kind, name in names.items():
+        r, c = shapes[kind]
+        W[name] = [K.synth_q4_0(r, c, w_std, M.tensor_seed(seed, kind, l), device=dev).cpu().numpy() for l in range(L)]
+    r, c = shapes[M.LM_HEAD]
+    W["lm_head"] = K.synth_q4_0(r, c, w_std, M.tensor_seed(seed, M.LM_HEAD, 0), device=dev).cpu().numpy()
+    return W
+
+
+def oracle_model(oracle, cfg, W):
+    c = {"n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_ff": cfg.n_ff, "n_head": cfg.n_head,
+         "n_head_kv": cfg.n_head_kv, "head_dim": cfg.head_dim, "vocab": cfg.vocab_size,
+         "rope_base": cfg.rope_freq_base, "eps": cfg.rms_eps}
+    return oracle.OracleModel(c, W, cfg.max_seq)
+
+
+SMALL = dict(n_layer=2, n_embd=256, n_ff=512, n_head=4, n_head_kv=2, head_dim=64, vocab_size=1000, max_seq=64,
+             max_batch=2, rope_freq_base=10000.0, rms_eps=1e-5)
+
+
+def test_small_decoder_logits_and_greedy(cuda, oracle):
+    from agent_harness_b200.model import Model, ModelConfig
+    cfg = ModelConfig(**SMALL)
+    m = Model(cfg)
+    m.init_random(123)
+    W = oracle_weights(cfg, 123, cuda)
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, cfg.vocab_size, (2, 6)).astype(np.int32)
+    om = [oracle_model(oracle, cfg, W) for _ in range(2)]
+    m.reset(2)
+    for t in range(prompt.shape[1]):
+        logits = m.forward(prompt[:, t]).cpu().numpy()
+        for b in range(2):
+            ref = om[b].forward(int(prompt[b, t]), t)
+            assert relerr(logits[b], ref) <= TOL, (t, b, relerr(logits[b], ref))
+    # greedy continuation through the graph-replayed generate path
+    new = m.generate(prompt, 10)
+    for b in range(2):
+        o = oracle_model(oracle, cfg, W)
+        for t in range(prompt.shape[1]):
+            lg = o.forward(int(prompt[b, t]), t)
+        toks = []
+        pos = prompt.shape[1]
+        for _ in range(10):
+            nxt = oracle.argmax(lg)
+            toks.append(nxt)
+            lg = o.forward(nxt, pos)
+            pos += 1
+        assert list(new[:, b]) == toks, (b, list(new[:, b]), toks)
+    m.close()
+
+
+def test_generate_is_deterministic_and_resettable(cuda):
+    from agent_harness_b200.model import Model, ModelConfig
+    cfg = ModelConfig(**SMALL)
+    m = Model(cfg)
+    m.init_random(7)
+    prompt = np.arange(12, dtype=np.int32).reshape(2, 6) * 37 % cfg.vocab_size
+    a = m.generate(prompt, 16)
+    b = m.generate(prompt, 16)
+    assert np.array_equal(a, b)
+    assert m.position == 6 + 16 - 1
+    m.close()
+
+
+def test_8b_width_two_layers(cuda, oracle):
+    # Llama-3-8B layer widths (d 4096, FFN 14336, 32/8 heads x 128, vocab 128256)
+    from agent_harness_b200.model import Model, ModelConfig
+    cfg = ModelConfig(n_layer=2, n_embd=4096, n_ff=14336, n_head=32, n_head_kv=8, head_dim=128,
+                      vocab_size=128256, max_seq=64, max_batch=1, rope_freq_base=500000.0, rms_eps=1e-5)
+    m = Model(cfg)
+    m.init_random(6)
+    W = oracle_weights(cfg, 6, cuda)
+    o = oracle_model(oracle, cfg, W)
+    m.reset(1)
+    for t, tok in enumerate([17, 40000, 128255]):
+        lg = m.forward([tok]).cpu().numpy()[0]
+        ref = o.forward(tok, t)
+        assert relerr(lg, ref) <= TOL, (t, relerr(lg, ref))
+        assert int(np.argmax(lg)) == oracle.argmax(ref)
+    m.close()
