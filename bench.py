@@ -36,8 +36,9 @@ GEMV_BYTES = ROWS * (COLS // 32) * 18 + COLS * 4 + ROWS * 4  # 9,469,952
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum per GEMV launch, from the ncu
-# capture summarised in profiles/gemv_q4_0_4096x4096.md (None until captured).
-NCU_TRAFFIC_PER_LAUNCH = None
+# capture summarised in profiles/gemv_q4_0_4096x4096_batch1.md (read 9,492,480 B,
+# write 0 B: y stays in L2 at kernel end).
+NCU_TRAFFIC_PER_LAUNCH = 9492480
 
 
 def peaks():
