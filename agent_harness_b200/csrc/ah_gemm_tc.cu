@@ -1,0 +1,545 @@
+// ah_gemm_tc.cu — Q4 prefill GEMM on the 5th-generation tensor cores
+// (tcgen05.mma, accumulators in tensor memory).
+//
+//   C[m][n] = sum_k A[m][k] * W[n][k],  W[n][k] = d(n, k/32) * (q(n,k) - 8)
+//
+// A (tokens x cols, f32) is converted once per call by k_gemm_prep into f16
+// tiles already in the tensor core's K-major SWIZZLE_128B shared-memory image
+// (128 tokens x 64 columns = 16 KB per tile), each token row scaled by an
+// exact power of two 2^s so its max |a| lies in [2^14, 2^15) (f16 keeps 11
+// significant bits over the row's whole range; C rows are multiplied by 2^-s
+// in the epilogue).  W stays in the GEMV's tiled Q4 layout in HBM (see
+// ah_gemv.cuh): the kernel bulk-copies the nibble and scale chunks of a
+// 208-row x 64-column tile into shared memory, four dequant warps expand them
+// to f16 d*(q-8) (one rounding, RNE) straight into the swizzled B image, and
+// one thread issues the MMAs:
+//
+//   warp 0      raw weight producer   (cp.async.bulk -> raw ring, 4 stages)
+//   warp 1      activation producer   (cp.async.bulk -> A ring, 3 stages)
+//   warp 2      TMEM owner + MMA issuer (tcgen05.mma M=128 N=208 K=16, f16 in,
+//               f32 accumulate; tcgen05.commit frees a stage)
+//   warps 3..6  dequant (raw ring -> B ring), then the epilogue
+//               (tcgen05.ld 32x32b -> registers -> C)
+//
+// A CTA owns 256 tokens (two M=128 accumulators, TMEM columns [0,208) and
+// [256,464)) x 208 weight rows over the full K.  For the MLP up-projection
+// shape (M 512, N 14336, K 4096) that is 2 x 69 = 138 CTAs: one wave on 148
+// SMs, one CTA per SM (shared memory ~207 KB).
+//
+// Every mbarrier wait is bounded; a wait that gives up records AH_ETIMEOUT in
+// the device error word, raises a CTA-wide abort flag, and the kernel drains
+// its own bulk copies and MMAs before freeing tensor memory and returning.
+//
+// Reference: the prefill of inference/mod.rs:547-562 runs forward() token by
+// token (mod.rs:550), i.e. one gemv_4bit_into (inference/math.rs:255-295) per
+// token and projection; this kernel computes the same products for all
+// tokens of a prompt at once.
+
+#include <algorithm>
+
+#include "ah_common.cuh"
+#include "ah_gemv_impl.cuh"
+#include "ah_sm100.cuh"
+
+struct AhQ4Weight;
+
+namespace ah {
+namespace {
+
+constexpr int kTokTile = 128;                       // tokens per MMA (TMEM lanes)
+constexpr int kRowTiles = 13;                       // 16-row weight tiles per CTA
+constexpr int kBN = kRowTiles * 16;                 // 208 = MMA N
+constexpr int kBK = 64;                             // columns per k-step (one block pair)
+constexpr int kStages = 3;                          // A/B operand ring
+constexpr int kRawStages = 4;                       // raw weight ring
+constexpr int kATileBytes = kTokTile * kBK * 2;     // 16384
+constexpr int kBBytes = kBN * kBK * 2;              // 26624
+constexpr int kRawNibBytes = kRowTiles * 512;       // 6656
+constexpr int kRawBytes = kRawNibBytes + kRowTiles * 128;  // + f32 scales worst case
+constexpr int kTmemCols = 512;
+constexpr int kAccColStride = 256;                  // TMEM column offset of token half 1
+constexpr int kDequantWarps = 4;
+constexpr int kGemmThreads = (3 + kDequantWarps) * 32;
+constexpr uint32_t kWaitLimit = 1u << 24;
+
+// Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B f16
+// (bits 7-9, 10-12 = 0), both K-major (bits 15, 16 = 0), N>>3 at bits 17-22,
+// M>>4 at bits 24-28.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kTokTile >> 4) << 24);
+
+template <int kHalves>
+struct GemmSmem {
+  static constexpr int kA = 0;
+  static constexpr int kB = kA + kStages * kHalves * kATileBytes;
+  static constexpr int kRaw = kB + kStages * kBBytes;
+  static constexpr int kBars = kRaw + kRawStages * kRawBytes;
+  static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
+  static constexpr int kMisc = kBars + kNumBars * 8;
+  static constexpr int kTotal = kMisc + 16;
+  static constexpr size_t kDynamic = (size_t)kTotal + 1024;  // slack for 1 KB alignment
+};
+
+struct GemmArgs {
+  Q4Tiled w;
+  const uint8_t* at;      // [M_pad/128][kp][16 KB] f16 swizzled activation tiles
+  const float* row_inv;   // [M_pad] 2^-s per token row
+  float* c;
+  int64_t ldc;
+  int64_t m;
+  int* err;
+  bool c_vec;  // ldc % 4 == 0 and c 16-byte aligned
+};
+
+// ---- tcgen05 wrappers -----------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), LBO 16 bytes (unused for swizzled K-major),
+// descriptor version 1 (bits 46-47), layout SWIZZLE_128B = 2 (bits 61-63).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma issued so far by this thread completes.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  // load and wait in one statement: the registers are undefined until the wait
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+// Waits on `bar`'s phase `parity`; on give-up raises the CTA abort flag.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag,
+                                              int code) {
+  if (mbar_wait_bounded(bar, parity, err, code, kWaitLimit)) return true;
+  *abort_flag = 1;
+  return false;
+}
+
+// ---- activation prep: f32 rows -> scaled f16 swizzled tiles ---------------------
+// One CTA per (padded) token row.  Element (m, k) of tile (m/128, k/64) sits at
+// byte (m%128)*128 + (((k%64)/8) ^ (m%8))*16 + (k%8)*2 — the SWIZZLE_128B
+// K-major image the MMA descriptors above describe.
+constexpr int kPrepThreads = 256;
+
+__global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restrict__ a, int64_t lda, int64_t m_rows,
+                                                            int64_t k_cols, int64_t kp, bool vec_rows,
+                                                            uint8_t* __restrict__ at, float* __restrict__ row_inv) {
+  const int64_t m = blockIdx.x;
+  const int tid = threadIdx.x;
+  const bool live = m < m_rows;
+  const float* row = a + m * lda;
+  const bool vec = live && vec_rows;
+  __shared__ float red[kPrepThreads / 32];
+  // pass 1: max |a| over the row (NaN ignored here; it still reaches C)
+  float amax = 0.0f;
+  if (live) {
+    if (vec) {
+      for (int64_t k = (int64_t)tid * 4; k < k_cols; k += kPrepThreads * 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(row + k));
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+    } else {
+      for (int64_t k = tid; k < k_cols; k += kPrepThreads) amax = fmaxf(amax, fabsf(row[k]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  __syncthreads();
+  amax = red[0];
+#pragma unroll
+  for (int i = 1; i < kPrepThreads / 32; ++i) amax = fmaxf(amax, red[i]);
+  // exponent s with amax * 2^s in [2^14, 2^15), clamped so 2^s and 2^-s are
+  // normal floats; zero rows and non-finite maxima keep s = 0
+  int s = 0;
+  const uint32_t ab = __float_as_uint(amax);
+  if (amax > 0.0f && ((ab >> 23) & 0xFF) != 0xFF) {
+    const int e = (int)((ab >> 23) & 0xFF) - 126;  // amax in [2^(e-1), 2^e)
+    s = min(max(15 - e, -120), 120);
+  }
+  const float scale = __uint_as_float((uint32_t)(127 + s) << 23);
+  if (tid == 0) row_inv[m] = live ? __uint_as_float((uint32_t)(127 - s) << 23) : 0.0f;
+  // pass 2: scaled f16, one 16-byte chunk (8 columns) per thread step
+  const int64_t mt = m >> 7;
+  const int ml = (int)(m & 127);
+  uint8_t* tile_row = at + (size_t)mt * kp * kATileBytes + (size_t)ml * 128;
+  const int64_t nchunks = kp * 8;
+  for (int64_t c = tid; c < nchunks; c += kPrepThreads) {
+    const int64_t k0 = c * 8;
+    float v[8];
+    if (vec && k0 + 8 <= k_cols) {
+      const float4 p0 = __ldg(reinterpret_cast<const float4*>(row + k0));
+      const float4 p1 = __ldg(reinterpret_cast<const float4*>(row + k0 + 4));
+      v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+      v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (live && k0 + i < k_cols) ? row[k0 + i] : 0.0f;
+    }
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 hv = __floats2half2_rn(v[2 * i] * scale, v[2 * i + 1] * scale);
+      h[i] = *reinterpret_cast<const uint32_t*>(&hv);
+    }
+    const int64_t kpi = c >> 3;
+    const int chunk = (int)(c & 7);
+    uint8_t* dst = tile_row + (size_t)kpi * kATileBytes + (size_t)((chunk ^ (ml & 7)) << 4);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+}
+
+// ---- the GEMM ------------------------------------------------------------------
+template <int kHalves, bool kF32>
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(GemmArgs g) {
+  using L = GemmSmem<kHalves>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBars);
+  uint64_t* a_full = bars;
+  uint64_t* b_full = bars + kStages;
+  uint64_t* ab_empty = bars + 2 * kStages;
+  uint64_t* raw_full = bars + 3 * kStages;
+  uint64_t* raw_empty = raw_full + kRawStages;
+  uint64_t* acc_full = raw_empty + kRawStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t kp = g.w.kp;
+  const int64_t rt0 = (int64_t)blockIdx.x * kRowTiles;
+  const int nrt = (int)(g.w.r16 - rt0 < kRowTiles ? g.w.r16 - rt0 : kRowTiles);
+  const int64_t mt0 = (int64_t)blockIdx.y * kHalves;
+  constexpr int kScaleBytes = kF32 ? 128 : 64;  // per (row tile, pair)
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&b_full[i], kDequantWarps);
+      mbar_init(&ab_empty[i], 1);
+    }
+    for (int i = 0; i < kRawStages; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], kDequantWarps);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- raw weight producer ----
+    int64_t issued = 0;
+    for (int64_t s = 0; s < kp; ++s) {
+      const int r = (int)(s % kRawStages);
+      bool ok = true;
+      if (lane == 0) {
+        if (*abort_flag) ok = false;
+        else if (s >= kRawStages)
+          ok = wait_or_abort(&raw_empty[r], (uint32_t)((s / kRawStages - 1) & 1), g.err, abort_flag, AH_ETIMEOUT);
+        if (ok) mbar_arrive_expect_tx(&raw_full[r], (uint32_t)(nrt * (512 + kScaleBytes)));
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      uint8_t* dst = smem + L::kRaw + r * kRawBytes;
+      if (lane < nrt) {
+        const uint4* src = g.w.nib + ((rt0 + lane) * kp + s) * 32;
+        bulk_g2s(dst + lane * 512, src, 512, &raw_full[r]);
+      } else if (lane >= 16 && lane < 16 + nrt) {
+        const int i = lane - 16;
+        const uint8_t* src = static_cast<const uint8_t*>(g.w.scales) + ((rt0 + i) * kp + s) * kScaleBytes;
+        bulk_g2s(dst + kRawNibBytes + i * kScaleBytes, src, kScaleBytes, &raw_full[r]);
+      }
+      ++issued;
+    }
+    // drain: the copies of the last stages have landed before the CTA can exit
+    if (lane == 0 && *abort_flag) {
+      for (int64_t s = issued > kRawStages ? issued - kRawStages : 0; s < issued; ++s)
+        mbar_wait_bounded(&raw_full[s % kRawStages], (uint32_t)((s / kRawStages) & 1), g.err, AH_ETIMEOUT,
+                          kWaitLimit);
+    }
+  } else if (warp == 1) {
+    // ---- activation producer ----
+    if (lane == 0) {
+      int64_t issued = 0;
+      for (int64_t s = 0; s < kp; ++s) {
+        const int st = (int)(s % kStages);
+        if (*abort_flag) break;
+        if (s >= kStages &&
+            !wait_or_abort(&ab_empty[st], (uint32_t)((s / kStages - 1) & 1), g.err, abort_flag, AH_ETIMEOUT))
+          break;
+        mbar_arrive_expect_tx(&a_full[st], (uint32_t)(kHalves * kATileBytes));
+        for (int h = 0; h < kHalves; ++h) {
+          const uint8_t* src = g.at + ((size_t)(mt0 + h) * kp + s) * kATileBytes;
+          bulk_g2s(smem + L::kA + (st * kHalves + h) * kATileBytes, src, kATileBytes, &a_full[st]);
+        }
+        ++issued;
+      }
+      if (*abort_flag) {
+        for (int64_t s = issued > kStages ? issued - kStages : 0; s < issued; ++s)
+          mbar_wait_bounded(&a_full[s % kStages], (uint32_t)((s / kStages) & 1), g.err, AH_ETIMEOUT, kWaitLimit);
+      }
+    }
+  } else if (warp == 2) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      for (int64_t s = 0; s < kp; ++s) {
+        const int st = (int)(s % kStages);
+        const uint32_t ph = (uint32_t)((s / kStages) & 1);
+        if (*abort_flag) break;
+        if (!wait_or_abort(&a_full[st], ph, g.err, abort_flag, AH_ETIMEOUT)) break;
+        if (!wait_or_abort(&b_full[st], ph, g.err, abort_flag, AH_ETIMEOUT)) break;
+        tc_fence_after();
+        const uint32_t b_addr = smem_u32(smem + L::kB + st * kBBytes);
+#pragma unroll
+        for (int h = 0; h < kHalves; ++h) {
+          const uint32_t a_addr = smem_u32(smem + L::kA + (st * kHalves + h) * kATileBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_f16(tmem_base + h * kAccColStride, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32),
+                    (s > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&ab_empty[st]);
+      }
+      // completes when every MMA above has (also on abort, so TMEM can be freed)
+      mma_commit(acc_full);
+    }
+  } else {
+    // ---- dequant warps, then epilogue ----
+    const int wd = warp - 3;
+    const int gq = lane >> 2, t = lane & 3;
+    for (int64_t s = 0; s < kp; ++s) {
+      const int r = (int)(s % kRawStages);
+      const int st = (int)(s % kStages);
+      bool ok = true;
+      if (lane == 0) {
+        if (*abort_flag) ok = false;
+        else {
+          ok = wait_or_abort(&raw_full[r], (uint32_t)((s / kRawStages) & 1), g.err, abort_flag, AH_ETIMEOUT);
+          if (ok && s >= kStages)
+            ok = wait_or_abort(&ab_empty[st], (uint32_t)((s / kStages - 1) & 1), g.err, abort_flag, AH_ETIMEOUT);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const uint8_t* raw = smem + L::kRaw + r * kRawBytes;
+      const uint32_t bst = smem_u32(smem + L::kB + st * kBBytes);
+      for (int rt = wd; rt < nrt; rt += kDequantWarps) {
+        const uint4 nv = *reinterpret_cast<const uint4*>(raw + rt * 512 + lane * 16);
+        const uint32_t wv[4] = {nv.x, nv.y, nv.z, nv.w};
+        float dsc[4];
+        __half dh[4];
+        if (kF32) {
+          const float4 d4 = *reinterpret_cast<const float4*>(raw + kRawNibBytes + rt * 128 + gq * 16);
+          dsc[0] = d4.x; dsc[1] = d4.y; dsc[2] = d4.z; dsc[3] = d4.w;
+        } else {
+          const uint2 d2 = *reinterpret_cast<const uint2*>(raw + kRawNibBytes + rt * 64 + gq * 8);
+          dh[0] = __ushort_as_half((unsigned short)(d2.x & 0xFFFFu));
+          dh[1] = __ushort_as_half((unsigned short)(d2.x >> 16));
+          dh[2] = __ushort_as_half((unsigned short)(d2.y & 0xFFFFu));
+          dh[3] = __ushort_as_half((unsigned short)(d2.y >> 16));
+        }
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          const int blk = wi >> 1, half = wi & 1;
+          const int row = rt * 16 + gq + 8 * half;  // (row & 7) == gq
+          const uint32_t row_addr = bst + row * 128 + 4 * t;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            // nibbles j and j+4 of the word are block elements 2t+off and
+            // 2t+off+1, off = {0,16,8,24}[j]; 1024+q is exact in f16.
+            const uint32_t bits = ((wv[wi] >> (4 * j)) & 0x000F000Fu) | 0x64006400u;
+            __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&bits), __float2half2_rn(1032.0f));
+            __half2 v;
+            if (kF32) {
+              const float2 qf = __half22float2(q);
+              v = __floats2half2_rn(qf.x * dsc[wi], qf.y * dsc[wi]);
+            } else {
+              v = __hmul2(q, __half2half2(dh[wi]));
+            }
+            const int chunk = 4 * blk + ((j & 1) << 1) + (j >> 1);  // k/8 for off {0,16,8,24}
+            sts32(row_addr + ((chunk ^ gq) << 4), *reinterpret_cast<const uint32_t*>(&v));
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&b_full[st]);
+        mbar_arrive(&raw_empty[r]);
+      }
+    }
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its token rows)
+    const bool have = mbar_wait_bounded(acc_full, 0, g.err, AH_ETIMEOUT, kWaitLimit);
+    tc_fence_after();
+    if (have && !*abort_flag) {
+      const int q = warp & 3;
+      const int64_t n0 = rt0 * 16;
+      const int64_t n_rows = g.w.rows;
+      const bool vec = g.c_vec;
+      for (int h = 0; h < kHalves; ++h) {
+        const int64_t m = (mt0 + h) * kTokTile + q * 32 + lane;
+        const float inv = m < g.m ? g.row_inv[m] : 0.0f;
+        float* crow = g.c + m * g.ldc;
+#pragma unroll 1
+        for (int c0 = 0; c0 < kBN; c0 += 16) {
+          float v[16];
+          tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * kAccColStride + c0), v);
+          if (m >= g.m) continue;
+          const int64_t n = n0 + c0;
+          if (vec && n + 16 <= n_rows) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              st_cs_f4(reinterpret_cast<float4*>(crow + n + i),
+                       make_float4(v[i] * inv, v[i + 1] * inv, v[i + 2] * inv, v[i + 3] * inv));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (n + i < n_rows) crow[n + i] = v[i] * inv;
+          }
+        }
+      }
+    }
+  }
+
+  // teardown: every MMA has completed (acc_full) before TMEM is released
+  if (warp == 2 && lane == 0 && *abort_flag) mbar_wait_bounded(acc_full, 0, g.err, AH_ETIMEOUT, kWaitLimit);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <int kHalves, bool kF32>
+int gemm_launch(const GemmArgs& a, int64_t grid_x, int64_t grid_y, cudaStream_t st) {
+  using L = GemmSmem<kHalves>;
+  static_assert(L::kDynamic <= 227 * 1024, "shared memory budget");
+  auto kern = k_gemm_q4_tc<kHalves, kF32>;
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynamic));
+    configured_device = dev;
+  }
+  kern<<<dim3((unsigned)grid_x, (unsigned)grid_y), kGemmThreads, L::kDynamic, st>>>(a);
+  AH_LAUNCH_CHECK();
+  return AH_OK;
+}
+
+inline int64_t gemm_halves(int64_t m) { return m > kTokTile ? 2 : 1; }
+inline int64_t gemm_m_pad(int64_t m) {
+  const int64_t tile = kTokTile * gemm_halves(m);
+  return (m + tile - 1) / tile * tile;
+}
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+// Workspace: f16 activation tiles (M_pad x kp*64 x 2 B) + one f32 per padded row.
+size_t gemm_workspace_bytes(const Q4Tiled& w, int64_t m) {
+  const int64_t mp = gemm_m_pad(m);
+  return align_up((size_t)mp * (size_t)w.kp * kBK * 2, 1024) + align_up((size_t)mp * 4, 256);
+}
+
+int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c, int64_t ldc, void* ws,
+             size_t ws_bytes, cudaStream_t st) {
+  AH_REQUIRE(m >= 0, "gemm: negative M");
+  if (m == 0) return AH_OK;
+  AH_REQUIRE(a != nullptr && c != nullptr && ws != nullptr, "gemm: null pointer");
+  AH_REQUIRE(lda >= w.cols && ldc >= w.rows, "gemm: lda must be >= cols and ldc >= rows");
+  AH_REQUIRE(ws_bytes >= gemm_workspace_bytes(w, m), "gemm: workspace of %zu bytes is below the %zu needed",
+             ws_bytes, gemm_workspace_bytes(w, m));
+  AH_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 1023) == 0, "gemm: workspace must be 1024-byte aligned");
+  const int64_t mp = gemm_m_pad(m);
+  uint8_t* at = static_cast<uint8_t*>(ws);
+  float* row_inv = reinterpret_cast<float*>(at + align_up((size_t)mp * (size_t)w.kp * kBK * 2, 1024));
+  const bool vec_rows = (lda % 4 == 0) && aligned16(a) && (w.cols % 8 == 0);
+  k_gemm_prep<<<(unsigned)mp, kPrepThreads, 0, st>>>(a, lda, m, w.cols, w.kp, vec_rows, at, row_inv);
+  AH_LAUNCH_CHECK();
+  GemmArgs g{};
+  g.w = w;
+  g.at = at;
+  g.row_inv = row_inv;
+  g.c = c;
+  g.ldc = ldc;
+  g.m = m;
+  g.err = device_error_word();
+  g.c_vec = (ldc % 4 == 0) && aligned16(c);
+  const int64_t gx = (w.r16 + kRowTiles - 1) / kRowTiles;
+  const int64_t halves = gemm_halves(m);
+  const int64_t gy = mp / (kTokTile * halves);
+  AH_REQUIRE(gy <= 65535, "gemm: M too large for one launch");
+  if (halves == 2)
+    return w.f32_scales ? gemm_launch<2, true>(g, gx, gy, st) : gemm_launch<2, false>(g, gx, gy, st);
+  return w.f32_scales ? gemm_launch<1, true>(g, gx, gy, st) : gemm_launch<1, false>(g, gx, gy, st);
+}
+
+}  // namespace ah
+
+extern "C" {
+
+AH_API int ah_q4w_gemm_workspace_bytes(const AhQ4Weight* w, int64_t m, size_t* bytes) {
+  AH_REQUIRE(w != nullptr && bytes != nullptr, "ah_q4w_gemm_workspace_bytes: null argument");
+  AH_REQUIRE(m >= 0, "ah_q4w_gemm_workspace_bytes: negative M");
+  *bytes = ah::gemm_workspace_bytes(ah::q4w_tiled(w), m);
+  return AH_OK;
+}
+
+AH_API int ah_q4w_gemm(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev, int64_t ldc,
+                       void* workspace_dev, size_t workspace_bytes, void* stream) {
+  AH_REQUIRE(w != nullptr, "ah_q4w_gemm: null weight");
+  return ah::gemm_run(ah::q4w_tiled(w), a_dev, lda, m, c_dev, ldc, workspace_dev, workspace_bytes,
+                      ah::as_stream(stream));
+}
+
+}  // extern "C"

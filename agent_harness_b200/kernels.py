@@ -168,6 +168,27 @@ class Q4Weight:
         call("ah_q4w_gemv", self._h, _ptr(xb), _ptr(out), batch, _stream(x.device))
         return out.reshape(self.rows) if squeeze else out
 
+    def gemm_workspace_bytes(self, m: int) -> int:
+        n = C.c_size_t()
+        call("ah_q4w_gemm_workspace_bytes", self._h, m, C.byref(n))
+        return int(n.value)
+
+    def gemm(self, a: torch.Tensor, out: torch.Tensor | None = None,
+             workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """C = A @ W^T on the tensor cores for A of shape [m, cols] f32 (prefill)."""
+        assert a.dtype == torch.float32 and a.dim() == 2 and a.shape[1] == self.cols and a.stride(1) == 1
+        m = a.shape[0]
+        if out is None:
+            out = torch.empty(m, self.rows, dtype=torch.float32, device=a.device)
+        need = self.gemm_workspace_bytes(m)
+        if workspace is None or workspace.numel() < need + 1024:
+            workspace = torch.empty(need + 1024, dtype=torch.uint8, device=a.device)
+        base = workspace.data_ptr()
+        aligned = (base + 1023) // 1024 * 1024
+        call("ah_q4w_gemm", self._h, _ptr(a), a.stride(0), m, _ptr(out), out.stride(0),
+             C.c_void_p(aligned), need, _stream(a.device))
+        return out
+
     def close(self):
         if self._h:
             lib().ah_q4w_destroy(self._h)

@@ -141,6 +141,20 @@ AH_API int64_t ah_q4w_weight_bytes(const AhQ4Weight* w);
  */
 AH_API int ah_q4w_gemv(const AhQ4Weight* w, const float* x_dev, float* y_dev, int batch, void* stream);
 
+/* ---- prefill GEMM (tcgen05 tensor cores) -------------------------------------------- */
+/* Reference: the prompt prefill of inference/mod.rs:547-562, which runs
+ * forward() token by token (mod.rs:550) and so one inference/math.rs:255-295
+ * gemv_4bit_into per token and projection; here all m tokens at once:
+ * c[i][r] = sum_j W[r][j] * a[i][j], a_dev [m][lda] f32 (lda >= cols), c_dev
+ * [m][ldc] f32 (ldc >= rows).  Tensor-core operands are f16: W as d*(q-8)
+ * rounded once, a per row scaled by a power of two into f16 range; f32
+ * accumulation.  `workspace_dev` (1024-byte aligned, at least
+ * ah_q4w_gemm_workspace_bytes(w, m) bytes) holds the converted activations;
+ * calls on different streams need different workspaces.  m == 0 is a no-op. */
+AH_API int ah_q4w_gemm_workspace_bytes(const AhQ4Weight* w, int64_t m, size_t* bytes);
+AH_API int ah_q4w_gemm(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev, int64_t ldc,
+                       void* workspace_dev, size_t workspace_bytes, void* stream);
+
 /* Reference: inference/math.rs:255-295 gemv_4bit_into on the engine format as
  * stored (f32 scales [rows][ceil(cols/gs)], linear nibbles), device pointers, any
  * group size; empty input -> zero output (math.rs:264-267). */
