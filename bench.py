@@ -298,6 +298,7 @@ def run_gpu(args):
     extra = {}
     if rank == 0 and not args.quick:
         extra = secondary_measurements(K, dev, stream, peak)
+        extra["prefill_gemm"] = prefill_gemm(K, dev, cpu_tokens=0 if args.no_cpu else 8)
     if not args.quick and not args.no_decode:
         dec = decode_8b(dev, args.decode_prompt, args.decode_new)
         if world > 1:
@@ -387,6 +388,72 @@ def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW):
             "note": "decode steps replayed as one CUDA graph each (5 fused kernels per layer + head + argmax)"}
 
 
+GEMM_M, GEMM_N, GEMM_K = 512, 14336, 4096
+GEMM_FLOP = 2 * GEMM_M * GEMM_N * GEMM_K  # 6.013e10
+
+
+def tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (bf16 cuBLAS burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def prefill_gemm(K, dev, iters=20, cpu_tokens=0):
+    """Q4_0 prefill GEMM, M 512 x N 14336 x K 4096 (MLP up-projection shape):
+    W ~ N(0,0.02) seed 4, A ~ N(0,1) seed 5, C f32.  Each timed launch (the
+    activation conversion + the tcgen05 GEMM, CUDA events on the launching
+    stream) follows a 256 MB write that flushes L2."""
+    import torch
+    blocks = K.synth_q4_0(GEMM_N, GEMM_K, 0.02, 4, device=dev)
+    W = K.Q4Weight.from_q4_0(blocks, GEMM_N, GEMM_K)
+    a = K.fill_normal(GEMM_M * GEMM_K, 0.0, 1.0, 5, device=dev).reshape(GEMM_M, GEMM_K)
+    c = torch.empty(GEMM_M, GEMM_N, dtype=torch.float32, device=dev)
+    ws = torch.empty(W.gemm_workspace_bytes(GEMM_M) + 1024, dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        W.gemm(a, c, ws)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        W.gemm(a, c, ws)
+        e1.record(st)
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    times.sort()
+    ms = times[len(times) // 2]
+    peak, kind = tensor_peak()
+    tf = GEMM_FLOP / (ms / 1e3) / 1e12
+    out = {"tflops": round(tf, 1), "us_per_call": round(ms * 1e3, 2), "frac_of_peak": round(tf / peak, 4),
+           "peak_tflops": peak, "peak_source": kind, "flop_per_call": GEMM_FLOP,
+           "shape": f"M{GEMM_M} N{GEMM_N} K{GEMM_K}", "l2": "flushed (256 MB write) before each timed launch",
+           "kernels": "k_gemm_prep + k_gemm_q4_tc<2,false>", "finite": bool(torch.isfinite(c).all().item())}
+    if cpu_tokens:
+        # the reference's prefill path: one AVX-512 gemv_4bit_into per token row
+        from oracle import oracle as O
+        rng = np.random.default_rng(4)
+        nb = GEMM_N * GEMM_K // 32
+        scales = (rng.random(nb) * 0.004).astype(np.float32)
+        packed = rng.integers(0, 256, GEMM_N * GEMM_K // 2, dtype=np.uint8)
+        ah = a[:cpu_tokens].cpu().numpy()
+        ch = np.empty((cpu_tokens, GEMM_N), np.float32)
+        nt = cpu_threads()
+        t0 = time.perf_counter()
+        O.lib().or_avx_gemm_rows(ch, scales, packed, np.ascontiguousarray(ah), cpu_tokens, GEMM_N, GEMM_K, nt)
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {"value": round(2.0 * cpu_tokens * GEMM_N * GEMM_K / dt / 1e12, 5),
+                               "unit": "TFLOP/s", "cores": nt, "kind": "port",
+                               "sample": f"{cpu_tokens} token rows through the AVX-512 gemv_4bit_into restatement "
+                                         f"(token-by-token prefill, inference/mod.rs:550), {dt:.2f} s"}
+    W.close()
+    return out
+
+
 def secondary_measurements(K, dev, stream, peak):
     """Config-1 dequant and f16->f32 throughput (each launch > L2)."""
     import torch
@@ -424,8 +491,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode"],
-                    help="decode: only the 8B decode measurement (for profiling)")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode", "gemm"],
+                    help="decode / gemm: only the 8B decode or the prefill GEMM measurement (for profiling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
@@ -441,6 +508,15 @@ def main():
         _lib.check(_lib.lib().ah_device_init(0))
         print(json.dumps({"workload": "decode_8b", **decode_8b(torch.device("cuda", 0), args.decode_prompt,
                                                                args.decode_new)}), flush=True)
+        return 0
+    if args.workload == "gemm":
+        import torch
+        torch.cuda.set_device(0)
+        from agent_harness_b200 import _lib
+        from agent_harness_b200 import kernels as K
+        _lib.check(_lib.lib().ah_device_init(0))
+        print(json.dumps({"workload": "prefill_gemm", **prefill_gemm(K, torch.device("cuda", 0),
+                                                                      iters=max(args.steps, 1))}), flush=True)
         return 0
     return run_gpu(args)
 
