@@ -52,6 +52,7 @@ SIGNATURES = {
     "ah_q4w_gemv": (i32, [vp, vp, vp, i32, vp]),
     "ah_q4w_gemm_workspace_bytes": (i32, [vp, i64, C.POINTER(C.c_size_t)]),
     "ah_q4w_gemm": (i32, [vp, vp, i64, i64, vp, i64, vp, C.c_size_t, vp]),
+    "ah_q4w_gemm_noalloc": (i32, [vp, vp, i64, i64, vp, i64, vp]),
     "ah_gemv_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, i64, vp]),
     "ah_matvec_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, vp]),
     "ah_model_create": (i32, [vp, C.POINTER(vp)]),

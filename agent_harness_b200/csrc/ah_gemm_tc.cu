@@ -36,6 +36,7 @@
 // tokens of a prompt at once.
 
 #include <algorithm>
+#include <mutex>
 
 #include "ah_common.cuh"
 #include "ah_gemv_impl.cuh"
@@ -524,9 +525,58 @@ int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c,
   return w.f32_scales ? gemm_launch<1, true>(g, gx, gy, st) : gemm_launch<1, false>(g, gx, gy, st);
 }
 
+// ---- allocation-free variant ------------------------------------------------------
+// ah_q4w_gemm_noalloc keeps its workspace in this fixed per-device buffer instead
+// of a caller allocation.  Every byte the GEMM reads from it is written by the
+// k_gemm_prep launch of the same call, so nothing needs clearing between calls;
+// calls that overlap in time on one device race on it.
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) uint8_t g_gemm_static_scratch[kStaticScratchBytes];
+
+// Device address of g_gemm_static_scratch in the current device's context,
+// looked up once per device.
+int static_scratch(void** out) {
+  int dev = 0;
+  AH_CUDA_TRY(cudaGetDevice(&dev));
+  constexpr int kMaxDevices = 64;
+  AH_REQUIRE(dev >= 0 && dev < kMaxDevices, "static scratch: device %d out of range", dev);
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_gemm_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(AH_ECUDA, "cudaGetSymbolAddress(g_gemm_static_scratch): %s", cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return AH_OK;
+}
+
 }  // namespace ah
 
 extern "C" {
+
+AH_API int ah_q4w_gemm_noalloc(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev,
+                               int64_t ldc, void* stream) {
+  AH_REQUIRE(w != nullptr, "ah_q4w_gemm_noalloc: null weight");
+  AH_REQUIRE(m >= 0, "ah_q4w_gemm_noalloc: negative M");
+  if (m == 0) return AH_OK;
+  const ah::Q4Tiled& t = ah::q4w_tiled(w);
+  void* base = nullptr;
+  const int rc = ah::static_scratch(&base);
+  if (rc != AH_OK) return rc;
+  // the GEMM wants a 1024-byte aligned workspace; the buffer is 256-aligned
+  const uintptr_t b = reinterpret_cast<uintptr_t>(base);
+  const uintptr_t al = (b + 1023) & ~uintptr_t(1023);
+  const size_t usable = ah::kStaticScratchBytes - (size_t)(al - b);
+  const size_t need = ah::gemm_workspace_bytes(t, m);
+  AH_REQUIRE(need <= usable,
+             "ah_q4w_gemm_noalloc: M=%lld x cols=%lld needs %zu scratch bytes; the static buffer holds %zu",
+             (long long)m, (long long)t.cols, need, usable);
+  return ah::gemm_run(t, a_dev, lda, m, c_dev, ldc, reinterpret_cast<void*>(al), usable, ah::as_stream(stream));
+}
 
 AH_API int ah_q4w_gemm_workspace_bytes(const AhQ4Weight* w, int64_t m, size_t* bytes) {
   AH_REQUIRE(w != nullptr && bytes != nullptr, "ah_q4w_gemm_workspace_bytes: null argument");

@@ -154,6 +154,12 @@ AH_API int ah_q4w_gemv(const AhQ4Weight* w, const float* x_dev, float* y_dev, in
 AH_API int ah_q4w_gemm_workspace_bytes(const AhQ4Weight* w, int64_t m, size_t* bytes);
 AH_API int ah_q4w_gemm(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev, int64_t ldc,
                        void* workspace_dev, size_t workspace_bytes, void* stream);
+/* No counterpart in the reference: ah_q4w_gemm without a caller workspace.  The
+ * workspace lives in a fixed 8 MiB static device buffer per device (at 4096
+ * columns: up to 768 tokens); larger requests return AH_EINVAL before any
+ * launch.  Calls that overlap in time on one device race on that buffer. */
+AH_API int ah_q4w_gemm_noalloc(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev,
+                               int64_t ldc, void* stream);
 
 /* Reference: inference/math.rs:255-295 gemv_4bit_into on the engine format as
  * stored (f32 scales [rows][ceil(cols/gs)], linear nibbles), device pointers, any
