@@ -14,12 +14,12 @@
 // to f16 d*(q-8) (one rounding, RNE) straight into the swizzled B image, and
 // one thread issues the MMAs:
 //
-//   warp 0      raw weight producer   (cp.async.bulk -> raw ring, 4 stages)
+//   warp 0      raw weight producer   (2-D TMA boxes of 13 row tiles -> raw ring)
 //   warp 1      activation producer   (cp.async.bulk -> A ring, 3 stages)
 //   warp 2      TMEM owner + MMA issuer (tcgen05.mma M=128 N=208 K=16, f16 in,
 //               f32 accumulate; tcgen05.commit frees a stage)
-//   warps 3..6  dequant (raw ring -> B ring), then the epilogue
-//               (tcgen05.ld 32x32b -> registers -> C)
+//   warps 3..10 dequant (raw ring -> B ring); warps 3..6 then run the
+//               epilogue (tcgen05.ld 32x32b -> shared staging -> bulk copy to C)
 //
 // A CTA owns 256 tokens (two M=128 accumulators, TMEM columns [0,208) and
 // [256,464)) x 208 weight rows over the full K.  For the MLP up-projection
@@ -34,6 +34,9 @@
 // token (mod.rs:550), i.e. one gemv_4bit_into (inference/math.rs:255-295) per
 // token and projection; this kernel computes the same products for all
 // tokens of a prompt at once.
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <mutex>
@@ -59,9 +62,10 @@ constexpr int kRawNibBytes = kRowTiles * 512;       // 6656
 constexpr int kRawBytes = kRawNibBytes + kRowTiles * 128;  // + f32 scales worst case
 constexpr int kTmemCols = 512;
 constexpr int kAccColStride = 256;                  // TMEM column offset of token half 1
-constexpr int kDequantWarps = 4;
+constexpr int kDequantWarps = 8;  // >= 4: the first four cover the TMEM lane quarters in the epilogue
 constexpr int kGemmThreads = (3 + kDequantWarps) * 32;
 constexpr uint32_t kWaitLimit = 1u << 24;
+constexpr int kStageStride = kBN + 4;  // f32 per staged C row: 848 B, 16-byte stores conflict-free
 
 // Instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A and B f16
 // (bits 7-9, 10-12 = 0), both K-major (bits 15, 16 = 0), N>>3 at bits 17-22,
@@ -74,6 +78,8 @@ struct GemmSmem {
   static constexpr int kB = kA + kStages * kHalves * kATileBytes;
   static constexpr int kRaw = kB + kStages * kBBytes;
   static constexpr int kBars = kRaw + kRawStages * kRawBytes;
+  // the epilogue stages 128 rows of C over the (then idle) operand rings
+  static_assert(kTokTile * kStageStride * 4 <= kBars, "C staging must fit below the barriers");
   static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
   static constexpr int kMisc = kBars + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16;
@@ -81,6 +87,8 @@ struct GemmSmem {
 };
 
 struct GemmArgs {
+  CUtensorMap tm_nib;     // nibble plane as uint32 [r16][kp*128], box 128 x kRowTiles
+  CUtensorMap tm_scale;   // scale plane as uint32 [r16][kp*16|32], box 16|32 x kRowTiles
   Q4Tiled w;
   const uint8_t* at;      // [M_pad/128][kp][16 KB] f16 swizzled activation tiles
   const float* row_inv;   // [M_pad] 2^-s per token row
@@ -143,6 +151,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Bulk copy shared -> global (one bulk group per commit); 16-byte aligned
+// addresses, size a multiple of 16.
+__device__ __forceinline__ void bulk_s2g(void* gdst, uint32_t ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until this thread's bulk groups have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until this thread's bulk groups have completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -161,29 +181,67 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
 // ---- activation prep: f32 rows -> scaled f16 swizzled tiles ---------------------
 // One CTA per (padded) token row.  Element (m, k) of tile (m/128, k/64) sits at
 // byte (m%128)*128 + (((k%64)/8) ^ (m%8))*16 + (k%8)*2 — the SWIZZLE_128B
-// K-major image the MMA descriptors above describe.
+// K-major image the MMA descriptors above describe.  The row is read once
+// into registers (up to kPrepChunks 8-column chunks per thread, i.e. 16384
+// columns); longer rows take a second read.
 constexpr int kPrepThreads = 256;
+constexpr int kPrepChunks = 8;
+
+__device__ __forceinline__ void prep_load8(const float* row, int64_t k0, int64_t k_cols, bool vec, bool live,
+                                           float (&v)[8]) {
+  if (vec && k0 + 8 <= k_cols) {
+    const float4 p0 = __ldg(reinterpret_cast<const float4*>(row + k0));
+    const float4 p1 = __ldg(reinterpret_cast<const float4*>(row + k0 + 4));
+    v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+    v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (live && k0 + i < k_cols) ? row[k0 + i] : 0.0f;
+  }
+}
+
+__device__ __forceinline__ void prep_store8(uint8_t* tile_row, int64_t c, int ml, const float (&v)[8], float scale) {
+  uint32_t h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 hv = __floats2half2_rn(v[2 * i] * scale, v[2 * i + 1] * scale);
+    h[i] = *reinterpret_cast<const uint32_t*>(&hv);
+  }
+  const int64_t kpi = c >> 3;
+  const int chunk = (int)(c & 7);
+  uint8_t* dst = tile_row + (size_t)kpi * kATileBytes + (size_t)((chunk ^ (ml & 7)) << 4);
+  *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
+}
 
 __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restrict__ a, int64_t lda, int64_t m_rows,
                                                             int64_t k_cols, int64_t kp, bool vec_rows,
                                                             uint8_t* __restrict__ at, float* __restrict__ row_inv) {
+  // the GEMM may start its prologue and weight loads now; it waits for this
+  // grid's completion before reading the tiles
+  pdl_launch_dependents();
   const int64_t m = blockIdx.x;
   const int tid = threadIdx.x;
   const bool live = m < m_rows;
-  const float* row = a + m * lda;
+  const float* row = a + (live ? m : 0) * lda;
   const bool vec = live && vec_rows;
+  const int64_t nchunks = kp * 8;
+  const bool in_regs = nchunks <= (int64_t)kPrepThreads * kPrepChunks;
   __shared__ float red[kPrepThreads / 32];
-  // pass 1: max |a| over the row (NaN ignored here; it still reaches C)
+  float v[kPrepChunks][8];
+  // max |a| over the row (NaN ignored here; it still reaches C)
   float amax = 0.0f;
-  if (live) {
-    if (vec) {
-      for (int64_t k = (int64_t)tid * 4; k < k_cols; k += kPrepThreads * 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(row + k));
-        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  if (in_regs) {
+#pragma unroll
+    for (int j = 0; j < kPrepChunks; ++j) {
+      const int64_t c = tid + (int64_t)j * kPrepThreads;
+      if (c < nchunks) {
+        prep_load8(row, c * 8, k_cols, vec, live, v[j]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[j][i]));
       }
-    } else {
-      for (int64_t k = tid; k < k_cols; k += kPrepThreads) amax = fmaxf(amax, fabsf(row[k]));
     }
+  } else if (live) {
+    for (int64_t k = tid; k < k_cols; k += kPrepThreads) amax = fmaxf(amax, fabsf(row[k]));
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -202,39 +260,26 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
   }
   const float scale = __uint_as_float((uint32_t)(127 + s) << 23);
   if (tid == 0) row_inv[m] = live ? __uint_as_float((uint32_t)(127 - s) << 23) : 0.0f;
-  // pass 2: scaled f16, one 16-byte chunk (8 columns) per thread step
-  const int64_t mt = m >> 7;
   const int ml = (int)(m & 127);
-  uint8_t* tile_row = at + (size_t)mt * kp * kATileBytes + (size_t)ml * 128;
-  const int64_t nchunks = kp * 8;
-  for (int64_t c = tid; c < nchunks; c += kPrepThreads) {
-    const int64_t k0 = c * 8;
-    float v[8];
-    if (vec && k0 + 8 <= k_cols) {
-      const float4 p0 = __ldg(reinterpret_cast<const float4*>(row + k0));
-      const float4 p1 = __ldg(reinterpret_cast<const float4*>(row + k0 + 4));
-      v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
-      v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
-    } else {
+  uint8_t* tile_row = at + (size_t)(m >> 7) * kp * kATileBytes + (size_t)ml * 128;
+  if (in_regs) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = (live && k0 + i < k_cols) ? row[k0 + i] : 0.0f;
+    for (int j = 0; j < kPrepChunks; ++j) {
+      const int64_t c = tid + (int64_t)j * kPrepThreads;
+      if (c < nchunks) prep_store8(tile_row, c, ml, v[j], scale);
     }
-    uint32_t h[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const __half2 hv = __floats2half2_rn(v[2 * i] * scale, v[2 * i + 1] * scale);
-      h[i] = *reinterpret_cast<const uint32_t*>(&hv);
+  } else {
+    for (int64_t c = tid; c < nchunks; c += kPrepThreads) {
+      float w[8];
+      prep_load8(row, c * 8, k_cols, vec, live, w);
+      prep_store8(tile_row, c, ml, w, scale);
     }
-    const int64_t kpi = c >> 3;
-    const int chunk = (int)(c & 7);
-    uint8_t* dst = tile_row + (size_t)kpi * kATileBytes + (size_t)((chunk ^ (ml & 7)) << 4);
-    *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
   }
 }
 
 // ---- the GEMM ------------------------------------------------------------------
 template <int kHalves, bool kF32>
-__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(GemmArgs g) {
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(const __grid_constant__ GemmArgs g) {
   using L = GemmSmem<kHalves>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -253,6 +298,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(GemmArgs g) {
   const int64_t rt0 = (int64_t)blockIdx.x * kRowTiles;
   const int nrt = (int)(g.w.r16 - rt0 < kRowTiles ? g.w.r16 - rt0 : kRowTiles);
   const int64_t mt0 = (int64_t)blockIdx.y * kHalves;
+  // CTAs sharing a token tile start their K walk at staggered block pairs, so
+  // at any moment they fetch different activation tiles from L2
+  const int64_t k_rot = (int64_t)blockIdx.x * kp / gridDim.x;
   constexpr int kScaleBytes = kF32 ? 128 : 64;  // per (row tile, pair)
 
   if (threadIdx.x == 0) {
@@ -276,39 +324,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(GemmArgs g) {
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---- raw weight producer ----
-    int64_t issued = 0;
-    for (int64_t s = 0; s < kp; ++s) {
-      const int r = (int)(s % kRawStages);
-      bool ok = true;
-      if (lane == 0) {
-        if (*abort_flag) ok = false;
-        else if (s >= kRawStages)
-          ok = wait_or_abort(&raw_empty[r], (uint32_t)((s / kRawStages - 1) & 1), g.err, abort_flag, AH_ETIMEOUT);
-        if (ok) mbar_arrive_expect_tx(&raw_full[r], (uint32_t)(nrt * (512 + kScaleBytes)));
+    // ---- raw weight producer: one nibble box + one scale box per k-step ----
+    if (lane == 0) {
+      // boxes are full size; rows past the matrix arrive zero-filled
+      constexpr uint32_t kStageTx = kRowTiles * (512 + kScaleBytes);
+      int64_t issued = 0;
+      for (int64_t s = 0; s < kp; ++s) {
+        const int r = (int)(s % kRawStages);
+        if (*abort_flag) break;
+        if (s >= kRawStages &&
+            !wait_or_abort(&raw_empty[r], (uint32_t)((s / kRawStages - 1) & 1), g.err, abort_flag, AH_ETIMEOUT))
+          break;
+        uint8_t* dst = smem + L::kRaw + r * kRawBytes;
+        mbar_arrive_expect_tx(&raw_full[r], kStageTx);
+        const int64_t kpos = (s + k_rot) % kp;
+        tma_load_2d(dst, &g.tm_nib, (int)(kpos * 128), (int)rt0, &raw_full[r]);
+        tma_load_2d(dst + kRawNibBytes, &g.tm_scale, (int)(kpos * (kScaleBytes / 4)), (int)rt0, &raw_full[r]);
+        ++issued;
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      uint8_t* dst = smem + L::kRaw + r * kRawBytes;
-      if (lane < nrt) {
-        const uint4* src = g.w.nib + ((rt0 + lane) * kp + s) * 32;
-        bulk_g2s(dst + lane * 512, src, 512, &raw_full[r]);
-      } else if (lane >= 16 && lane < 16 + nrt) {
-        const int i = lane - 16;
-        const uint8_t* src = static_cast<const uint8_t*>(g.w.scales) + ((rt0 + i) * kp + s) * kScaleBytes;
-        bulk_g2s(dst + kRawNibBytes + i * kScaleBytes, src, kScaleBytes, &raw_full[r]);
+      // drain: the copies of the last stages have landed before the CTA can exit
+      if (*abort_flag) {
+        for (int64_t s = issued > kRawStages ? issued - kRawStages : 0; s < issued; ++s)
+          mbar_wait_bounded(&raw_full[s % kRawStages], (uint32_t)((s / kRawStages) & 1), g.err, AH_ETIMEOUT,
+                            kWaitLimit);
       }
-      ++issued;
-    }
-    // drain: the copies of the last stages have landed before the CTA can exit
-    if (lane == 0 && *abort_flag) {
-      for (int64_t s = issued > kRawStages ? issued - kRawStages : 0; s < issued; ++s)
-        mbar_wait_bounded(&raw_full[s % kRawStages], (uint32_t)((s / kRawStages) & 1), g.err, AH_ETIMEOUT,
-                          kWaitLimit);
     }
   } else if (warp == 1) {
     // ---- activation producer ----
     if (lane == 0) {
+      pdl_wait();  // the tiles come from the preceding prep grid
       int64_t issued = 0;
       for (int64_t s = 0; s < kp; ++s) {
         const int st = (int)(s % kStages);
@@ -318,7 +362,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(GemmArgs g) {
           break;
         mbar_arrive_expect_tx(&a_full[st], (uint32_t)(kHalves * kATileBytes));
         for (int h = 0; h < kHalves; ++h) {
-          const uint8_t* src = g.at + ((size_t)(mt0 + h) * kp + s) * kATileBytes;
+          const uint8_t* src = g.at + ((size_t)(mt0 + h) * kp + (s + k_rot) % kp) * kATileBytes;
           bulk_g2s(smem + L::kA + (st * kHalves + h) * kATileBytes, src, kATileBytes, &a_full[st]);
         }
         ++issued;
@@ -417,25 +461,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(GemmArgs g) {
         mbar_arrive(&raw_empty[r]);
       }
     }
-    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its token rows)
-    const bool have = mbar_wait_bounded(acc_full, 0, g.err, AH_ETIMEOUT, kWaitLimit);
+    // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its token rows).
+    // Each thread stages its row segment (208 columns, scaled by 2^-s) in the
+    // now idle operand rings and writes it with one bulk copy, so C leaves the
+    // SM as whole 832-byte row runs instead of 16-byte pieces of 32 rows.
+    // Where the bulk copy cannot address C (unaligned, ragged by a non
+    // multiple of 4 columns), threads store their 16-column pieces directly.
+    // Dequant warps past the first four have no epilogue work.
+    const bool have =
+        __all_sync(0xffffffffu, wd < 4 && mbar_wait_bounded(acc_full, 0, g.err, AH_ETIMEOUT, kWaitLimit));
     tc_fence_after();
+    pdl_wait();  // row_inv comes from the preceding prep grid
     if (have && !*abort_flag) {
       const int q = warp & 3;
       const int64_t n0 = rt0 * 16;
       const int64_t n_rows = g.w.rows;
-      const bool vec = g.c_vec;
+      const int ncols = (int)(n_rows - n0 < kBN ? n_rows - n0 : kBN);
+      const bool bulk = g.c_vec && (ncols % 4) == 0;
+      float* stage = reinterpret_cast<float*>(smem) + (q * 32 + lane) * kStageStride;
       for (int h = 0; h < kHalves; ++h) {
         const int64_t m = (mt0 + h) * kTokTile + q * 32 + lane;
         const float inv = m < g.m ? g.row_inv[m] : 0.0f;
         float* crow = g.c + m * g.ldc;
+        if (bulk && h > 0) bulk_wait_read0();  // the previous row's copy has read the stage
 #pragma unroll 1
         for (int c0 = 0; c0 < kBN; c0 += 16) {
           float v[16];
           tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * kAccColStride + c0), v);
+          if (bulk) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(stage + c0 + i) =
+                  make_float4(v[i] * inv, v[i + 1] * inv, v[i + 2] * inv, v[i + 3] * inv);
+            continue;
+          }
           if (m >= g.m) continue;
           const int64_t n = n0 + c0;
-          if (vec && n + 16 <= n_rows) {
+          if (g.c_vec && n + 16 <= n_rows) {
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
               st_cs_f4(reinterpret_cast<float4*>(crow + n + i),
@@ -446,7 +508,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(GemmArgs g) {
               if (n + i < n_rows) crow[n + i] = v[i] * inv;
           }
         }
+        if (bulk && m < g.m) {
+          fence_proxy_async_smem();
+          bulk_s2g(crow + n0, smem_u32(stage), (uint32_t)ncols * 4u);
+          bulk_commit();
+        }
       }
+      if (bulk) bulk_wait_all();  // C written before the CTA retires
     }
   }
 
@@ -472,8 +540,19 @@ int gemm_launch(const GemmArgs& a, int64_t grid_x, int64_t grid_y, cudaStream_t 
     AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynamic));
     configured_device = dev;
   }
-  kern<<<dim3((unsigned)grid_x, (unsigned)grid_y), kGemmThreads, L::kDynamic, st>>>(a);
-  AH_LAUNCH_CHECK();
+  // programmatic dependent launch: the prologue (barriers, TMEM, the first
+  // weight stages) overlaps the activation prep; A is read after pdl_wait()
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)grid_x, (unsigned)grid_y);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = L::kDynamic;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  AH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
   return AH_OK;
 }
 
@@ -485,6 +564,35 @@ inline int64_t gemm_m_pad(int64_t m) {
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// A [rows][inner] uint32 plane read in boxes of box_inner x kRowTiles.
+int encode_plane(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner) {
+  auto fn = tensor_map_encoder();
+  if (!fn) return fail(AH_ECUDA, "gemm: cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {inner * 4};
+  const cuuint32_t box[2] = {box_inner, (cuuint32_t)kRowTiles};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AH_ECUDA, "gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return AH_OK;
+}
 
 // Workspace: f16 activation tiles (M_pad x kp*64 x 2 B) + one f32 per padded row.
 size_t gemm_workspace_bytes(const Q4Tiled& w, int64_t m) {
@@ -507,7 +615,7 @@ int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c,
   const bool vec_rows = (lda % 4 == 0) && aligned16(a) && (w.cols % 8 == 0);
   k_gemm_prep<<<(unsigned)mp, kPrepThreads, 0, st>>>(a, lda, m, w.cols, w.kp, vec_rows, at, row_inv);
   AH_LAUNCH_CHECK();
-  GemmArgs g{};
+  alignas(64) GemmArgs g{};
   g.w = w;
   g.at = at;
   g.row_inv = row_inv;
@@ -516,6 +624,11 @@ int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c,
   g.m = m;
   g.err = device_error_word();
   g.c_vec = (ldc % 4 == 0) && aligned16(c);
+  int rc = encode_plane(&g.tm_nib, w.nib, (uint64_t)w.kp * 128, (uint64_t)w.r16, 128);
+  if (rc != AH_OK) return rc;
+  const uint32_t sc_u32 = w.f32_scales ? 32 : 16;  // per (row tile, pair)
+  rc = encode_plane(&g.tm_scale, w.scales, (uint64_t)w.kp * sc_u32, (uint64_t)w.r16, sc_u32);
+  if (rc != AH_OK) return rc;
   const int64_t gx = (w.r16 + kRowTiles - 1) / kRowTiles;
   const int64_t halves = gemm_halves(m);
   const int64_t gy = mp / (kTokTile * halves);
