@@ -3,12 +3,12 @@
 //
 //   C[m][n] = sum_k A[m][k] * W[n][k],  W[n][k] = d(n, k/32) * (q(n,k) - 8)
 //
-// A (tokens x cols, f32) is converted once per call by k_gemm_prep into f16
-// tiles already in the tensor core's K-major SWIZZLE_128B shared-memory image
-// (128 tokens x 64 columns = 16 KB per tile), each token row scaled by an
-// exact power of two 2^s so its max |a| lies in [2^14, 2^15) (f16 keeps 11
-// significant bits over the row's whole range; C rows are multiplied by 2^-s
-// in the epilogue).  W stays in the GEMV's tiled Q4 layout in HBM (see
+// A (tokens x cols, f32) is converted once per call by k_gemm_prep into a
+// row-major f16 copy, each token row scaled by an exact power of two 2^s so
+// its max |a| lies in [2^14, 2^15) (f16 keeps 11 significant bits over the
+// row's whole range; C rows are multiplied by 2^-s in the epilogue).  A TMA
+// tensor map with 128-byte swizzle brings 128-token x 64-column boxes of it
+// into shared memory in the tensor core's K-major SWIZZLE_128B image.  W stays in the GEMV's tiled Q4 layout in HBM (see
 // ah_gemv.cuh): the kernel bulk-copies the nibble and scale chunks of a
 // 208-row x 64-column tile into shared memory, four dequant warps expand them
 // to f16 d*(q-8) (one rounding, RNE) straight into the swizzled B image, and
@@ -90,7 +90,8 @@ struct GemmArgs {
   CUtensorMap tm_nib;     // nibble plane as uint32 [r16][kp*128], box 128 x kRowTiles
   CUtensorMap tm_scale;   // scale plane as uint32 [r16][kp*16|32], box 16|32 x kRowTiles
   Q4Tiled w;
-  const uint8_t* at;      // [M_pad/128][kp][16 KB] f16 swizzled activation tiles
+  CUtensorMap tm_a;       // f16 activations [M_pad][kp*64], box 64 x 128, 128-byte swizzle
+  const uint8_t* at;      // the same activations (row-major f16)
   const float* row_inv;   // [M_pad] 2^-s per token row
   float* c;
   int64_t ldc;
@@ -178,10 +179,9 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
   return false;
 }
 
-// ---- activation prep: f32 rows -> scaled f16 swizzled tiles ---------------------
-// One CTA per (padded) token row.  Element (m, k) of tile (m/128, k/64) sits at
-// byte (m%128)*128 + (((k%64)/8) ^ (m%8))*16 + (k%8)*2 — the SWIZZLE_128B
-// K-major image the MMA descriptors above describe.  The row is read once
+// ---- activation prep: f32 rows -> scaled row-major f16 -------------------------
+// One CTA per (padded) token row of kp*64 f16 (columns past K are zero).  The
+// row is read once
 // into registers (up to kPrepChunks 8-column chunks per thread, i.e. 16384
 // columns); longer rows take a second read.
 constexpr int kPrepThreads = 256;
@@ -200,17 +200,14 @@ __device__ __forceinline__ void prep_load8(const float* row, int64_t k0, int64_t
   }
 }
 
-__device__ __forceinline__ void prep_store8(uint8_t* tile_row, int64_t c, int ml, const float (&v)[8], float scale) {
+__device__ __forceinline__ void prep_store8(uint8_t* out_row, int64_t c, const float (&v)[8], float scale) {
   uint32_t h[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const __half2 hv = __floats2half2_rn(v[2 * i] * scale, v[2 * i + 1] * scale);
     h[i] = *reinterpret_cast<const uint32_t*>(&hv);
   }
-  const int64_t kpi = c >> 3;
-  const int chunk = (int)(c & 7);
-  uint8_t* dst = tile_row + (size_t)kpi * kATileBytes + (size_t)((chunk ^ (ml & 7)) << 4);
-  *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(out_row + c * 16) = make_uint4(h[0], h[1], h[2], h[3]);
 }
 
 __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restrict__ a, int64_t lda, int64_t m_rows,
@@ -260,19 +257,18 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
   }
   const float scale = __uint_as_float((uint32_t)(127 + s) << 23);
   if (tid == 0) row_inv[m] = live ? __uint_as_float((uint32_t)(127 - s) << 23) : 0.0f;
-  const int ml = (int)(m & 127);
-  uint8_t* tile_row = at + (size_t)(m >> 7) * kp * kATileBytes + (size_t)ml * 128;
+  uint8_t* out_row = at + (size_t)m * (size_t)kp * 128;
   if (in_regs) {
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j) {
       const int64_t c = tid + (int64_t)j * kPrepThreads;
-      if (c < nchunks) prep_store8(tile_row, c, ml, v[j], scale);
+      if (c < nchunks) prep_store8(out_row, c, v[j], scale);
     }
   } else {
     for (int64_t c = tid; c < nchunks; c += kPrepThreads) {
       float w[8];
       prep_load8(row, c * 8, k_cols, vec, live, w);
-      prep_store8(tile_row, c, ml, w, scale);
+      prep_store8(out_row, c, w, scale);
     }
   }
 }
@@ -362,8 +358,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(const __grid_con
           break;
         mbar_arrive_expect_tx(&a_full[st], (uint32_t)(kHalves * kATileBytes));
         for (int h = 0; h < kHalves; ++h) {
-          const uint8_t* src = g.at + ((size_t)(mt0 + h) * kp + (s + k_rot) % kp) * kATileBytes;
-          bulk_g2s(smem + L::kA + (st * kHalves + h) * kATileBytes, src, kATileBytes, &a_full[st]);
+          tma_load_2d(smem + L::kA + (st * kHalves + h) * kATileBytes, &g.tm_a, (int)(((s + k_rot) % kp) * kBK),
+                      (int)((mt0 + h) * kTokTile), &a_full[st]);
         }
         ++issued;
       }
@@ -579,16 +575,18 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// A [rows][inner] uint32 plane read in boxes of box_inner x kRowTiles.
-int encode_plane(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner) {
+// A row-major [rows][inner] matrix of `elem`-byte elements read in boxes of
+// box_inner x box_rows.
+int encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem, uint64_t inner,
+              uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   auto fn = tensor_map_encoder();
   if (!fn) return fail(AH_ECUDA, "gemm: cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t dims[2] = {inner, rows};
-  const cuuint64_t strides[1] = {inner * 4};
-  const cuuint32_t box[2] = {box_inner, (cuuint32_t)kRowTiles};
+  const cuuint64_t strides[1] = {inner * elem};
+  const cuuint32_t box[2] = {box_inner, box_rows};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  const CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(AH_ECUDA, "gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return AH_OK;
@@ -624,10 +622,16 @@ int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c,
   g.m = m;
   g.err = device_error_word();
   g.c_vec = (ldc % 4 == 0) && aligned16(c);
-  int rc = encode_plane(&g.tm_nib, w.nib, (uint64_t)w.kp * 128, (uint64_t)w.r16, 128);
+  // weight planes as uint32 rows of 16-row tiles; activations as f16 rows
+  int rc = encode_2d(&g.tm_nib, w.nib, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)w.kp * 128, (uint64_t)w.r16, 128,
+                     kRowTiles, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc != AH_OK) return rc;
   const uint32_t sc_u32 = w.f32_scales ? 32 : 16;  // per (row tile, pair)
-  rc = encode_plane(&g.tm_scale, w.scales, (uint64_t)w.kp * sc_u32, (uint64_t)w.r16, sc_u32);
+  rc = encode_2d(&g.tm_scale, w.scales, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)w.kp * sc_u32, (uint64_t)w.r16,
+                 sc_u32, kRowTiles, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc != AH_OK) return rc;
+  rc = encode_2d(&g.tm_a, at, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)w.kp * kBK, (uint64_t)mp, kBK, kTokTile,
+                 CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != AH_OK) return rc;
   const int64_t gx = (w.r16 + kRowTiles - 1) / kRowTiles;
   const int64_t halves = gemm_halves(m);
