@@ -720,6 +720,8 @@ int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
   static std::mutex mu;
   struct Entry { int dev; void* k; size_t smem; int cap; };
   static std::vector<Entry> cache;
+  struct Cap { int dev; void* k; size_t smem; };  // the largest cap set per (device, kernel)
+  static std::vector<Cap> caps;
   int dev = 0;
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lk(mu);
@@ -728,7 +730,16 @@ int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
       *capacity = e.cap;
       return AH_OK;
     }
-  AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem));
+  // the attribute is per kernel: raise it, never lower it below a size an
+  // earlier plan of the same kernel still launches with
+  Cap* cp = nullptr;
+  for (auto& c : caps)
+    if (c.dev == dev && c.k == (void*)kern) cp = &c;
+  if (!cp || cp->smem < plan.smem) {
+    AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem));
+    if (cp) cp->smem = plan.smem;
+    else caps.push_back({dev, (void*)kern, plan.smem});
+  }
   int n = 0;
   if (plan.rows_mode) {
     AH_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, plan.smem));

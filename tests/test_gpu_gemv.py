@@ -158,3 +158,34 @@ def test_golden_gemv(cuda):
     W2 = K.Q4Weight.from_engine(torch.from_numpy(g["gemv_eng_scales"]).to(cuda),
                                 torch.from_numpy(g["gemv_eng_packed"]).to(cuda), 48, 256)
     assert relerr(W2.gemv(x).cpu().numpy(), g["gemv_eng_y"]) <= TOL
+
+
+@pytest.mark.parametrize("rows,cols,batch", [(1200, 96, 1), (1504, 4096 + 32, 1), (2048, 4096, 3),
+                                             (4096, 14336, 1), (1216, 1024, 2)])
+def test_many_row_tile_shapes(cuda, oracle, rows, cols, batch):
+    # 75 .. 256 row tiles (cluster and rows schedules), incl. K = 4096+32
+    # columns (65 block pairs) and K = 14336
+    from agent_harness_b200 import kernels as K
+    blocks, W = _q4_0_weight(K, rows, cols, rows + cols + batch, cuda)
+    x = K.fill_normal(batch * cols, 0.0, 1.0, 7 + batch, device=cuda).reshape(batch, cols)
+    bh, xh = blocks.cpu().numpy(), x.cpu().numpy()
+    for _ in range(2):  # two calls: no state carried between launches
+        y = W.gemv(x).cpu().numpy()
+        for b in range(batch):
+            ref = oracle.gemv_q4_0(bh, xh[b], rows, cols)
+            assert relerr(y[b], ref) <= TOL, (rows, cols, b, relerr(y[b], ref))
+    from agent_harness_b200._lib import lib
+    torch.cuda.synchronize()
+    assert lib().ah_check_device_error(None) == 0
+
+
+def test_many_row_tiles_engine_format(cuda, oracle):
+    from agent_harness_b200 import kernels as K
+    rng = np.random.default_rng(41)
+    rows, cols = 1536, 512
+    Wf = (rng.standard_normal(rows * cols) * 0.02).astype(np.float32)
+    s, p = oracle.quantize_q4(Wf, 32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    W = K.Q4Weight.from_engine(torch.from_numpy(s).to(cuda), torch.from_numpy(p).to(cuda), rows, cols)
+    y = W.gemv(torch.from_numpy(x).to(cuda)).cpu().numpy()
+    assert relerr(y, oracle.gemv_4bit_into(s, p, x, rows, cols, 32)) <= TOL
