@@ -56,6 +56,10 @@ SIGNATURES = {
     "ah_gemv_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, i64, vp]),
     "ah_matvec_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, vp]),
     "ah_model_create": (i32, [vp, C.POINTER(vp)]),
+    "ah_nccl_unique_id": (i32, [vp, C.c_size_t]),
+    "ah_model_create_tp": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),
+    "ah_model_shard": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32),
+                             C.POINTER(i32)]),
     "ah_model_destroy": (i32, [vp]),
     "ah_model_load_tensor": (i32, [vp, i32, i32, vp, vp]),
     "ah_model_init_random": (i32, [vp, u64, f32, f32, f32]),

@@ -14,11 +14,22 @@
 //   advance    pos += 1 (and, while prefilling, the next prompt token)
 // RMSNorm statistics travel as per-16-row partial sums of squares written by
 // the kernel that produced `hidden` (embed or a residual epilogue).
+//
+// Tensor parallelism over `world` ranks (one process or thread per GPU):
+//   * q/k/v and gate/up keep this rank's heads / FFN rows (column split);
+//   * o and down keep this rank's K columns (row split), so their GEMVs give
+//     partial sums that one NCCL all-reduce per attention / MLP block adds
+//     before the residual add (k_residual_add);
+//   * the LM head keeps a vocab slice: each rank takes its argmax and an
+//     all-gather of (max, index) pairs picks the first global maximum;
+//   * embeddings, norms and `hidden` are replicated (identical on all ranks).
 #include <algorithm>
 #include <climits>
 #include <cmath>
 #include <cstring>
 #include <vector>
+
+#include <nccl.h>
 
 #include "ah_gemv_impl.cuh"
 
@@ -252,8 +263,12 @@ __global__ void __launch_bounds__(256) k_embed(const uint16_t* __restrict__ emb,
 
 // Greedy next token per sequence (sampling.rs:4-14: the first strict maximum;
 // NaN never wins; all -inf or NaN gives 0).  grid (kArgmaxChunks, B).
+// With `pair` set (tensor parallelism) the shard's candidate (value, index +
+// idx_base) is written there instead of the token.
+struct ArgPair;
 __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits, int vocab, float* pv, int* pi,
-                                                int* cnt, int* tok, int* tok_log, const int* pos, int batch) {
+                                                int* cnt, int* tok, int* tok_log, const int* pos, int batch,
+                                                ArgPair* pair, int idx_base) {
   const int b = blockIdx.y, c = blockIdx.x, tid = threadIdx.x;
   pdl_launch_dependents();
   pdl_wait();
@@ -295,10 +310,63 @@ __global__ void __launch_bounds__(256) k_argmax(const float* __restrict__ logits
     const int i = __ldcg(pi + b * kArgmaxChunks + k);
     if (v > best || (v == best && i < besti)) { best = v; besti = i; }
   }
+  cnt[b] = 0;
+  if (pair) {
+    float* pp = reinterpret_cast<float*>(pair) + 2 * b;
+    pp[0] = best;
+    reinterpret_cast<int*>(pp)[1] = besti == INT_MAX ? INT_MAX : besti + idx_base;
+    return;
+  }
   const int next = (besti == INT_MAX) ? 0 : besti;
   tok[b] = next;
   tok_log[(size_t)(*pos) * batch + b] = next;
-  cnt[b] = 0;
+}
+
+// hidden += part (the all-reduced o / down projection) and the per-16-row
+// sums of squares of the new hidden.  grid ((d + 255) / 256, B).
+__global__ void __launch_bounds__(256) k_residual_add(float* __restrict__ hidden, const float* __restrict__ part,
+                                                      float* __restrict__ ss, int d) {
+  const int b = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool live = i < d;
+  pdl_launch_dependents();
+  pdl_wait();
+  float h = 0.0f;
+  if (live) {
+    h = hidden[(size_t)b * d + i] + part[(size_t)b * d + i];  // inference/mod.rs:505 residual
+    hidden[(size_t)b * d + i] = h;
+  }
+  float q = h * h;
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
+  if (live && (i & 15) == 0) ss[(size_t)b * (d / 16) + i / 16] = q;
+}
+
+// Candidate of one vocab shard: value and global index (INT_MAX: none).
+struct ArgPair {
+  float v;
+  int i;
+};
+
+// The first global maximum over the ranks' shard candidates (shards hold
+// increasing vocab ranges, and each candidate is its shard's first maximum).
+__global__ void k_argmax_merge(const ArgPair* __restrict__ all, int world, int* tok, int* tok_log, const int* pos,
+                               int batch) {
+  pdl_wait();
+  const int b = threadIdx.x;
+  if (b >= batch) return;
+  float best = -INFINITY;
+  int besti = INT_MAX;
+  for (int r = 0; r < world; ++r) {
+    const ArgPair p = all[(size_t)r * batch + b];
+    if (p.i != INT_MAX && (p.v > best || (p.v == best && p.i < besti))) {
+      best = p.v;
+      besti = p.i;
+    }
+  }
+  const int next = besti == INT_MAX ? 0 : besti;
+  tok[b] = next;
+  tok_log[(size_t)(*pos) * batch + b] = next;
 }
 
 // pos += 1; while prefilling, also load the next prompt token.
@@ -343,9 +411,12 @@ int launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, size_t smem, cudaSt
 // Model object
 // ---------------------------------------------------------------------------
 struct AhModel {
-  AhModelConfig c{};
+  AhModelConfig c{};  // the full (unsharded) model
   int device = 0;
-  int dq = 0, dkv = 0;
+  int tp_rank = 0, tp_world = 1;
+  ncclComm_t comm = nullptr;
+  int nh = 0, nkv = 0, nff = 0, nvoc = 0;  // this rank's heads, kv heads, FFN rows, vocab rows
+  int dq = 0, dkv = 0;                     // this rank's q and k/v widths
   std::vector<AhQ4Weight*> wqkv, wo, wgu, wd;
   AhQ4Weight* lm = nullptr;
   std::vector<void*> pend[5];  // q, k, v, gate, up Q4_0 blocks awaiting fusion
@@ -355,6 +426,9 @@ struct AhModel {
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr, *ss = nullptr;
   float* att_part = nullptr;
   int* att_cnt = nullptr;
+  float* part = nullptr;   // [B][d] o / down partial sums (tensor parallelism)
+  void* am_pair = nullptr; // [B] this shard's argmax candidate
+  void* am_all = nullptr;  // [world][B] all shards' candidates
   float* am_v = nullptr;
   int* am_i = nullptr;
   int* am_cnt = nullptr;
@@ -412,13 +486,24 @@ GemvArgs gemv_args(const AhQ4Weight* w, const float* x, int64_t xs, float* y, in
   return a;
 }
 
+// Sums the o / down partials over the tensor-parallel ranks and adds them to
+// hidden (with the RMSNorm partial sums of the result).
+int reduce_residual(AhModel* m, cudaStream_t st) {
+  const int B = m->batch, d = m->c.n_embd;
+  if (ncclAllReduce(m->part, m->part, (size_t)B * d, ncclFloat, ncclSum, m->comm, st) != ncclSuccess)
+    return fail(AH_ENCCL, "model: all-reduce of the block output failed");
+  return launch_pdl(k_residual_add, dim3((d + 255) / 256, B), dim3(256), 0, st, m->hidden, (const float*)m->part,
+                    m->ss, d);
+}
+
 // Enqueues one decoder step (all layers; with_head adds LM head + argmax).
 int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cudaStream_t st) {
   const AhModelConfig& c = m->c;
   const int B = m->batch, d = c.n_embd;
+  const bool tp = m->tp_world > 1;
   AH_TRY(launch_pdl(k_embed, dim3((d + 255) / 256, B), dim3(256), 0, st, (const uint16_t*)m->tok_embd,
                     (const int*)m->d_tok, m->hidden, m->ss, d, c.vocab_size));
-  const size_t attn_smem = attn_smem_bytes(c.n_head / c.n_head_kv, c.head_dim);
+  const size_t attn_smem = attn_smem_bytes(m->nh / m->nkv, c.head_dim);
   for (int l = 0; l < c.n_layer; ++l) {
     GemvArgs q = gemv_args(m->wqkv[l], m->hidden, d, m->qkv, m->dq + 2 * m->dkv, B);
     q.norm_w = m->attn_norm + (size_t)l * d;
@@ -437,35 +522,53 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     at.out = m->attn;
     at.layer = l;
     at.n_layer = c.n_layer;
-    at.n_head = c.n_head;
-    at.n_kv = c.n_head_kv;
+    at.n_head = m->nh;
+    at.n_kv = m->nkv;
     at.hd = c.head_dim;
     at.max_seq = c.max_seq;
     at.scale = 1.0f / sqrtf((float)c.head_dim);  // mod.rs:478
     at.err = m->err;
-    AH_TRY(launch_pdl(k_attention, dim3(c.n_head_kv, kAttnSplits, B), dim3(kAttnThreads), attn_smem, st, at));
-    GemvArgs o = gemv_args(m->wo[l], m->attn, m->dq, m->hidden, d, B);
-    o.ss_out = m->ss;
-    AH_TRY(gemv_launch(o, kProPlain, kEpiAdd, st, true));
-    GemvArgs gu = gemv_args(m->wgu[l], m->hidden, d, m->act, c.n_ff, B);
+    AH_TRY(launch_pdl(k_attention, dim3(m->nkv, kAttnSplits, B), dim3(kAttnThreads), attn_smem, st, at));
+    if (tp) {
+      AH_TRY(gemv_launch(gemv_args(m->wo[l], m->attn, m->dq, m->part, d, B), kProPlain, kEpiStore, st, true));
+      AH_TRY(reduce_residual(m, st));
+    } else {
+      GemvArgs o = gemv_args(m->wo[l], m->attn, m->dq, m->hidden, d, B);
+      o.ss_out = m->ss;
+      AH_TRY(gemv_launch(o, kProPlain, kEpiAdd, st, true));
+    }
+    GemvArgs gu = gemv_args(m->wgu[l], m->hidden, d, m->act, m->nff, B);
     gu.norm_w = m->ffn_norm + (size_t)l * d;
     gu.eps = c.rms_eps;
     gu.ss_in = m->ss;
     gu.n_ss_in = d / 16;
     AH_TRY(gemv_launch(gu, kProRmsNorm, kEpiSwiglu, st, true));
-    GemvArgs dn = gemv_args(m->wd[l], m->act, c.n_ff, m->hidden, d, B);
-    dn.ss_out = m->ss;
-    AH_TRY(gemv_launch(dn, kProPlain, kEpiAdd, st, true));
+    if (tp) {
+      AH_TRY(gemv_launch(gemv_args(m->wd[l], m->act, m->nff, m->part, d, B), kProPlain, kEpiStore, st, true));
+      AH_TRY(reduce_residual(m, st));
+    } else {
+      GemvArgs dn = gemv_args(m->wd[l], m->act, m->nff, m->hidden, d, B);
+      dn.ss_out = m->ss;
+      AH_TRY(gemv_launch(dn, kProPlain, kEpiAdd, st, true));
+    }
   }
   if (with_head) {
-    GemvArgs h = gemv_args(m->lm, m->hidden, d, m->logits, c.vocab_size, B);
+    GemvArgs h = gemv_args(m->lm, m->hidden, d, m->logits, m->nvoc, B);
     h.norm_w = m->out_norm;
     h.eps = c.rms_eps;
     h.ss_in = m->ss;
     h.n_ss_in = d / 16;
     AH_TRY(gemv_launch(h, kProRmsNorm, kEpiStore, st, true));
-    AH_TRY(launch_pdl(k_argmax, dim3(kArgmaxChunks, B), dim3(256), 0, st, (const float*)m->logits, c.vocab_size,
-                      m->am_v, m->am_i, m->am_cnt, m->d_tok, m->tok_log, (const int*)m->d_pos, B));
+    ArgPair* pair = tp ? static_cast<ArgPair*>(m->am_pair) : nullptr;
+    AH_TRY(launch_pdl(k_argmax, dim3(kArgmaxChunks, B), dim3(256), 0, st, (const float*)m->logits, m->nvoc, m->am_v,
+                      m->am_i, m->am_cnt, m->d_tok, m->tok_log, (const int*)m->d_pos, B, pair,
+                      m->tp_rank * m->nvoc));
+    if (tp) {
+      if (ncclAllGather(m->am_pair, m->am_all, (size_t)B * sizeof(ArgPair), ncclUint8, m->comm, st) != ncclSuccess)
+        return fail(AH_ENCCL, "model: all-gather of the argmax candidates failed");
+      AH_TRY(launch_pdl(k_argmax_merge, dim3(1), dim3(32), 0, st, (const ArgPair*)m->am_all, m->tp_world, m->d_tok,
+                        m->tok_log, (const int*)m->d_pos, B));
+    }
   }
   AH_TRY(launch_pdl(k_advance, dim3(1), dim3(32), 0, st, m->d_pos, m->d_tok, prompt, n_prompt, B));
   return AH_OK;
@@ -477,10 +580,11 @@ int prepare_step(AhModel* m) {
   const int B = m->batch;
   AH_TRY(gemv_prepare(q4w_tiled(m->lm), B, kProRmsNorm, kEpiStore));
   AH_TRY(gemv_prepare(q4w_tiled(m->wqkv[0]), B, kProRmsNorm, kEpiStore));
-  AH_TRY(gemv_prepare(q4w_tiled(m->wo[0]), B, kProPlain, kEpiAdd));
+  const int ro = m->tp_world > 1 ? kEpiStore : kEpiAdd;
+  AH_TRY(gemv_prepare(q4w_tiled(m->wo[0]), B, kProPlain, ro));
   AH_TRY(gemv_prepare(q4w_tiled(m->wgu[0]), B, kProRmsNorm, kEpiSwiglu));
-  AH_TRY(gemv_prepare(q4w_tiled(m->wd[0]), B, kProPlain, kEpiAdd));
-  const size_t attn_smem = attn_smem_bytes(c.n_head / c.n_head_kv, c.head_dim);
+  AH_TRY(gemv_prepare(q4w_tiled(m->wd[0]), B, kProPlain, ro));
+  const size_t attn_smem = attn_smem_bytes(m->nh / m->nkv, c.head_dim);
   AH_CUDA_TRY(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem));
   return AH_OK;
 }
@@ -523,24 +627,40 @@ uint64_t ah_model_tensor_seed(uint64_t seed, int kind, int layer) {
   return splitmix64(splitmix64(seed + 0x1000003ull * (uint64_t)(kind + 1)) + (uint64_t)layer);
 }
 
-int ah_model_create(const AhModelConfig* cfg, AhModel** out) {
+}  // extern "C"
+
+namespace {
+// Creates the model (tensor-parallel shard `rank` of `world`, or the whole
+// model for world 1) on the current device; takes ownership of `comm`.
+int model_create(const AhModelConfig* cfg, int rank, int world, ncclComm_t comm, AhModel** out) {
   AH_REQUIRE(cfg && out, "model_create: null argument");
   *out = nullptr;
   const AhModelConfig& c = *cfg;
   AH_REQUIRE(c.n_layer > 0 && c.n_embd > 0 && c.n_ff > 0 && c.n_head > 0 && c.n_head_kv > 0 && c.head_dim > 0 &&
                  c.vocab_size > 0 && c.max_seq > 0 && c.max_batch >= 1 && c.max_batch <= kGemvMaxBatch,
              "model_create: non-positive dimension or batch outside 1..16");
-  AH_REQUIRE(c.n_embd % 64 == 0 && c.n_ff % 64 == 0 && (c.n_head * c.head_dim) % 64 == 0,
-             "model_create: n_embd, n_ff and n_head*head_dim must be multiples of 64");
+  AH_REQUIRE(world >= 1 && rank >= 0 && rank < world, "model_create: rank %d of %d", rank, world);
+  AH_REQUIRE(c.n_head_kv % world == 0 && c.n_ff % world == 0 && c.vocab_size % world == 0,
+             "model_create: %d ranks must divide n_head_kv, n_ff and vocab_size", world);
+  const int nh = c.n_head / world, nkv = c.n_head_kv / world, nff = c.n_ff / world, nvoc = c.vocab_size / world;
+  AH_REQUIRE(c.n_embd % 64 == 0 && nff % 64 == 0 && (nh * c.head_dim) % 64 == 0,
+             "model_create: n_embd, n_ff / ranks and heads per rank * head_dim must be multiples of 64");
   AH_REQUIRE(c.n_head % c.n_head_kv == 0 && c.n_head / c.n_head_kv <= 8, "model_create: GQA group must divide, <= 8");
   AH_REQUIRE(c.head_dim % 32 == 0 && c.head_dim <= 128, "model_create: head_dim must be 32, 64, 96 or 128");
   AH_REQUIRE(c.max_seq <= kAttnSplits * kAttnMaxChunk, "model_create: max_seq above %d", kAttnSplits * kAttnMaxChunk);
   AhModel* m = new (std::nothrow) AhModel();
   if (!m) return fail(AH_ENOMEM, "model_create: host allocation");
   m->c = c;
+  m->tp_rank = rank;
+  m->tp_world = world;
+  m->comm = comm;
+  m->nh = nh;
+  m->nkv = nkv;
+  m->nff = nff;
+  m->nvoc = nvoc;
   cudaGetDevice(&m->device);
-  m->dq = c.n_head * c.head_dim;
-  m->dkv = c.n_head_kv * c.head_dim;
+  m->dq = nh * c.head_dim;
+  m->dkv = nkv * c.head_dim;
   const int L = c.n_layer, B = c.max_batch, d = c.n_embd;
   m->wqkv.assign(L, nullptr);
   m->wo.assign(L, nullptr);
@@ -555,25 +675,30 @@ int ah_model_create(const AhModelConfig* cfg, AhModel** out) {
   A((void**)&m->attn_norm, (size_t)L * d * 2);
   A((void**)&m->ffn_norm, (size_t)L * d * 2);
   A((void**)&m->out_norm, (size_t)d * 2);
-  const size_t kv = (size_t)B * L * c.n_head_kv * c.max_seq * c.head_dim * 2;
+  const size_t kv = (size_t)B * L * nkv * c.max_seq * c.head_dim * 2;
   A((void**)&m->kc, kv);
   A((void**)&m->vc, kv);
   A((void**)&m->rope, (size_t)c.max_seq * (c.head_dim / 2) * sizeof(float2));
   A((void**)&m->hidden, (size_t)B * d * 4);
   A((void**)&m->qkv, (size_t)B * (m->dq + 2 * m->dkv) * 4);
   A((void**)&m->attn, (size_t)B * m->dq * 4);
-  A((void**)&m->act, (size_t)B * c.n_ff * 4);
-  A((void**)&m->logits, (size_t)B * c.vocab_size * 4);
+  A((void**)&m->act, (size_t)B * nff * 4);
+  A((void**)&m->logits, (size_t)B * nvoc * 4);
   A((void**)&m->ss, (size_t)B * (d / 16) * 4);
-  const int G = c.n_head / c.n_head_kv;
-  A((void**)&m->att_part, (size_t)B * c.n_head_kv * kAttnSplits * G * (c.head_dim + 2) * 4 + 16);
-  A((void**)&m->att_cnt, (size_t)B * c.n_head_kv * 4);
+  const int G = nh / nkv;
+  A((void**)&m->att_part, (size_t)B * nkv * kAttnSplits * G * (c.head_dim + 2) * 4 + 16);
+  A((void**)&m->att_cnt, (size_t)B * nkv * 4);
   A((void**)&m->am_v, (size_t)B * kArgmaxChunks * 4);
   A((void**)&m->am_i, (size_t)B * kArgmaxChunks * 4);
   A((void**)&m->am_cnt, (size_t)B * 4);
   A((void**)&m->d_pos, 16);
   A((void**)&m->d_tok, (size_t)B * 4);
   A((void**)&m->tok_log, (size_t)c.max_seq * B * 4);
+  if (world > 1) {
+    A((void**)&m->part, (size_t)B * d * 4);
+    A(&m->am_pair, (size_t)B * sizeof(ArgPair));
+    A(&m->am_all, (size_t)world * B * sizeof(ArgPair));
+  }
   if (rc == AH_OK) {
     m->err = device_error_word();
     if (!m->err) rc = fail(AH_ENOMEM, "model_create: device error word");
@@ -582,7 +707,7 @@ int ah_model_create(const AhModelConfig* cfg, AhModel** out) {
     ah_model_destroy(m);
     return rc;
   }
-  cudaMemset(m->att_cnt, 0, (size_t)B * c.n_head_kv * 4);
+  cudaMemset(m->att_cnt, 0, (size_t)B * nkv * 4);
   cudaMemset(m->am_cnt, 0, (size_t)B * 4);
   cudaMemset(m->kc, 0, kv);
   cudaMemset(m->vc, 0, kv);
@@ -597,6 +722,45 @@ int ah_model_create(const AhModelConfig* cfg, AhModel** out) {
     return fail(AH_ECUDA, "model_create: %s", cudaGetErrorString(e));
   }
   *out = m;
+  return AH_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int ah_model_create(const AhModelConfig* cfg, AhModel** out) { return model_create(cfg, 0, 1, nullptr, out); }
+
+int ah_nccl_unique_id(void* id_out, size_t bytes) {
+  AH_REQUIRE(id_out && bytes >= sizeof(ncclUniqueId), "nccl_unique_id: need a %zu-byte buffer", sizeof(ncclUniqueId));
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return fail(AH_ENCCL, "ncclGetUniqueId failed");
+  std::memcpy(id_out, &id, sizeof(id));
+  return AH_OK;
+}
+
+int ah_model_create_tp(const AhModelConfig* cfg, int rank, int world, const void* nccl_id, AhModel** out) {
+  AH_REQUIRE(cfg && out && nccl_id, "model_create_tp: null argument");
+  AH_REQUIRE(world >= 1 && rank >= 0 && rank < world, "model_create_tp: rank %d of %d", rank, world);
+  ncclComm_t comm = nullptr;
+  if (world > 1) {
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof(id));
+    if (ncclCommInitRank(&comm, world, id, rank) != ncclSuccess)
+      return fail(AH_ENCCL, "ncclCommInitRank(rank %d of %d) failed", rank, world);
+  }
+  const int rc = model_create(cfg, rank, world, comm, out);
+  if (rc != AH_OK && comm) ncclCommDestroy(comm);
+  return rc;
+}
+
+int ah_model_shard(const AhModel* m, int* rank, int* world, int* n_head, int* n_head_kv, int* n_ff, int* vocab) {
+  AH_REQUIRE(m, "model_shard: null model");
+  if (rank) *rank = m->tp_rank;
+  if (world) *world = m->tp_world;
+  if (n_head) *n_head = m->nh;
+  if (n_head_kv) *n_head_kv = m->nkv;
+  if (n_ff) *n_ff = m->nff;
+  if (vocab) *vocab = m->nvoc;
   return AH_OK;
 }
 
@@ -617,6 +781,7 @@ int ah_model_destroy(AhModel* m) {
       if (p) cudaFree(p);
   for (void* p : m->allocs) cudaFree(p);
   if (m->d_prompt) cudaFree(m->d_prompt);
+  if (m->comm) ncclCommDestroy(m->comm);
   cudaSetDevice(cur);
   delete m;
   return AH_OK;
@@ -650,14 +815,14 @@ int ah_model_load_tensor(AhModel* m, int kind, int layer, const void* data, void
     case AH_T_WDOWN:
       if (m->wd[layer]) ah_q4w_destroy(m->wd[layer]);
       m->wd[layer] = nullptr;
-      return ah_q4w_from_q4_0(data, d, c.n_ff, &m->wd[layer], stream);
+      return ah_q4w_from_q4_0(data, d, m->nff, &m->wd[layer], stream);
     case AH_T_LM_HEAD:
       if (m->lm) ah_q4w_destroy(m->lm);
       m->lm = nullptr;
-      return ah_q4w_from_q4_0(data, c.vocab_size, d, &m->lm, stream);
+      return ah_q4w_from_q4_0(data, m->nvoc, d, &m->lm, stream);
     case AH_T_WQ: case AH_T_WK: case AH_T_WV: case AH_T_WGATE: case AH_T_WUP: {
       const int slot = kind == AH_T_WQ ? 0 : kind == AH_T_WK ? 1 : kind == AH_T_WV ? 2 : kind == AH_T_WGATE ? 3 : 4;
-      const int64_t rows = slot == 0 ? m->dq : slot <= 2 ? m->dkv : c.n_ff;
+      const int64_t rows = slot == 0 ? m->dq : slot <= 2 ? m->dkv : m->nff;
       const size_t bytes = q4_bytes(rows, d);
       void*& p = m->pend[slot][layer];
       if (!p && cudaMalloc(&p, bytes) != cudaSuccess) {
@@ -680,7 +845,7 @@ int ah_model_load_tensor(AhModel* m, int kind, int layer, const void* data, void
       }
       if (slot >= 3 && m->pend[3][layer] && m->pend[4][layer]) {
         const void* srcs[2] = {m->pend[3][layer], m->pend[4][layer]};
-        const int64_t rws[2] = {c.n_ff, c.n_ff};
+        const int64_t rws[2] = {m->nff, m->nff};
         if (m->wgu[layer]) ah_q4w_destroy(m->wgu[layer]);
         m->wgu[layer] = nullptr;
         AH_TRY(q4w_create_q4_0_multi(srcs, rws, 2, 1, d, &m->wgu[layer], st));
@@ -705,18 +870,29 @@ int ah_model_init_random(AhModel* m, uint64_t seed, float w_std, float emb_std, 
   AH_TRY(ah_synth_f16(m->tok_embd, (int64_t)c.vocab_size * d, 0.0f, emb_std, ah_model_tensor_seed(seed, AH_T_TOK_EMBD, 0),
                       0, st));
   AH_TRY(ah_synth_f16(m->out_norm, d, 1.0f, norm_std, ah_model_tensor_seed(seed, AH_T_OUT_NORM, 0), 0, st));
-  const int64_t max_rows = std::max<int64_t>({(int64_t)m->dq, (int64_t)c.n_ff, (int64_t)d});
-  const int64_t max_cols = std::max<int64_t>({(int64_t)m->dq, (int64_t)c.n_ff, (int64_t)d});
+  // each rank draws its slice of the same full logical tensors, so a sharded
+  // model computes what the whole one does: row slices of q/k/v/gate/up/LM
+  // head, column slices of o/down (synth draws element (r, c) of the full
+  // matrix wherever the slice starts)
+  const int R = m->tp_rank;
+  const int64_t max_rows = std::max<int64_t>({(int64_t)m->dq, (int64_t)m->nff, (int64_t)d});
+  const int64_t max_cols = std::max<int64_t>({(int64_t)m->dq, (int64_t)m->nff, (int64_t)d});
   void* tmp = nullptr;
   const size_t tmp_bytes = (size_t)std::max<int64_t>(max_rows * (d / 32), (int64_t)d * (max_cols / 32)) * 18;
   if (cudaMalloc(&tmp, tmp_bytes) != cudaSuccess) {
     cudaGetLastError();
     return fail(AH_ENOMEM, "model_init_random: staging of %zu bytes", tmp_bytes);
   }
-  struct Spec { int kind; int64_t rows, cols; };
-  const Spec specs[7] = {{AH_T_WQ, m->dq, d},      {AH_T_WK, m->dkv, d},   {AH_T_WV, m->dkv, d},
-                         {AH_T_WO, d, m->dq},      {AH_T_WGATE, c.n_ff, d}, {AH_T_WUP, c.n_ff, d},
-                         {AH_T_WDOWN, d, c.n_ff}};
+  struct Spec { int kind; int64_t row0, rows, col0, cols, full_cols; };
+  const int64_t dq_full = (int64_t)c.n_head * c.head_dim, dkv_full = (int64_t)c.n_head_kv * c.head_dim;
+  const Spec specs[7] = {{AH_T_WQ, (int64_t)R * m->dq, m->dq, 0, d, d},
+                         {AH_T_WK, (int64_t)R * m->dkv, m->dkv, 0, d, d},
+                         {AH_T_WV, (int64_t)R * m->dkv, m->dkv, 0, d, d},
+                         {AH_T_WO, 0, d, (int64_t)R * m->dq, m->dq, dq_full},
+                         {AH_T_WGATE, (int64_t)R * m->nff, m->nff, 0, d, d},
+                         {AH_T_WUP, (int64_t)R * m->nff, m->nff, 0, d, d},
+                         {AH_T_WDOWN, 0, d, (int64_t)R * m->nff, m->nff, (int64_t)c.n_ff}};
+  (void)dkv_full;
   int rc = AH_OK;
   for (int l = 0; l < c.n_layer && rc == AH_OK; ++l) {
     rc = ah_synth_f16(m->attn_norm + (size_t)l * d, d, 1.0f, norm_std, ah_model_tensor_seed(seed, AH_T_ATTN_NORM, l),
@@ -724,20 +900,22 @@ int ah_model_init_random(AhModel* m, uint64_t seed, float w_std, float emb_std, 
     if (rc == AH_OK)
       rc = ah_synth_f16(m->ffn_norm + (size_t)l * d, d, 1.0f, norm_std, ah_model_tensor_seed(seed, AH_T_FFN_NORM, l),
                         0, st);
-    for (const Spec& s : specs) {
+    for (const Spec& sp : specs) {
       if (rc != AH_OK) break;
-      rc = ah_synth_q4_0(tmp, 0, s.rows, 0, s.cols, s.cols, w_std, ah_model_tensor_seed(seed, s.kind, l), st);
-      if (rc == AH_OK) rc = ah_model_load_tensor(m, s.kind, l, tmp, st);
+      rc = ah_synth_q4_0(tmp, sp.row0, sp.rows, sp.col0, sp.cols, sp.full_cols, w_std,
+                         ah_model_tensor_seed(seed, sp.kind, l), st);
+      if (rc == AH_OK) rc = ah_model_load_tensor(m, sp.kind, l, tmp, st);
     }
   }
   if (rc == AH_OK) {
-    // the LM head is the largest tensor: generate it in its own buffer
+    // the LM head is the largest tensor: generate this rank's rows in their own buffer
     void* lmb = nullptr;
-    if (cudaMalloc(&lmb, (size_t)c.vocab_size * (d / 32) * 18) != cudaSuccess) {
+    if (cudaMalloc(&lmb, (size_t)m->nvoc * (d / 32) * 18) != cudaSuccess) {
       cudaGetLastError();
       rc = fail(AH_ENOMEM, "model_init_random: output.weight staging");
     } else {
-      rc = ah_synth_q4_0(lmb, 0, c.vocab_size, 0, d, d, w_std, ah_model_tensor_seed(seed, AH_T_LM_HEAD, 0), st);
+      rc = ah_synth_q4_0(lmb, (int64_t)R * m->nvoc, m->nvoc, 0, d, d, w_std,
+                         ah_model_tensor_seed(seed, AH_T_LM_HEAD, 0), st);
       if (rc == AH_OK) rc = ah_model_load_tensor(m, AH_T_LM_HEAD, 0, lmb, st);
       cudaStreamSynchronize(st);
       cudaFree(lmb);
@@ -771,7 +949,7 @@ int ah_model_forward(AhModel* m, const int32_t* tokens, float* logits, void* str
   AH_CUDA_TRY(cudaMemcpyAsync(m->d_tok, tokens, (size_t)m->batch * 4, cudaMemcpyDeviceToDevice, st));
   AH_TRY(run_step_graph(m, 1, nullptr, 0, st));
   if (logits)
-    AH_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)m->batch * m->c.vocab_size * 4, cudaMemcpyDeviceToDevice,
+    AH_CUDA_TRY(cudaMemcpyAsync(logits, m->logits, (size_t)m->batch * m->nvoc * 4, cudaMemcpyDeviceToDevice,
                                 st));
   return AH_OK;
 }

@@ -46,7 +46,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       : "memory");
 }
 
-// Two-dimensional tiled TMA load global -> shared (no multicast), completing
+// Two-dimensional tiled TMA load global -> shared (one destination CTA), completing
 // on `bar`; (x, y) are element coordinates of the box origin.  x times the
 // element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(void* dst_smem, const void* tmap, int x, int y, uint64_t* bar) {

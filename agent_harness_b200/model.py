@@ -57,15 +57,46 @@ def tensor_seed(seed: int, kind: int, layer: int) -> int:
     return int(lib().ah_model_tensor_seed(C.c_uint64(seed), kind, layer))
 
 
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL id (128 bytes) for ah_model_create_tp; make it on one rank
+    and share it (e.g. torch.distributed.broadcast_object_list)."""
+    buf = C.create_string_buffer(128)
+    call("ah_nccl_unique_id", buf, 128)
+    return buf.raw
+
+
+def shard_rows(cfg: ModelConfig, rank: int, world: int) -> dict:
+    """Rows / columns of each full tensor that tensor-parallel rank `rank`
+    holds: {kind: (row0, rows, col0, cols)} (row split for q, k, v, gate, up
+    and the LM head; column split for o and down)."""
+    dq, dkv = cfg.n_head * cfg.head_dim // world, cfg.n_head_kv * cfg.head_dim // world
+    nff, nv, d = cfg.n_ff // world, cfg.vocab_size // world, cfg.n_embd
+    return {WQ: (rank * dq, dq, 0, d), WK: (rank * dkv, dkv, 0, d), WV: (rank * dkv, dkv, 0, d),
+            WO: (0, d, rank * dq, dq), WGATE: (rank * nff, nff, 0, d), WUP: (rank * nff, nff, 0, d),
+            WDOWN: (0, d, rank * nff, nff), LM_HEAD: (rank * nv, nv, 0, d)}
+
+
 class Model:
-    def __init__(self, cfg: ModelConfig, device="cuda"):
+    """The decoder on one GPU, or rank `tp_rank` of a `tp_world`-way
+    tensor-parallel group (pass the group's NCCL id from nccl_unique_id)."""
+
+    def __init__(self, cfg: ModelConfig, device="cuda", tp_rank: int = 0, tp_world: int = 1,
+                 nccl_id: bytes | None = None):
         self.cfg = cfg
         dev = torch.device(device)
         self.device = torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
         torch.cuda.set_device(self.device)
         self._h = C.c_void_p()
         c = cfg.to_c()
-        call("ah_model_create", C.byref(c), C.byref(self._h))
+        self.tp_rank, self.tp_world = tp_rank, tp_world
+        if tp_world == 1:
+            call("ah_model_create", C.byref(c), C.byref(self._h))
+        else:
+            if nccl_id is None or len(nccl_id) < 128:
+                raise ValueError("tensor parallelism needs the group's 128-byte NCCL id")
+            idb = C.create_string_buffer(bytes(nccl_id[:128]), 128)
+            call("ah_model_create_tp", C.byref(c), tp_rank, tp_world, idb, C.byref(self._h))
+        self.vocab_local = cfg.vocab_size // tp_world
 
     def _stream(self):
         return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
@@ -81,9 +112,10 @@ class Model:
         call("ah_model_reset", self._h, batch, self._stream())
 
     def forward(self, tokens) -> torch.Tensor:
-        """One forward() per sequence; returns logits [batch][vocab]."""
+        """One forward() per sequence; returns logits [batch][vocab] (this
+        rank's vocab slice [batch][vocab/world] under tensor parallelism)."""
         t = torch.as_tensor(np.asarray(tokens, np.int32)).to(self.device)
-        out = torch.empty(t.numel(), self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+        out = torch.empty(t.numel(), self.vocab_local, dtype=torch.float32, device=self.device)
         call("ah_model_forward", self._h, C.c_void_p(t.data_ptr()), C.c_void_p(out.data_ptr()), self._stream())
         return out
 

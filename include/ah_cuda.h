@@ -200,6 +200,22 @@ typedef struct AhModel AhModel;
  * device side: allocates the weight arena, f16 KV cache [batch][layer][kv_head]
  * [max_seq][head_dim] and activations on the current device. */
 AH_API int ah_model_create(const AhModelConfig* cfg, AhModel** out);
+/* Tensor parallelism (no reference counterpart: the reference runs on one CPU).
+ * Rank `rank` of `world` (one process or thread per GPU, each with its own
+ * current device) holds heads [rank*n_head/world, ...), the matching kv heads,
+ * FFN rows and vocab rows: q/k/v, gate/up and the LM head are split by rows,
+ * o and down by columns, with one NCCL all-reduce per attention and MLP block
+ * and an all-gather of per-shard argmax candidates.  `nccl_id` is the
+ * 128-byte id from ah_nccl_unique_id on one rank, shared by the caller.
+ * world must divide n_head_kv, n_ff and vocab_size.  ah_model_load_tensor then
+ * takes this rank's slices; ah_model_forward writes this rank's vocab slice
+ * of the logits [batch][vocab/world]; generated tokens are identical on all
+ * ranks.  ah_model_create(cfg) equals ah_model_create_tp(cfg, 0, 1, ...). */
+AH_API int ah_nccl_unique_id(void* id_out, size_t bytes);
+AH_API int ah_model_create_tp(const AhModelConfig* cfg, int rank, int world, const void* nccl_id, AhModel** out);
+/* This rank's shard: heads, kv heads, FFN rows and vocab rows it holds. */
+AH_API int ah_model_shard(const AhModel* m, int* rank, int* world, int* n_head, int* n_head_kv, int* n_ff,
+                          int* vocab);
 AH_API int ah_model_destroy(AhModel* m);
 /* Loads one tensor from device memory (f16 bits or Q4_0 blocks, per kind);
  * Q4_0 projections are repacked into the GEMV layout (q|k|v fused, gate/up

@@ -1,0 +1,83 @@
+"""GPU tensor parallelism: a 2-rank decoder (one process per GPU, NCCL
+all-reduce per block, argmax-candidate all-gather) against the same model on
+one GPU.  The ranks' vocab slices of the logits, concatenated, match the
+single-GPU logits (1e-3 normwise, as the decoder parity bar) and greedy tokens
+are identical on every rank and equal to the single-GPU ones.  Skipped on
+boxes with fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(n_layer=2, n_embd=256, n_ff=512, n_head=4, n_head_kv=2, head_dim=64, vocab_size=1000, max_seq=64,
+             max_batch=2, rope_freq_base=10000.0, rms_eps=1e-5)
+PROMPT = np.array([[3, 14, 159, 265, 358, 979], [2, 71, 828, 182, 845, 904]], np.int32)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from agent_harness_b200 import _lib
+        from agent_harness_b200.model import Model, ModelConfig, nccl_unique_id
+        _lib.check(_lib.lib().ah_device_init(rank))
+        ids = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        m = Model(ModelConfig(**SMALL), device=f"cuda:{rank}", tp_rank=rank, tp_world=world, nccl_id=ids[0])
+        m.init_random(123)
+        m.reset(2)
+        logits = [m.forward(PROMPT[:, t]).cpu().numpy() for t in range(PROMPT.shape[1])]
+        gen = m.generate(PROMPT, 8)
+        torch.cuda.synchronize()
+        err = _lib.lib().ah_check_device_error(None)
+        m.close()
+        q.put((rank, logits, gen, err))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_matches_single_gpu(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, lg, gen, err = q.get(timeout=600)
+        res[r] = (lg, gen, err)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res[0][2] == 0 and res[1][2] == 0
+    from agent_harness_b200.model import Model, ModelConfig
+    m = Model(ModelConfig(**SMALL), device="cuda:0")
+    m.init_random(123)
+    m.reset(2)
+    for t in range(PROMPT.shape[1]):
+        ref = m.forward(PROMPT[:, t]).cpu().numpy()
+        full = np.concatenate([res[0][0][t], res[1][0][t]], axis=1)
+        err = np.max(np.abs(full - ref)) / np.max(np.abs(ref))
+        assert err <= 1e-3, (t, err)
+    gen1 = m.generate(PROMPT, 8)
+    m.close()
+    assert np.array_equal(res[0][1], res[1][1])
+    assert np.array_equal(res[0][1], gen1)
