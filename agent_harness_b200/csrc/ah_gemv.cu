@@ -796,15 +796,49 @@ int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, G
 }
 }  // namespace
 
+namespace {
+// The largest token count (<= batch) whose split of x fits one CTA's shared
+// memory; larger batches run as several launches over token slices.
+int max_sub_batch(const Q4Tiled& w, int batch) {
+  for (int b = batch; b >= 1; --b)
+    if (gemv_plan(w, b, false).smem <= (size_t)kGemvSmemLimit) return b;
+  return 0;
+}
+int gemv_launch_one(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl);
+}  // namespace
+
 int gemv_prepare(const Q4Tiled& w, int batch, int pro, int epi) {
   AH_REQUIRE(batch >= 1 && batch <= kGemvMaxBatch, "gemv: batch must be 1..16");
+  const int sb = max_sub_batch(w, batch);
+  AH_REQUIRE(sb >= 1, "gemv: %lld columns do not fit one CTA even for one token", (long long)w.cols);
   GemvPlan plan;
   GemvKernel kern;
   int cap;
-  return choose_plan(w, batch, pro, epi, &plan, &kern, &cap);
+  AH_TRY_GEMV(choose_plan(w, sb, pro, epi, &plan, &kern, &cap));
+  if (batch % sb) AH_TRY_GEMV(choose_plan(w, batch % sb, pro, epi, &plan, &kern, &cap));
+  return AH_OK;
 }
 
 int gemv_launch(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
+  AH_REQUIRE(a.batch >= 1 && a.batch <= kGemvMaxBatch, "gemv: batch must be 1..16");
+  const int sb = max_sub_batch(a.w, a.batch);
+  AH_REQUIRE(sb >= 1, "gemv: %lld columns do not fit one CTA even for one token", (long long)a.w.cols);
+  if (sb == a.batch) return gemv_launch_one(a, pro, epi, st, pdl);
+  // token slices: every per-token operand moves by the slice start
+  for (int b0 = 0; b0 < a.batch; b0 += sb) {
+    GemvArgs s = a;
+    s.batch = std::min(sb, a.batch - b0);
+    s.x = a.x + (int64_t)b0 * a.x_stride;
+    s.y = a.y + (int64_t)b0 * a.y_stride;
+    if (a.ss_in) s.ss_in = a.ss_in + (int64_t)b0 * a.n_ss_in;
+    if (a.ss_out) s.ss_out = a.ss_out + (int64_t)b0 * a.w.r16;
+    AH_TRY_GEMV(gemv_launch_one(s, pro, epi, st, pdl));
+  }
+  return AH_OK;
+}
+
+namespace {
+int gemv_launch_one(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   AH_REQUIRE(a.batch >= 1 && a.batch <= kGemvMaxBatch, "gemv: batch must be 1..16");
   AH_REQUIRE(pro != kProRmsNorm || (a.norm_w != nullptr && a.ss_in != nullptr && a.n_ss_in > 0),
              "gemv: RMSNorm prologue needs a norm weight and the producer's partial sums of squares");
@@ -844,6 +878,7 @@ int gemv_launch(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   AH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
   return AH_OK;
 }
+}  // namespace
 
 }  // namespace ah
 

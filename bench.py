@@ -306,6 +306,8 @@ def run_gpu(args):
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             dec["tokens_per_s_all_replicas"] = round(world * 1e3 / float(t.item()), 2)
         extra["decode_8b"] = dec
+    if not args.quick and not args.no_tp:
+        extra["decode_70b_tp"] = decode_70b_tp(dev, rank, world, args.tp_prompt, args.tp_new)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = time_cpu_gemv(seconds=args.cpu_seconds)
@@ -351,6 +353,55 @@ def run_gpu(args):
 
 DECODE_PROMPT, DECODE_NEW = 2048, 256
 DECODE_BYTES_PER_TOKEN_WEIGHTS = 4221370368  # all Q4_0 projections + LM head of the 8B shape
+
+
+TP_PROMPT, TP_NEW, TP_BATCH = 128, 64, 16
+# all Q4_0 projections + LM head of the 70B shape (80 x (q 8192^2 + k,v 1024x8192
+# + o 8192^2 + gate,up,down 3 x 28672x8192) + 128256x8192) x 18/32 bytes
+DECODE70_WEIGHT_BYTES = 39094714368
+
+
+def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_BATCH):
+    """70B-shape greedy decode, batch 16, tensor-parallel over the job's ranks
+    (80 layers, d 8192, FFN 28672, 64/8 heads x 128, vocab 128256; Q4_0
+    N(0,0.02) seed 8; prompts of uniform ids seed 9).  Decode steps are timed
+    with CUDA events on every rank; the max over ranks is reported."""
+    import torch
+    from agent_harness_b200.model import LLAMA_70B, Model, ModelConfig, nccl_unique_id
+    cfg = ModelConfig(**{**LLAMA_70B.__dict__, "max_seq": n_prompt + n_new + 8, "max_batch": batch})
+    nid = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    m = Model(cfg, device=dev, tp_rank=rank, tp_world=world, nccl_id=nid)
+    m.init_random(8, w_std=0.02, emb_std=1.0, norm_std=0.02)
+    prompt = np.random.default_rng(9).integers(0, cfg.vocab_size, (batch, n_prompt)).astype(np.int32)
+    t0 = time.perf_counter()
+    m.generate(prompt, 1)  # token-by-token prefill (inference/mod.rs:550) + first token
+    prefill_s = time.perf_counter() - t0
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    toks = m.decode(n_new + 1, batch)
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms, prefill_s * 1e3], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, prefill_s = float(t[0].item()), float(t[1].item()) / 1e3
+    first = toks[1, :4].cpu().numpy().tolist()
+    m.close()
+    per_step = ms / 1e3 / n_new
+    return {"tokens_per_s": round(batch * n_new / (ms / 1e3), 1), "ms_per_step": round(per_step * 1e3, 3),
+            "batch": batch, "n_prompt": n_prompt, "n_new": n_new, "tp": world,
+            "weight_gbs_per_gpu": round(DECODE70_WEIGHT_BYTES / world / per_step / 1e9, 1),
+            "prefill_tokens_per_s_token_by_token": round(batch * (n_prompt - 1) / prefill_s, 1),
+            "first_tokens_seq0_3": first,
+            "note": "tensor parallel over the job's ranks: row/column-sharded projections, one NCCL all-reduce "
+                    "per attention/MLP block, argmax-candidate all-gather; steps replayed as CUDA graphs"}
 
 
 def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW):
@@ -491,13 +542,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode", "gemm"],
-                    help="decode / gemm: only the 8B decode or the prefill GEMM measurement (for profiling)")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode", "gemm", "tp"],
+                    help="decode / gemm / tp: only the 8B decode, the prefill GEMM or the 70B tensor-parallel "
+                         "decode measurement (for profiling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
     ap.add_argument("--decode-prompt", type=int, default=DECODE_PROMPT)
     ap.add_argument("--decode-new", type=int, default=DECODE_NEW)
+    ap.add_argument("--no-tp", action="store_true", help="skip the 70B tensor-parallel decode measurement")
+    ap.add_argument("--tp-prompt", type=int, default=TP_PROMPT)
+    ap.add_argument("--tp-new", type=int, default=TP_NEW)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -508,6 +563,24 @@ def main():
         _lib.check(_lib.lib().ah_device_init(0))
         print(json.dumps({"workload": "decode_8b", **decode_8b(torch.device("cuda", 0), args.decode_prompt,
                                                                args.decode_new)}), flush=True)
+        return 0
+    if args.workload == "tp":
+        import torch
+        rank, world, local = dist_env()
+        torch.cuda.set_device(local)
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                    timeout=datetime.timedelta(seconds=300))
+        from agent_harness_b200 import _lib
+        _lib.check(_lib.lib().ah_device_init(local))
+        r = decode_70b_tp(torch.device("cuda", local), rank, world, args.tp_prompt, args.tp_new)
+        if rank == 0:
+            print(json.dumps({"workload": "decode_70b_tp", **r}), flush=True)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
         return 0
     if args.workload == "gemm":
         import torch

@@ -189,3 +189,16 @@ def test_many_row_tiles_engine_format(cuda, oracle):
     W = K.Q4Weight.from_engine(torch.from_numpy(s).to(cuda), torch.from_numpy(p).to(cuda), rows, cols)
     y = W.gemv(torch.from_numpy(x).to(cuda)).cpu().numpy()
     assert relerr(y, oracle.gemv_4bit_into(s, p, x, rows, cols, 32)) <= TOL
+
+
+def test_batch_split_when_x_exceeds_shared_memory(cuda, oracle):
+    # batch 16 x K 28672: the split of x needs more shared memory than one CTA
+    # has, so the launch runs over token slices (each token independent)
+    from agent_harness_b200 import kernels as K
+    rows, cols, batch = 48, 28672, 16
+    blocks, W = _q4_0_weight(K, rows, cols, 99, cuda)
+    x = K.fill_normal(batch * cols, 0.0, 1.0, 98, device=cuda).reshape(batch, cols)
+    y = W.gemv(x).cpu().numpy()
+    bh, xh = blocks.cpu().numpy(), x.cpu().numpy()
+    for b in (0, 5, 9, 15):
+        assert relerr(y[b], oracle.gemv_q4_0(bh, xh[b], rows, cols)) <= TOL, b
