@@ -437,6 +437,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
   float* part = reinterpret_cast<float*>(blk_info + B * kbc);                   // [warps][16][B]
   float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
   float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
+  float* slots = wred + kGemvWarps * BM + 16 * B;  // [2][cluster][16][B] pushed chunk partials
+  int64_t iter = 0;
 
   // Weights do not depend on the previous kernel: start streaming them now
   // (two batches of kGemvU pairs in flight per lane).
@@ -487,31 +489,36 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
     }
     if (rg_next >= n_rg && !a.early_trigger) pdl_launch_dependents();
 
-    // chunk partials -> cluster CTA `warp` over DSMEM
+    // push the chunk partials to their owners: row tile `warp` of this group is
+    // finalised by cluster CTA `warp`, which gathers chunk c's partial in its
+    // slot c (slots double-buffered by row-group parity).  One cluster barrier
+    // then makes every push visible; afterwards each CTA reads only its own
+    // shared memory, so no second barrier guards the slots or the exit.
+    float* slot_base = slots + (size_t)(iter & 1) * kGemvCluster * 16 * B;
+    if (warp_live) {
+      const uint32_t dst = mapa_shared(smem_u32(slot_base + crank * 16 * B), (uint32_t)warp);
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
-      if (b < B) {
-        part[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
-        part[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
+      for (int j = 0; j < NT; ++j) {
+        const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
+        if (b < B) {
+          st_dsmem_f32(dst + (uint32_t)((g * B + b) * 4), tot[j][0] + tot[j][1]);
+          st_dsmem_f32(dst + (uint32_t)(((g + 8) * B + b) * 4), tot[j][2] + tot[j][3]);
+        }
       }
     }
     cluster_arrive();
-    cluster_wait();  // every CTA's partials are visible cluster-wide
+    cluster_wait();  // every push into this CTA's slots has landed
     const int64_t my_rt = rg * kGemvWarps + crank;  // the row tile this CTA finalises
     const bool fin_live = my_rt < a.w.r16;
     float* fin = wred;  // [16][B]
     if (fin_live) {
-      // partial of chunk c for row tile `crank` sits at part[crank] in cluster CTA c
-      const uint32_t local = smem_u32(part + crank * 16 * B);
       for (int i = tid; i < 16 * B; i += kGemvThreads) {
         float v = 0.0f;
 #pragma unroll
-        for (int c = 0; c < kGemvCluster; ++c) v += ld_dsmem_f32(mapa_shared(local + i * 4, (uint32_t)c));
+        for (int c = 0; c < kGemvCluster; ++c) v += slot_base[c * 16 * B + i];  // chunk order
         fin[i] = v;
       }
     }
-    cluster_arrive();  // this CTA's DSMEM reads are done
     __syncthreads();
     if (fin_live) {
       if (EPI == kEpiSwiglu) {
@@ -544,10 +551,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
         }
       }
     }
-    cluster_wait();  // every CTA has read the partials: they may be overwritten (or the CTA may leave)
-    __syncthreads();
+    __syncthreads();  // fin is reused by the next row group
     rt = rt_next;
     warp_live = next_live;
+    ++iter;
   }
 }
 
@@ -691,6 +698,7 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
   const int64_t plane = kbc * 64 + 64;
   p.smem = (size_t)2 * batch * plane + (size_t)batch * kbc * 16 + (size_t)kGemvWarps * 16 * batch * 4 +
            (size_t)kGemvMaxBatch * 4 + (size_t)kGemvWarps * (4 * p.nt) * 4 + (size_t)16 * batch * 4 + 16;
+  if (!rows_mode) p.smem += (size_t)2 * kGemvCluster * 16 * batch * 4;  // DSMEM partial slots
   return p;
 }
 
