@@ -141,19 +141,43 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
       Vs[(pos - p0) * hd + d] = __half_as_ushort(__float2half_rn(vnew[d]));
     }
   __syncthreads();
-  // scores: one warp per position, lanes over head dims (hd = 32 * per_lane)
+  // scores: one warp per position, lanes over head dims (hd = 32 * per_lane).
+  // Loops run to the compile-time maxima (4 dims per lane, 8 heads per group)
+  // under uniform predicates, so kv[] and dot[] stay in registers.
   const int per_lane = hd / 32;
   for (int i = warp; i < n; i += kAttnThreads / 32) {
     float kv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     const uint16_t* kr = Ks + i * hd + lane * per_lane;
-    for (int e = 0; e < per_lane; ++e) kv[e] = __half2float(__ushort_as_half(kr[e]));
-    for (int g = 0; g < G; ++g) {
-      float dot = 0.0f;
-      for (int e = 0; e < per_lane; ++e) dot = fmaf(q[g * hd + lane * per_lane + e], kv[e], dot);
+    if (per_lane == 4) {
+      const uint2 u = *reinterpret_cast<const uint2*>(kr);  // 8-byte aligned: hd = 128
+      kv[0] = __half2float(__ushort_as_half((unsigned short)(u.x & 0xFFFFu)));
+      kv[1] = __half2float(__ushort_as_half((unsigned short)(u.x >> 16)));
+      kv[2] = __half2float(__ushort_as_half((unsigned short)(u.y & 0xFFFFu)));
+      kv[3] = __half2float(__ushort_as_half((unsigned short)(u.y >> 16)));
+    } else {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
-      if (lane == 0) sc[g * kAttnMaxChunk + i] = dot * a.scale;
+      for (int e = 0; e < 4; ++e)
+        if (e < per_lane) kv[e] = __half2float(__ushort_as_half(kr[e]));
     }
+    float dot[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      dot[g] = 0.0f;
+      if (g < G) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (e < per_lane) dot[g] = fmaf(q[g * hd + lane * per_lane + e], kv[e], dot[g]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        if (g < G) dot[g] += __shfl_xor_sync(0xFFFFFFFFu, dot[g], o);
+    if (lane == 0)
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        if (g < G) sc[g * kAttnMaxChunk + i] = dot[g] * a.scale;
   }
   __syncthreads();
   // softmax pieces per head: m = max, weights exp(s - m), l = sum
@@ -182,12 +206,17 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
   float* pml = a.part + (size_t)gridDim.z * a.n_kv * kAttnSplits * G * hd + (bh * kAttnSplits + s) * G * 2;
   for (int d = tid; d < hd; d += kAttnThreads) {
     float acc[8];
-    for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) acc[g] = 0.0f;
     for (int i = 0; i < n; ++i) {
       const float v = __half2float(__ushort_as_half(Vs[i * hd + d]));
-      for (int g = 0; g < G; ++g) acc[g] = fmaf(sc[g * kAttnMaxChunk + i], v, acc[g]);
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        if (g < G) acc[g] = fmaf(sc[g * kAttnMaxChunk + i], v, acc[g]);
     }
-    for (int g = 0; g < G; ++g) pacc[g * hd + d] = acc[g];
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      if (g < G) pacc[g * hd + d] = acc[g];
   }
   if (tid < G) {
     pml[tid * 2] = n > 0 ? red[tid * 2] : -INFINITY;
