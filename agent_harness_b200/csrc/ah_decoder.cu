@@ -371,6 +371,76 @@ __global__ void __launch_bounds__(256) k_residual_add(float* __restrict__ hidden
   if (live && (i & 15) == 0) ss[(size_t)b * (d / 16) + i / 16] = q;
 }
 
+// ---- tensor-parallel all-reduce over NVLink peer memory ------------------------
+// Each rank's o / down GEMV stores its partial into slot `rank` of every rank's
+// receive buffer (peer stores); k_peer_signal then publishes the collective's
+// sequence number into every rank's flag slot `rank`, and k_residual_add_peer
+// waits for all ranks' flags before summing the slots in rank order (so every
+// rank computes the identical sum).  Waits are bounded: a rank that never
+// signals makes the wait record AH_ETIMEOUT and leave hidden untouched.
+struct PeerFlags {
+  unsigned* flag[8];  // each rank's flag array, as mapped on this GPU
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void k_peer_signal(unsigned* seq, PeerFlags f, int rank, int world) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  const unsigned s = *seq + 1u;
+  *seq = s;
+  for (int r = 0; r < world; ++r) st_release_sys(f.flag[r] + rank, s);
+}
+
+constexpr uint32_t kPeerWaitLimit = 1u << 22;  // x ~100 ns sleeps: ~0.4 s
+
+// hidden += sum_r slot[r] (rank order), and the per-16-row sums of squares.
+// grid ((d + 255) / 256, B).
+__global__ void __launch_bounds__(256) k_residual_add_peer(float* __restrict__ hidden, const float* __restrict__ slots,
+                                                           int world, int batch, float* __restrict__ ss, int d,
+                                                           const unsigned* flag, const unsigned* seq, int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    const unsigned s = *seq;
+    int good = 1;
+    for (int r = 0; r < world && good; ++r) {
+      uint32_t it = 0;
+      while (ld_acquire_sys(flag + r) < s) {
+        if (++it > kPeerWaitLimit) {
+          atomicExch(err, AH_ETIMEOUT);
+          good = 0;
+          break;
+        }
+        __nanosleep(100);
+      }
+    }
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int b = blockIdx.y;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const bool live = i < d;
+  float h = 0.0f;
+  if (live) {
+    float sum = 0.0f;
+    for (int r = 0; r < world; ++r) sum += slots[((size_t)r * batch + b) * d + i];
+    h = hidden[(size_t)b * d + i] + sum;
+    hidden[(size_t)b * d + i] = h;
+  }
+  float q = h * h;
+#pragma unroll
+  for (int o = 1; o < 16; o <<= 1) q += __shfl_xor_sync(0xFFFFFFFFu, q, o);
+  if (live && (i & 15) == 0) ss[(size_t)b * (d / 16) + i / 16] = q;
+}
+
 // Candidate of one vocab shard: value and global index (INT_MAX: none).
 struct ArgPair {
   float v;
@@ -456,6 +526,13 @@ struct AhModel {
   float* att_part = nullptr;
   int* att_cnt = nullptr;
   float* part = nullptr;   // [B][d] o / down partial sums (tensor parallelism)
+  // peer-memory all-reduce: one block per rank holding the receive slots
+  // [2 parities][world][B][d] f32, the flags [world] and the local sequence
+  // counter; peer_block[r] is rank r's block as mapped here (IPC)
+  void* comm_block = nullptr;
+  size_t comm_flags_off = 0;
+  void* peer_block[8] = {};
+  bool p2p = false;
   void* am_pair = nullptr; // [B] this shard's argmax candidate
   void* am_all = nullptr;  // [world][B] all shards' candidates
   float* am_v = nullptr;
@@ -525,6 +602,34 @@ int reduce_residual(AhModel* m, cudaStream_t st) {
                     m->ss, d);
 }
 
+// Peer-memory variant.  Parity `par` selects the receive slots: a step has 2
+// collectives per layer (even), so o-projections always use parity 0 and
+// down-projections parity 1, and a rank can only reuse a parity's slots after
+// every rank has read them (it has waited for their next collective's flags).
+float* peer_slots(const AhModel* m, int r, int par) {
+  return static_cast<float*>(m->peer_block[r]) + (size_t)par * m->tp_world * m->c.max_batch * m->c.n_embd +
+         (size_t)m->tp_rank * m->c.max_batch * m->c.n_embd;
+}
+void set_peer_scatter(const AhModel* m, GemvArgs& a, int par) {
+  a.n_peer = m->tp_world;
+  for (int r = 0; r < m->tp_world; ++r) a.peer_y[r] = peer_slots(m, r, par);
+}
+int reduce_residual_peer(AhModel* m, int par, cudaStream_t st) {
+  const int B = m->batch, d = m->c.n_embd, W = m->tp_world;
+  PeerFlags f{};
+  for (int r = 0; r < W; ++r)
+    f.flag[r] = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(m->peer_block[r]) + m->comm_flags_off);
+  unsigned* local_flags = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(m->comm_block) + m->comm_flags_off);
+  unsigned* seq = local_flags + 64;  // the local counter sits after the flag slots
+  k_peer_signal<<<1, 32, 0, st>>>(seq, f, m->tp_rank, W);
+  AH_LAUNCH_CHECK();
+  const float* slots = static_cast<const float*>(m->comm_block) + (size_t)par * W * m->c.max_batch * d;
+  k_residual_add_peer<<<dim3((d + 255) / 256, B), 256, 0, st>>>(m->hidden, slots, W, m->c.max_batch, m->ss, d,
+                                                                local_flags, seq, m->err);
+  AH_LAUNCH_CHECK();
+  return AH_OK;
+}
+
 // Enqueues one decoder step (all layers; with_head adds LM head + argmax).
 int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cudaStream_t st) {
   const AhModelConfig& c = m->c;
@@ -558,7 +663,12 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     at.scale = 1.0f / sqrtf((float)c.head_dim);  // mod.rs:478
     at.err = m->err;
     AH_TRY(launch_pdl(k_attention, dim3(m->nkv, kAttnSplits, B), dim3(kAttnThreads), attn_smem, st, at));
-    if (tp) {
+    if (tp && m->p2p) {
+      GemvArgs o = gemv_args(m->wo[l], m->attn, m->dq, m->part, d, B);
+      set_peer_scatter(m, o, 0);
+      AH_TRY(gemv_launch(o, kProPlain, kEpiStore, st, true));
+      AH_TRY(reduce_residual_peer(m, 0, st));
+    } else if (tp) {
       AH_TRY(gemv_launch(gemv_args(m->wo[l], m->attn, m->dq, m->part, d, B), kProPlain, kEpiStore, st, true));
       AH_TRY(reduce_residual(m, st));
     } else {
@@ -572,7 +682,12 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     gu.ss_in = m->ss;
     gu.n_ss_in = d / 16;
     AH_TRY(gemv_launch(gu, kProRmsNorm, kEpiSwiglu, st, true));
-    if (tp) {
+    if (tp && m->p2p) {
+      GemvArgs dn = gemv_args(m->wd[l], m->act, m->nff, m->part, d, B);
+      set_peer_scatter(m, dn, 1);
+      AH_TRY(gemv_launch(dn, kProPlain, kEpiStore, st, true));
+      AH_TRY(reduce_residual_peer(m, 1, st));
+    } else if (tp) {
       AH_TRY(gemv_launch(gemv_args(m->wd[l], m->act, m->nff, m->part, d, B), kProPlain, kEpiStore, st, true));
       AH_TRY(reduce_residual(m, st));
     } else {
@@ -724,6 +839,8 @@ int model_create(const AhModelConfig* cfg, int rank, int world, ncclComm_t comm,
   A((void**)&m->d_tok, (size_t)B * 4);
   A((void**)&m->tok_log, (size_t)c.max_seq * B * 4);
   if (world > 1) {
+    m->comm_flags_off = ((size_t)2 * world * B * d * 4 + 255) / 256 * 256;
+    A(&m->comm_block, m->comm_flags_off + 256 + 64);
     A((void**)&m->part, (size_t)B * d * 4);
     A(&m->am_pair, (size_t)B * sizeof(ArgPair));
     A(&m->am_all, (size_t)world * B * sizeof(ArgPair));
@@ -736,6 +853,7 @@ int model_create(const AhModelConfig* cfg, int rank, int world, ncclComm_t comm,
     ah_model_destroy(m);
     return rc;
   }
+  if (m->comm_block) cudaMemset(m->comm_block, 0, m->comm_flags_off + 256 + 64);
   cudaMemset(m->att_cnt, 0, (size_t)B * nkv * 4);
   cudaMemset(m->am_cnt, 0, (size_t)B * 4);
   cudaMemset(m->kc, 0, kv);
@@ -782,6 +900,46 @@ int ah_model_create_tp(const AhModelConfig* cfg, int rank, int world, const void
   return rc;
 }
 
+int ah_model_ipc_handle(AhModel* m, void* handle_out, size_t bytes) {
+  AH_REQUIRE(m && handle_out && bytes >= sizeof(cudaIpcMemHandle_t), "model_ipc_handle: need a %zu-byte buffer",
+             sizeof(cudaIpcMemHandle_t));
+  AH_REQUIRE(m->tp_world > 1 && m->comm_block, "model_ipc_handle: not a tensor-parallel model");
+  cudaIpcMemHandle_t h;
+  AH_CUDA_TRY(cudaIpcGetMemHandle(&h, m->comm_block));
+  std::memcpy(handle_out, &h, sizeof(h));
+  return AH_OK;
+}
+
+int ah_model_ipc_open(AhModel* m, const void* handles, size_t bytes) {
+  AH_REQUIRE(m && handles, "model_ipc_open: null argument");
+  const int W = m->tp_world;
+  AH_REQUIRE(W > 1 && W <= 8 && m->comm_block, "model_ipc_open: not a tensor-parallel model of <= 8 ranks");
+  AH_REQUIRE(bytes >= (size_t)W * sizeof(cudaIpcMemHandle_t), "model_ipc_open: need %d handles", W);
+  AH_REQUIRE(!m->p2p, "model_ipc_open: already open");
+  const auto* hs = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int r = 0; r < W; ++r) {
+    if (r == m->tp_rank) {
+      m->peer_block[r] = m->comm_block;
+      continue;
+    }
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, hs[r], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != m->tp_rank && m->peer_block[q]) cudaIpcCloseMemHandle(m->peer_block[q]);
+      return fail(AH_ECUDA, "model_ipc_open: rank %d's buffer: %s", r, cudaGetErrorString(e));
+    }
+    m->peer_block[r] = p;
+  }
+  m->p2p = true;
+  for (auto& g : m->g_step)  // graphs captured with the NCCL path are stale
+    if (g) {
+      cudaGraphExecDestroy(g);
+      g = nullptr;
+    }
+  return AH_OK;
+}
+
 int ah_model_shard(const AhModel* m, int* rank, int* world, int* n_head, int* n_head_kv, int* n_ff, int* vocab) {
   AH_REQUIRE(m, "model_shard: null model");
   if (rank) *rank = m->tp_rank;
@@ -808,6 +966,9 @@ int ah_model_destroy(AhModel* m) {
   for (auto& v : m->pend)
     for (void* p : v)
       if (p) cudaFree(p);
+  if (m->p2p)
+    for (int r = 0; r < m->tp_world; ++r)
+      if (r != m->tp_rank && m->peer_block[r]) cudaIpcCloseMemHandle(m->peer_block[r]);
   for (void* p : m->allocs) cudaFree(p);
   if (m->d_prompt) cudaFree(m->d_prompt);
   if (m->comm) ncclCommDestroy(m->comm);

@@ -534,12 +534,19 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
           const int64_t R = my_rt * 16 + r;
           float h = 0.0f;
           if (R < a.w.rows) {
-            float* d = a.y + b * a.y_stride + R;
-            h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
-            *d = h;
+            if (EPI == kEpiStore && a.n_peer > 0) {
+              h = fin[i];
+              for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][b * a.y_stride + R] = h;  // NVLink stores
+            } else {
+              float* d = a.y + b * a.y_stride + R;
+              h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
+              *d = h;
+            }
           }
           fin[i] = h;
         }
+        // peer slots: the stores reach the other GPUs before this grid completes
+        if (EPI == kEpiStore && a.n_peer > 0) __threadfence_system();
         if (a.ss_out) {
           // per-tile partial sum of squares of the values written (next RMSNorm)
           __syncthreads();
@@ -646,13 +653,20 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4_rows(const GemvArgs a)
         const int64_t R = rt * 16 + r;
         float h = 0.0f;
         if (R < a.w.rows) {
-          float* d = a.y + b * a.y_stride + R;
-          h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
-          *d = h;
+          if (EPI == kEpiStore && a.n_peer > 0) {
+            h = fin[i];
+            for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][b * a.y_stride + R] = h;  // NVLink stores
+          } else {
+            float* d = a.y + b * a.y_stride + R;
+            h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
+            *d = h;
+          }
         }
         fin[i] = h;
       }
-      if (a.ss_out) {
+      // peer slots: the stores reach the other GPUs before this grid completes
+        if (EPI == kEpiStore && a.n_peer > 0) __threadfence_system();
+        if (a.ss_out) {
         __syncthreads();
         if (tid < B) {
           float q = 0.0f;
@@ -840,6 +854,7 @@ int gemv_launch(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
     s.y = a.y + (int64_t)b0 * a.y_stride;
     if (a.ss_in) s.ss_in = a.ss_in + (int64_t)b0 * a.n_ss_in;
     if (a.ss_out) s.ss_out = a.ss_out + (int64_t)b0 * a.w.r16;
+    for (int p = 0; p < a.n_peer; ++p) s.peer_y[p] = a.peer_y[p] + (int64_t)b0 * a.y_stride;
     AH_TRY_GEMV(gemv_launch_one(s, pro, epi, st, pdl));
   }
   return AH_OK;

@@ -69,6 +69,11 @@ struct GemvArgs {
   float* ss_out;
   int64_t pairs_per_chunk; // block pairs per K-chunk (cluster CTA)
   int early_trigger;       // set by the launcher: grid fits in one resident wave
+  // Store epilogue scatter (tensor-parallel all-reduce over peer memory): with
+  // n_peer > 0 every output element goes to peer_y[p] + b*y_stride + row for
+  // p < n_peer (local and peer GPUs' receive buffers) instead of y.
+  int n_peer;
+  float* peer_y[8];
 };
 
 // ---- small PTX helpers -------------------------------------------------------

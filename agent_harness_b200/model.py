@@ -98,6 +98,16 @@ class Model:
             call("ah_model_create_tp", C.byref(c), tp_rank, tp_world, idb, C.byref(self._h))
         self.vocab_local = cfg.vocab_size // tp_world
 
+    def enable_peer_allreduce(self, allgather):
+        """Switch the block all-reduce from NCCL to stores into the other ranks'
+        memory over NVLink.  `allgather(bytes) -> [bytes per rank]` shares this
+        rank's 64-byte IPC handle (e.g. torch.distributed.all_gather_object)."""
+        h = C.create_string_buffer(64)
+        call("ah_model_ipc_handle", self._h, h, 64)
+        hs = allgather(h.raw)
+        buf = C.create_string_buffer(b"".join(bytes(x) for x in hs), 64 * len(hs))
+        call("ah_model_ipc_open", self._h, buf, 64 * len(hs))
+
     def _stream(self):
         return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
 

@@ -307,7 +307,8 @@ def run_gpu(args):
             dec["tokens_per_s_all_replicas"] = round(world * 1e3 / float(t.item()), 2)
         extra["decode_8b"] = dec
     if not args.quick and not args.no_tp:
-        extra["decode_70b_tp"] = decode_70b_tp(dev, rank, world, args.tp_prompt, args.tp_new)
+        extra["decode_70b_tp"] = decode_70b_tp(dev, rank, world, args.tp_prompt, args.tp_new,
+                                               allreduce=args.tp_allreduce)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = time_cpu_gemv(seconds=args.cpu_seconds)
@@ -361,7 +362,7 @@ TP_PROMPT, TP_NEW, TP_BATCH = 128, 64, 16
 DECODE70_WEIGHT_BYTES = 39094714368
 
 
-def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_BATCH):
+def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_BATCH, allreduce="peer"):
     """70B-shape greedy decode, batch 16, tensor-parallel over the job's ranks
     (80 layers, d 8192, FFN 28672, 64/8 heads x 128, vocab 128256; Q4_0
     N(0,0.02) seed 8; prompts of uniform ids seed 9).  Decode steps are timed
@@ -377,6 +378,14 @@ def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_B
         nid = obj[0]
     m = Model(cfg, device=dev, tp_rank=rank, tp_world=world, nccl_id=nid)
     m.init_random(8, w_std=0.02, emb_std=1.0, norm_std=0.02)
+    if world > 1 and allreduce == "peer":
+        import torch.distributed as dist
+
+        def allgather(blob):
+            out = [None] * world
+            dist.all_gather_object(out, blob)
+            return out
+        m.enable_peer_allreduce(allgather)
     prompt = np.random.default_rng(9).integers(0, cfg.vocab_size, (batch, n_prompt)).astype(np.int32)
     t0 = time.perf_counter()
     m.generate(prompt, 1)  # token-by-token prefill (inference/mod.rs:550) + first token
@@ -397,11 +406,13 @@ def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_B
     per_step = ms / 1e3 / n_new
     return {"tokens_per_s": round(batch * n_new / (ms / 1e3), 1), "ms_per_step": round(per_step * 1e3, 3),
             "batch": batch, "n_prompt": n_prompt, "n_new": n_new, "tp": world,
+            "block_allreduce": (allreduce if world > 1 else "none"),
             "weight_gbs_per_gpu": round(DECODE70_WEIGHT_BYTES / world / per_step / 1e9, 1),
             "prefill_tokens_per_s_token_by_token": round(batch * (n_prompt - 1) / prefill_s, 1),
             "first_tokens_seq0_3": first,
-            "note": "tensor parallel over the job's ranks: row/column-sharded projections, one NCCL all-reduce "
-                    "per attention/MLP block, argmax-candidate all-gather; steps replayed as CUDA graphs"}
+            "note": "tensor parallel over the job's ranks: row/column-sharded projections, one all-reduce per "
+                    "attention/MLP block (peer: GEMV epilogue stores into every rank's slots over NVLink + flag; "
+                    "nccl: ncclAllReduce), argmax-candidate all-gather; steps replayed as CUDA graphs"}
 
 
 def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW):
@@ -553,6 +564,8 @@ def main():
     ap.add_argument("--no-tp", action="store_true", help="skip the 70B tensor-parallel decode measurement")
     ap.add_argument("--tp-prompt", type=int, default=TP_PROMPT)
     ap.add_argument("--tp-new", type=int, default=TP_NEW)
+    ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
+                    help="block all-reduce of the tensor-parallel decoder")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -575,7 +588,8 @@ def main():
                                     timeout=datetime.timedelta(seconds=300))
         from agent_harness_b200 import _lib
         _lib.check(_lib.lib().ah_device_init(local))
-        r = decode_70b_tp(torch.device("cuda", local), rank, world, args.tp_prompt, args.tp_new)
+        r = decode_70b_tp(torch.device("cuda", local), rank, world, args.tp_prompt, args.tp_new,
+                          allreduce=args.tp_allreduce)
         if rank == 0:
             print(json.dumps({"workload": "decode_70b_tp", **r}), flush=True)
         if world > 1:

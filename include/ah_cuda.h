@@ -213,6 +213,15 @@ AH_API int ah_model_create(const AhModelConfig* cfg, AhModel** out);
  * ranks.  ah_model_create(cfg) equals ah_model_create_tp(cfg, 0, 1, ...). */
 AH_API int ah_nccl_unique_id(void* id_out, size_t bytes);
 AH_API int ah_model_create_tp(const AhModelConfig* cfg, int rank, int world, const void* nccl_id, AhModel** out);
+/* Block all-reduce over NVLink peer memory instead of NCCL (no reference
+ * counterpart): the o / down GEMVs store their partials straight into every
+ * rank's receive slots, a flag per rank publishes completion, and each rank
+ * sums the slots in rank order (bounded waits; a missing rank gives
+ * AH_ETIMEOUT from ah_check_device_error).  Every rank passes its 64-byte
+ * ah_model_ipc_handle to all ranks; ah_model_ipc_open takes the world's handles
+ * in rank order.  Ranks must be processes on GPUs with peer access. */
+AH_API int ah_model_ipc_handle(AhModel* m, void* handle_out, size_t bytes);
+AH_API int ah_model_ipc_open(AhModel* m, const void* handles, size_t bytes);
 /* This rank's shard: heads, kv heads, FFN rows and vocab rows it holds. */
 AH_API int ah_model_shard(const AhModel* m, int* rank, int* world, int* n_head, int* n_head_kv, int* n_ff,
                           int* vocab);

@@ -26,7 +26,7 @@ def _free_port():
     return p
 
 
-def _rank(rank, world, port, q):
+def _rank(rank, world, port, q, p2p=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -39,6 +39,12 @@ def _rank(rank, world, port, q):
         dist.broadcast_object_list(ids, src=0)
         m = Model(ModelConfig(**SMALL), device=f"cuda:{rank}", tp_rank=rank, tp_world=world, nccl_id=ids[0])
         m.init_random(123)
+        if p2p:
+            def allgather(blob):
+                out = [None] * world
+                dist.all_gather_object(out, blob)
+                return out
+            m.enable_peer_allreduce(allgather)
         m.reset(2)
         logits = [m.forward(PROMPT[:, t]).cpu().numpy() for t in range(PROMPT.shape[1])]
         gen = m.generate(PROMPT, 8)
@@ -50,14 +56,15 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_tp2_matches_single_gpu(cuda):
+@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "nvlink_peer"])
+def test_tp2_matches_single_gpu(cuda, p2p):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, q, p2p)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
