@@ -373,7 +373,8 @@ __global__ void __launch_bounds__(256) k_residual_add(float* __restrict__ hidden
 
 // ---- tensor-parallel all-reduce over NVLink peer memory ------------------------
 // Each rank's o / down GEMV stores its partial into slot `rank` of every rank's
-// receive buffer (peer stores); k_peer_signal then publishes the collective's
+// receive buffer (peer stores, [d][max_batch] so a tile's 16 rows x batch
+// outputs are one contiguous run); k_peer_signal then publishes the collective's
 // sequence number into every rank's flag slot `rank`, and k_residual_add_peer
 // waits for all ranks' flags before summing the slots in rank order (so every
 // rank computes the identical sum).  Waits are bounded: a rank that never
@@ -431,7 +432,7 @@ __global__ void __launch_bounds__(256) k_residual_add_peer(float* __restrict__ h
   float h = 0.0f;
   if (live) {
     float sum = 0.0f;
-    for (int r = 0; r < world; ++r) sum += slots[((size_t)r * batch + b) * d + i];
+    for (int r = 0; r < world; ++r) sum += slots[((size_t)r * d + i) * batch + b];  // slot r: [d][batch]
     h = hidden[(size_t)b * d + i] + sum;
     hidden[(size_t)b * d + i] = h;
   }
@@ -612,6 +613,7 @@ float* peer_slots(const AhModel* m, int r, int par) {
 }
 void set_peer_scatter(const AhModel* m, GemvArgs& a, int par) {
   a.n_peer = m->tp_world;
+  a.peer_row = m->c.max_batch;  // slots are [d][max_batch]
   for (int r = 0; r < m->tp_world; ++r) a.peer_y[r] = peer_slots(m, r, par);
 }
 int reduce_residual_peer(AhModel* m, int par, cudaStream_t st) {

@@ -536,7 +536,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
           if (R < a.w.rows) {
             if (EPI == kEpiStore && a.n_peer > 0) {
               h = fin[i];
-              for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][b * a.y_stride + R] = h;  // NVLink stores
+              for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][R * a.peer_row + b] = h;  // NVLink stores
             } else {
               float* d = a.y + b * a.y_stride + R;
               h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
@@ -655,7 +655,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4_rows(const GemvArgs a)
         if (R < a.w.rows) {
           if (EPI == kEpiStore && a.n_peer > 0) {
             h = fin[i];
-            for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][b * a.y_stride + R] = h;  // NVLink stores
+            for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][R * a.peer_row + b] = h;  // NVLink stores
           } else {
             float* d = a.y + b * a.y_stride + R;
             h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
@@ -854,7 +854,7 @@ int gemv_launch(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
     s.y = a.y + (int64_t)b0 * a.y_stride;
     if (a.ss_in) s.ss_in = a.ss_in + (int64_t)b0 * a.n_ss_in;
     if (a.ss_out) s.ss_out = a.ss_out + (int64_t)b0 * a.w.r16;
-    for (int p = 0; p < a.n_peer; ++p) s.peer_y[p] = a.peer_y[p] + (int64_t)b0 * a.y_stride;
+    for (int p = 0; p < a.n_peer; ++p) s.peer_y[p] = a.peer_y[p] + b0;
     AH_TRY_GEMV(gemv_launch_one(s, pro, epi, st, pdl));
   }
   return AH_OK;

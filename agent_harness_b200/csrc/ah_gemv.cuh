@@ -70,9 +70,12 @@ struct GemvArgs {
   int64_t pairs_per_chunk; // block pairs per K-chunk (cluster CTA)
   int early_trigger;       // set by the launcher: grid fits in one resident wave
   // Store epilogue scatter (tensor-parallel all-reduce over peer memory): with
-  // n_peer > 0 every output element goes to peer_y[p] + b*y_stride + row for
-  // p < n_peer (local and peer GPUs' receive buffers) instead of y.
+  // n_peer > 0 every output element goes to peer_y[p] + row*peer_row + b for
+  // p < n_peer (local and peer GPUs' receive buffers) instead of y: rows of
+  // `peer_row` floats with the tokens contiguous, so a tile's outputs leave
+  // as one contiguous run per destination.
   int n_peer;
+  int peer_row;
   float* peer_y[8];
 };
 
