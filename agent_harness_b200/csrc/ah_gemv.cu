@@ -273,7 +273,7 @@ __device__ __forceinline__ void mma_pairs(float (&tot)[NT][4], const uint4 (&w)[
           uint4 bf = make_uint4(0u, 0u, 0u, 0u);
           if (col < 2 * B) bf = *reinterpret_cast<const uint4*>(xs + col * plane + kb * 64 + t * 16);
           const int tok = 4 * j + t;  // accumulator columns 2t, 2t+1 = token tok (hi, lo)
-          const float4 bi = tok < B ? blk_info[tok * kbc + kb] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          const float4 bi = tok < B ? blk_info[tok * (kbc + 1) + kb] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
           float acc[4] = {bi.y, bi.z, bi.y, bi.z};  // -8 * sum(x) start value, rows g and g+8
           mma16816(acc, s0a0, s0a1, s0a2, s0a3, bf.x, bf.y, acc);
           mma16816(acc, s1a0, s1a1, s1a2, s1a3, bf.z, bf.w, acc);
@@ -405,7 +405,7 @@ __device__ __forceinline__ void split_x(const GemvArgs& a, uint8_t* xs, float4* 
           pl[4] = l23;
           if (sub == 0) {
             const float c = -8.0f * 5.9604644775390625e-8f;  // -8 * 2^-24
-            blk_info[b * kbc + kb] = make_float4(__uint_as_float((uint32_t)(127 + 24 - sc) << 23), c * shi, c * slo,
+            blk_info[b * (kbc + 1) + kb] = make_float4(__uint_as_float((uint32_t)(127 + 24 - sc) << 23), c * shi, c * slo,
                                                  0.0f);
           }
         }
@@ -433,8 +433,9 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
   const int kbc = 2 * ppc;          // blocks per chunk
   const int plane = kbc * 64 + 64;  // bytes per x plane (64 B pad staggers banks)
   uint8_t* xs = smem;                                                           // [2B][plane]
-  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc]
-  float* part = reinterpret_cast<float*>(blk_info + B * kbc);                   // [warps][16][B]
+  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc+1]: rows padded
+                                                                                // so tokens hit different banks
+  float* part = reinterpret_cast<float*>(blk_info + B * (kbc + 1));             // [warps][16][B]
   float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
   float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
   float* slots = wred + kGemvWarps * BM + 16 * B;  // [2][cluster][16][B] pushed chunk partials
@@ -584,8 +585,9 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4_rows(const GemvArgs a)
   const int kbc = 2 * (int)KP;             // the whole K
   const int plane = kbc * 64 + 64;
   uint8_t* xs = smem;                                                           // [2B][plane]
-  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc]
-  float* part = reinterpret_cast<float*>(blk_info + B * kbc);                   // [warps][16][B]
+  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc+1]: rows padded
+                                                                                // so tokens hit different banks
+  float* part = reinterpret_cast<float*>(blk_info + B * (kbc + 1));             // [warps][16][B]
   float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
   float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
   int64_t rt = blockIdx.x;
@@ -710,7 +712,7 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
   p.ksplit = 1;
   const int64_t kbc = rows_mode ? 2 * w.kp : 2 * p.pairs_per_chunk;
   const int64_t plane = kbc * 64 + 64;
-  p.smem = (size_t)2 * batch * plane + (size_t)batch * kbc * 16 + (size_t)kGemvWarps * 16 * batch * 4 +
+  p.smem = (size_t)2 * batch * plane + (size_t)batch * (kbc + 1) * 16 + (size_t)kGemvWarps * 16 * batch * 4 +
            (size_t)kGemvMaxBatch * 4 + (size_t)kGemvWarps * (4 * p.nt) * 4 + (size_t)16 * batch * 4 + 16;
   if (!rows_mode) p.smem += (size_t)2 * kGemvCluster * 16 * batch * 4;  // DSMEM partial slots
   return p;
