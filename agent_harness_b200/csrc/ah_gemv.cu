@@ -235,24 +235,24 @@ __device__ __forceinline__ float silu_ref(float x) {  // inference/math.rs:83-95
 // scratch, fences or atomics) and runs the epilogue.  The grid holds at most
 // as many clusters as are resident at once (persistent).
 // ---------------------------------------------------------------------------
-template <bool kF32>
-__device__ __forceinline__ void load_pairs(uint4 (&w)[kGemvU], typename ScaleT<kF32>::V (&sv)[kGemvU],
+template <bool kF32, int U>
+__device__ __forceinline__ void load_pairs(uint4 (&w)[U], typename ScaleT<kF32>::V (&sv)[U],
                                            const uint4* nibp, const typename ScaleT<kF32>::V* sclp, int p, int np) {
 #pragma unroll
-  for (int u = 0; u < kGemvU; ++u)
+  for (int u = 0; u < U; ++u)
     if (p + u < np) {
       w[u] = ldg_stream_v4(nibp + (p + u) * 32);
       sv[u] = ScaleT<kF32>::load(sclp + (p + u) * 8);
     }
 }
 
-template <int NT, bool kF32>
-__device__ __forceinline__ void mma_pairs(float (&tot)[NT][4], const uint4 (&w)[kGemvU],
-                                          const typename ScaleT<kF32>::V (&sv)[kGemvU], int p, int np, int B,
+template <int NT, bool kF32, int U>
+__device__ __forceinline__ void mma_pairs(float (&tot)[NT][4], const uint4 (&w)[U],
+                                          const typename ScaleT<kF32>::V (&sv)[U], int p, int np, int B,
                                           int g, int t, const uint8_t* xs, const float4* blk_info, int plane,
                                           int kbc, int kb0) {
 #pragma unroll
-  for (int u = 0; u < kGemvU; ++u) {
+  for (int u = 0; u < U; ++u) {
     if (p + u < np) {
 #pragma unroll
       for (int blk = 0; blk < 2; ++blk) {
@@ -415,9 +415,10 @@ __device__ __forceinline__ void split_x(const GemvArgs& a, uint8_t* xs, float4* 
 }
 
 template <int NT, bool kF32, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, NT >= 3 ? 2 : 1) k_gemv_q4(const GemvArgs a) {
   constexpr int BM = 4 * NT;  // tokens this instantiation can hold
   using SV = typename ScaleT<kF32>::V;
+  constexpr int U = kGemvBatchPairs<NT>;  // block pairs per register batch
   extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -449,11 +450,11 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
   const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + (rt * KP + p0) * 8 + g;
   const int64_t tile_nib = KP * 32 * kGemvWarps * n_cl;  // uint4 stride to the next row group of this CTA
   const int64_t tile_scl = KP * 8 * kGemvWarps * n_cl;
-  uint4 wa[kGemvU], wb[kGemvU];
-  SV sa[kGemvU], sb[kGemvU];
+  uint4 wa[U], wb[U];
+  SV sa[U], sb[U];
   if (warp_live) {
-    load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
-    load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+    load_pairs<kF32, U>(wa, sa, nibp, sclp, 0, np);
+    load_pairs<kF32, U>(wb, sb, nibp, sclp, U, np);
   }
   // A grid resident in one wave lets the next kernel launch now, so its weight
   // prefetch overlaps this kernel; larger grids trigger after the main loop.
@@ -471,11 +472,11 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
 #pragma unroll
     for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
     if (warp_live) {
-      for (int p = 0; p < np; p += 2 * kGemvU) {
-        mma_pairs<NT, kF32>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, 0);
-        if (p + 2 * kGemvU < np) load_pairs<kF32>(wa, sa, nibp, sclp, p + 2 * kGemvU, np);
-        mma_pairs<NT, kF32>(tot, wb, sb, p + kGemvU, np, B, g, t, xs, blk_info, plane, kbc, 0);
-        if (p + 3 * kGemvU < np) load_pairs<kF32>(wb, sb, nibp, sclp, p + 3 * kGemvU, np);
+      for (int p = 0; p < np; p += 2 * U) {
+        mma_pairs<NT, kF32, U>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, 0);
+        if (p + 2 * U < np) load_pairs<kF32, U>(wa, sa, nibp, sclp, p + 2 * U, np);
+        mma_pairs<NT, kF32, U>(tot, wb, sb, p + U, np, B, g, t, xs, blk_info, plane, kbc, 0);
+        if (p + 3 * U < np) load_pairs<kF32, U>(wb, sb, nibp, sclp, p + 3 * U, np);
       }
     }
     // prefetch the next row group's first two batches while this one is reduced
@@ -485,8 +486,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
     nibp += tile_nib;
     sclp += tile_scl;
     if (next_live) {
-      load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
-      load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+      load_pairs<kF32, U>(wa, sa, nibp, sclp, 0, np);
+      load_pairs<kF32, U>(wb, sb, nibp, sclp, U, np);
     }
     if (rg_next >= n_rg && !a.early_trigger) pdl_launch_dependents();
 
@@ -573,9 +574,10 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4(const GemvArgs a) {
 // costs one CTA barrier instead of a cluster exchange.  The next tile's weights
 // are in flight while the current one is reduced.
 template <int NT, bool kF32, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) k_gemv_q4_rows(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, NT >= 3 ? 2 : 1) k_gemv_q4_rows(const GemvArgs a) {
   constexpr int BM = 4 * NT;
   using SV = typename ScaleT<kF32>::V;
+  constexpr int U = kGemvBatchPairs<NT>;  // block pairs per register batch
   extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -596,11 +598,11 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4_rows(const GemvArgs a)
   const uint4* nibp = a.w.nib + (rt * KP + p0) * 32 + lane;
   const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + (rt * KP + p0) * 8 + g;
   const int64_t tile_nib = KP * 32 * gridDim.x, tile_scl = KP * 8 * gridDim.x;
-  uint4 wa[kGemvU], wb[kGemvU];
-  SV sa[kGemvU], sb[kGemvU];
+  uint4 wa[U], wb[U];
+  SV sa[U], sb[U];
   if (rt < r16) {
-    load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
-    load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+    load_pairs<kF32, U>(wa, sa, nibp, sclp, 0, np);
+    load_pairs<kF32, U>(wb, sb, nibp, sclp, U, np);
   }
   if (a.early_trigger) pdl_launch_dependents();
   pdl_wait();
@@ -612,18 +614,18 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv_q4_rows(const GemvArgs a)
     float tot[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
-    for (int p = 0; p < np; p += 2 * kGemvU) {
-      mma_pairs<NT, kF32>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
-      if (p + 2 * kGemvU < np) load_pairs<kF32>(wa, sa, nibp, sclp, p + 2 * kGemvU, np);
-      mma_pairs<NT, kF32>(tot, wb, sb, p + kGemvU, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
-      if (p + 3 * kGemvU < np) load_pairs<kF32>(wb, sb, nibp, sclp, p + 3 * kGemvU, np);
+    for (int p = 0; p < np; p += 2 * U) {
+      mma_pairs<NT, kF32, U>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
+      if (p + 2 * U < np) load_pairs<kF32, U>(wa, sa, nibp, sclp, p + 2 * U, np);
+      mma_pairs<NT, kF32, U>(tot, wb, sb, p + U, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
+      if (p + 3 * U < np) load_pairs<kF32, U>(wb, sb, nibp, sclp, p + 3 * U, np);
     }
     const bool has_next = rt + gridDim.x < r16;
     nibp += tile_nib;
     sclp += tile_scl;
     if (has_next) {
-      load_pairs<kF32>(wa, sa, nibp, sclp, 0, np);
-      load_pairs<kF32>(wb, sb, nibp, sclp, kGemvU, np);
+      load_pairs<kF32, U>(wa, sa, nibp, sclp, 0, np);
+      load_pairs<kF32, U>(wb, sb, nibp, sclp, U, np);
     } else if (!a.early_trigger) {
       pdl_launch_dependents();
     }

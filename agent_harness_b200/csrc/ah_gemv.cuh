@@ -35,6 +35,10 @@ constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kGemvMaxBatch = 16;
 constexpr int kGemvCluster = kGemvWarps;  // CTAs per cluster = K-chunks = warps per CTA
 constexpr int kGemvU = 4;                 // block pairs per register batch (two batches in flight)
+// Wide batches (3-4 n8 tiles) keep 2 pairs per batch and cap registers so two
+// CTAs fit per SM.
+template <int NT>
+constexpr int kGemvBatchPairs = NT >= 3 ? 2 : kGemvU;
 constexpr int kGemvSmemLimit = 200 * 1024;
 constexpr int kGemvRowsSmem = 96 * 1024;   // rows mode only while two CTAs fit per SM
 
