@@ -362,7 +362,7 @@ TP_PROMPT, TP_NEW, TP_BATCH = 128, 64, 16
 DECODE70_WEIGHT_BYTES = 39094714368
 
 
-def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_BATCH, allreduce="nccl"):
+def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_BATCH, allreduce="peer"):
     """70B-shape greedy decode, batch 16, tensor-parallel over the job's ranks
     (80 layers, d 8192, FFN 28672, 64/8 heads x 128, vocab 128256; Q4_0
     N(0,0.02) seed 8; prompts of uniform ids seed 9).  Decode steps are timed
@@ -564,7 +564,7 @@ def main():
     ap.add_argument("--no-tp", action="store_true", help="skip the 70B tensor-parallel decode measurement")
     ap.add_argument("--tp-prompt", type=int, default=TP_PROMPT)
     ap.add_argument("--tp-new", type=int, default=TP_NEW)
-    ap.add_argument("--tp-allreduce", default="nccl", choices=["nccl", "peer"],
+    ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
                     help="block all-reduce of the tensor-parallel decoder")
     args = ap.parse_args()
     if args.impl == "reference":
