@@ -415,7 +415,7 @@ __device__ __forceinline__ void split_x(const GemvArgs& a, uint8_t* xs, float4* 
 }
 
 template <int NT, bool kF32, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, NT >= 3 ? 2 : 1) k_gemv_q4(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4(const GemvArgs a) {
   constexpr int BM = 4 * NT;  // tokens this instantiation can hold
   using SV = typename ScaleT<kF32>::V;
   constexpr int U = kGemvBatchPairs<NT>;  // block pairs per register batch
@@ -574,7 +574,7 @@ __global__ void __launch_bounds__(kGemvThreads, NT >= 3 ? 2 : 1) k_gemv_q4(const
 // costs one CTA barrier instead of a cluster exchange.  The next tile's weights
 // are in flight while the current one is reduced.
 template <int NT, bool kF32, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, NT >= 3 ? 2 : 1) k_gemv_q4_rows(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4_rows(const GemvArgs a) {
   constexpr int BM = 4 * NT;
   using SV = typename ScaleT<kF32>::V;
   constexpr int U = kGemvBatchPairs<NT>;  // block pairs per register batch
