@@ -32,6 +32,7 @@
 #include <nccl.h>
 
 #include "ah_gemv_impl.cuh"
+#include "ah_tma.cuh"
 
 using namespace ah;
 
@@ -54,6 +55,7 @@ struct AttnArgs {
   float* out;             // [B][dq]
   int* err;               // device error word (bounded waits)
   int layer, n_layer, n_head, n_kv, hd, max_seq;
+  int batch;              // sequences in this step
   float scale;
 };
 
@@ -269,6 +271,361 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
     o[3] = acc.w * inv;
   }
   if (tid == 0) a.cnt[bh] = 0;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core decode attention for head_dim 64 / 128 and GQA groups <= 8.
+//
+// Work items (sequence b, kv head h, context split s) are spread over a
+// persistent grid sized to the resident CTAs, so no wave of idle CTAs is
+// launched for short contexts or large batches.  Per item:
+//   * K and V rows [p0, p1) arrive by TMA in 32-row boxes of 128-byte column
+//     halves with the 128-byte swizzle, so the fragment loads below are free of
+//     bank conflicts; this step's k / v (after RoPE, f16-rounded) replace row
+//     `pos` in shared memory and split 0 appends them to the cache.
+//   * S = Q K^T on mma.sync m16n8k16: the G query heads are the M rows, q is
+//     scaled by a power of two and split into f16 hi + lo parts (two MMAs), so
+//     the scores carry f32 accuracy against the f16 keys.
+//   * softmax pieces per warp, then O^T = V^T P^T: V^T comes from transposed
+//     fragment loads and P^T is the S accumulator itself (its C layout is the
+//     B operand layout), again split hi + lo.
+//   * the four warps' (max, sum, O) merge in shared memory; one split writes
+//     the output, several write partials and the last to finish combines them.
+// Same arithmetic as k_attention (inference/mod.rs:469-502, per-head RoPE as in
+// attention.rs:126-139), up to f32 rounding order.
+// ---------------------------------------------------------------------------
+constexpr int kAttnBoxRows = 32;  // rows per TMA box of the cache views
+
+template <int HD>
+struct AttnTcSmem {
+  static constexpr int kHalves = HD / 64;                 // 128-byte column halves per row
+  static constexpr int kHalfBytes = kAttnMaxChunk * 128;  // one column half of the K or V tile
+  static constexpr int kQStride = HD + 8;                 // halves per staged q row (conflict-free)
+  static constexpr int kK = 0;
+  static constexpr int kV = kK + kHalves * kHalfBytes;
+  static constexpr int kQ = kV + kHalves * kHalfBytes;    // q hi, q lo: [2][8][kQStride] f16
+  static constexpr int kRed = kQ + 2 * 8 * kQStride * 2;  // [4 warps][HD][8] f32 partial O^T
+  static constexpr int kMl = kRed + 4 * HD * 8 * 4;       // [4 warps][8][2] (max, sum)
+  static constexpr int kNew = kMl + 4 * 8 * 2 * 4;        // k, v of this step: [2][HD] f32
+  static constexpr int kWmax = kNew + 2 * HD * 4;         // [4] per-warp max |q|
+  static constexpr int kBytes = kWmax + 16;
+  static constexpr int kAlloc = kBytes + 1024;            // the tiles need a 1024-byte aligned base
+};
+
+struct AttnTcParams {
+  CUtensorMap tm_k;  // K cache as [B*L*nkv*max_seq][HD] f16, box 64 x 32, 128-byte swizzle
+  CUtensorMap tm_v;  // V cache, same view
+  AttnArgs a;
+};
+
+// Byte offset of 16-byte chunk `c` of row `r` inside a 128-byte-swizzled half.
+__device__ __forceinline__ uint32_t swz128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ uint32_t pack_h2(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+// x = hi + lo with hi, lo f16 (lo holds the rounding error of hi).
+__device__ __forceinline__ void split_h2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  hi = pack_h2(h0, h1);
+  lo = pack_h2(__float2half_rn(x0 - __half2float(h0)), __float2half_rn(x1 - __half2float(h1)));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) k_attention_tc(const __grid_constant__ AttnTcParams p) {
+  using S = AttnTcSmem<HD>;
+  constexpr int KS = HD / 16;                            // 16-wide k-steps over the head dims
+  constexpr int kQPer = 8 * (HD / 2) / kAttnThreads;     // rotated q pairs per thread (8 head slots)
+  const AttnArgs& a = p.a;
+  extern __shared__ uint8_t smraw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Ks = sm + S::kK;
+  uint8_t* Vs = sm + S::kV;
+  __half* Qh = reinterpret_cast<__half*>(sm + S::kQ);
+  __half* Ql = Qh + 8 * S::kQStride;
+  float* red = reinterpret_cast<float*>(sm + S::kRed);
+  float* mls = reinterpret_cast<float*>(sm + S::kMl);
+  float* knew = reinterpret_cast<float*>(sm + S::kNew);
+  float* vnew = knew + HD;
+  float* wmax = reinterpret_cast<float*>(sm + S::kWmax);
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+  const int G = a.n_head / a.n_kv, half = HD / 2;
+  const int dq = a.n_head * HD, dkv = a.n_kv * HD;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int pos = *a.pos;
+  const int n_ctx = pos + 1;
+  const int n_split = min(kAttnSplits, (n_ctx + 63) / 64);
+  const int chunk = (n_ctx + n_split - 1) / n_split;  // <= kAttnMaxChunk (max_seq is checked at creation)
+  const int kw = (chunk + 63) >> 6;                   // 16-position k-steps per warp (1 or 2)
+  const int n_items = a.batch * a.n_kv * n_split;
+  if ((int)blockIdx.x >= n_items) return;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const float2* cs = a.rope + (size_t)pos * half;
+  uint32_t phase = 0;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x, phase ^= 1u) {
+    const int s = item % n_split, bh = item / n_split;
+    const int h = bh % a.n_kv, b = bh / a.n_kv;
+    const int p0 = min(s * chunk, n_ctx), p1 = min(p0 + chunk, n_ctx), n = p1 - p0;
+    const int nbox = (n + kAttnBoxRows - 1) / kAttnBoxRows;
+    const size_t head_row = (((size_t)b * a.n_layer + a.layer) * a.n_kv + h) * a.max_seq;
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&bar, (uint32_t)(nbox * 2 * S::kHalves * kAttnBoxRows * 128));
+      for (int j = 0; j < nbox; ++j)
+#pragma unroll
+        for (int hf = 0; hf < S::kHalves; ++hf) {
+          const int y = (int)(head_row + p0 + j * kAttnBoxRows);
+          tma_load_2d(Ks + hf * S::kHalfBytes + j * kAttnBoxRows * 128, &p.tm_k, hf * 64, y, &bar);
+          tma_load_2d(Vs + hf * S::kHalfBytes + j * kAttnBoxRows * 128, &p.tm_v, hf * 64, y, &bar);
+        }
+    }
+    // RoPE on adjacent pairs (2i, 2i+1), theta_i = pos * base^(-i/half) (math.rs:119-151)
+    const float* row = a.qkv + (size_t)b * (dq + 2 * dkv);
+    float2 qr[kQPer];
+    float mx = 0.0f;
+#pragma unroll
+    for (int u = 0; u < kQPer; ++u) {
+      const int i = tid + u * kAttnThreads;  // pair index over [8 head slots][half]
+      const int gg = i / half, k = i - gg * half;
+      float2 v = make_float2(0.0f, 0.0f);
+      if (gg < G) {
+        const float2 x = *reinterpret_cast<const float2*>(row + (h * G + gg) * HD + 2 * k);
+        const float2 c = cs[k];
+        v = make_float2(x.x * c.x - x.y * c.y, x.x * c.y + x.y * c.x);
+      }
+      qr[u] = v;
+      mx = fmaxf(mx, fmaxf(fabsf(v.x), fabsf(v.y)));
+    }
+    for (int k = tid; k < half; k += kAttnThreads) {
+      const float2 x = *reinterpret_cast<const float2*>(row + dq + h * HD + 2 * k);
+      const float2 c = cs[k];
+      // the cache holds f16 (the decode configs' f16 KV); use the rounded values
+      knew[2 * k] = __half2float(__float2half_rn(x.x * c.x - x.y * c.y));
+      knew[2 * k + 1] = __half2float(__float2half_rn(x.x * c.y + x.y * c.x));
+    }
+    for (int d = tid; d < HD; d += kAttnThreads) vnew[d] = __half2float(__float2half_rn(row[dq + dkv + h * HD + d]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+    if (lane == 0) wmax[warp] = mx;
+    __syncthreads();  // wmax, knew, vnew ready
+    // q * 2^e with max |q| * 2^e in [2^14, 2^15): f16 hi / lo parts keep f32 accuracy
+    const float qm = fmaxf(fmaxf(wmax[0], wmax[1]), fmaxf(wmax[2], wmax[3]));
+    int ex = 0;
+    if (qm > 0.0f) frexpf(qm, &ex);
+    const int sh = qm > 0.0f ? min(15 - ex, 100) : 0;
+    const float qs = ldexpf(1.0f, sh);
+#pragma unroll
+    for (int u = 0; u < kQPer; ++u) {
+      const int i = tid + u * kAttnThreads;
+      const int gg = i / half, k = i - gg * half;
+      uint32_t hi, lo;
+      split_h2(qr[u].x * qs, qr[u].y * qs, hi, lo);
+      *reinterpret_cast<uint32_t*>(Qh + gg * S::kQStride + 2 * k) = hi;
+      *reinterpret_cast<uint32_t*>(Ql + gg * S::kQStride + 2 * k) = lo;
+    }
+    if (s == 0) {
+      uint16_t* kh = a.kc + (head_row + pos) * HD;
+      uint16_t* vh = a.vc + (head_row + pos) * HD;
+      for (int d = tid; d < HD; d += kAttnThreads) {
+        kh[d] = __half_as_ushort(__float2half_rn(knew[d]));
+        vh[d] = __half_as_ushort(__float2half_rn(vnew[d]));
+      }
+    }
+    const bool ok = mbar_wait_bounded(&bar, phase, a.err, 0x403);
+    if (__syncthreads_or(!ok)) {
+      if (tid == 0) mbar_wait_bounded(&bar, phase, a.err, 0x404);  // let copies in flight land
+      return;
+    }
+    // this step's row replaces the cache row at pos; V rows past n up to the end
+    // of the last working warp's range (read with zero weight) are cleared so
+    // stale values cannot leak
+    if (pos >= p0 && pos < p1) {
+      const int r = pos - p0;
+      for (int d = tid; d < HD; d += kAttnThreads) {
+        const uint32_t off = (d >> 6) * S::kHalfBytes + swz128(r, (d & 63) >> 3) + (d & 7) * 2;
+        *reinterpret_cast<uint16_t*>(Ks + off) = __half_as_ushort(__float2half_rn(knew[d]));
+        *reinterpret_cast<uint16_t*>(Vs + off) = __half_as_ushort(__float2half_rn(vnew[d]));
+      }
+    }
+    const int nz = (n + 16 * kw - 1) / (16 * kw) * (16 * kw);  // <= 32 * nbox: inside the loaded boxes
+    for (int i = tid; i < (nz - n) * (HD / 8); i += kAttnThreads) {
+      const int r = n + i / (HD / 8), cc = i % (HD / 8);
+      *reinterpret_cast<uint4*>(Vs + (cc >> 3) * S::kHalfBytes + swz128(r, cc & 7)) = make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();  // q parts and K / V tiles final
+
+    // ---- this warp's positions [wp0, wp0 + 16 kw) of the tile ----
+    const int wp0 = warp * 16 * kw;
+    float oacc[KS][4];
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.0f;
+    float mrow = -INFINITY, lrow = 0.0f;  // softmax pieces of head g over this warp's positions
+    if (wp0 < n) {
+      uint32_t qh[KS][2], ql[KS][2];  // A fragments, rows 0-7 = heads (rows 8-15 are zero)
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        qh[kk][0] = *reinterpret_cast<const uint32_t*>(Qh + g * S::kQStride + kk * 16 + 2 * t);
+        qh[kk][1] = *reinterpret_cast<const uint32_t*>(Qh + g * S::kQStride + kk * 16 + 8 + 2 * t);
+        ql[kk][0] = *reinterpret_cast<const uint32_t*>(Ql + g * S::kQStride + kk * 16 + 2 * t);
+        ql[kk][1] = *reinterpret_cast<const uint32_t*>(Ql + g * S::kQStride + kk * 16 + 8 + 2 * t);
+      }
+      float sacc[4][4];
+      const uint32_t kbase = smem_u32(Ks);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
+        if (j < 2 * kw) {
+          const int prow = wp0 + 8 * j + (lane & 7);  // the position whose row this lane addresses
+#pragma unroll
+          for (int k2 = 0; k2 < HD / 32; ++k2) {
+            const int d0 = k2 * 32 + (lane >> 3) * 8;  // matrix lane/8: dims d0..d0+7
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(kbase + (d0 >> 6) * S::kHalfBytes + swz128(prow, (d0 & 63) >> 3), b0, b1, b2, b3);
+            mma16816(sacc[j], qh[2 * k2][0], 0u, qh[2 * k2][1], 0u, b0, b1, sacc[j]);
+            mma16816(sacc[j], ql[2 * k2][0], 0u, ql[2 * k2][1], 0u, b0, b1, sacc[j]);
+            mma16816(sacc[j], qh[2 * k2 + 1][0], 0u, qh[2 * k2 + 1][1], 0u, b2, b3, sacc[j]);
+            mma16816(sacc[j], ql[2 * k2 + 1][0], 0u, ql[2 * k2 + 1][1], 0u, b2, b3, sacc[j]);
+          }
+        }
+      }
+      // scores of head g at positions wp0 + 8j + 2t + e; -inf past n
+      const float mult = a.scale / qs;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const bool live = j < 2 * kw && wp0 + 8 * j + 2 * t + e < n;
+          sacc[j][e] = live ? sacc[j][e] * mult : -INFINITY;
+          mrow = fmaxf(mrow, sacc[j][e]);
+        }
+      mrow = fmaxf(mrow, __shfl_xor_sync(0xFFFFFFFFu, mrow, 1));
+      mrow = fmaxf(mrow, __shfl_xor_sync(0xFFFFFFFFu, mrow, 2));
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float w = sacc[j][e] == -INFINITY ? 0.0f : expf(sacc[j][e] - mrow);
+          sacc[j][e] = w;
+          lrow += w;
+        }
+      lrow += __shfl_xor_sync(0xFFFFFFFFu, lrow, 1);
+      lrow += __shfl_xor_sync(0xFFFFFFFFu, lrow, 2);
+      // O^T[dim][head] += V^T[dim][pos] . P^T[pos][head], 16 positions per k-step
+      const uint32_t vbase = smem_u32(Vs);
+      const int mi = lane >> 3;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        if (q < kw) {
+          uint32_t ph0, pl0, ph1, pl1;
+          split_h2(sacc[2 * q][0], sacc[2 * q][1], ph0, pl0);
+          split_h2(sacc[2 * q + 1][0], sacc[2 * q + 1][1], ph1, pl1);
+          const int prow = wp0 + 16 * q + ((mi >> 1) << 3) + (lane & 7);
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            const int d0 = mt * 16 + ((mi & 1) << 3);
+            uint32_t a0, a1, a2, a3;
+            ldsm_x4_trans(vbase + (d0 >> 6) * S::kHalfBytes + swz128(prow, (d0 & 63) >> 3), a0, a1, a2, a3);
+            mma16816(oacc[mt], a0, a1, a2, a3, ph0, ph1, oacc[mt]);
+            mma16816(oacc[mt], a0, a1, a2, a3, pl0, pl1, oacc[mt]);
+          }
+        }
+      }
+    }
+    // per-warp pieces: O^T[dim][head slot] and (max, sum) per head
+    float* rw = red + warp * HD * 8;
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      *reinterpret_cast<float2*>(rw + (mt * 16 + g) * 8 + 2 * t) = make_float2(oacc[mt][0], oacc[mt][1]);
+      *reinterpret_cast<float2*>(rw + (mt * 16 + g + 8) * 8 + 2 * t) = make_float2(oacc[mt][2], oacc[mt][3]);
+    }
+    if (t == 0) {
+      mls[(warp * 8 + g) * 2] = mrow;
+      mls[(warp * 8 + g) * 2 + 1] = lrow;
+    }
+    __syncthreads();
+    float* pacc = a.part + (((size_t)bh * kAttnSplits + s) * G) * HD;  // [G][hd]
+    float* pml = a.part + (size_t)a.batch * a.n_kv * kAttnSplits * G * HD + ((size_t)bh * kAttnSplits + s) * G * 2;
+    for (int i = tid; i < 8 * HD; i += kAttnThreads) {
+      const int gg = i & 7, d = i >> 3;
+      if (gg < G) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, mls[(w * 8 + gg) * 2]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const float mw = mls[(w * 8 + gg) * 2];
+          const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+          L = fmaf(f, mls[(w * 8 + gg) * 2 + 1], L);
+          O = fmaf(f, red[w * HD * 8 + i], O);
+        }
+        if (n_split == 1) {
+          a.out[(size_t)b * dq + (size_t)(h * G + gg) * HD + d] = O / L;  // mod.rs:492-500
+        } else {
+          pacc[gg * HD + d] = O;
+          if (d == 0) {
+            pml[gg * 2] = M;
+            pml[gg * 2 + 1] = L;
+          }
+        }
+      }
+    }
+    if (n_split > 1) {
+      // the last split of (b, h) to finish combines (deterministic split order)
+      __syncthreads();
+      if (tid == 0) {
+        __threadfence();
+        last = atomicAdd(&a.cnt[bh], 1) == n_split - 1;
+        if (last) __threadfence();
+      }
+      __syncthreads();
+      if (last) {
+        const float* acc_base = a.part + ((size_t)bh * kAttnSplits * G) * HD;
+        const float* ml_base = a.part + (size_t)a.batch * a.n_kv * kAttnSplits * G * HD + (size_t)bh * kAttnSplits * G * 2;
+        float* fm = red;                 // [G][kAttnSplits] split weights exp(m_s - M)
+        float* inv = red + 8 * kAttnSplits;  // [G] 1 / L
+        if (tid < G) {
+          float M = -INFINITY;
+          for (int u = 0; u < n_split; ++u) M = fmaxf(M, __ldcg(ml_base + (u * G + tid) * 2));
+          float L = 0.0f;
+          for (int u = 0; u < n_split; ++u) {
+            const float mt = __ldcg(ml_base + (u * G + tid) * 2);
+            const float f = (mt == -INFINITY) ? 0.0f : expf(mt - M);
+            fm[tid * kAttnSplits + u] = f;
+            L = fmaf(__ldcg(ml_base + (u * G + tid) * 2 + 1), f, L);
+          }
+          inv[tid] = 1.0f / L;
+        }
+        __syncthreads();
+        for (int i4 = tid; i4 < G * HD / 4; i4 += kAttnThreads) {  // four consecutive head dims per thread
+          const int gg = (i4 * 4) / HD;
+          float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll 8
+          for (int u = 0; u < n_split; ++u) {
+            const float f = fm[gg * kAttnSplits + u];
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(acc_base + (size_t)u * G * HD) + i4);
+            acc.x = fmaf(v.x, f, acc.x);
+            acc.y = fmaf(v.y, f, acc.y);
+            acc.z = fmaf(v.z, f, acc.z);
+            acc.w = fmaf(v.w, f, acc.w);
+          }
+          const float iv = inv[gg];
+          *reinterpret_cast<float4*>(a.out + (size_t)b * dq + (size_t)h * G * HD + i4 * 4) =
+              make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv);
+        }
+        if (tid == 0) a.cnt[bh] = 0;
+      }
+    }
+    // generic-proxy writes to the tiles are ordered before the next item's TMA
+    fence_proxy_async_smem();
+    __syncthreads();
+  }
 }
 
 // hidden = f16 -> f32 (token_embd[token]) (mod.rs:392-397); ss partials per 16.
@@ -522,6 +879,9 @@ struct AhModel {
   std::vector<void*> pend[5];  // q, k, v, gate, up Q4_0 blocks awaiting fusion
   uint16_t *tok_embd = nullptr, *attn_norm = nullptr, *ffn_norm = nullptr, *out_norm = nullptr;
   uint16_t *kc = nullptr, *vc = nullptr;
+  CUtensorMap tm_k{}, tm_v{};  // TMA views of kc / vc for the tensor-core attention
+  bool attn_tc = false;        // head_dim 64 or 128: k_attention_tc
+  int attn_grid = 0;           // its persistent grid (resident CTAs)
   float2* rope = nullptr;
   float *hidden = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr, *ss = nullptr;
   float* att_part = nullptr;
@@ -632,6 +992,22 @@ int reduce_residual_peer(AhModel* m, int par, cudaStream_t st) {
   return AH_OK;
 }
 
+// Decode attention of one layer: the tensor-core kernel for head_dim 64 / 128,
+// the scalar one otherwise.
+int launch_attention(AhModel* m, const AttnArgs& at, size_t attn_smem, cudaStream_t st) {
+  if (!m->attn_tc)
+    return launch_pdl(k_attention, dim3(m->nkv, kAttnSplits, at.batch), dim3(kAttnThreads), attn_smem, st, at);
+  AttnTcParams p;
+  p.tm_k = m->tm_k;
+  p.tm_v = m->tm_v;
+  p.a = at;
+  if (m->c.head_dim == 128)
+    return launch_pdl(k_attention_tc<128>, dim3(m->attn_grid), dim3(kAttnThreads), (size_t)AttnTcSmem<128>::kAlloc,
+                      st, p);
+  return launch_pdl(k_attention_tc<64>, dim3(m->attn_grid), dim3(kAttnThreads), (size_t)AttnTcSmem<64>::kAlloc, st,
+                    p);
+}
+
 // Enqueues one decoder step (all layers; with_head adds LM head + argmax).
 int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cudaStream_t st) {
   const AhModelConfig& c = m->c;
@@ -664,7 +1040,8 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     at.max_seq = c.max_seq;
     at.scale = 1.0f / sqrtf((float)c.head_dim);  // mod.rs:478
     at.err = m->err;
-    AH_TRY(launch_pdl(k_attention, dim3(m->nkv, kAttnSplits, B), dim3(kAttnThreads), attn_smem, st, at));
+    at.batch = B;
+    AH_TRY(launch_attention(m, at, attn_smem, st));
     if (tp && m->p2p) {
       GemvArgs o = gemv_args(m->wo[l], m->attn, m->dq, m->part, d, B);
       set_peer_scatter(m, o, 0);
@@ -732,6 +1109,17 @@ int prepare_step(AhModel* m) {
   AH_TRY(gemv_prepare(q4w_tiled(m->wd[0]), B, kProPlain, ro));
   const size_t attn_smem = attn_smem_bytes(m->nh / m->nkv, c.head_dim);
   AH_CUDA_TRY(cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem));
+  if (m->attn_tc) {
+    // persistent grid: every resident CTA, capped at the largest item count
+    const bool w128 = c.head_dim == 128;
+    const void* kern = w128 ? (const void*)k_attention_tc<128> : (const void*)k_attention_tc<64>;
+    const int smem = w128 ? AttnTcSmem<128>::kAlloc : AttnTcSmem<64>::kAlloc;
+    AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    int per_sm = 0;
+    AH_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kAttnThreads, smem));
+    AH_REQUIRE(per_sm >= 1, "model: the attention kernel does not fit on an SM");
+    m->attn_grid = std::min(per_sm * sm_count(), B * m->nkv * kAttnSplits);
+  }
   return AH_OK;
 }
 
@@ -862,6 +1250,19 @@ int model_create(const AhModelConfig* cfg, int rank, int world, ncclComm_t comm,
   cudaMemset(m->vc, 0, kv);
   cudaMemset(m->d_pos, 0, 16);
   cudaMemset(m->d_tok, 0, (size_t)B * 4);
+  if (c.head_dim == 64 || c.head_dim == 128) {
+    const uint64_t kv_rows = (uint64_t)B * L * nkv * c.max_seq;
+    rc = encode_2d(&m->tm_k, m->kc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)c.head_dim, kv_rows, 64,
+                   kAttnBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc == AH_OK)
+      rc = encode_2d(&m->tm_v, m->vc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)c.head_dim, kv_rows, 64,
+                     kAttnBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != AH_OK) {
+      ah_model_destroy(m);
+      return rc;
+    }
+    m->attn_tc = true;
+  }
   const int n = c.max_seq * (c.head_dim / 2);
   k_rope_table<<<(n + 255) / 256, 256>>>(m->rope, c.max_seq, c.head_dim / 2, c.rope_freq_base);
   cudaError_t e = cudaGetLastError();

@@ -35,15 +35,13 @@
 // token and projection; this kernel computes the same products for all
 // tokens of a prompt at once.
 
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <mutex>
 
 #include "ah_common.cuh"
 #include "ah_gemv_impl.cuh"
 #include "ah_sm100.cuh"
+#include "ah_tma.cuh"
 
 struct AhQ4Weight;
 
@@ -558,7 +556,6 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 }  // namespace
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -572,12 +569,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// A row-major [rows][inner] matrix of `elem`-byte elements read in boxes of
-// box_inner x box_rows.
 int encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint32_t elem, uint64_t inner,
               uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
   auto fn = tensor_map_encoder();
-  if (!fn) return fail(AH_ECUDA, "gemm: cuTensorMapEncodeTiled is unavailable");
+  if (!fn) return fail(AH_ECUDA, "tensor map: cuTensorMapEncodeTiled is unavailable");
   const cuuint64_t dims[2] = {inner, rows};
   const cuuint64_t strides[1] = {inner * elem};
   const cuuint32_t box[2] = {box_inner, box_rows};
@@ -585,7 +580,7 @@ int encode_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uin
   const CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(AH_ECUDA, "gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  if (r != CUDA_SUCCESS) return fail(AH_ECUDA, "tensor map: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return AH_OK;
 }
 

@@ -120,4 +120,20 @@ __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.w
 // Streaming (evict-first) 16-byte global store for write-once outputs.
 __device__ __forceinline__ void st_cs_f4(float4* p, float4 v) { __stcs(p, v); }
 
+// ---- shared-memory fragment loads for mma.sync ------------------------------
+// Four 8x8 b16 matrices; lanes 8i..8i+7 give the row addresses of matrix i and
+// register i receives its fragment (thread 4g+t: row g, elements 2t, 2t+1).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// Transposed: thread 4g+t receives rows 2t, 2t+1 of column g.
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
 }  // namespace ah

@@ -509,6 +509,8 @@ typedef struct {
     const uint8_t* lm_head;          /* [vocab][n_embd] */
     uint16_t* k_cache;               /* [n_layer][n_kv][max_seq][hd] f16 */
     uint16_t* v_cache;
+    float* k_cache_f32;              /* the same rows as f32 (or_f16_to_f32 of the stored bits), */
+    float* v_cache_f32;              /* converted once at append instead of at every read */
 } or_model;
 
 static void f16_row(const uint16_t* src, float* dst, int64_t n) { for (int64_t i = 0; i < n; ++i) dst[i] = or_f16_to_f32(src[i]); }
@@ -542,10 +544,15 @@ OR_API int or_model_forward(const or_model* m, int32_t token, int64_t pos, float
         for (int64_t h = 0; h < nkv; ++h) or_rope_multi(k + h * hd, hd, pos, sections, m->rope_base);
         uint16_t* kc = m->k_cache + il * nkv * m->max_seq * hd;
         uint16_t* vc = m->v_cache + il * nkv * m->max_seq * hd;
+        float* kf = m->k_cache_f32 + il * nkv * m->max_seq * hd;
+        float* vf = m->v_cache_f32 + il * nkv * m->max_seq * hd;
         for (int64_t h = 0; h < nkv; ++h)
             for (int64_t e = 0; e < hd; ++e) {
-                kc[(h * m->max_seq + pos) * hd + e] = or_f32_to_f16(k[h * hd + e]);
-                vc[(h * m->max_seq + pos) * hd + e] = or_f32_to_f16(v[h * hd + e]);
+                const int64_t at = (h * m->max_seq + pos) * hd + e;
+                kc[at] = or_f32_to_f16(k[h * hd + e]);
+                vc[at] = or_f32_to_f16(v[h * hd + e]);
+                kf[at] = or_f16_to_f32(kc[at]);
+                vf[at] = or_f16_to_f32(vc[at]);
             }
         float scale = 1.0f / sqrtf((float)hd);
         for (int64_t h = 0; h < nh; ++h) {
@@ -553,20 +560,25 @@ OR_API int or_model_forward(const or_model* m, int32_t token, int64_t pos, float
             const float* qh = q + h * hd;
             float max_s = -INFINITY;
             for (int64_t p = 0; p <= pos; ++p) {
-                const uint16_t* kr = kc + (kvh * m->max_seq + p) * hd;
+                const float* kr = kf + (kvh * m->max_seq + p) * hd;
                 float dot = 0.0f;
-                for (int64_t e = 0; e < hd; ++e) dot += qh[e] * or_f16_to_f32(kr[e]);
+                for (int64_t e = 0; e < hd; ++e) dot += qh[e] * kr[e];
                 scores[p] = dot * scale;
                 if (scores[p] > max_s) max_s = scores[p];
             }
             float sum_exp = 0.0f;
             for (int64_t p = 0; p <= pos; ++p) { scores[p] = expf(scores[p] - max_s); sum_exp += scores[p]; }
             float inv = 1.0f / sum_exp;
-            for (int64_t e = 0; e < hd; ++e) {
-                float acc = 0.0f;
-                for (int64_t p = 0; p <= pos; ++p) acc += scores[p] * or_f16_to_f32(vc[(kvh * m->max_seq + p) * hd + e]);
-                att[h * hd + e] = acc * inv;
+            /* acc[e] sums scores[p] * v[p][e] over p in ascending order, as a
+             * loop over p per e would; positions outer keeps the reads row-wise */
+            float* acc = att + h * hd;
+            for (int64_t e = 0; e < hd; ++e) acc[e] = 0.0f;
+            for (int64_t p = 0; p <= pos; ++p) {
+                const float* vr = vf + (kvh * m->max_seq + p) * hd;
+                const float sp = scores[p];
+                for (int64_t e = 0; e < hd; ++e) acc[e] += sp * vr[e];
             }
+            for (int64_t e = 0; e < hd; ++e) acc[e] *= inv;
         }
         or_gemv_q4_0(tmp, m->wo[il], att, d, dq);
         for (int64_t i = 0; i < d; ++i) hidden[i] += tmp[i];

@@ -206,6 +206,7 @@ class _OrModel(C.Structure):
         ("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
         ("wg", C.c_void_p), ("wu", C.c_void_p), ("wd", C.c_void_p),
         ("lm_head", C.c_void_p), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p),
+        ("k_cache_f32", C.c_void_p), ("v_cache_f32", C.c_void_p),
     ]
 
 
@@ -234,13 +235,16 @@ class OracleModel:
         hd = cfg["head_dim"]
         self.k_cache = np.zeros((L, cfg["n_head_kv"], max_seq, hd), np.uint16)
         self.v_cache = np.zeros_like(self.k_cache)
+        self.k_cache_f32 = np.zeros(self.k_cache.shape, np.float32)
+        self.v_cache_f32 = np.zeros(self.k_cache.shape, np.float32)
         self.m = _OrModel(L, cfg["n_embd"], cfg["n_ff"], cfg["n_head"], cfg["n_head_kv"], hd, cfg["vocab"], max_seq,
                           cfg["rope_base"], cfg["eps"],
                           ptr(weights["tok_embd"]), ptr(weights["attn_norm"]), ptr(weights["ffn_norm"]),
                           ptr(weights["out_norm"]),
                           ptrs(weights["wq"]), ptrs(weights["wk"]), ptrs(weights["wv"]), ptrs(weights["wo"]),
                           ptrs(weights["wg"]), ptrs(weights["wu"]), ptrs(weights["wd"]),
-                          ptr(weights["lm_head"]), self.k_cache.ctypes.data, self.v_cache.ctypes.data)
+                          ptr(weights["lm_head"]), self.k_cache.ctypes.data, self.v_cache.ctypes.data,
+                          self.k_cache_f32.ctypes.data, self.v_cache_f32.ctypes.data)
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         logits = np.empty(self.cfg["vocab"], np.float32)

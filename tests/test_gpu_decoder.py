@@ -109,3 +109,33 @@ def test_8b_width_two_layers(cuda, oracle):
         assert relerr(lg, ref) <= TOL, (t, relerr(lg, ref))
         assert int(np.argmax(lg)) == oracle.argmax(ref)
     m.close()
+
+
+@pytest.mark.parametrize("shape", ["hd64_g2_batch2", "hd128_g8"])
+def test_long_context_attention_splits(cuda, oracle, shape):
+    # Contexts long enough for the attention to split the cached positions over
+    # several CTAs and combine them (64+ positions per split), and, at head_dim
+    # 128, past 4096 positions where each warp takes 32 positions per split.
+    from agent_harness_b200.model import Model, ModelConfig
+    if shape == "hd64_g2_batch2":
+        cfg = ModelConfig(n_layer=2, n_embd=256, n_ff=512, n_head=4, n_head_kv=2, head_dim=64, vocab_size=1000,
+                          max_seq=640, max_batch=2, rope_freq_base=10000.0, rms_eps=1e-5)
+        n_pos, check = 600, set(range(0, 600, 7)) | {63, 64, 65, 127, 128, 129, 599}
+    else:
+        cfg = ModelConfig(n_layer=2, n_embd=256, n_ff=512, n_head=8, n_head_kv=1, head_dim=128, vocab_size=1000,
+                          max_seq=4200, max_batch=1, rope_freq_base=500000.0, rms_eps=1e-5)
+        n_pos, check = 4160, set(range(0, 4160, 97)) | {4095, 4096, 4097} | set(range(4150, 4160))
+    B = cfg.max_batch
+    m = Model(cfg)
+    m.init_random(31)
+    W = oracle_weights(cfg, 31, cuda)
+    om = [oracle_model(oracle, cfg, W) for _ in range(B)]
+    toks = np.random.default_rng(8).integers(0, cfg.vocab_size, (B, n_pos)).astype(np.int32)
+    m.reset(B)
+    for t in range(n_pos):
+        logits = m.forward(toks[:, t]).cpu().numpy()
+        for b in range(B):
+            ref = om[b].forward(int(toks[b, t]), t)
+            if t in check:
+                assert relerr(logits[b], ref) <= TOL, (t, b, relerr(logits[b], ref))
+    m.close()
