@@ -577,47 +577,54 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_tc(const __grid_cons
       }
     }
     if (n_split > 1) {
-      // the last split of (b, h) to finish combines (deterministic split order)
+      // the last split of (b, h) to finish combines; the counter's acq_rel add
+      // publishes this CTA's partials (ordered by the barrier) and, in the last
+      // CTA, makes every split's partials visible
       __syncthreads();
-      if (tid == 0) {
-        __threadfence();
-        last = atomicAdd(&a.cnt[bh], 1) == n_split - 1;
-        if (last) __threadfence();
-      }
+      if (tid == 0) last = atom_add_acq_rel_gpu(&a.cnt[bh], 1) == n_split - 1;
       __syncthreads();
       if (last) {
         const float* acc_base = a.part + ((size_t)bh * kAttnSplits * G) * HD;
-        const float* ml_base = a.part + (size_t)a.batch * a.n_kv * kAttnSplits * G * HD + (size_t)bh * kAttnSplits * G * 2;
-        float* fm = red;                 // [G][kAttnSplits] split weights exp(m_s - M)
-        float* inv = red + 8 * kAttnSplits;  // [G] 1 / L
-        if (tid < G) {
-          float M = -INFINITY;
-          for (int u = 0; u < n_split; ++u) M = fmaxf(M, __ldcg(ml_base + (u * G + tid) * 2));
-          float L = 0.0f;
-          for (int u = 0; u < n_split; ++u) {
-            const float mt = __ldcg(ml_base + (u * G + tid) * 2);
-            const float f = (mt == -INFINITY) ? 0.0f : expf(mt - M);
-            fm[tid * kAttnSplits + u] = f;
-            L = fmaf(__ldcg(ml_base + (u * G + tid) * 2 + 1), f, L);
-          }
-          inv[tid] = 1.0f / L;
+        const float2* ml_base = reinterpret_cast<const float2*>(
+            a.part + (size_t)a.batch * a.n_kv * kAttnSplits * G * HD + (size_t)bh * kAttnSplits * G * 2);
+        float* fm = red;                     // [G][kAttnSplits] split weights exp(m_s - M) / L
+        static_assert(kAttnSplits <= 64, "two splits per lane");
+        for (int gg = warp; gg < G; gg += kAttnThreads / 32) {  // one warp per head, lanes over splits
+          const float2 v0 = lane < n_split ? __ldcg(ml_base + lane * G + gg) : make_float2(-INFINITY, 0.0f);
+          const float2 v1 =
+              lane + 32 < n_split ? __ldcg(ml_base + (lane + 32) * G + gg) : make_float2(-INFINITY, 0.0f);
+          float M = fmaxf(v0.x, v1.x);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+          const float f0 = v0.x == -INFINITY ? 0.0f : expf(v0.x - M);
+          const float f1 = v1.x == -INFINITY ? 0.0f : expf(v1.x - M);
+          float L = fmaf(f1, v1.y, f0 * v0.y);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
+          const float inv = 1.0f / L;
+          fm[gg * kAttnSplits + lane] = f0 * inv;
+          fm[gg * kAttnSplits + lane + 32] = f1 * inv;
         }
         __syncthreads();
         for (int i4 = tid; i4 < G * HD / 4; i4 += kAttnThreads) {  // four consecutive head dims per thread
           const int gg = (i4 * 4) / HD;
           float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 8
-          for (int u = 0; u < n_split; ++u) {
-            const float f = fm[gg * kAttnSplits + u];
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(acc_base + (size_t)u * G * HD) + i4);
-            acc.x = fmaf(v.x, f, acc.x);
-            acc.y = fmaf(v.y, f, acc.y);
-            acc.z = fmaf(v.z, f, acc.z);
-            acc.w = fmaf(v.w, f, acc.w);
+          for (int u0 = 0; u0 < n_split; u0 += 16) {  // 16 independent loads in flight
+            float4 v[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              if (u0 + k < n_split) v[k] = __ldcg(reinterpret_cast<const float4*>(acc_base + (size_t)(u0 + k) * G * HD) + i4);
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              if (u0 + k < n_split) {
+                const float f = fm[gg * kAttnSplits + u0 + k];
+                acc.x = fmaf(v[k].x, f, acc.x);
+                acc.y = fmaf(v[k].y, f, acc.y);
+                acc.z = fmaf(v[k].z, f, acc.z);
+                acc.w = fmaf(v[k].w, f, acc.w);
+              }
           }
-          const float iv = inv[gg];
-          *reinterpret_cast<float4*>(a.out + (size_t)b * dq + (size_t)h * G * HD + i4 * 4) =
-              make_float4(acc.x * iv, acc.y * iv, acc.z * iv, acc.w * iv);
+          *reinterpret_cast<float4*>(a.out + (size_t)b * dq + (size_t)h * G * HD + i4 * 4) = acc;
         }
         if (tid == 0) a.cnt[bh] = 0;
       }

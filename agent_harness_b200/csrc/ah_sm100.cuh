@@ -117,6 +117,13 @@ __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
+// Device-scope atomic add with acquire-release semantics; returns the old value.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // Streaming (evict-first) 16-byte global store for write-once outputs.
 __device__ __forceinline__ void st_cs_f4(float4* p, float4 v) { __stcs(p, v); }
 
