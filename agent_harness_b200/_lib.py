@@ -49,6 +49,15 @@ SIGNATURES = {
     "ah_q4w_destroy": (i32, [vp]),
     "ah_q4w_shape": (i32, [vp, C.POINTER(i64), C.POINTER(i64)]),
     "ah_q4w_weight_bytes": (i64, [vp]),
+    "ah_q4w_planes": (i32, [vp, C.POINTER(vp), C.POINTER(sz), C.POINTER(vp), C.POINTER(sz), C.POINTER(i32)]),
+    "ah_dedup_table_local": (i32, [vp, i64, vp, i64, i32, i32, C.c_float, C.POINTER(vp)]),
+    "ah_dedup_table_global": (i32, [vp, i64, vp, i64, i32, i32, C.c_float, i32, vp, i64, vp, vp, C.POINTER(vp)]),
+    "ah_dedup_table_remap": (i32, [vp, i64, i32, i32, C.c_float, i32, vp, i64, vp, vp, vp, i64, C.POINTER(vp)]),
+    "ah_dedup_table_destroy": (i32, [vp]),
+    "ah_dedup_decompress_f32": (i32, [vp, vp, i64, vp, i64, vp, i64, i64, vp, vp]),
+    "ah_dedup_to_q4w": (i32, [vp, vp, i64, vp, i64, vp, i64, i64, i64, C.POINTER(vp), vp]),
+    "ah_host_dedup_decompress_all": (i32, [vp, i64, vp, i64, i64, i32, i32, C.c_float, vp, i64, vp, i64, vp, i64,
+                                           vp]),
     "ah_q4w_gemv": (i32, [vp, vp, vp, i32, vp]),
     "ah_q4w_gemm_workspace_bytes": (i32, [vp, i64, C.POINTER(C.c_size_t)]),
     "ah_q4w_gemm": (i32, [vp, vp, i64, i64, vp, i64, vp, C.c_size_t, vp]),

@@ -45,6 +45,9 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // bounded waits set when a wait gives up; read and cleared by
 // ah_check_device_error.  Allocated on first use for the current device.
 int* device_error_word();
+// Codes in the error word: 0x5xxx input indices a kernel found out of range
+// (AH_EINVAL); every other code is a bounded wait that gave up (AH_ETIMEOUT).
+constexpr int kDeviceIndexError = 0x5000;
 
 // ---- bit-exact scalar semantics ------------------------------------------------
 // f16 bits -> f32 with the reference's NaN rule (formats/gguf.rs:93-120): every

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(kThreads) k_repack(uint4* __restrict__ nib, vo
 
 }  // namespace
 
-int q4w_create(const RowSource& src, bool engine, int64_t rows, int64_t cols, AhQ4Weight** out, cudaStream_t st) {
+int q4w_alloc(int64_t rows, int64_t cols, bool engine, AhQ4Weight** out) {
   AH_REQUIRE(out != nullptr, "q4w_create: null out");
   *out = nullptr;
   AH_REQUIRE(rows > 0 && cols > 0, "q4w_create: rows and cols must be positive");
@@ -149,6 +149,14 @@ int q4w_create(const RowSource& src, bool engine, int64_t rows, int64_t cols, Ah
   w->t.nib = static_cast<const uint4*>(w->nib_alloc);
   w->t.scales = w->scale_alloc;
   w->weight_bytes = engine ? rows * ((cols + 1) / 2) + rows * nb * 4 : rows * nb * 18;
+  *out = w;
+  return AH_OK;
+}
+
+int q4w_create(const RowSource& src, bool engine, int64_t rows, int64_t cols, AhQ4Weight** out, cudaStream_t st) {
+  AhQ4Weight* w = nullptr;
+  const int rc = q4w_alloc(rows, cols, engine, &w);
+  if (rc != AH_OK) return rc;
   const int64_t total = w->t.r16 * w->t.kp * 32;
   int64_t grid = (total + kThreads - 1) / kThreads;
   grid = std::min<int64_t>(grid, (int64_t)sm_count() * 16);
@@ -189,6 +197,8 @@ int q4w_create_q4_0_multi(const void* const* srcs, const int64_t* src_rows, int 
 }
 
 const Q4Tiled& q4w_tiled(const AhQ4Weight* w) { return w->t; }
+uint4* q4w_nib_mut(AhQ4Weight* w) { return static_cast<uint4*>(w->nib_alloc); }
+void* q4w_scales_mut(AhQ4Weight* w) { return w->scale_alloc; }
 
 // ---------------------------------------------------------------------------
 // The fused GEMV kernel
@@ -983,6 +993,17 @@ int ah_q4w_shape(const AhQ4Weight* w, int64_t* rows, int64_t* cols) {
 }
 
 int64_t ah_q4w_weight_bytes(const AhQ4Weight* w) { return w ? w->weight_bytes : 0; }
+
+int ah_q4w_planes(const AhQ4Weight* w, const void** nib, size_t* nib_bytes, const void** scales, size_t* scale_bytes,
+                  int* f32_scales) {
+  AH_REQUIRE(w && nib && nib_bytes && scales && scale_bytes && f32_scales, "q4w_planes: null argument");
+  *nib = w->nib_alloc;
+  *nib_bytes = (size_t)w->t.r16 * w->t.kp * 32 * 16;
+  *scales = w->scale_alloc;
+  *scale_bytes = (size_t)w->t.r16 * w->t.kp * 8 * (w->t.f32_scales ? 16 : 8);
+  *f32_scales = w->t.f32_scales ? 1 : 0;
+  return AH_OK;
+}
 
 int ah_q4w_gemv(const AhQ4Weight* w, const float* x, float* y, int batch, void* stream) {
   AH_REQUIRE(w && x && y, "q4w_gemv: null argument");

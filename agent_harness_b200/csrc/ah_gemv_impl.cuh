@@ -27,6 +27,11 @@ int gemv_launch(GemvArgs a, int prologue, int epilogue, cudaStream_t st, bool pd
 int gemv_prepare(const Q4Tiled& w, int batch, int prologue, int epilogue);
 
 const Q4Tiled& q4w_tiled(const AhQ4Weight* w);
+// An uninitialised tiled weight of the given shape (f32 scales when `engine`);
+// its planes are filled by the caller's kernel.
+int q4w_alloc(int64_t rows, int64_t cols, bool engine, AhQ4Weight** out);
+uint4* q4w_nib_mut(AhQ4Weight* w);
+void* q4w_scales_mut(AhQ4Weight* w);
 int q4w_create_q4_0_multi(const void* const* srcs, const int64_t* src_rows, int nsrc, int mode, int64_t cols,
                           AhQ4Weight** out, cudaStream_t st);
 

@@ -98,6 +98,8 @@ int ah_check_device_error(void* stream) {
   AH_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
   if (v != 0) {
     AH_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
+    if ((v & 0xF000) == kDeviceIndexError)
+      return fail(AH_EINVAL, "a device-side index check failed (code 0x%x)", v);
     return fail(AH_ETIMEOUT, "a bounded device-side wait gave up (code 0x%x)", v);
   }
   return AH_OK;

@@ -131,6 +131,18 @@ def synth_f16(n: int, mean: float, std: float, seed: int, device="cuda", index_o
 
 # --- fused GEMV ----------------------------------------------------------------------------
 
+class _DeviceBuffer:
+    """A raw device allocation seen through __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+def _device_bytes(ptr: int, nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.as_tensor(_DeviceBuffer(ptr, int(nbytes)), device=device)
+
+
 class Q4Weight:
     """A device-resident quantised matrix in the GEMV's tiled layout."""
 
@@ -157,6 +169,16 @@ class Q4Weight:
     @property
     def weight_bytes(self) -> int:
         return int(lib().ah_q4w_weight_bytes(self._h))
+
+    def planes(self):
+        """Copies of the device planes (nibbles, scales) as uint8 tensors, and
+        whether the scales are f32 (engine format) rather than f16 (Q4_0)."""
+        nib, scl = C.c_void_p(), C.c_void_p()
+        nb, sb = C.c_size_t(), C.c_size_t()
+        f32 = C.c_int()
+        call("ah_q4w_planes", self._h, C.byref(nib), C.byref(nb), C.byref(scl), C.byref(sb), C.byref(f32))
+        return (_device_bytes(nib.value, nb.value, self.device).clone(),
+                _device_bytes(scl.value, sb.value, self.device).clone(), bool(f32.value))
 
     def gemv(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """y[b] = W @ x[b] for x of shape [cols] or [batch, cols] (batch <= 16)."""

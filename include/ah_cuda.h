@@ -133,6 +133,11 @@ AH_API int ah_q4w_destroy(AhQ4Weight* w);
 AH_API int ah_q4w_shape(const AhQ4Weight* w, int64_t* rows, int64_t* cols);
 /* Bytes the algorithm must read per GEMV (nibbles + scales, unpadded). */
 AH_API int64_t ah_q4w_weight_bytes(const AhQ4Weight* w);
+/* Read-only view of a resident weight's device planes (no reference
+ * counterpart): the tiled nibbles, the scales (f16x4 or, for f32_scales,
+ * float4 per row pair of a block pair) and their sizes in bytes. */
+AH_API int ah_q4w_planes(const AhQ4Weight* w, const void** nib, size_t* nib_bytes, const void** scales,
+                         size_t* scale_bytes, int* f32_scales);
 
 /* Reference: inference/math.rs:255-295 gemv_4bit_into (batch 1) and its
  * token-by-token use in inference/mod.rs:411-538, batched to `batch` <= 16
@@ -253,7 +258,55 @@ AH_API int ah_model_decode(AhModel* m, int n, int32_t* out_tokens_dev, void* str
 /* Current position (tokens consumed per sequence). */
 AH_API int ah_model_position(const AhModel* m, int* pos);
 
+/* ---- DedupCount weight decoding (models/dedup/) --------------------------------------
+ * A decode table holds one tensor's lookups flattened to f32 values on the
+ * device; the sandbag arrays (prefix_idx, tail_idx: u16; sign_bits: one bit per
+ * element, LSB first) are device arrays that may be shorter than `count`
+ * (missing entries read 0, as the reference's .get(i).unwrap_or(0) does). */
+typedef struct AhDedupTable AhDedupTable;
+/* Replaces the per-element arithmetic of dedup/decompressor.rs:7-27
+ * DedupCountTensor::decompress_all: prefix_int / 10^pd + tail / 10^(pd+td). */
+AH_API int ah_dedup_table_local(const uint16_t* prefixes, int64_t n_prefix, const uint16_t* tail_values, int64_t n_tail,
+                                int prefix_digits, int tail_digits, float avg_precision_lost, AhDedupTable** out);
+/* Replaces dedup/decompressor.rs:29-85 DedupCountTensor::decompress_all_global's
+ * prefix and tail lookups against a GlobalTable (dedup/types.rs:23-28) given as
+ * g_prefixes[n_gp] and tails_for_prefix in CSR form (g_tail_off[n_gp + 1]). */
+AH_API int ah_dedup_table_global(const uint16_t* prefixes, int64_t n_prefix, const uint16_t* tail_values,
+                                 int64_t n_tail, int prefix_digits, int tail_digits, float avg_precision_lost,
+                                 int g_prefix_digits, const float* g_prefixes, int64_t n_gp, const uint32_t* g_tail_off,
+                                 const uint32_t* g_tails, AhDedupTable** out);
+/* Replaces dedup/global_lookup.rs:89-113 GlobalTable::decompress_with_remap's
+ * lookups for a ChunkRemap (global_tail_indices = remap[n_remap]).  A prefix
+ * index past the tensor's prefixes (a panic in the reference) sets the device
+ * error word: ah_check_device_error then returns AH_EINVAL. */
+AH_API int ah_dedup_table_remap(const uint16_t* prefixes, int64_t n_prefix, int prefix_digits, int tail_digits,
+                                float avg_precision_lost, int g_prefix_digits, const float* g_prefixes, int64_t n_gp,
+                                const uint32_t* g_tail_off, const uint32_t* g_tails, const uint16_t* remap,
+                                int64_t n_remap, AhDedupTable** out);
+AH_API int ah_dedup_table_destroy(AhDedupTable* t);
+/* decompress_all / decompress_all_global / decompress_with_remap on device
+ * arrays: out[count] f32 (count: the tensor's count; for a remap table, the
+ * sandbag's count, and the arrays must hold that many entries). */
+AH_API int ah_dedup_decompress_f32(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t n_prefix_idx,
+                                   const uint16_t* tail_idx, int64_t n_tail_idx, const uint8_t* sign_bits,
+                                   int64_t n_sign_bytes, int64_t count, float* out, void* stream);
+/* Load path of inference/mod.rs:255-271 (decompress_tensor_global_single, then
+ * quantization.rs:369-404 quantize with group 32) in one pass: decodes a
+ * [rows][cols] tensor (cols % 32 == 0) and writes a resident engine-format
+ * weight (f32 scales) in the GEMV's tiled layout, bit-identical to quantize()
+ * of the decoded values followed by ah_q4w_from_engine. */
+AH_API int ah_dedup_to_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t n_prefix_idx,
+                           const uint16_t* tail_idx, int64_t n_tail_idx, const uint8_t* sign_bits,
+                           int64_t n_sign_bytes, int64_t rows, int64_t cols, AhQ4Weight** out, void* stream);
+
 /* ---- host-slice drop-ins (synchronous; reference signatures) ---------------------- */
+/* Reference: dedup/decompressor.rs:7-27 DedupCountTensor::decompress_all(&self,
+ * sandbag) -> Vec<f32> (count = self.count; host arrays in, out[count]). */
+AH_API int ah_host_dedup_decompress_all(const uint16_t* prefixes, int64_t n_prefix, const uint16_t* tail_values,
+                                        int64_t n_tail, int64_t count, int prefix_digits, int tail_digits,
+                                        float avg_precision_lost, const uint16_t* prefix_idx, int64_t n_prefix_idx,
+                                        const uint16_t* tail_idx, int64_t n_tail_idx, const uint8_t* sign_bits,
+                                        int64_t n_sign_bytes, float* out);
 /* Reference: inference/math.rs:255-295 gemv_4bit_into(out, scales, packed, x, rows, cols, gs). */
 AH_API int ah_host_gemv_4bit_into(float* out, const float* scales, const uint8_t* packed, const float* x, size_t rows,
                            size_t cols, size_t group_size);

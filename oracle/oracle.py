@@ -71,6 +71,24 @@ def lib():
         L.or_avx_dequant_layer.argtypes = [f32p, u8p, f32p, i64]
         L.or_avx_f16_bytes_to_f32.argtypes = [u8p, i64, f32p]; L.or_avx_f16_bytes_to_f32.restype = i64
         L.or_avx_bf16_bytes_to_f32.argtypes = [u8p, i64, f32p]; L.or_avx_bf16_bytes_to_f32.restype = i64
+        # DedupCount codec
+        u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+        i64p = np.ctypeslib.ndpointer(dtype=np.int64, flags="C_CONTIGUOUS")
+        i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+        L.or_dedup_compress.argtypes = [f32p, i64, C.c_int, C.c_int, u16p, u32p, C.POINTER(i64), u16p, u32p,
+                                        C.POINTER(i64), C.POINTER(i64), C.POINTER(C.c_float), u16p, u16p, u8p]
+        L.or_dedup_compress.restype = C.c_int
+        L.or_dedup_decompress_all.argtypes = [u16p, i64, u16p, i64, i64, C.c_int, C.c_int, C.c_float, u16p, i64,
+                                              u16p, i64, u8p, i64, f32p]
+        L.or_dedup_decompress_all_global.argtypes = [u16p, i64, u16p, i64, i64, C.c_int, C.c_int, C.c_float, u16p,
+                                                     i64, u16p, i64, u8p, i64, C.c_int, f32p, i64, u32p, u32p, f32p]
+        L.or_dedup_decompress_all_global.restype = C.c_int
+        L.or_dedup_global_table_new.argtypes = [C.c_int, i32p, u16p, i64p, u16p, i64p, f32p, u32p, u32p, i64]
+        L.or_dedup_global_table_new.restype = i64
+        L.or_dedup_build_chunk_remap.argtypes = [u16p, i64, u16p, i64, C.c_int, C.c_int, f32p, i64, u32p, u32p, u16p]
+        L.or_dedup_decompress_with_remap.argtypes = [u16p, i64, C.c_int, C.c_int, C.c_float, u16p, i64, u16p, i64,
+                                                     u8p, i64, i64, C.c_int, f32p, i64, u32p, u32p, u16p, i64, f32p]
+        L.or_dedup_decompress_with_remap.restype = C.c_int
         _lib = L
     return _lib
 
@@ -193,6 +211,142 @@ def argmax(logits) -> int:
 
 def silu(v: float) -> float:
     return float(lib().or_silu(v))
+
+
+# --- DedupCount codec (models/dedup/) ----------------------------------------
+
+class DedupTensor:
+    """DedupCountTensor's decode-relevant fields (dedup/tensor.rs:4-13):
+    prefixes (u16), unique tail values (u16) and counts, count, prefix_digits,
+    tail_digits, avg_precision_lost."""
+
+    def __init__(self, prefixes, tail_values, count, prefix_digits, tail_digits, avg_precision_lost,
+                 prefix_counts=None, tail_counts=None):
+        self.prefixes = np.ascontiguousarray(prefixes, np.uint16)
+        self.tail_values = np.ascontiguousarray(tail_values, np.uint16)
+        self.count = int(count)
+        self.prefix_digits = int(prefix_digits)
+        self.tail_digits = int(tail_digits)
+        self.avg_precision_lost = float(np.float32(avg_precision_lost))
+        self.prefix_counts = prefix_counts
+        self.tail_counts = tail_counts
+
+
+class Sandbag:
+    """Per-element indices (dedup/types.rs:14-21): prefix_idx, tail_idx (u16),
+    sign_bits (one bit per element, LSB first) and count."""
+
+    def __init__(self, prefix_idx, tail_idx, sign_bits, count):
+        self.prefix_idx = np.ascontiguousarray(prefix_idx, np.uint16)
+        self.tail_idx = np.ascontiguousarray(tail_idx, np.uint16)
+        self.sign_bits = np.ascontiguousarray(sign_bits, np.uint8)
+        self.count = int(count)
+
+
+class GlobalTable:
+    """dedup/types.rs:23-28: prefix_digits, f32 prefixes and tails_for_prefix
+    (CSR: tail_off[n + 1], tails)."""
+
+    def __init__(self, prefix_digits, prefixes, tail_off, tails):
+        self.prefix_digits = int(prefix_digits)
+        self.prefixes = np.ascontiguousarray(prefixes, np.float32)
+        self.tail_off = np.ascontiguousarray(tail_off, np.uint32)
+        self.tails = np.ascontiguousarray(tails, np.uint32)
+
+    def row(self, gi):
+        return self.tails[self.tail_off[gi]:self.tail_off[gi + 1]]
+
+
+def _arr(a, dt):
+    a = np.ascontiguousarray(a, dt)
+    return a if a.size else np.zeros(1, dt)
+
+
+def dedup_compress(w, prefix_digits: int, truncate_rounds: int):
+    """DedupCountTensor::compress (compressor.rs:8-160, scalar tail path)."""
+    w = _c(w, np.float32)
+    n = w.size
+    pre = np.zeros(65536, np.uint16); pc = np.zeros(65536, np.uint32)
+    tv = np.zeros(65536, np.uint16); tc = np.zeros(65536, np.uint32)
+    pidx = np.zeros(max(n, 1), np.uint16); tidx = np.zeros(max(n, 1), np.uint16)
+    signs = np.zeros(max((n + 7) // 8, 1), np.uint8)
+    np_, nt, td = i64(), i64(), i64()
+    avg = C.c_float()
+    rc = lib().or_dedup_compress(_arr(w, np.float32), n, prefix_digits, truncate_rounds, pre, pc, C.byref(np_), tv, tc,
+                                 C.byref(nt), C.byref(td), C.byref(avg), pidx, tidx, signs)
+    if rc != 0:
+        raise MemoryError("oracle compress")
+    t = DedupTensor(pre[:np_.value].copy(), tv[:nt.value].copy(), n, prefix_digits, td.value, avg.value,
+                    pc[:np_.value].copy(), tc[:nt.value].copy())
+    return t, Sandbag(pidx[:n].copy(), tidx[:n].copy(), signs[:(n + 7) // 8].copy(), n)
+
+
+def dedup_decompress_all(t: DedupTensor, s: Sandbag) -> np.ndarray:
+    """DedupCountTensor::decompress_all (decompressor.rs:7-27)."""
+    out = np.empty(max(t.count, 1), np.float32)
+    lib().or_dedup_decompress_all(_arr(t.prefixes, np.uint16), t.prefixes.size, _arr(t.tail_values, np.uint16),
+                                  t.tail_values.size, t.count, t.prefix_digits, t.tail_digits, t.avg_precision_lost,
+                                  _arr(s.prefix_idx, np.uint16), s.prefix_idx.size, _arr(s.tail_idx, np.uint16),
+                                  s.tail_idx.size, _arr(s.sign_bits, np.uint8), s.sign_bits.size, out)
+    return out[:t.count]
+
+
+def dedup_decompress_all_global(t: DedupTensor, s: Sandbag, g: GlobalTable) -> np.ndarray:
+    """DedupCountTensor::decompress_all_global (decompressor.rs:29-85); raises
+    where the reference panics."""
+    out = np.empty(max(t.count, 1), np.float32)
+    rc = lib().or_dedup_decompress_all_global(
+        _arr(t.prefixes, np.uint16), t.prefixes.size, _arr(t.tail_values, np.uint16), t.tail_values.size, t.count,
+        t.prefix_digits, t.tail_digits, t.avg_precision_lost, _arr(s.prefix_idx, np.uint16), s.prefix_idx.size,
+        _arr(s.tail_idx, np.uint16), s.tail_idx.size, _arr(s.sign_bits, np.uint8), s.sign_bits.size, g.prefix_digits,
+        _arr(g.prefixes, np.float32), g.prefixes.size, _arr(g.tail_off, np.uint32), _arr(g.tails, np.uint32), out)
+    if rc != 0:
+        raise IndexError("decompress_all_global: index out of range (the reference panics)")
+    return out[:t.count]
+
+
+def dedup_global_table_new(chunks) -> GlobalTable:
+    """GlobalTable::new (global_lookup.rs:7-59)."""
+    n = len(chunks)
+    if n == 0:
+        return GlobalTable(0, np.zeros(0, np.float32), np.zeros(1, np.uint32), np.zeros(0, np.uint32))
+    pd = np.array([c.prefix_digits for c in chunks], np.int32)
+    npre = np.array([c.prefixes.size for c in chunks], np.int64)
+    ntl = np.array([c.tail_values.size for c in chunks], np.int64)
+    pre = _arr(np.concatenate([c.prefixes for c in chunks]), np.uint16)
+    tl = _arr(np.concatenate([c.tail_values for c in chunks]), np.uint16)
+    cap = int(max(1, ntl.sum() * max(1, npre.sum())))
+    gp = np.zeros(65536, np.float32); off = np.zeros(65537, np.uint32); tails = np.zeros(min(cap, 1 << 26), np.uint32)
+    ng = lib().or_dedup_global_table_new(n, pd, pre, npre, tl, ntl, gp, off, tails, tails.size)
+    if ng < 0:
+        raise MemoryError("global table capacity")
+    return GlobalTable(int(pd[0]), gp[:ng].copy(), off[:ng + 1].copy(), tails[:off[ng]].copy())
+
+
+def dedup_build_chunk_remap(g: GlobalTable, t: DedupTensor) -> np.ndarray:
+    """GlobalTable::build_chunk_remap (global_lookup.rs:62-86)."""
+    out = np.zeros(max(t.tail_values.size, 1), np.uint16)
+    lib().or_dedup_build_chunk_remap(_arr(t.prefixes, np.uint16), t.prefixes.size, _arr(t.tail_values, np.uint16),
+                                     t.tail_values.size, t.prefix_digits, g.prefix_digits,
+                                     _arr(g.prefixes, np.float32), g.prefixes.size, _arr(g.tail_off, np.uint32),
+                                     _arr(g.tails, np.uint32), out)
+    return out[:t.tail_values.size]
+
+
+def dedup_decompress_with_remap(g: GlobalTable, s: Sandbag, t: DedupTensor, remap) -> np.ndarray:
+    """GlobalTable::decompress_with_remap with a remap (global_lookup.rs:89-113);
+    raises where the reference panics."""
+    remap = np.ascontiguousarray(remap, np.uint16)
+    out = np.empty(max(s.count, 1), np.float32)
+    rc = lib().or_dedup_decompress_with_remap(
+        _arr(t.prefixes, np.uint16), t.prefixes.size, t.prefix_digits, t.tail_digits, t.avg_precision_lost,
+        _arr(s.prefix_idx, np.uint16), s.prefix_idx.size, _arr(s.tail_idx, np.uint16), s.tail_idx.size,
+        _arr(s.sign_bits, np.uint8), s.sign_bits.size, s.count, g.prefix_digits, _arr(g.prefixes, np.float32),
+        g.prefixes.size, _arr(g.tail_off, np.uint32), _arr(g.tails, np.uint32), _arr(remap, np.uint16), remap.size,
+        out)
+    if rc != 0:
+        raise IndexError("decompress_with_remap: index out of range (the reference panics)")
+    return out[:s.count]
 
 
 # --- decoder ----------------------------------------------------------------
