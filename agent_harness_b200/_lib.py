@@ -56,6 +56,7 @@ SIGNATURES = {
     "ah_dedup_table_destroy": (i32, [vp]),
     "ah_dedup_decompress_f32": (i32, [vp, vp, i64, vp, i64, vp, i64, i64, vp, vp]),
     "ah_dedup_to_q4w": (i32, [vp, vp, i64, vp, i64, vp, i64, i64, i64, C.POINTER(vp), vp]),
+    "ah_dedup_into_q4w": (i32, [vp, vp, i64, vp, i64, vp, i64, vp, vp]),
     "ah_host_dedup_decompress_all": (i32, [vp, i64, vp, i64, i64, i32, i32, C.c_float, vp, i64, vp, i64, vp, i64,
                                            vp]),
     "ah_q4w_gemv": (i32, [vp, vp, vp, i32, vp]),

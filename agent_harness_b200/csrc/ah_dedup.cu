@@ -14,7 +14,7 @@
 // element; the table adds are the reference's own f32 operations, in its order.
 //
 // The load-time path (inference/mod.rs:255-271: decompress, quantise, write)
-// runs as one kernel: each warp decodes four 32-element groups, quantises them
+// runs as one kernel: each warp decodes eight 32-element groups, quantises them
 // exactly as quantization.rs:369-404 does, and writes nibbles and f32 scales
 // straight into the tiled GEMV layout — no f32 tensor in HBM, 4.75 bytes per
 // element in total.
@@ -157,83 +157,102 @@ __global__ void __launch_bounds__(kThreads) k_dedup_decompress(const DedupArgs a
   }
 }
 
-// Decode + quantise + tiled write.  A warp takes row R and blocks b0..b0+3
-// (32 elements each); lane 8s+l holds elements 4l..4l+3 of block b0+s.  The
+// Decode + quantise + tiled write.  A warp takes row R and blocks b0..b0+7
+// (32 elements each); lane 4s+l holds elements 8l..8l+7 of block b0+s.  The
 // tiled word t of a 16-row tile packs, for lane (g, t) of the MMA fragment,
 // element e = 2t + (pp>>2) + 16(pp&1) + 8((pp>>1)&1) in nibble pp (the layout
-// the GEMV reads); for element 4l + j that is word 2(l&1) + (j>>1), nibble
-// ((j&1)<<2) | (((l>>1)&1)<<1) | ((l>>2)&1).  Rows past `rows` and blocks past
-// cols/32 are written as zero weights (nibble 8, scale 0).
+// the GEMV reads); for element 8l + j that is word j>>1, nibble
+// ((j&1)<<2) | ((l&1)<<1) | (l>>1).  Rows past `rows` and blocks past cols/32
+// are written as zero weights (nibble 8, scale 0).  Each warp loads its next
+// item's indices before it decodes the current one.
+struct Q4wItem {
+  uint4 p, t;   // eight prefix / tail indices
+  uint32_t sb;  // their sign bits
+  bool live;
+};
+
+__device__ __forceinline__ Q4wItem q4w_load(const DedupArgs& a, int64_t it, int64_t items, int64_t quads,
+                                            int64_t rows, int64_t cols, int sub, int l4) {
+  Q4wItem x{};
+  if (it >= items) return x;
+  const int64_t R = it / quads, b = (it - R * quads) * 8 + sub;
+  x.live = R < rows && b < cols / 32;
+  if (!x.live) return x;
+  const int64_t i0 = R * cols + b * 32 + l4 * 8;
+  if (i0 + 8 <= a.n_pidx) {
+    x.p = ldg_stream_v4(reinterpret_cast<const uint4*>(a.pidx + i0));
+  } else {
+    uint32_t v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = i0 + k < a.n_pidx ? a.pidx[i0 + k] : 0u;
+    x.p = make_uint4(v[0] | v[1] << 16, v[2] | v[3] << 16, v[4] | v[5] << 16, v[6] | v[7] << 16);
+  }
+  if (i0 + 8 <= a.n_tidx) {
+    x.t = ldg_stream_v4(reinterpret_cast<const uint4*>(a.tidx + i0));
+  } else {
+    uint32_t v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = i0 + k < a.n_tidx ? a.tidx[i0 + k] : 0u;
+    x.t = make_uint4(v[0] | v[1] << 16, v[2] | v[3] << 16, v[4] | v[5] << 16, v[6] | v[7] << 16);
+  }
+  x.sb = (i0 >> 3) < a.n_sign ? a.signs[i0 >> 3] : 0u;
+  return x;
+}
+
 template <bool k2d>
 __global__ void __launch_bounds__(kThreads) k_dedup_q4w(const DedupArgs a, uint32_t* __restrict__ nib,
                                                         float* __restrict__ scales, int64_t rows, int64_t cols,
                                                         int64_t r16, int64_t kp) {
-  const int lane = threadIdx.x & 31, sub = lane >> 3, l8 = lane & 7;
-  const int64_t nb = cols / 32;
-  const int64_t quads = (2 * kp + 3) / 4;
+  const int lane = threadIdx.x & 31, sub = lane >> 2, l4 = lane & 3;
+  const int64_t quads = (2 * kp + 7) / 8;  // 8-block groups per row (blocks past 2 kp are skipped)
   const int64_t items = r16 * 16 * quads;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t it = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
-    const int64_t R = it / quads, b = (it - R * quads) * 4 + sub;
-    const bool live = R < rows && b < nb;
-    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (live) {
-      const int64_t i0 = R * cols + b * 32 + l8 * 4;
-      uint32_t p[4], t[4];
-      if (i0 + 4 <= a.n_pidx) {
-        unpack4(ldg_nc_v2(reinterpret_cast<const uint2*>(a.pidx + i0)), p);
-      } else {
+  int64_t it = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  Q4wItem cur = q4w_load(a, it, items, quads, rows, cols, sub, l4);
+  for (; it < items; it += warps) {
+    const Q4wItem nxt = q4w_load(a, it + warps, items, quads, rows, cols, sub, l4);
+    const int64_t R = it / quads, b = (it - R * quads) * 8 + sub;
+    float v[8];
+    uint32_t p[8], t[8];
+    unpack8(cur.p, p);
+    unpack8(cur.t, t);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) p[k] = i0 + k < a.n_pidx ? a.pidx[i0 + k] : 0u;
-      }
-      if (i0 + 4 <= a.n_tidx) {
-        unpack4(ldg_nc_v2(reinterpret_cast<const uint2*>(a.tidx + i0)), t);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) t[k] = i0 + k < a.n_tidx ? a.tidx[i0 + k] : 0u;
-      }
-      const uint32_t sb = (i0 >> 3) < a.n_sign ? a.signs[i0 >> 3] : 0u;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float val = dedup_value<k2d>(a, p[k], t[k]);
-        v[k] = (sb >> ((i0 & 7) + k)) & 1u ? -val : val;
-        if (a.strict && p[k] >= (uint32_t)a.np) atomicExch(a.err, kErrPrefixIndex);
-      }
+    for (int k = 0; k < 8; ++k) {
+      const float val = cur.live ? dedup_value<k2d>(a, p[k], t[k]) : 0.0f;
+      v[k] = (cur.sb >> k) & 1u ? -val : val;
+      if (a.strict && cur.live && p[k] >= (uint32_t)a.np) atomicExch(a.err, kErrPrefixIndex);
     }
     // quantise the 32-element group (quantization.rs:369-404): scale = max|w| / 7,
     // q = clamp(round(w * (1 / scale)), -8, 7) + 8
-    float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(v[k]));
     m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
     m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-    m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
     const float scale = m > 0.0f ? __fdiv_rn(m, 7.0f) : 0.0f;
     const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-    uint32_t q[4];
+    const int pp0 = ((l4 & 1) << 1) | (l4 >> 1);  // nibble of even j; odd j adds 4
+    uint32_t w[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int qi = scale > 0.0f ? rust_f32_as_i32(roundf(__fmul_rn(v[k], inv))) : 0;
-      q[k] = (uint32_t)(min(max(qi, -8), 7) + 8);
+      int q0 = scale > 0.0f ? rust_f32_as_i32(roundf(__fmul_rn(v[2 * k], inv))) : 0;
+      int q1 = scale > 0.0f ? rust_f32_as_i32(roundf(__fmul_rn(v[2 * k + 1], inv))) : 0;
+      q0 = min(max(q0, -8), 7) + 8;
+      q1 = min(max(q1, -8), 7) + 8;
+      w[k] = ((uint32_t)q0 << (4 * pp0)) | ((uint32_t)q1 << (4 * (pp0 + 4)));
+      w[k] |= __shfl_xor_sync(0xFFFFFFFFu, w[k], 1);
+      w[k] |= __shfl_xor_sync(0xFFFFFFFFu, w[k], 2);
     }
-    const int pp0 = (((l8 >> 1) & 1) << 1) | ((l8 >> 2) & 1);  // nibble of j = 0 / 2; j = 1 / 3 add 4
-    uint32_t w_lo = (q[0] << (4 * pp0)) | (q[1] << (4 * (pp0 + 4)));  // word 2(l&1)
-    uint32_t w_hi = (q[2] << (4 * pp0)) | (q[3] << (4 * (pp0 + 4)));  // word 2(l&1) + 1
-    w_lo |= __shfl_xor_sync(0xFFFFFFFFu, w_lo, 2);
-    w_hi |= __shfl_xor_sync(0xFFFFFFFFu, w_hi, 2);
-    w_lo |= __shfl_xor_sync(0xFFFFFFFFu, w_lo, 4);
-    w_hi |= __shfl_xor_sync(0xFFFFFFFFu, w_hi, 4);
-    if (b < 2 * kp && l8 < 3) {
+    if (b < 2 * kp) {
       const int64_t rt = R >> 4;
       const int r = (int)(R & 15), g = r & 7, half = r >> 3;
       const int64_t tp = rt * kp + (b >> 1);
       const int wi = (int)(b & 1) * 2 + half;
-      if (l8 < 2) {
-        const int t0 = 2 * l8;  // lane 0 holds words 0, 1; lane 1 words 2, 3
-        nib[((tp * 32 + g * 4 + t0) * 4) + wi] = w_lo;
-        nib[((tp * 32 + g * 4 + t0 + 1) * 4) + wi] = w_hi;
-      } else {
-        scales[(tp * 8 + g) * 4 + wi] = scale;
-      }
+      const uint32_t word = l4 == 0 ? w[0] : l4 == 1 ? w[1] : l4 == 2 ? w[2] : w[3];
+      nib[((tp * 32 + g * 4 + l4) * 4) + wi] = word;  // lane l writes word l
+      if (l4 == 0) scales[(tp * 8 + g) * 4 + wi] = scale;
     }
+    cur = nxt;
   }
 }
 
@@ -459,21 +478,19 @@ int ah_dedup_decompress_f32(const AhDedupTable* t, const uint16_t* prefix_idx, i
   return AH_OK;
 }
 
-int ah_dedup_to_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t n_pidx, const uint16_t* tail_idx,
-                    int64_t n_tidx, const uint8_t* sign_bits, int64_t n_sign, int64_t rows, int64_t cols,
-                    AhQ4Weight** out, void* stream) {
-  AH_REQUIRE(t && out, "dedup_to_q4w: null argument");
-  *out = nullptr;
-  AH_REQUIRE(rows > 0 && cols > 0 && cols % 32 == 0, "dedup_to_q4w: rows > 0 and cols a multiple of 32 required");
+int ah_dedup_into_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t n_pidx, const uint16_t* tail_idx,
+                      int64_t n_tidx, const uint8_t* sign_bits, int64_t n_sign, AhQ4Weight* w, void* stream) {
+  AH_REQUIRE(t && w, "dedup_into_q4w: null argument");
+  const Q4Tiled& tw = q4w_tiled(w);
+  const int64_t rows = tw.rows, cols = tw.cols;
+  AH_REQUIRE(tw.f32_scales && cols % 32 == 0,
+             "dedup_into_q4w: the weight must be engine format (f32 scales) with cols a multiple of 32");
   AH_TRY_DEDUP(check_sandbag(t, n_pidx, n_tidx, n_sign, rows * cols));
   AH_REQUIRE(((uintptr_t)prefix_idx & 7u) == 0 && ((uintptr_t)tail_idx & 7u) == 0,
-             "dedup_to_q4w: index arrays must be 8-byte aligned");
+             "dedup_into_q4w: index arrays must be 8-byte aligned");
   const DedupArgs a = make_args(t, prefix_idx, n_pidx, tail_idx, n_tidx, sign_bits, n_sign);
-  AH_REQUIRE(a.err, "dedup_to_q4w: device error word unavailable");
-  AhQ4Weight* w = nullptr;
-  AH_TRY_DEDUP(q4w_alloc(rows, cols, true, &w));
-  const Q4Tiled& tw = q4w_tiled(w);
-  const int64_t warps = tw.r16 * 16 * ((2 * tw.kp + 3) / 4);
+  AH_REQUIRE(a.err, "dedup_into_q4w: device error word unavailable");
+  const int64_t warps = tw.r16 * 16 * ((2 * tw.kp + 7) / 8);
   const int grid = grid_for(warps * 32);
   uint32_t* nib = reinterpret_cast<uint32_t*>(q4w_nib_mut(w));
   float* sc = static_cast<float*>(q4w_scales_mut(w));
@@ -481,10 +498,23 @@ int ah_dedup_to_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t n
     k_dedup_q4w<false><<<grid, kThreads, 0, as_stream(stream)>>>(a, nib, sc, rows, cols, tw.r16, tw.kp);
   else
     k_dedup_q4w<true><<<grid, kThreads, 0, as_stream(stream)>>>(a, nib, sc, rows, cols, tw.r16, tw.kp);
-  const cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) {
+  AH_LAUNCH_CHECK();
+  return AH_OK;
+}
+
+int ah_dedup_to_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t n_pidx, const uint16_t* tail_idx,
+                    int64_t n_tidx, const uint8_t* sign_bits, int64_t n_sign, int64_t rows, int64_t cols,
+                    AhQ4Weight** out, void* stream) {
+  AH_REQUIRE(t && out, "dedup_to_q4w: null argument");
+  *out = nullptr;
+  AH_REQUIRE(rows > 0 && cols > 0 && cols % 32 == 0, "dedup_to_q4w: rows > 0 and cols a multiple of 32 required");
+  AH_TRY_DEDUP(check_sandbag(t, n_pidx, n_tidx, n_sign, rows * cols));
+  AhQ4Weight* w = nullptr;
+  AH_TRY_DEDUP(q4w_alloc(rows, cols, true, &w));
+  const int rc = ah_dedup_into_q4w(t, prefix_idx, n_pidx, tail_idx, n_tidx, sign_bits, n_sign, w, stream);
+  if (rc != AH_OK) {
     ah_q4w_destroy(w);
-    return fail(AH_ECUDA, "dedup_to_q4w: launch failed: %s", cudaGetErrorString(e));
+    return rc;
   }
   *out = w;
   return AH_OK;

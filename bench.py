@@ -17,6 +17,7 @@ restated in C) on the host cores instead.
 from __future__ import annotations
 
 import argparse
+import ctypes as C
 import json
 import os
 import subprocess
@@ -297,7 +298,7 @@ def run_gpu(args):
     Ws = []
     extra = {}
     if rank == 0 and not args.quick:
-        extra = secondary_measurements(K, dev, stream, peak)
+        extra = secondary_measurements(K, dev, stream, peak, no_cpu=args.no_cpu)
         extra["prefill_gemm"] = prefill_gemm(K, dev, cpu_tokens=0 if args.no_cpu else 8)
     if not args.quick and not args.no_decode:
         dec = decode_8b(dev, args.decode_prompt, args.decode_new)
@@ -516,8 +517,9 @@ def prefill_gemm(K, dev, iters=20, cpu_tokens=0):
     return out
 
 
-def secondary_measurements(K, dev, stream, peak):
-    """Config-1 dequant and f16->f32 throughput (each launch > L2)."""
+def secondary_measurements(K, dev, stream, peak, no_cpu=False):
+    """Config-1 dequant and f16->f32 throughput (each launch > L2), and the
+    DedupCount load path."""
     import torch
     out = {}
     n = 4096 * 11008
@@ -543,7 +545,81 @@ def secondary_measurements(K, dev, stream, peak):
         out[name] = {"gbs": round(gbs, 2), "pct_of_8tbs": round(100 * gbs / NOMINAL_HBM_GBS, 2),
                      "frac_of_measured_peak": round(gbs / peak, 4), "bytes_per_call": nbytes,
                      "us_per_call": round(s * 1e6, 2), "shape": "4096x11008"}
+    del q8, f, h
+    out["dedup_load"] = dedup_load(K, dev, stream, peak, cpu=not no_cpu)
     return out
+
+
+DEDUP_ROWS, DEDUP_COLS = 14336, 4096  # an 8B FFN gate/up matrix
+
+
+def dedup_load(K, dev, stream, peak, cpu=True):
+    """DedupCount load path on one FFN matrix: the fused decode + quantize +
+    tiled repack (inference/mod.rs:255-271) and the decode alone
+    (decompressor.rs:7-27).  Synthetic sandbag: 12 prefixes, 900 unique tails,
+    uniform indices and signs (inputs 242 MB, larger than L2)."""
+    import torch
+    from agent_harness_b200 import dedup as D
+    rows, cols = DEDUP_ROWS, DEDUP_COLS
+    n = rows * cols
+    g = torch.Generator(device=dev).manual_seed(11)
+    rng = np.random.default_rng(11)
+    t = D.DedupCountTensor(np.arange(12, dtype=np.uint16) * 3, np.sort(rng.choice(60000, 900, replace=False)), n, 2, 3,
+                           2e-6)
+    s = D.Sandbag(torch.randint(0, 12, (n,), dtype=torch.int16, device=dev, generator=g),
+                  torch.randint(0, 900, (n,), dtype=torch.int16, device=dev, generator=g),
+                  torch.randint(0, 256, ((n + 7) // 8,), dtype=torch.uint8, device=dev, generator=g), n)
+    p_idx, t_idx, signs = s.on(dev)
+    table = t._table_local()
+    w = t.to_q4weight(s, rows, cols)
+    f = torch.empty(n, dtype=torch.float32, device=dev)
+    st = C.c_void_p(stream.cuda_stream)
+    args = (table, C.c_void_p(p_idx.data_ptr()), n, C.c_void_p(t_idx.data_ptr()), n, C.c_void_p(signs.data_ptr()),
+            signs.numel())
+    from agent_harness_b200 import _lib
+    fused = lambda: _lib.call("ah_dedup_into_q4w", *args, w.handle, st)                       # noqa: E731
+    decode = lambda: _lib.call("ah_dedup_decompress_f32", *args, n, C.c_void_p(f.data_ptr()), st)  # noqa: E731
+    res = {"shape": f"{rows}x{cols}", "table": "local (12 prefixes, 900 tails)"}
+    for name, fn, per in (("fused_decode_quantize_repack", fused, 2 + 2 + 0.125 + 0.5 + 0.125),
+                          ("decode_f32", decode, 2 + 2 + 0.125 + 4)):
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            iters = 20
+            e0.record(stream)
+            for _ in range(iters):
+                fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        sec = e0.elapsed_time(e1) / 1e3 / iters
+        nbytes = int(per * n)
+        res[name] = {"gbs": round(nbytes / sec / 1e9, 2), "frac_of_measured_peak": round(nbytes / sec / 1e9 / peak, 4),
+                     "us_per_call": round(sec * 1e6, 2), "bytes_per_call": nbytes,
+                     "bytes_per_element": per, "gelem_per_s": round(n / sec / 1e9, 3)}
+    _lib.call("ah_dedup_table_destroy", table)
+    w.close()
+    if cpu:
+        res["cpu_baseline"] = dedup_cpu_baseline()
+    return res
+
+
+def dedup_cpu_baseline(n=1 << 21):
+    """The oracle's decompress_all + quantize (scalar restatements of
+    decompressor.rs:7-27 and quantization.rs:369-404), one thread, on a
+    2M-element sample compressed by the oracle's compress."""
+    from oracle import oracle as O
+    w = (np.random.default_rng(12).standard_normal(n) * 0.02).astype(np.float32)
+    t, s = O.dedup_compress(w, 2, 2)
+    scales = np.empty(n // 32, np.float32)
+    packed = np.empty(n // 2, np.uint8)
+    t0 = time.perf_counter()
+    dec = O.dedup_decompress_all(t, s)
+    O.lib().or_quantize_q4(dec, n, 32, scales, packed)
+    dt = time.perf_counter() - t0
+    per = 2 + 2 + 0.125 + 0.5 + 0.125
+    return {"gbs": round(per * n / dt / 1e9, 3), "gelem_per_s": round(n / dt / 1e9, 4), "cores": 1, "kind": "port",
+            "sample": f"{n} elements: oracle compress(pd 2, 2 rounds), then decompress_all + quantize timed"}
 
 
 def main():
@@ -553,9 +629,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode", "gemm", "tp"],
-                    help="decode / gemm / tp: only the 8B decode, the prefill GEMM or the 70B tensor-parallel "
-                         "decode measurement (for profiling)")
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode", "gemm", "tp", "load"],
+                    help="decode / gemm / tp / load: only the 8B decode, the prefill GEMM, the 70B tensor-parallel "
+                         "decode or the DedupCount load-path measurement (for profiling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
@@ -569,6 +645,16 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "load":
+        import torch
+        torch.cuda.set_device(0)
+        from agent_harness_b200 import _lib
+        from agent_harness_b200 import kernels as K
+        _lib.check(_lib.lib().ah_device_init(0))
+        dev = torch.device("cuda", 0)
+        print(json.dumps({"workload": "dedup_load", **dedup_load(K, dev, torch.cuda.Stream(device=dev), peaks()[0],
+                                                                 cpu=not args.no_cpu)}), flush=True)
+        return 0
     if args.workload == "decode":
         import torch
         torch.cuda.set_device(0)

@@ -298,6 +298,11 @@ AH_API int ah_dedup_decompress_f32(const AhDedupTable* t, const uint16_t* prefix
 AH_API int ah_dedup_to_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t n_prefix_idx,
                            const uint16_t* tail_idx, int64_t n_tail_idx, const uint8_t* sign_bits,
                            int64_t n_sign_bytes, int64_t rows, int64_t cols, AhQ4Weight** out, void* stream);
+/* The same into an existing engine-format weight of the tensor's shape (a
+ * resident arena slot reloaded in place; allocates nothing). */
+AH_API int ah_dedup_into_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t n_prefix_idx,
+                             const uint16_t* tail_idx, int64_t n_tail_idx, const uint8_t* sign_bits,
+                             int64_t n_sign_bytes, AhQ4Weight* w, void* stream);
 
 /* ---- host-slice drop-ins (synchronous; reference signatures) ---------------------- */
 /* Reference: dedup/decompressor.rs:7-27 DedupCountTensor::decompress_all(&self,
