@@ -68,6 +68,8 @@ SIGNATURES = {
     "ah_model_create": (i32, [vp, C.POINTER(vp)]),
     "ah_nccl_unique_id": (i32, [vp, C.c_size_t]),
     "ah_model_create_tp": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),
+    "ah_model_load_tensor_engine": (i32, [vp, i32, i32, vp, vp, vp]),
+    "ah_model_load_tensor_f32": (i32, [vp, i32, i32, vp, vp]),
     "ah_model_ipc_handle": (i32, [vp, vp, C.c_size_t]),
     "ah_model_ipc_open": (i32, [vp, vp, C.c_size_t]),
     "ah_model_shard": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32),

@@ -883,7 +883,8 @@ struct AhModel {
   int dq = 0, dkv = 0;                     // this rank's q and k/v widths
   std::vector<AhQ4Weight*> wqkv, wo, wgu, wd;
   AhQ4Weight* lm = nullptr;
-  std::vector<void*> pend[5];  // q, k, v, gate, up Q4_0 blocks awaiting fusion
+  std::vector<void*> pend[5];  // q, k, v, gate, up awaiting fusion (Q4_0 blocks or scales + packed)
+  std::vector<int> pend_fmt[5];  // kProjQ4_0 / kProjEngine per pending buffer
   uint16_t *tok_embd = nullptr, *attn_norm = nullptr, *ffn_norm = nullptr, *out_norm = nullptr;
   uint16_t *kc = nullptr, *vc = nullptr;
   CUtensorMap tm_k{}, tm_v{};  // TMA views of kc / vc for the tensor-core attention
@@ -1208,6 +1209,7 @@ int model_create(const AhModelConfig* cfg, int rank, int world, ncclComm_t comm,
   m->wgu.assign(L, nullptr);
   m->wd.assign(L, nullptr);
   for (auto& p : m->pend) p.assign(L, nullptr);
+  for (auto& f : m->pend_fmt) f.assign(L, 0);
   int rc = AH_OK;
   auto A = [&](void** p, size_t bytes) {
     if (rc == AH_OK) rc = dalloc(m, p, bytes);
@@ -1387,6 +1389,97 @@ int ah_model_destroy(AhModel* m) {
   return AH_OK;
 }
 
+}  // extern "C"
+
+namespace {
+// One projection's source: Q4_0 blocks, or the engine format that quantize()
+// returns (quantization.rs:369-404: f32 scale per 32-column group, packed
+// nibbles with the even element in the low nibble).
+enum ProjFormat : int { kProjQ4_0 = 0, kProjEngine = 1 };
+struct ProjSrc {
+  int fmt;
+  const void* q4;
+  const float* scales;
+  const uint8_t* packed;
+};
+
+size_t proj_scale_bytes(int64_t rows, int64_t cols) { return (size_t)rows * (cols / 32) * 4; }
+size_t proj_bytes(int fmt, int64_t rows, int64_t cols) {
+  return fmt == kProjQ4_0 ? (size_t)rows * (cols / 32) * 18 : proj_scale_bytes(rows, cols) + (size_t)rows * cols / 2;
+}
+
+// Loads (or replaces) one projection.  o, down and the LM head are repacked at
+// once; q/k/v and gate/up wait in staging until their group is complete, then
+// become one fused weight (q|k|v stacked, gate/up interleaved by 8 rows).  The
+// parts of a group must share a format.
+int load_projection(AhModel* m, int kind, int layer, const ProjSrc& src, cudaStream_t st) {
+  const int d = m->c.n_embd;
+  auto direct = [&](AhQ4Weight*& w, int64_t rows, int64_t cols) -> int {
+    if (w) ah_q4w_destroy(w);
+    w = nullptr;
+    if (src.fmt == kProjQ4_0) return ah_q4w_from_q4_0(src.q4, rows, cols, &w, st);
+    return ah_q4w_from_engine(src.scales, src.packed, rows, cols, &w, st);
+  };
+  if (kind == AH_T_WO) return direct(m->wo[layer], d, m->dq);
+  if (kind == AH_T_WDOWN) return direct(m->wd[layer], d, m->nff);
+  if (kind == AH_T_LM_HEAD) return direct(m->lm, m->nvoc, d);
+  const int slot = kind == AH_T_WQ ? 0 : kind == AH_T_WK ? 1 : kind == AH_T_WV ? 2 : kind == AH_T_WGATE ? 3 : 4;
+  const int64_t rows = slot == 0 ? m->dq : slot <= 2 ? m->dkv : m->nff;
+  void*& p = m->pend[slot][layer];
+  if (p && m->pend_fmt[slot][layer] != src.fmt) {
+    cudaFree(p);
+    p = nullptr;
+  }
+  if (!p && cudaMalloc(&p, proj_bytes(src.fmt, rows, d)) != cudaSuccess) {
+    cudaGetLastError();
+    p = nullptr;
+    return fail(AH_ENOMEM, "model_load_tensor: staging of %zu bytes", proj_bytes(src.fmt, rows, d));
+  }
+  m->pend_fmt[slot][layer] = src.fmt;
+  if (src.fmt == kProjQ4_0) {
+    AH_CUDA_TRY(cudaMemcpyAsync(p, src.q4, proj_bytes(src.fmt, rows, d), cudaMemcpyDeviceToDevice, st));
+  } else {
+    const size_t sb = proj_scale_bytes(rows, d);
+    AH_CUDA_TRY(cudaMemcpyAsync(p, src.scales, sb, cudaMemcpyDeviceToDevice, st));
+    AH_CUDA_TRY(cudaMemcpyAsync(static_cast<uint8_t*>(p) + sb, src.packed, (size_t)rows * d / 2,
+                                cudaMemcpyDeviceToDevice, st));
+  }
+  const bool qkv = slot <= 2;
+  const int k0 = qkv ? 0 : 3, nsrc = qkv ? 3 : 2;
+  for (int k = k0; k < k0 + nsrc; ++k)
+    if (!m->pend[k][layer]) return AH_OK;  // the group is not complete yet
+  for (int k = k0; k < k0 + nsrc; ++k)
+    AH_REQUIRE(m->pend_fmt[k][layer] == src.fmt, "model_load_tensor: %s of layer %d mix Q4_0 and engine formats",
+               qkv ? "q, k and v" : "gate and up", layer);
+  const int64_t rws[3] = {qkv ? m->dq : m->nff, qkv ? m->dkv : m->nff, m->dkv};
+  AhQ4Weight*& w = qkv ? m->wqkv[layer] : m->wgu[layer];
+  if (w) ah_q4w_destroy(w);
+  w = nullptr;
+  if (src.fmt == kProjQ4_0) {
+    const void* srcs[3] = {m->pend[k0][layer], m->pend[k0 + 1][layer], qkv ? m->pend[2][layer] : nullptr};
+    AH_TRY(q4w_create_q4_0_multi(srcs, rws, nsrc, qkv ? 0 : 1, d, &w, st));
+  } else {
+    const float* sc[3] = {};
+    const uint8_t* pk[3] = {};
+    for (int k = 0; k < nsrc; ++k) {
+      sc[k] = static_cast<const float*>(m->pend[k0 + k][layer]);
+      pk[k] = static_cast<const uint8_t*>(m->pend[k0 + k][layer]) + proj_scale_bytes(rws[k], d);
+    }
+    AH_TRY(q4w_create_engine_multi(sc, pk, rws, nsrc, qkv ? 0 : 1, d, &w, st));
+  }
+  AH_CUDA_TRY(cudaStreamSynchronize(st));
+  for (int k = k0; k < k0 + nsrc; ++k) {
+    cudaFree(m->pend[k][layer]);
+    m->pend[k][layer] = nullptr;
+  }
+  return AH_OK;
+}
+
+bool is_projection(int kind) { return kind >= AH_T_WQ && kind <= AH_T_LM_HEAD; }
+}  // namespace
+
+extern "C" {
+
 int ah_model_load_tensor(AhModel* m, int kind, int layer, const void* data, void* stream) {
   AH_REQUIRE(m && data, "model_load_tensor: null argument");
   const AhModelConfig& c = m->c;
@@ -1394,7 +1487,6 @@ int ah_model_load_tensor(AhModel* m, int kind, int layer, const void* data, void
   cudaStream_t st = as_stream(stream);
   const bool per_layer = !(kind == AH_T_TOK_EMBD || kind == AH_T_OUT_NORM || kind == AH_T_LM_HEAD);
   AH_REQUIRE(!per_layer || (layer >= 0 && layer < c.n_layer), "model_load_tensor: layer %d out of range", layer);
-  auto q4_bytes = [](int64_t rows, int64_t cols) { return (size_t)rows * (cols / 32) * 18; };
   switch (kind) {
     case AH_T_TOK_EMBD:
       AH_CUDA_TRY(cudaMemcpyAsync(m->tok_embd, data, (size_t)c.vocab_size * d * 2, cudaMemcpyDeviceToDevice, st));
@@ -1408,58 +1500,68 @@ int ah_model_load_tensor(AhModel* m, int kind, int layer, const void* data, void
     case AH_T_OUT_NORM:
       AH_CUDA_TRY(cudaMemcpyAsync(m->out_norm, data, (size_t)d * 2, cudaMemcpyDeviceToDevice, st));
       return AH_OK;
-    case AH_T_WO:
-      if (m->wo[layer]) ah_q4w_destroy(m->wo[layer]);
-      m->wo[layer] = nullptr;
-      return ah_q4w_from_q4_0(data, d, m->dq, &m->wo[layer], stream);
-    case AH_T_WDOWN:
-      if (m->wd[layer]) ah_q4w_destroy(m->wd[layer]);
-      m->wd[layer] = nullptr;
-      return ah_q4w_from_q4_0(data, d, m->nff, &m->wd[layer], stream);
-    case AH_T_LM_HEAD:
-      if (m->lm) ah_q4w_destroy(m->lm);
-      m->lm = nullptr;
-      return ah_q4w_from_q4_0(data, m->nvoc, d, &m->lm, stream);
-    case AH_T_WQ: case AH_T_WK: case AH_T_WV: case AH_T_WGATE: case AH_T_WUP: {
-      const int slot = kind == AH_T_WQ ? 0 : kind == AH_T_WK ? 1 : kind == AH_T_WV ? 2 : kind == AH_T_WGATE ? 3 : 4;
-      const int64_t rows = slot == 0 ? m->dq : slot <= 2 ? m->dkv : m->nff;
-      const size_t bytes = q4_bytes(rows, d);
-      void*& p = m->pend[slot][layer];
-      if (!p && cudaMalloc(&p, bytes) != cudaSuccess) {
-        cudaGetLastError();
-        p = nullptr;
-        return fail(AH_ENOMEM, "model_load_tensor: staging of %zu bytes", bytes);
-      }
-      AH_CUDA_TRY(cudaMemcpyAsync(p, data, bytes, cudaMemcpyDeviceToDevice, st));
-      if (slot <= 2 && m->pend[0][layer] && m->pend[1][layer] && m->pend[2][layer]) {
-        const void* srcs[3] = {m->pend[0][layer], m->pend[1][layer], m->pend[2][layer]};
-        const int64_t rws[3] = {m->dq, m->dkv, m->dkv};
-        if (m->wqkv[layer]) ah_q4w_destroy(m->wqkv[layer]);
-        m->wqkv[layer] = nullptr;
-        AH_TRY(q4w_create_q4_0_multi(srcs, rws, 3, 0, d, &m->wqkv[layer], st));
-        AH_CUDA_TRY(cudaStreamSynchronize(st));
-        for (int k = 0; k < 3; ++k) {
-          cudaFree(m->pend[k][layer]);
-          m->pend[k][layer] = nullptr;
-        }
-      }
-      if (slot >= 3 && m->pend[3][layer] && m->pend[4][layer]) {
-        const void* srcs[2] = {m->pend[3][layer], m->pend[4][layer]};
-        const int64_t rws[2] = {m->nff, m->nff};
-        if (m->wgu[layer]) ah_q4w_destroy(m->wgu[layer]);
-        m->wgu[layer] = nullptr;
-        AH_TRY(q4w_create_q4_0_multi(srcs, rws, 2, 1, d, &m->wgu[layer], st));
-        AH_CUDA_TRY(cudaStreamSynchronize(st));
-        for (int k = 3; k < 5; ++k) {
-          cudaFree(m->pend[k][layer]);
-          m->pend[k][layer] = nullptr;
-        }
-      }
-      return AH_OK;
+    case AH_T_WO: case AH_T_WDOWN: case AH_T_LM_HEAD: case AH_T_WQ: case AH_T_WK: case AH_T_WV: case AH_T_WGATE:
+    case AH_T_WUP: {
+      ProjSrc src{};
+      src.fmt = kProjQ4_0;
+      src.q4 = data;
+      return load_projection(m, kind, layer, src, st);
     }
     default:
       return fail(AH_EINVAL, "model_load_tensor: unknown kind %d", kind);
   }
+}
+
+int ah_model_load_tensor_engine(AhModel* m, int kind, int layer, const float* scales, const uint8_t* packed,
+                                void* stream) {
+  AH_REQUIRE(m && scales && packed, "model_load_tensor_engine: null argument");
+  AH_REQUIRE(is_projection(kind), "model_load_tensor_engine: kind %d is not a projection", kind);
+  AH_REQUIRE(kind == AH_T_LM_HEAD || (layer >= 0 && layer < m->c.n_layer),
+             "model_load_tensor_engine: layer %d out of range", layer);
+  ProjSrc src{};
+  src.fmt = kProjEngine;
+  src.scales = scales;
+  src.packed = packed;
+  return load_projection(m, kind, layer, src, as_stream(stream));
+}
+
+int ah_model_load_tensor_f32(AhModel* m, int kind, int layer, const float* data, void* stream) {
+  AH_REQUIRE(m && data, "model_load_tensor_f32: null argument");
+  const AhModelConfig& c = m->c;
+  const int d = c.n_embd;
+  const bool per_layer = !(kind == AH_T_TOK_EMBD || kind == AH_T_OUT_NORM || kind == AH_T_LM_HEAD);
+  AH_REQUIRE(!per_layer || (layer >= 0 && layer < c.n_layer), "model_load_tensor_f32: layer %d out of range", layer);
+  if (!is_projection(kind)) {  // embeddings and norms are held as f16 (round to nearest even)
+    uint16_t* dst = kind == AH_T_TOK_EMBD    ? m->tok_embd
+                    : kind == AH_T_ATTN_NORM ? m->attn_norm + (size_t)layer * d
+                    : kind == AH_T_FFN_NORM  ? m->ffn_norm + (size_t)layer * d
+                    : kind == AH_T_OUT_NORM  ? m->out_norm
+                                             : nullptr;
+    AH_REQUIRE(dst, "model_load_tensor_f32: unknown kind %d", kind);
+    return ah_f32_to_f16(data, dst, kind == AH_T_TOK_EMBD ? (int64_t)c.vocab_size * d : d, stream);
+  }
+  // quantize() with group 32 (inference/mod.rs:267), then the engine-format load
+  const int64_t rows = kind == AH_T_WQ || kind == AH_T_WO ? (kind == AH_T_WQ ? m->dq : d)
+                       : kind == AH_T_WK || kind == AH_T_WV ? m->dkv
+                       : kind == AH_T_WGATE || kind == AH_T_WUP ? m->nff
+                       : kind == AH_T_LM_HEAD ? m->nvoc
+                                              : d;
+  const int64_t cols = kind == AH_T_WO ? m->dq : kind == AH_T_WDOWN ? m->nff : d;
+  const int64_t n = rows * cols;
+  float* sc = nullptr;
+  uint8_t* pk = nullptr;
+  if (cudaMalloc(&sc, (size_t)(n / 32) * 4) != cudaSuccess || cudaMalloc(&pk, (size_t)n / 2) != cudaSuccess) {
+    cudaGetLastError();
+    if (sc) cudaFree(sc);
+    return fail(AH_ENOMEM, "model_load_tensor_f32: quantization buffers of %lld elements", (long long)n);
+  }
+  int rc = ah_quantize_q4(data, n, 32, sc, pk, stream);
+  if (rc == AH_OK) rc = ah_model_load_tensor_engine(m, kind, layer, sc, pk, stream);
+  if (rc == AH_OK && cudaStreamSynchronize(as_stream(stream)) != cudaSuccess)
+    rc = fail(AH_ECUDA, "model_load_tensor_f32: %s", cudaGetErrorString(cudaGetLastError()));
+  cudaFree(sc);
+  cudaFree(pk);
+  return rc;
 }
 
 int ah_model_init_random(AhModel* m, uint64_t seed, float w_std, float emb_std, float norm_std) {

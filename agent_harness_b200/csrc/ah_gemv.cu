@@ -196,6 +196,26 @@ int q4w_create_q4_0_multi(const void* const* srcs, const int64_t* src_rows, int 
   return q4w_create(s, false, rows, cols, out, st);
 }
 
+int q4w_create_engine_multi(const float* const* scales, const uint8_t* const* packed, const int64_t* src_rows,
+                            int nsrc, int mode, int64_t cols, AhQ4Weight** out, cudaStream_t st) {
+  AH_REQUIRE(nsrc >= 1 && nsrc <= 3, "q4w_create: 1..3 sources");
+  RowSource s{};
+  s.mode = mode;
+  int64_t rows = 0;
+  for (int k = 0; k < nsrc; ++k) {
+    AH_REQUIRE(scales[k] != nullptr && packed[k] != nullptr && src_rows[k] > 0, "q4w_create: null source");
+    s.eng_s[k] = scales[k];
+    s.eng_p[k] = packed[k];
+    s.rows[k] = src_rows[k];
+    rows += src_rows[k];
+  }
+  if (mode == 1) {
+    AH_REQUIRE(nsrc == 2 && src_rows[0] == src_rows[1] && src_rows[0] % 8 == 0,
+               "q4w_create: interleave needs two sources of equal rows, rows %% 8 == 0");
+  }
+  return q4w_create(s, true, rows, cols, out, st);
+}
+
 const Q4Tiled& q4w_tiled(const AhQ4Weight* w) { return w->t; }
 uint4* q4w_nib_mut(AhQ4Weight* w) { return static_cast<uint4*>(w->nib_alloc); }
 void* q4w_scales_mut(AhQ4Weight* w) { return w->scale_alloc; }
@@ -699,19 +719,25 @@ using GemvKernel = void (*)(const GemvArgs);
     if (_rc != AH_OK) return _rc; \
   } while (0)
 
+// Every prologue / epilogue for both scale formats: Q4_0 blocks (f16 scales)
+// and the engine format of quantize() (f32 scales).
+template <int NT, bool kRows, bool F>
+GemvKernel pick_format(int pro, int epi) {
+#define AH_K(P, E) (kRows ? k_gemv_q4_rows<NT, F, P, E> : k_gemv_q4<NT, F, P, E>)
+  if (pro == kProPlain) {
+    if (epi == kEpiStore) return AH_K(kProPlain, kEpiStore);
+    if (epi == kEpiAdd) return AH_K(kProPlain, kEpiAdd);
+    return AH_K(kProPlain, kEpiSwiglu);
+  }
+  if (epi == kEpiStore) return AH_K(kProRmsNorm, kEpiStore);
+  if (epi == kEpiAdd) return AH_K(kProRmsNorm, kEpiAdd);
+  return AH_K(kProRmsNorm, kEpiSwiglu);
+#undef AH_K
+}
+
 template <int NT, bool kRows>
 GemvKernel pick_kernel(bool f32s, int pro, int epi) {
-#define AH_K(F, P, E) (kRows ? k_gemv_q4_rows<NT, F, P, E> : k_gemv_q4<NT, F, P, E>)
-  if (f32s) return (pro == kProPlain && epi == kEpiStore) ? AH_K(true, kProPlain, kEpiStore) : nullptr;
-  if (pro == kProPlain) {
-    if (epi == kEpiStore) return AH_K(false, kProPlain, kEpiStore);
-    if (epi == kEpiAdd) return AH_K(false, kProPlain, kEpiAdd);
-    return AH_K(false, kProPlain, kEpiSwiglu);
-  }
-  if (epi == kEpiStore) return AH_K(false, kProRmsNorm, kEpiStore);
-  if (epi == kEpiAdd) return AH_K(false, kProRmsNorm, kEpiAdd);
-  return AH_K(false, kProRmsNorm, kEpiSwiglu);
-#undef AH_K
+  return f32s ? pick_format<NT, kRows, true>(pro, epi) : pick_format<NT, kRows, false>(pro, epi);
 }
 
 }  // namespace
@@ -808,7 +834,7 @@ int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, G
     return fail(AH_EUNSUPPORTED, "gemv: batch %d x %lld columns needs %zu B of shared memory per CTA (limit %d)",
                 batch, (long long)w.cols, pc.smem, kGemvSmemLimit);
   GemvKernel kc = select_kernel(pc, w.f32_scales, pro, epi);
-  if (!kc) return fail(AH_EUNSUPPORTED, "gemv: engine-format weights support only the plain GEMV");
+  if (!kc) return fail(AH_EUNSUPPORTED, "gemv: no kernel for prologue %d / epilogue %d", pro, epi);
   int ccap = 0;
   AH_TRY_GEMV(kernel_setup(kc, pc, &ccap));
   const int64_t n_rg = (w.r16 + kGemvWarps - 1) / kGemvWarps;

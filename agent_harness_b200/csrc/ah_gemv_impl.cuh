@@ -34,5 +34,9 @@ uint4* q4w_nib_mut(AhQ4Weight* w);
 void* q4w_scales_mut(AhQ4Weight* w);
 int q4w_create_q4_0_multi(const void* const* srcs, const int64_t* src_rows, int nsrc, int mode, int64_t cols,
                           AhQ4Weight** out, cudaStream_t st);
+// The same from engine-format sources (quantize() output: f32 scales per
+// 32-column group, packed nibbles, low nibble first).
+int q4w_create_engine_multi(const float* const* scales, const uint8_t* const* packed, const int64_t* src_rows,
+                            int nsrc, int mode, int64_t cols, AhQ4Weight** out, cudaStream_t st);
 
 }  // namespace ah

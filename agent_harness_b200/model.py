@@ -118,6 +118,17 @@ class Model:
     def load_tensor(self, kind: int, layer: int, data: torch.Tensor):
         call("ah_model_load_tensor", self._h, kind, layer, C.c_void_p(data.data_ptr()), self._stream())
 
+    def load_tensor_engine(self, kind: int, layer: int, scales: torch.Tensor, packed: torch.Tensor):
+        """A projection in quantize()'s engine format (f32 group-32 scales, packed nibbles)."""
+        call("ah_model_load_tensor_engine", self._h, kind, layer, C.c_void_p(scales.data_ptr()),
+             C.c_void_p(packed.data_ptr()), self._stream())
+
+    def load_tensor_f32(self, kind: int, layer: int, data: torch.Tensor):
+        """An f32 tensor: projections are quantized on the device (engine format),
+        embeddings and norms stored as f16."""
+        assert data.dtype == torch.float32 and data.is_cuda and data.is_contiguous()
+        call("ah_model_load_tensor_f32", self._h, kind, layer, C.c_void_p(data.data_ptr()), self._stream())
+
     def reset(self, batch: int = 1):
         call("ah_model_reset", self._h, batch, self._stream())
 

@@ -227,6 +227,19 @@ AH_API int ah_model_create_tp(const AhModelConfig* cfg, int rank, int world, con
  * in rank order.  Ranks must be processes on GPUs with peer access. */
 AH_API int ah_model_ipc_handle(AhModel* m, void* handle_out, size_t bytes);
 AH_API int ah_model_ipc_open(AhModel* m, const void* handles, size_t bytes);
+/* Loads a projection (AH_T_WQ .. AH_T_LM_HEAD) in the engine format that
+ * models/quantization.rs:369-404 quantize(weights, 32) returns: scales_dev
+ * [rows * cols / 32] f32 and packed_dev [rows * cols / 2] (even element in the
+ * low nibble), as inference/mod.rs:255-271 writes them per tensor.  The GEMVs
+ * then run on f32 scales (inference/math.rs:255-418 arithmetic).  q/k/v and
+ * gate/up of a layer must share one format. */
+AH_API int ah_model_load_tensor_engine(AhModel* m, int kind, int layer, const float* scales_dev,
+                                       const uint8_t* packed_dev, void* stream);
+/* Loads an f32 tensor as the reference's loader does (inference/mod.rs:255-271):
+ * projections are quantized on the device with quantize(weights, 32) and
+ * loaded in the engine format; embeddings and norms are stored as f16 (round
+ * to nearest even), the decoder's storage for them. */
+AH_API int ah_model_load_tensor_f32(AhModel* m, int kind, int layer, const float* data_dev, void* stream);
 /* This rank's shard: heads, kv heads, FFN rows and vocab rows it holds. */
 AH_API int ah_model_shard(const AhModel* m, int* rank, int* world, int* n_head, int* n_head_kv, int* n_ff,
                           int* vocab);

@@ -511,7 +511,21 @@ typedef struct {
     uint16_t* v_cache;
     float* k_cache_f32;              /* the same rows as f32 (or_f16_to_f32 of the stored bits), */
     float* v_cache_f32;              /* converted once at append instead of at every read */
+    int64_t engine;                  /* 0: projections are Q4_0 blocks; 1: each points at quantize()'s
+                                      * output, scales [rows*cols/32] f32 then packed [rows*cols/2] */
 } or_model;
+
+/* y = W x for one projection in the model's format: Q4_0 blocks, or the
+ * engine format through the scalar gemv_4bit worker (inference/math.rs:382-418). */
+static void model_mv(const or_model* m, float* out, const uint8_t* w, const float* x, int64_t rows, int64_t cols) {
+    if (!m->engine) {
+        or_gemv_q4_0(out, w, x, rows, cols);
+        return;
+    }
+    const float* scales = (const float*)w;
+    const uint8_t* packed = w + (size_t)rows * (cols / 32) * 4;
+    or_gemv_4bit_worker_scalar(out, scales, packed, x, 0, rows, cols, 32);
+}
 
 static void f16_row(const uint16_t* src, float* dst, int64_t n) { for (int64_t i = 0; i < n; ++i) dst[i] = or_f16_to_f32(src[i]); }
 
@@ -537,9 +551,9 @@ OR_API int or_model_forward(const or_model* m, int32_t token, int64_t pos, float
     for (int64_t il = 0; il < m->n_layer; ++il) {
         f16_row(m->attn_norm + il * d, nw, d);
         or_rms_norm_into(normed, hidden, nw, d, m->eps);
-        or_gemv_q4_0(q, m->wq[il], normed, dq, d);
-        or_gemv_q4_0(k, m->wk[il], normed, dkv, d);
-        or_gemv_q4_0(v, m->wv[il], normed, dkv, d);
+        model_mv(m, q, m->wq[il], normed, dq, d);
+        model_mv(m, k, m->wk[il], normed, dkv, d);
+        model_mv(m, v, m->wv[il], normed, dkv, d);
         for (int64_t h = 0; h < nh; ++h) or_rope_multi(q + h * hd, hd, pos, sections, m->rope_base);
         for (int64_t h = 0; h < nkv; ++h) or_rope_multi(k + h * hd, hd, pos, sections, m->rope_base);
         uint16_t* kc = m->k_cache + il * nkv * m->max_seq * hd;
@@ -580,19 +594,19 @@ OR_API int or_model_forward(const or_model* m, int32_t token, int64_t pos, float
             }
             for (int64_t e = 0; e < hd; ++e) acc[e] *= inv;
         }
-        or_gemv_q4_0(tmp, m->wo[il], att, d, dq);
+        model_mv(m, tmp, m->wo[il], att, d, dq);
         for (int64_t i = 0; i < d; ++i) hidden[i] += tmp[i];
         f16_row(m->ffn_norm + il * d, nw, d);
         or_rms_norm_into(normed, hidden, nw, d, m->eps);
-        or_gemv_q4_0(g, m->wg[il], normed, ff, d);
-        or_gemv_q4_0(u, m->wu[il], normed, ff, d);
+        model_mv(m, g, m->wg[il], normed, ff, d);
+        model_mv(m, u, m->wu[il], normed, ff, d);
         for (int64_t i = 0; i < ff; ++i) g[i] = or_silu(g[i]) * u[i];
-        or_gemv_q4_0(tmp, m->wd[il], g, d, ff);
+        model_mv(m, tmp, m->wd[il], g, d, ff);
         for (int64_t i = 0; i < d; ++i) hidden[i] += tmp[i];
     }
     f16_row(m->out_norm, nw, d);
     or_rms_norm_into(normed, hidden, nw, d, m->eps);
-    or_gemv_q4_0(logits, m->lm_head, normed, m->vocab, d);
+    model_mv(m, logits, m->lm_head, normed, m->vocab, d);
     free(hidden); free(normed); free(nw); free(q); free(k); free(v); free(att); free(tmp); free(g); free(u); free(scores);
     return 0;
 }

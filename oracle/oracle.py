@@ -360,7 +360,7 @@ class _OrModel(C.Structure):
         ("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
         ("wg", C.c_void_p), ("wu", C.c_void_p), ("wd", C.c_void_p),
         ("lm_head", C.c_void_p), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p),
-        ("k_cache_f32", C.c_void_p), ("v_cache_f32", C.c_void_p),
+        ("k_cache_f32", C.c_void_p), ("v_cache_f32", C.c_void_p), ("engine", i64),
     ]
 
 
@@ -368,10 +368,12 @@ class OracleModel:
     """Host-side decoder oracle over Q4_0 blocks (inference/mod.rs:333-545).
 
     `weights` is a dict with numpy arrays: tok_embd/attn_norm/ffn_norm/out_norm
-    (uint16 f16 bits) and per-layer lists wq..wd plus lm_head (uint8 Q4_0 blocks).
+    (uint16 f16 bits) and per-layer lists wq..wd plus lm_head: uint8 Q4_0
+    blocks, or with engine=True quantize()'s output as one uint8 blob per
+    matrix (f32 scales [rows*cols/32] then packed [rows*cols/2]).
     """
 
-    def __init__(self, cfg: dict, weights: dict, max_seq: int):
+    def __init__(self, cfg: dict, weights: dict, max_seq: int, engine: bool = False):
         self.cfg = cfg
         self._keep = []
         L = cfg["n_layer"]
@@ -398,7 +400,7 @@ class OracleModel:
                           ptrs(weights["wq"]), ptrs(weights["wk"]), ptrs(weights["wv"]), ptrs(weights["wo"]),
                           ptrs(weights["wg"]), ptrs(weights["wu"]), ptrs(weights["wd"]),
                           ptr(weights["lm_head"]), self.k_cache.ctypes.data, self.v_cache.ctypes.data,
-                          self.k_cache_f32.ctypes.data, self.v_cache_f32.ctypes.data)
+                          self.k_cache_f32.ctypes.data, self.v_cache_f32.ctypes.data, 1 if engine else 0)
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         logits = np.empty(self.cfg["vocab"], np.float32)

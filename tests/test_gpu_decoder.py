@@ -139,3 +139,101 @@ def test_long_context_attention_splits(cuda, oracle, shape):
             if t in check:
                 assert relerr(logits[b], ref) <= TOL, (t, b, relerr(logits[b], ref))
     m.close()
+
+
+def _engine_weights(oracle, cfg, seed):
+    """f32 projections (N(0, 0.05)) and their quantize(w, 32) engine blobs, f16
+    embeddings and norms; returns (f32 tensors, oracle weight dict)."""
+    rng = np.random.default_rng(seed)
+    d, L = cfg.n_embd, cfg.n_layer
+    dq, dkv = cfg.n_head * cfg.head_dim, cfg.n_head_kv * cfg.head_dim
+    shapes = {"wq": (dq, d), "wk": (dkv, d), "wv": (dkv, d), "wo": (d, dq), "wg": (cfg.n_ff, d),
+              "wu": (cfg.n_ff, d), "wd": (d, cfg.n_ff)}
+
+    def engine(w):
+        n = w.size
+        sc, pk = np.empty(n // 32, np.float32), np.empty(n // 2, np.uint8)
+        oracle.lib().or_quantize_q4(np.ascontiguousarray(w.ravel()), n, 32, sc, pk)
+        return np.concatenate([sc.view(np.uint8), pk])
+
+    def f16(n, mean, std):
+        return (mean + std * rng.standard_normal(n)).astype(np.float16)
+
+    F = {"tok_embd": f16(cfg.vocab_size * d, 0.0, 1.0), "out_norm": f16(d, 1.0, 0.02),
+         "attn_norm": [f16(d, 1.0, 0.02) for _ in range(L)], "ffn_norm": [f16(d, 1.0, 0.02) for _ in range(L)]}
+    W = {"tok_embd": F["tok_embd"].view(np.uint16), "out_norm": F["out_norm"].view(np.uint16),
+         "attn_norm": np.concatenate(F["attn_norm"]).view(np.uint16),
+         "ffn_norm": np.concatenate(F["ffn_norm"]).view(np.uint16)}
+    for name, (r, c) in shapes.items():
+        F[name] = [(rng.standard_normal((r, c)) * 0.05).astype(np.float32) for _ in range(L)]
+        W[name] = [engine(w) for w in F[name]]
+    F["lm_head"] = (rng.standard_normal((cfg.vocab_size, d)) * 0.05).astype(np.float32)
+    W["lm_head"] = engine(F["lm_head"])
+    return F, W
+
+
+def test_engine_format_decoder(cuda, oracle):
+    # A model loaded the reference's way (inference/mod.rs:255-271): projections
+    # in quantize()'s engine format, f32 group scales.  Loaded from the engine
+    # blobs it matches the oracle decoder on the same weights; loaded from the
+    # f32 tensors (quantized on the device) it is bit-identical to that model.
+    from agent_harness_b200 import model as M
+    cfg = M.ModelConfig(**SMALL)
+    F, W = _engine_weights(oracle, cfg, 21)
+    kinds = {"wq": M.WQ, "wk": M.WK, "wv": M.WV, "wo": M.WO, "wg": M.WGATE, "wu": M.WUP, "wd": M.WDOWN}
+    dev = torch.device("cuda")
+
+    def bits(a):
+        return torch.as_tensor(np.ascontiguousarray(a).view(np.int16)).to(dev)
+
+    def f32(a):
+        return torch.as_tensor(np.ascontiguousarray(a, np.float32)).to(dev)
+
+    models = []
+    for mode in ("engine", "f32"):
+        m = M.Model(cfg)
+        if mode == "engine":
+            m.load_tensor(M.TOK_EMBD, 0, bits(F["tok_embd"]))
+            m.load_tensor(M.OUT_NORM, 0, bits(F["out_norm"]))
+        else:
+            m.load_tensor_f32(M.TOK_EMBD, 0, f32(F["tok_embd"]))
+            m.load_tensor_f32(M.OUT_NORM, 0, f32(F["out_norm"]))
+        for l in range(cfg.n_layer):
+            for key, kind in (("attn_norm", M.ATTN_NORM), ("ffn_norm", M.FFN_NORM)):
+                if mode == "engine":
+                    m.load_tensor(kind, l, bits(F[key][l]))
+                else:
+                    m.load_tensor_f32(kind, l, f32(F[key][l]))
+            for name, kind in kinds.items():
+                if mode == "engine":
+                    blob = W[name][l]
+                    n = F[name][l].size
+                    m.load_tensor_engine(kind, l, f32(blob[:n // 8].view(np.float32)),
+                                         torch.as_tensor(blob[n // 8:]).to(dev))
+                else:
+                    m.load_tensor_f32(kind, l, f32(F[name][l]))
+        if mode == "engine":
+            n = F["lm_head"].size
+            m.load_tensor_engine(M.LM_HEAD, 0, f32(W["lm_head"][:n // 8].view(np.float32)),
+                                 torch.as_tensor(W["lm_head"][n // 8:]).to(dev))
+        else:
+            m.load_tensor_f32(M.LM_HEAD, 0, f32(F["lm_head"]))
+        models.append(m)
+    c = {"n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_ff": cfg.n_ff, "n_head": cfg.n_head,
+         "n_head_kv": cfg.n_head_kv, "head_dim": cfg.head_dim, "vocab": cfg.vocab_size,
+         "rope_base": cfg.rope_freq_base, "eps": cfg.rms_eps}
+    om = [oracle.OracleModel(c, W, cfg.max_seq, engine=True) for _ in range(2)]
+    prompt = np.random.default_rng(9).integers(0, cfg.vocab_size, (2, 6)).astype(np.int32)
+    for m in models:
+        m.reset(2)
+    for t in range(prompt.shape[1]):
+        lg = [m.forward(prompt[:, t]).cpu().numpy() for m in models]
+        assert np.array_equal(lg[0], lg[1]), t
+        for b in range(2):
+            ref = om[b].forward(int(prompt[b, t]), t)
+            assert relerr(lg[0][b], ref) <= TOL, (t, b, relerr(lg[0][b], ref))
+            assert int(np.argmax(lg[0][b])) == oracle.argmax(ref)
+    gen = [m.generate(prompt, 6) for m in models]
+    assert np.array_equal(gen[0], gen[1])
+    for m in models:
+        m.close()
