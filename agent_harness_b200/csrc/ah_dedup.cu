@@ -90,16 +90,46 @@ struct DedupArgs {
   const float* tab;  // 2-D table
   int64_t np, nt;    // fallback row / column index
   float avg;
-  int strict;  // remap: a prefix index >= np is an error (the reference panics)
   int* err;
 };
 
+// Decode tables larger than this stay in global memory (L1 / L2 gathers);
+// smaller ones are staged in shared memory, where a warp's 32 random lookups
+// cost a few bank wavefronts instead of one L1 wavefront per distinct sector.
+constexpr int kSmemTableBytes = 64 * 1024;
+
+// The value tables a kernel reads: staged in shared memory (kSmem) or global.
+struct DedupTables {
+  const float* pre;
+  const float* tl;
+  const float* tab;
+};
+
+template <bool k2d, bool kSmem>
+__device__ __forceinline__ DedupTables stage_tables(const DedupArgs& a) {
+  if (!kSmem) return DedupTables{a.pre, a.tl, a.tab};
+  extern __shared__ float dsm[];
+  if (k2d) {
+    const int64_t n = (a.np + 1) * (a.nt + 1);
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) dsm[i] = __ldg(a.tab + i);
+    __syncthreads();
+    return DedupTables{nullptr, nullptr, dsm};
+  }
+  const int64_t n1 = a.np + 1, n2 = a.nt + 1;
+  for (int64_t i = threadIdx.x; i < n1; i += blockDim.x) dsm[i] = __ldg(a.pre + i);
+  for (int64_t i = threadIdx.x; i < n2; i += blockDim.x) dsm[n1 + i] = __ldg(a.tl + i);
+  __syncthreads();
+  return DedupTables{dsm, dsm + n1, nullptr};
+}
+
+// value = table lookup + avg_precision_lost, negated when `neg` (bit 0) is set.
+// Table indices fit 32 bits: at most 65536 + 1 per side and 2^26 entries.
 template <bool k2d>
-__device__ __forceinline__ float dedup_value(const DedupArgs& a, uint32_t p, uint32_t t) {
-  const int64_t pp = p < a.np ? (int64_t)p : a.np;
-  const int64_t tt = t < a.nt ? (int64_t)t : a.nt;
-  const float v = k2d ? __ldg(a.tab + pp * (a.nt + 1) + tt) : __fadd_rn(__ldg(a.pre + pp), __ldg(a.tl + tt));
-  return __fadd_rn(v, a.avg);  // value += avg_precision_lost
+__device__ __forceinline__ float dedup_value(const DedupArgs& a, const DedupTables& tb, uint32_t p, uint32_t t,
+                                             uint32_t neg) {
+  const uint32_t pp = min(p, (uint32_t)a.np), tt = min(t, (uint32_t)a.nt);
+  const float v = k2d ? tb.tab[pp * (uint32_t)(a.nt + 1) + tt] : __fadd_rn(tb.pre[pp], tb.tl[tt]);
+  return __uint_as_float(__float_as_uint(__fadd_rn(v, a.avg)) ^ (neg << 31));  // value += avg; -value
 }
 
 __device__ __forceinline__ void unpack4(uint2 u, uint32_t (&o)[4]) {
@@ -118,9 +148,10 @@ __device__ __forceinline__ void unpack8(uint4 u, uint32_t (&o)[8]) {
 }
 
 // decompress_all / _global / _with_remap: one thread per 8 elements (one sign byte).
-template <bool k2d>
+template <bool k2d, bool kSmem, bool kStrict>
 __global__ void __launch_bounds__(kThreads) k_dedup_decompress(const DedupArgs a, int64_t count,
                                                                float* __restrict__ out, int vec) {
+  const DedupTables tb = stage_tables<k2d, kSmem>(a);
   const int64_t n8 = (count + 7) / 8;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t g8 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g8 < n8; g8 += stride) {
@@ -142,9 +173,8 @@ __global__ void __launch_bounds__(kThreads) k_dedup_decompress(const DedupArgs a
     float o[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float v = dedup_value<k2d>(a, p[k], t[k]);
-      o[k] = (sb >> k) & 1u ? -v : v;
-      if (a.strict && i0 + k < count && p[k] >= (uint32_t)a.np) atomicExch(a.err, kErrPrefixIndex);
+      o[k] = dedup_value<k2d>(a, tb, p[k], t[k], (sb >> k) & 1u);
+      if (kStrict && i0 + k < count && p[k] >= (uint32_t)a.np) atomicExch(a.err, kErrPrefixIndex);
     }
     if (vec && i0 + 8 <= count) {
       reinterpret_cast<float4*>(out + i0)[0] = make_float4(o[0], o[1], o[2], o[3]);
@@ -199,10 +229,11 @@ __device__ __forceinline__ Q4wItem q4w_load(const DedupArgs& a, int64_t it, int6
   return x;
 }
 
-template <bool k2d>
+template <bool k2d, bool kSmem, bool kStrict>
 __global__ void __launch_bounds__(kThreads) k_dedup_q4w(const DedupArgs a, uint32_t* __restrict__ nib,
                                                         float* __restrict__ scales, int64_t rows, int64_t cols,
                                                         int64_t r16, int64_t kp) {
+  const DedupTables tb = stage_tables<k2d, kSmem>(a);
   const int lane = threadIdx.x & 31, sub = lane >> 2, l4 = lane & 3;
   const int64_t quads = (2 * kp + 7) / 8;  // 8-block groups per row (blocks past 2 kp are skipped)
   const int64_t items = r16 * 16 * quads;
@@ -218,9 +249,8 @@ __global__ void __launch_bounds__(kThreads) k_dedup_q4w(const DedupArgs a, uint3
     unpack8(cur.t, t);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float val = cur.live ? dedup_value<k2d>(a, p[k], t[k]) : 0.0f;
-      v[k] = (cur.sb >> k) & 1u ? -val : val;
-      if (a.strict && cur.live && p[k] >= (uint32_t)a.np) atomicExch(a.err, kErrPrefixIndex);
+      v[k] = cur.live ? dedup_value<k2d>(a, tb, p[k], t[k], (cur.sb >> k) & 1u) : 0.0f;
+      if (kStrict && cur.live && p[k] >= (uint32_t)a.np) atomicExch(a.err, kErrPrefixIndex);
     }
     // quantise the 32-element group (quantization.rs:369-404): scale = max|w| / 7,
     // q = clamp(round(w * (1 / scale)), -8, 7) + 8
@@ -254,6 +284,51 @@ __global__ void __launch_bounds__(kThreads) k_dedup_q4w(const DedupArgs a, uint3
     }
     cur = nxt;
   }
+}
+
+// Shared-memory bytes of the table staging, or 0 when the tables stay global.
+size_t table_smem_bytes(const AhDedupTable* t) {
+  const size_t n = t->mode == kLocal ? (size_t)(t->n_prefix + 1) + (size_t)(t->n_tail + 1)
+                                     : (size_t)(t->n_prefix + 1) * (size_t)(t->n_tail + 1);
+  return n * 4 <= (size_t)kSmemTableBytes ? n * 4 : 0;
+}
+
+template <typename K>
+int allow_smem(K kern, size_t bytes) {
+  AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return AH_OK;
+}
+
+// The kernel variant for a table: 1-D (local) or 2-D lookups, staged in shared
+// memory when small enough, with the prefix-index check only for remap tables.
+struct DecompressKernel {
+  template <bool k2d, bool kSmem, bool kStrict>
+  static auto get() { return k_dedup_decompress<k2d, kSmem, kStrict>; }
+};
+struct Q4wKernel {
+  template <bool k2d, bool kSmem, bool kStrict>
+  static auto get() { return k_dedup_q4w<k2d, kSmem, kStrict>; }
+};
+
+template <typename KS, bool k2d, bool kSmem, bool kStrict, typename... Args>
+int launch_variant(size_t smem, int grid, cudaStream_t st, Args... args) {
+  auto kern = KS::template get<k2d, kSmem, kStrict>();
+  if (kSmem) AH_TRY_DEDUP(allow_smem(kern, smem));
+  kern<<<grid, kThreads, kSmem ? smem : 0, st>>>(args...);
+  return AH_OK;
+}
+
+template <typename KS, typename... Args>
+int launch_table_kernel(const AhDedupTable* t, int grid, cudaStream_t st, Args... args) {
+  const size_t smem = table_smem_bytes(t);
+  if (t->mode == kLocal)
+    return smem ? launch_variant<KS, false, true, false>(smem, grid, st, args...)
+                : launch_variant<KS, false, false, false>(smem, grid, st, args...);
+  if (t->mode == kGlobal)
+    return smem ? launch_variant<KS, true, true, false>(smem, grid, st, args...)
+                : launch_variant<KS, true, false, false>(smem, grid, st, args...);
+  return smem ? launch_variant<KS, true, true, true>(smem, grid, st, args...)
+              : launch_variant<KS, true, false, true>(smem, grid, st, args...);
 }
 
 int grid_for(int64_t threads_needed) {
@@ -303,7 +378,6 @@ DedupArgs make_args(const AhDedupTable* t, const uint16_t* pidx, int64_t n_pidx,
   a.np = t->n_prefix;
   a.nt = t->n_tail;
   a.avg = t->avg;
-  a.strict = t->mode == kRemap ? 1 : 0;
   a.err = device_error_word();
   return a;
 }
@@ -470,10 +544,7 @@ int ah_dedup_decompress_f32(const AhDedupTable* t, const uint16_t* prefix_idx, i
   AH_REQUIRE(a.err, "dedup_decompress: device error word unavailable");
   const int vec = aligned16(prefix_idx) && aligned16(tail_idx) && aligned16(out);
   const int grid = grid_for((count + 7) / 8);
-  if (t->mode == kLocal)
-    k_dedup_decompress<false><<<grid, kThreads, 0, as_stream(stream)>>>(a, count, out, vec);
-  else
-    k_dedup_decompress<true><<<grid, kThreads, 0, as_stream(stream)>>>(a, count, out, vec);
+  AH_TRY_DEDUP(launch_table_kernel<DecompressKernel>(t, grid, as_stream(stream), a, count, out, vec));
   AH_LAUNCH_CHECK();
   return AH_OK;
 }
@@ -494,10 +565,7 @@ int ah_dedup_into_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, int64_t
   const int grid = grid_for(warps * 32);
   uint32_t* nib = reinterpret_cast<uint32_t*>(q4w_nib_mut(w));
   float* sc = static_cast<float*>(q4w_scales_mut(w));
-  if (t->mode == kLocal)
-    k_dedup_q4w<false><<<grid, kThreads, 0, as_stream(stream)>>>(a, nib, sc, rows, cols, tw.r16, tw.kp);
-  else
-    k_dedup_q4w<true><<<grid, kThreads, 0, as_stream(stream)>>>(a, nib, sc, rows, cols, tw.r16, tw.kp);
+  AH_TRY_DEDUP(launch_table_kernel<Q4wKernel>(t, grid, as_stream(stream), a, nib, sc, rows, cols, tw.r16, tw.kp));
   AH_LAUNCH_CHECK();
   return AH_OK;
 }
