@@ -21,6 +21,9 @@ struct AhQ4Weight {
   int64_t weight_bytes = 0;
   void* nib_alloc = nullptr;
   void* scale_alloc = nullptr;
+  // device staging for host-buffer calls (ah_q4w_gemv_host), allocated on the
+  // first such call for the largest batch; mu serialises those calls
+  void* stage = nullptr;
   std::mutex mu;
 };
 
@@ -1006,8 +1009,33 @@ int ah_q4w_destroy(AhQ4Weight* w) {
   cudaSetDevice(w->device);
   cudaFree(w->nib_alloc);
   cudaFree(w->scale_alloc);
+  if (w->stage) cudaFree(w->stage);
   cudaSetDevice(cur);
   delete w;
+  return AH_OK;
+}
+
+int ah_q4w_gemv_host(const AhQ4Weight* cw, const float* x_host, float* y_host, int batch, void* stream) {
+  AH_REQUIRE(cw && x_host && y_host, "q4w_gemv_host: null argument");
+  AH_REQUIRE(batch >= 1 && batch <= kGemvMaxBatch, "q4w_gemv_host: batch must be 1..16");
+  AhQ4Weight* w = const_cast<AhQ4Weight*>(cw);
+  std::lock_guard<std::mutex> lk(w->mu);
+  const size_t x_max = ((size_t)kGemvMaxBatch * w->t.cols * 4 + 255) / 256 * 256;
+  if (!w->stage) {
+    if (cudaMalloc(&w->stage, x_max + (size_t)kGemvMaxBatch * w->t.rows * 4) != cudaSuccess) {
+      cudaGetLastError();
+      w->stage = nullptr;
+      return fail(AH_ENOMEM, "q4w_gemv_host: staging allocation failed");
+    }
+  }
+  float* xd = static_cast<float*>(w->stage);
+  float* yd = reinterpret_cast<float*>(static_cast<uint8_t*>(w->stage) + x_max);
+  cudaStream_t st = as_stream(stream);
+  AH_CUDA_TRY(cudaMemcpyAsync(xd, x_host, (size_t)batch * w->t.cols * 4, cudaMemcpyHostToDevice, st));
+  const int rc = ah_q4w_gemv(w, xd, yd, batch, stream);
+  if (rc != AH_OK) return rc;
+  AH_CUDA_TRY(cudaMemcpyAsync(y_host, yd, (size_t)batch * w->t.rows * 4, cudaMemcpyDeviceToHost, st));
+  AH_CUDA_TRY(cudaStreamSynchronize(st));
   return AH_OK;
 }
 

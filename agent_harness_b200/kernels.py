@@ -190,6 +190,19 @@ class Q4Weight:
         call("ah_q4w_gemv", self._h, _ptr(xb), _ptr(out), batch, _stream(x.device))
         return out.reshape(self.rows) if squeeze else out
 
+    def gemv_host(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """y = W @ x for host tensors (pinned for asynchronous copies): copy in,
+        GEMV on the resident weight, copy out, wait -- one library call."""
+        assert not x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+        xb = x.reshape(-1, self.cols)
+        batch = xb.shape[0]
+        if out is None:
+            out = torch.empty(batch, self.rows, dtype=torch.float32).pin_memory()
+        assert not out.is_cuda and out.is_contiguous() and out.numel() == batch * self.rows
+        st = _stream(self.device) if stream is None else C.c_void_p(stream.cuda_stream)
+        call("ah_q4w_gemv_host", self._h, C.c_void_p(xb.data_ptr()), C.c_void_p(out.data_ptr()), batch, st)
+        return out.reshape(self.rows) if x.dim() == 1 else out
+
     def gemm_workspace_bytes(self, m: int) -> int:
         n = C.c_size_t()
         call("ah_q4w_gemm_workspace_bytes", self._h, m, C.byref(n))

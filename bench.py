@@ -267,26 +267,27 @@ def run_gpu(args):
     # correctness spot check of the timed kernel's output (cheap, outside timing)
     ok = bool(torch.isfinite(y).all().item())
 
-    # --- end to end through the public API: host x in, host y out, per GEMV ---
+    # --- end to end through the C-ABI with host buffers, per GEMV: the
+    # gemv_4bit_into calling convention (host x in, host y out, synchronous)
+    # on resident weights: ah_q4w_gemv_host copies x in, runs the GEMV, copies
+    # y out and waits, all inside the timed region ---
     x_host = torch.empty(COLS, dtype=torch.float32).pin_memory()
     x_host.copy_(x.cpu())
     y_host = torch.empty(ROWS, dtype=torch.float32).pin_memory()
-    xd = torch.empty_like(x)
     e2e_steps = max(1, min(args.steps, 200))
-    with torch.cuda.stream(stream):
-        for W in Ws[:4]:
-            xd.copy_(x_host, non_blocking=True)
-            W.gemv(xd, out=y)
-            y_host.copy_(y, non_blocking=True)
-            stream.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            for W in Ws:
-                xd.copy_(x_host, non_blocking=True)
-                W.gemv(xd, out=y)
-                y_host.copy_(y, non_blocking=True)
-                stream.synchronize()
-        e2e_dt = time.perf_counter() - t0
+    gemv_host = _lib.lib().ah_q4w_gemv_host
+    xp, yp, sp = C.c_void_p(x_host.data_ptr()), C.c_void_p(y_host.data_ptr()), C.c_void_p(stream.cuda_stream)
+    handles = [W.handle for W in Ws]
+    for h in handles:  # first call per weight allocates its staging: keep it untimed
+        _lib.check(gemv_host(h, xp, yp, 1, sp))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        for h in handles:
+            rc = gemv_host(h, xp, yp, 1, sp)
+            if rc != 0:
+                _lib.check(rc)
+    e2e_dt = time.perf_counter() - t0
+    e2e_ok = bool(np.isfinite(y_host.numpy()).all())
     e2e_val = world * e2e_steps * N_COPIES * GEMV_BYTES / e2e_dt / 1e9
     if world > 1:
         t = torch.tensor([e2e_dt], device=dev)
@@ -333,11 +334,11 @@ def run_gpu(args):
                          "avg_launch_us": round(per_launch_s * 1e6, 4)},
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": N_COPIES * COLS * 4,
                     "d2h_bytes_per_step": N_COPIES * ROWS * 4,
-                    "path": "kernels.Q4Weight.gemv per GEMV: pinned x H2D, GEMV, y D2H, stream sync; weights "
+                    "path": "ah_q4w_gemv_host per GEMV: pinned x H2D, GEMV, y D2H, stream sync in one C-ABI call; weights "
                             "resident from load"},
             "gpu_launches": launches,
             "clocks": clocks,
-            "output_finite": ok,
+            "output_finite": ok and e2e_ok,
         }
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}

@@ -133,6 +133,13 @@ AH_API int ah_q4w_destroy(AhQ4Weight* w);
 AH_API int ah_q4w_shape(const AhQ4Weight* w, int64_t* rows, int64_t* cols);
 /* Bytes the algorithm must read per GEMV (nibbles + scales, unpadded). */
 AH_API int64_t ah_q4w_weight_bytes(const AhQ4Weight* w);
+/* Reference: inference/math.rs:255-295 gemv_4bit_into(out, ..., x, ...) with
+ * host slices, for a weight already resident: copies x_host [batch][cols] to
+ * the device, runs ah_q4w_gemv, copies y_host [batch][rows] back and waits for
+ * the stream.  Host buffers should be pinned for asynchronous copies.  The
+ * device staging is allocated on the first call for each weight; calls on one
+ * weight from several host threads are serialised. */
+AH_API int ah_q4w_gemv_host(const AhQ4Weight* w, const float* x_host, float* y_host, int batch, void* stream);
 /* Read-only view of a resident weight's device planes (no reference
  * counterpart): the tiled nibbles, the scales (f16x4 or, for f32_scales,
  * float4 per row pair of a block pair) and their sizes in bytes. */

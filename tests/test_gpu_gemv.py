@@ -202,3 +202,19 @@ def test_batch_split_when_x_exceeds_shared_memory(cuda, oracle):
     bh, xh = blocks.cpu().numpy(), x.cpu().numpy()
     for b in (0, 5, 9, 15):
         assert relerr(y[b], oracle.gemv_q4_0(bh, xh[b], rows, cols)) <= TOL, b
+
+
+@pytest.mark.parametrize("batch", [1, 5, 16])
+def test_gemv_host_buffers_match_device_gemv(cuda, batch):
+    # ah_q4w_gemv_host (host x in, host y out, synchronous; the gemv_4bit_into
+    # calling convention on a resident weight) gives exactly the device GEMV's
+    # result, on repeated calls through the same staging.
+    from agent_harness_b200 import kernels as K
+    rows, cols = 1000, 4096
+    W = K.Q4Weight.from_q4_0(K.synth_q4_0(rows, cols, 0.02, 4, device="cuda"), rows, cols)
+    for seed in (5, 6):
+        x = K.fill_normal(batch * cols, 0.0, 1.0, seed, device="cuda").reshape(batch, cols)
+        want = W.gemv(x).cpu()
+        got = W.gemv_host(x.cpu().pin_memory())
+        assert torch.equal(got, want)
+    W.close()
