@@ -977,6 +977,21 @@ __global__ void __launch_bounds__(256) k_gemv_engine_generic(float* __restrict__
     if (lane == 0) out[r] = sum;
   }
 }
+// Copies n floats from device-mapped (pinned) host memory over the bus:
+// avoids the copy engine's start-up for the small activation vectors.
+__global__ void __launch_bounds__(256) k_pull_f32(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+// The device address of a pinned, device-mapped host buffer, or null (pageable).
+const void* mapped_host_ptr(const void* p) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+}
 __global__ void k_zero(float* p, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) p[i] = 0.0f;
 }
@@ -1031,10 +1046,21 @@ int ah_q4w_gemv_host(const AhQ4Weight* cw, const float* x_host, float* y_host, i
   float* xd = static_cast<float*>(w->stage);
   float* yd = reinterpret_cast<float*>(static_cast<uint8_t*>(w->stage) + x_max);
   cudaStream_t st = as_stream(stream);
-  AH_CUDA_TRY(cudaMemcpyAsync(xd, x_host, (size_t)batch * w->t.cols * 4, cudaMemcpyHostToDevice, st));
-  const int rc = ah_q4w_gemv(w, xd, yd, batch, stream);
+  // pinned host buffers are reached directly: a small kernel pulls x over the
+  // bus and the GEMV stores y into the mapped buffer; pageable ones go
+  // through the copy engine
+  const int64_t nx = (int64_t)batch * w->t.cols;
+  const float* xm = static_cast<const float*>(mapped_host_ptr(x_host));
+  float* ym = static_cast<float*>(const_cast<void*>(mapped_host_ptr(y_host)));
+  if (xm) {
+    k_pull_f32<<<(int)std::min<int64_t>((nx + 1023) / 1024, 64), 256, 0, st>>>(xd, xm, nx);
+    AH_LAUNCH_CHECK();
+  } else {
+    AH_CUDA_TRY(cudaMemcpyAsync(xd, x_host, (size_t)nx * 4, cudaMemcpyHostToDevice, st));
+  }
+  const int rc = ah_q4w_gemv(w, xd, ym ? ym : yd, batch, stream);
   if (rc != AH_OK) return rc;
-  AH_CUDA_TRY(cudaMemcpyAsync(y_host, yd, (size_t)batch * w->t.rows * 4, cudaMemcpyDeviceToHost, st));
+  if (!ym) AH_CUDA_TRY(cudaMemcpyAsync(y_host, yd, (size_t)batch * w->t.rows * 4, cudaMemcpyDeviceToHost, st));
   AH_CUDA_TRY(cudaStreamSynchronize(st));
   return AH_OK;
 }

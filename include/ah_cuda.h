@@ -136,7 +136,8 @@ AH_API int64_t ah_q4w_weight_bytes(const AhQ4Weight* w);
 /* Reference: inference/math.rs:255-295 gemv_4bit_into(out, ..., x, ...) with
  * host slices, for a weight already resident: copies x_host [batch][cols] to
  * the device, runs ah_q4w_gemv, copies y_host [batch][rows] back and waits for
- * the stream.  Host buffers should be pinned for asynchronous copies.  The
+ * the stream.  Pinned (device-mapped) host buffers are read and written by the
+ * kernels over the bus; pageable ones go through the copy engine.  The
  * device staging is allocated on the first call for each weight; calls on one
  * weight from several host threads are serialised. */
 AH_API int ah_q4w_gemv_host(const AhQ4Weight* w, const float* x_host, float* y_host, int batch, void* stream);

@@ -215,6 +215,9 @@ def test_gemv_host_buffers_match_device_gemv(cuda, batch):
     for seed in (5, 6):
         x = K.fill_normal(batch * cols, 0.0, 1.0, seed, device="cuda").reshape(batch, cols)
         want = W.gemv(x).cpu()
-        got = W.gemv_host(x.cpu().pin_memory())
+        got = W.gemv_host(x.cpu().pin_memory())  # pinned: read and written by the kernels over the bus
         assert torch.equal(got, want)
+        paged = torch.empty(batch, rows, dtype=torch.float32)
+        got = W.gemv_host(x.cpu(), out=paged)  # pageable: through the copy engine
+        assert torch.equal(got.reshape(batch, rows), want.reshape(batch, rows))
     W.close()
