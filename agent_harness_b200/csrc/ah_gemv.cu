@@ -24,6 +24,13 @@ struct AhQ4Weight {
   // device staging for host-buffer calls (ah_q4w_gemv_host), allocated on the
   // first such call for the largest batch; mu serialises those calls
   void* stage = nullptr;
+  // the pull + GEMV of the last pinned-buffer call as one graph, reused while
+  // the caller passes the same buffers and batch
+  cudaGraphExec_t host_graph = nullptr;
+  cudaStream_t host_cap = nullptr;
+  const void* hg_x = nullptr;
+  const void* hg_y = nullptr;
+  int hg_batch = 0;
   std::mutex mu;
 };
 
@@ -1025,6 +1032,8 @@ int ah_q4w_destroy(AhQ4Weight* w) {
   cudaFree(w->nib_alloc);
   cudaFree(w->scale_alloc);
   if (w->stage) cudaFree(w->stage);
+  if (w->host_graph) cudaGraphExecDestroy(w->host_graph);
+  if (w->host_cap) cudaStreamDestroy(w->host_cap);
   cudaSetDevice(cur);
   delete w;
   return AH_OK;
@@ -1052,8 +1061,39 @@ int ah_q4w_gemv_host(const AhQ4Weight* cw, const float* x_host, float* y_host, i
   const int64_t nx = (int64_t)batch * w->t.cols;
   const float* xm = static_cast<const float*>(mapped_host_ptr(x_host));
   float* ym = static_cast<float*>(const_cast<void*>(mapped_host_ptr(y_host)));
+  const int pull_grid = (int)std::min<int64_t>((nx + 1023) / 1024, 64);
+  if (xm && ym) {  // both pinned: one graph launch for the pull and the GEMV
+    if (!w->host_graph || w->hg_x != xm || w->hg_y != ym || w->hg_batch != batch) {
+      if (w->host_graph) cudaGraphExecDestroy(w->host_graph);
+      w->host_graph = nullptr;
+      AH_TRY_GEMV(gemv_prepare(w->t, batch, kProPlain, kEpiStore));  // kernel attributes before the capture
+      if (!w->host_cap) AH_CUDA_TRY(cudaStreamCreateWithFlags(&w->host_cap, cudaStreamNonBlocking));
+      cudaGraph_t g = nullptr;
+      AH_CUDA_TRY(cudaStreamBeginCapture(w->host_cap, cudaStreamCaptureModeThreadLocal));
+      k_pull_f32<<<pull_grid, 256, 0, w->host_cap>>>(xd, xm, nx);
+      const int rc = ah_q4w_gemv(w, xd, ym, batch, w->host_cap);
+      const cudaError_t e = cudaStreamEndCapture(w->host_cap, &g);
+      if (rc != AH_OK || e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return rc != AH_OK ? rc : fail(AH_ECUDA, "q4w_gemv_host: capture failed: %s", cudaGetErrorString(e));
+      }
+      const cudaError_t ei = cudaGraphInstantiate(&w->host_graph, g, 0);
+      cudaGraphDestroy(g);
+      if (ei != cudaSuccess) {
+        w->host_graph = nullptr;
+        return fail(AH_ECUDA, "q4w_gemv_host: graph instantiate: %s", cudaGetErrorString(ei));
+      }
+      w->hg_x = xm;
+      w->hg_y = ym;
+      w->hg_batch = batch;
+    }
+    AH_CUDA_TRY(cudaGraphLaunch(w->host_graph, st));
+    AH_CUDA_TRY(cudaStreamSynchronize(st));
+    return AH_OK;
+  }
   if (xm) {
-    k_pull_f32<<<(int)std::min<int64_t>((nx + 1023) / 1024, 64), 256, 0, st>>>(xd, xm, nx);
+    k_pull_f32<<<pull_grid, 256, 0, st>>>(xd, xm, nx);
     AH_LAUNCH_CHECK();
   } else {
     AH_CUDA_TRY(cudaMemcpyAsync(xd, x_host, (size_t)nx * 4, cudaMemcpyHostToDevice, st));

@@ -137,7 +137,9 @@ AH_API int64_t ah_q4w_weight_bytes(const AhQ4Weight* w);
  * host slices, for a weight already resident: copies x_host [batch][cols] to
  * the device, runs ah_q4w_gemv, copies y_host [batch][rows] back and waits for
  * the stream.  Pinned (device-mapped) host buffers are read and written by the
- * kernels over the bus; pageable ones go through the copy engine.  The
+ * kernels over the bus, the pull of x and the GEMV replayed as one graph while
+ * the caller keeps passing the same buffers; pageable ones go through the copy
+ * engine.  The
  * device staging is allocated on the first call for each weight; calls on one
  * weight from several host threads are serialised. */
 AH_API int ah_q4w_gemv_host(const AhQ4Weight* w, const float* x_host, float* y_host, int batch, void* stream);
