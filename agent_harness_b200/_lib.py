@@ -50,6 +50,8 @@ SIGNATURES = {
     "ah_q4w_shape": (i32, [vp, C.POINTER(i64), C.POINTER(i64)]),
     "ah_q4w_weight_bytes": (i64, [vp]),
     "ah_q4w_gemv_host": (i32, [vp, vp, vp, i32, vp]),
+    "ah_ssm_workspace_bytes": (i32, [vp, C.POINTER(sz)]),
+    "ah_ssm_forward": (i32, [vp, vp, vp, vp, vp, vp, vp, sz, vp]),
     "ah_q4w_planes": (i32, [vp, C.POINTER(vp), C.POINTER(sz), C.POINTER(vp), C.POINTER(sz), C.POINTER(i32)]),
     "ah_dedup_table_local": (i32, [vp, i64, vp, i64, i32, i32, C.c_float, C.POINTER(vp)]),
     "ah_dedup_table_global": (i32, [vp, i64, vp, i64, i32, i32, C.c_float, i32, vp, i64, vp, vp, C.POINTER(vp)]),

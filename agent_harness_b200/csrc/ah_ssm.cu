@@ -1,0 +1,310 @@
+// ah_ssm.cu — the gated delta-net SSM block (inference/ssm.rs:171-296), one
+// token step on the device.
+//
+// Four launches per step, all on the caller's stream:
+//   k_ssm_gemv (4 segments)  qkv_mixed = Wqkv x; z = Wgate x;
+//                            beta = sigmoid(Wbeta x); gate = softplus(Walpha x + dt_bias) * a
+//   k_ssm_conv               depthwise conv1d over the (d_conv - 1)-step window,
+//                            SiLU, window shift (math.rs:165-190)
+//   k_ssm_delta              per value head: L2 norm of q and k (their key head),
+//                            S *= exp(gate); sk = S k; delta = (v - sk) beta;
+//                            S += delta k^T; o = S q / sqrt(d); gated RMSNorm * silu(z)
+//   k_ssm_gemv (1 segment)   out = Wout result
+// The recurrence is row-parallel: row i of a head's state needs only k, q, v_i
+// and beta, so one warp owns each row and S streams through HBM once per step
+// (2 x 4 B per state element).  The projections are HBM-bound f32 GEMVs, a
+// warp per row.  Sums are warp trees rather than the reference's sequential
+// loops, so results agree to f32 rounding, not bit for bit; the state update
+// uses separately rounded multiply and add, as the Rust code does.
+#include <algorithm>
+
+#include "ah_common.cuh"
+
+#define AH_TRY_SSM(expr)          \
+  do {                            \
+    const int _rc = (expr);       \
+    if (_rc != AH_OK) return _rc; \
+  } while (0)
+
+namespace ah {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxHeadDim = 256;  // head_k_dim = head_v_dim
+
+__device__ __forceinline__ float sigmoid_ref(float x) {  // math.rs:88-96
+  if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
+  const float e = expf(x);
+  return e / (1.0f + e);
+}
+__device__ __forceinline__ float silu_ssm(float x) { return x * sigmoid_ref(x); }      // math.rs:83-86
+__device__ __forceinline__ float softplus_ref(float x) { return x > 20.0f ? x : logf(1.0f + expf(x)); }  // :98-104
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+// Sum over the CTA; every thread gets the result.  `red` holds one float per warp.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.0f;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+enum SegEpi : int { kSegPlain = 0, kSegSigmoid = 1, kSegSoftplusGate = 2 };
+struct GemvSeg {
+  const float* w;  // [rows][cols]
+  float* y;        // [rows]
+  int rows;
+  int epi;
+  const float* bias;  // softplus gate: dt_bias
+  const float* mul;   // softplus gate: a
+};
+struct SsmGemvArgs {
+  GemvSeg seg[4];
+  int nseg;
+  int cols;
+  int vec;  // float4 loads (cols % 4 == 0, 16-byte aligned rows and x)
+  const float* x;
+};
+
+// A warp per output row over the concatenated segments.
+__global__ void __launch_bounds__(kThreads) k_ssm_gemv(const SsmGemvArgs a) {
+  const int lane = threadIdx.x & 31;
+  int total = 0;
+  for (int s = 0; s < a.nseg; ++s) total += a.seg[s].rows;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < total; r += warps) {
+    int s = 0, rr = r;
+    while (rr >= a.seg[s].rows) rr -= a.seg[s++].rows;
+    const GemvSeg& g = a.seg[s];
+    const float* row = g.w + (int64_t)rr * a.cols;
+    float acc = 0.0f;
+    if (a.vec) {
+      const float4* r4 = reinterpret_cast<const float4*>(row);
+      const float4* x4 = reinterpret_cast<const float4*>(a.x);
+      for (int j = lane; j < a.cols / 4; j += 32) {
+        const float4 w = __ldg(r4 + j), x = __ldg(x4 + j);
+        acc += w.x * x.x + w.y * x.y + w.z * x.z + w.w * x.w;
+      }
+    } else {
+      for (int j = lane; j < a.cols; j += 32) acc += __ldg(row + j) * __ldg(a.x + j);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      if (g.epi == kSegSigmoid) acc = sigmoid_ref(acc);
+      else if (g.epi == kSegSoftplusGate) acc = softplus_ref(acc + g.bias[rr]) * g.mul[rr];
+      g.y[rr] = acc;
+    }
+  }
+}
+
+// conv_out[c] = silu(sum_k state[k][c] w[c][k] + x[c] w[c][d_conv-1]); then
+// the window moves one step (math.rs:165-190).  A thread per channel.
+__global__ void __launch_bounds__(kThreads) k_ssm_conv(const float* __restrict__ qkv, const float* __restrict__ w,
+                                                       float* __restrict__ state, float* __restrict__ out, int channels,
+                                                       int d_conv) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= channels) return;
+  float sum = 0.0f;
+  for (int k = 0; k < d_conv - 1; ++k) sum += state[(int64_t)k * channels + c] * w[(int64_t)c * d_conv + k];
+  const float x = qkv[c];
+  sum += x * w[(int64_t)c * d_conv + (d_conv - 1)];
+  for (int k = 0; k + 1 < d_conv - 1; ++k) state[(int64_t)k * channels + c] = state[(int64_t)(k + 1) * channels + c];
+  if (d_conv > 1) state[(int64_t)(d_conv - 2) * channels + c] = x;
+  out[c] = silu_ssm(sum);
+}
+
+struct DeltaArgs {
+  const float* conv_out;  // [2 key_dim + value_dim]: q | k | v
+  const float* z;         // [value_dim]
+  const float* beta;      // [nv]
+  const float* gate;      // [nv]
+  const float* norm_w;    // [D]
+  float* state;           // [nv][D][D]
+  float* result;          // [value_dim]
+  int D, nk, nv;
+  float eps, scale;
+};
+
+// One CTA per value head h: its key head is h / (nv / nk).
+__global__ void __launch_bounds__(kThreads) k_ssm_delta(const DeltaArgs a) {
+  __shared__ float qs[kMaxHeadDim], kn[kMaxHeadDim], o[kMaxHeadDim], red[kThreads / 32];
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const int D = a.D, key_dim = a.nk * D;
+  const int src = h / (a.nv / a.nk);
+  const float* q = a.conv_out + (int64_t)src * D;
+  const float* k = a.conv_out + key_dim + (int64_t)src * D;
+  const float* v = a.conv_out + 2 * key_dim + (int64_t)h * D;
+  // L2 norm per key head (math.rs:71-80): x / max(sqrt(sum x^2), eps); q then scaled
+  float sq = 0.0f, sk2 = 0.0f;
+  for (int i = tid; i < D; i += blockDim.x) {
+    sq += q[i] * q[i];
+    sk2 += k[i] * k[i];
+  }
+  const float nq = block_sum(sq, red);
+  const float nkk = block_sum(sk2, red);
+  const float iq = 1.0f / fmaxf(sqrtf(nq), a.eps), ik = 1.0f / fmaxf(sqrtf(nkk), a.eps);
+  for (int i = tid; i < D; i += blockDim.x) {
+    qs[i] = (q[i] * iq) * a.scale;
+    kn[i] = k[i] * ik;
+  }
+  __syncthreads();
+  const float decay = expf(a.gate[h]), beta = a.beta[h];
+  float* S = a.state + (int64_t)h * D * D;
+  const int per = (D + 31) / 32;
+  for (int i = warp; i < D; i += nw) {
+    float s[kMaxHeadDim / 32];
+    float dot = 0.0f;
+#pragma unroll
+    for (int e = 0; e < kMaxHeadDim / 32; ++e)
+      if (e < per && lane + 32 * e < D) {
+        s[e] = S[(int64_t)i * D + lane + 32 * e] * decay;
+        dot += s[e] * kn[lane + 32 * e];
+      }
+    const float delta = (v[i] - warp_sum(dot)) * beta;
+    float od = 0.0f;
+#pragma unroll
+    for (int e = 0; e < kMaxHeadDim / 32; ++e)
+      if (e < per && lane + 32 * e < D) {
+        s[e] = __fadd_rn(s[e], __fmul_rn(delta, kn[lane + 32 * e]));  // S += delta k^T, unfused like the reference
+        S[(int64_t)i * D + lane + 32 * e] = s[e];
+        od += s[e] * qs[lane + 32 * e];
+      }
+    od = warp_sum(od);
+    if (lane == 0) o[i] = od;
+  }
+  __syncthreads();
+  // gated RMSNorm (math.rs:53-63) times silu(z)
+  float ss = 0.0f;
+  for (int i = tid; i < D; i += blockDim.x) ss += o[i] * o[i];
+  const float tot = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(tot / (float)D + a.eps);
+  for (int i = tid; i < D; i += blockDim.x)
+    a.result[(int64_t)h * D + i] = (o[i] * inv * a.norm_w[i]) * silu_ssm(a.z[(int64_t)h * D + i]);
+}
+
+struct SsmDims {
+  int64_t d, D, nk, nv, key_dim, value_dim, conv_dim, d_conv;
+};
+
+inline int64_t pad4(int64_t n) { return (n + 3) / 4 * 4; }
+
+int ssm_dims(const AhSsmConfig* c, SsmDims* s) {
+  AH_REQUIRE(c, "ssm: null config");
+  AH_REQUIRE(c->n_embd > 0 && c->d_state > 0 && c->n_group > 0 && c->dt_rank > 0 && c->d_inner > 0 && c->d_conv >= 1,
+             "ssm: non-positive dimension");
+  AH_REQUIRE(c->d_inner % c->dt_rank == 0 && c->d_inner / c->dt_rank == c->d_state,
+             "ssm: head_v_dim (d_inner / dt_rank) must equal head_k_dim (d_state), as ssm.rs:239 asserts");
+  AH_REQUIRE(c->dt_rank % c->n_group == 0, "ssm: dt_rank must be a multiple of n_group");
+  AH_REQUIRE(c->d_state <= kMaxHeadDim, "ssm: head dim at most %d", kMaxHeadDim);
+  s->d = c->n_embd;
+  s->D = c->d_state;
+  s->nk = c->n_group;
+  s->nv = c->dt_rank;
+  s->key_dim = s->D * s->nk;
+  s->value_dim = s->D * s->nv;
+  s->conv_dim = 2 * s->key_dim + s->value_dim;
+  s->d_conv = c->d_conv;
+  return AH_OK;
+}
+
+size_t ws_floats(const SsmDims& s) {
+  return (size_t)(2 * pad4(s.conv_dim) + 2 * pad4(s.value_dim) + 2 * pad4(s.nv));
+}
+
+bool aligned16f(const float* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int launch_gemv(const SsmGemvArgs& g, int total_rows, cudaStream_t st) {
+  const int warps_per_cta = kThreads / 32;
+  int grid = (total_rows + warps_per_cta - 1) / warps_per_cta;
+  grid = std::min(grid, sm_count() * 8);
+  k_ssm_gemv<<<grid, kThreads, 0, st>>>(g);
+  AH_LAUNCH_CHECK();
+  return AH_OK;
+}
+
+}  // namespace
+}  // namespace ah
+
+using namespace ah;
+
+extern "C" {
+
+int ah_ssm_workspace_bytes(const AhSsmConfig* cfg, size_t* bytes) {
+  AH_REQUIRE(bytes, "ssm_workspace_bytes: null out");
+  SsmDims s;
+  const int rc = ssm_dims(cfg, &s);
+  if (rc != AH_OK) return rc;
+  *bytes = ws_floats(s) * sizeof(float);
+  return AH_OK;
+}
+
+int ah_ssm_forward(const AhSsmConfig* cfg, const AhSsmWeights* w, float* conv_state, float* ssm_state,
+                   const float* x, float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  SsmDims s;
+  const int rc = ssm_dims(cfg, &s);
+  if (rc != AH_OK) return rc;
+  AH_REQUIRE(w && w->wqkv && w->wqkv_gate && w->conv1d && w->dt_bias && w->a && w->alpha && w->beta && w->norm &&
+                 w->out,
+             "ssm_forward: null weight");
+  AH_REQUIRE(ssm_state && x && out && (conv_state || s.d_conv == 1), "ssm_forward: null state or vector");
+  AH_REQUIRE(workspace && workspace_bytes >= ws_floats(s) * sizeof(float) && aligned16f((const float*)workspace),
+             "ssm_forward: workspace of %zu bytes (16-byte aligned) required", ws_floats(s) * sizeof(float));
+  cudaStream_t st = as_stream(stream);
+  float* ws = static_cast<float*>(workspace);
+  float* qkv = ws;
+  float* cout = qkv + pad4(s.conv_dim);
+  float* z = cout + pad4(s.conv_dim);
+  float* res = z + pad4(s.value_dim);
+  float* beta = res + pad4(s.value_dim);
+  float* gate = beta + pad4(s.nv);
+  // input projections, beta and the decay gate in one launch (ssm.rs:184-199)
+  SsmGemvArgs g{};
+  g.x = x;
+  g.cols = (int)s.d;
+  g.nseg = 4;
+  g.seg[0] = GemvSeg{w->wqkv, qkv, (int)s.conv_dim, kSegPlain, nullptr, nullptr};
+  g.seg[1] = GemvSeg{w->wqkv_gate, z, (int)s.value_dim, kSegPlain, nullptr, nullptr};
+  g.seg[2] = GemvSeg{w->beta, beta, (int)s.nv, kSegSigmoid, nullptr, nullptr};
+  g.seg[3] = GemvSeg{w->alpha, gate, (int)s.nv, kSegSoftplusGate, w->dt_bias, w->a};
+  g.vec = s.d % 4 == 0 && aligned16f(x) && aligned16f(w->wqkv) && aligned16f(w->wqkv_gate) &&
+          aligned16f(w->beta) && aligned16f(w->alpha);
+  AH_TRY_SSM(launch_gemv(g, (int)(s.conv_dim + s.value_dim + 2 * s.nv), st));
+  // conv1d + SiLU + window shift (ssm.rs:202-207)
+  k_ssm_conv<<<(int)((s.conv_dim + kThreads - 1) / kThreads), kThreads, 0, st>>>(qkv, w->conv1d, conv_state, cout,
+                                                                                 (int)s.conv_dim, (int)s.d_conv);
+  AH_LAUNCH_CHECK();
+  // L2 norms, gated delta rule, gated RMSNorm (ssm.rs:216-292)
+  DeltaArgs da{};
+  da.conv_out = cout;
+  da.z = z;
+  da.beta = beta;
+  da.gate = gate;
+  da.norm_w = w->norm;
+  da.state = ssm_state;
+  da.result = res;
+  da.D = (int)s.D;
+  da.nk = (int)s.nk;
+  da.nv = (int)s.nv;
+  da.eps = cfg->rms_eps;
+  da.scale = 1.0f / sqrtf((float)s.D);
+  k_ssm_delta<<<(int)s.nv, kThreads, 0, st>>>(da);
+  AH_LAUNCH_CHECK();
+  // output projection (ssm.rs:295)
+  SsmGemvArgs go{};
+  go.x = res;
+  go.cols = (int)s.value_dim;
+  go.nseg = 1;
+  go.seg[0] = GemvSeg{w->out, out, (int)s.d, kSegPlain, nullptr, nullptr};
+  go.vec = s.value_dim % 4 == 0 && aligned16f(w->out);
+  return launch_gemv(go, (int)s.d, st);
+}
+
+}  // extern "C"

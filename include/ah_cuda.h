@@ -327,6 +327,31 @@ AH_API int ah_dedup_into_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, 
                              const uint16_t* tail_idx, int64_t n_tail_idx, const uint8_t* sign_bits,
                              int64_t n_sign_bytes, AhQ4Weight* w, void* stream);
 
+/* ---- gated delta-net SSM block (inference/ssm.rs) ------------------------------------ */
+/* ModelConfig's SSM fields (inference/config.rs:31-39): head_k_dim = d_state,
+ * num_k_heads = n_group, num_v_heads = dt_rank, head_v_dim = d_inner / dt_rank
+ * (must equal d_state), conv kernel d_conv. */
+typedef struct {
+  int32_t n_embd, d_state, n_group, dt_rank, d_inner, d_conv;
+  float rms_eps;
+} AhSsmConfig;
+/* SsmBlock's weights (ssm.rs:25-44), device f32, row-major as the reference
+ * multiplies them: wqkv [conv_dim][n_embd], wqkv_gate [value_dim][n_embd],
+ * conv1d [conv_dim][d_conv], dt_bias / a [dt_rank], alpha / beta
+ * [dt_rank][n_embd], norm [head_v_dim], out [n_embd][value_dim]
+ * (conv_dim = 2 * n_group * d_state + value_dim, value_dim = d_inner). */
+typedef struct {
+  const float *wqkv, *wqkv_gate, *conv1d, *dt_bias, *a, *alpha, *beta, *norm, *out;
+} AhSsmWeights;
+/* Device workspace one step needs (caller-allocated, 16-byte aligned). */
+AH_API int ah_ssm_workspace_bytes(const AhSsmConfig* cfg, size_t* bytes);
+/* Replaces inference/ssm.rs:171-296 SsmBlock::forward(input, state, config):
+ * one token, x [n_embd] -> out [n_embd], updating the state in place:
+ * conv_state [(d_conv - 1)][conv_dim] and ssm_state [dt_rank][d_state][d_state]
+ * (SsmState::new zero-initialises both, ssm.rs:78-91).  head_dim at most 256. */
+AH_API int ah_ssm_forward(const AhSsmConfig* cfg, const AhSsmWeights* w, float* conv_state, float* ssm_state,
+                          const float* x, float* out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- host-slice drop-ins (synchronous; reference signatures) ---------------------- */
 /* Reference: dedup/decompressor.rs:7-27 DedupCountTensor::decompress_all(&self,
  * sandbag) -> Vec<f32> (count = self.count; host arrays in, out[count]). */

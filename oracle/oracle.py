@@ -89,6 +89,8 @@ def lib():
         L.or_dedup_decompress_with_remap.argtypes = [u16p, i64, C.c_int, C.c_int, C.c_float, u16p, i64, u16p, i64,
                                                      u8p, i64, i64, C.c_int, f32p, i64, u32p, u32p, u16p, i64, f32p]
         L.or_dedup_decompress_with_remap.restype = C.c_int
+        L.or_ssm_forward.argtypes = [i64, i64, i64, i64, i64, i64, C.c_float] + [f32p] * 13
+        L.or_ssm_forward.restype = C.c_int
         _lib = L
     return _lib
 
@@ -347,6 +349,23 @@ def dedup_decompress_with_remap(g: GlobalTable, s: Sandbag, t: DedupTensor, rema
     if rc != 0:
         raise IndexError("decompress_with_remap: index out of range (the reference panics)")
     return out[:s.count]
+
+
+# --- gated delta-net SSM block (inference/ssm.rs) ------------------------------
+
+SSM_WEIGHTS = ("wqkv", "wqkv_gate", "conv1d", "dt_bias", "a", "alpha", "beta", "norm", "out")
+
+
+def ssm_forward(cfg: dict, w: dict, conv_state: np.ndarray, ssm_state: np.ndarray, x) -> np.ndarray:
+    """SsmBlock::forward (ssm.rs:171-296) for one token; conv_state and
+    ssm_state (float32 arrays) are updated in place."""
+    out = np.empty(cfg["n_embd"], np.float32)
+    rc = lib().or_ssm_forward(cfg["n_embd"], cfg["d_state"], cfg["n_group"], cfg["dt_rank"], cfg["d_inner"],
+                              cfg["d_conv"], cfg["eps"], *[_c(w[k], np.float32) for k in SSM_WEIGHTS],
+                              conv_state, ssm_state, _c(x, np.float32), out)
+    if rc != 0:
+        raise ValueError("ssm_forward: head_k_dim != head_v_dim (the reference asserts)")
+    return out
 
 
 # --- decoder ----------------------------------------------------------------
