@@ -1,14 +1,15 @@
 // ah_ssm.cu — the gated delta-net SSM block (inference/ssm.rs:171-296), one
 // token step on the device.
 //
-// Four launches per step, all on the caller's stream:
+// Five launches per step, all on the caller's stream:
 //   k_ssm_gemv (4 segments)  qkv_mixed = Wqkv x; z = Wgate x;
 //                            beta = sigmoid(Wbeta x); gate = softplus(Walpha x + dt_bias) * a
 //   k_ssm_conv               depthwise conv1d over the (d_conv - 1)-step window,
 //                            SiLU, window shift (math.rs:165-190)
-//   k_ssm_delta              per value head: L2 norm of q and k (their key head),
-//                            S *= exp(gate); sk = S k; delta = (v - sk) beta;
-//                            S += delta k^T; o = S q / sqrt(d); gated RMSNorm * silu(z)
+//   k_ssm_delta              per value head and 16-row slice of its state: L2 norm
+//                            of q and k (their key head), S *= exp(gate); sk = S k;
+//                            delta = (v - sk) beta; S += delta k^T; o = S q / sqrt(d)
+//   k_ssm_norm               per value head: gated RMSNorm of o, times silu(z)
 //   k_ssm_gemv (1 segment)   out = Wout result
 // The recurrence is row-parallel: row i of a head's state needs only k, q, v_i
 // and beta, so one warp owns each row and S streams through HBM once per step
@@ -89,6 +90,7 @@ __global__ void __launch_bounds__(kThreads) k_ssm_gemv(const SsmGemvArgs a) {
     if (a.vec) {
       const float4* r4 = reinterpret_cast<const float4*>(row);
       const float4* x4 = reinterpret_cast<const float4*>(a.x);
+#pragma unroll 4
       for (int j = lane; j < a.cols / 4; j += 32) {
         const float4 w = __ldg(r4 + j), x = __ldg(x4 + j);
         acc += w.x * x.x + w.y * x.y + w.z * x.z + w.w * x.w;
@@ -128,15 +130,18 @@ struct DeltaArgs {
   const float* gate;      // [nv]
   const float* norm_w;    // [D]
   float* state;           // [nv][D][D]
+  float* obuf;            // [value_dim]: o = S q, before the gated norm
   float* result;          // [value_dim]
-  int D, nk, nv;
+  int D, nk, nv, rows_per_cta;
   float eps, scale;
 };
 
-// One CTA per value head h: its key head is h / (nv / nk).
+// CTA (h, c): value head h (its key head is h / (nv / nk)), state rows
+// [c * rows_per_cta, (c + 1) * rows_per_cta).
 __global__ void __launch_bounds__(kThreads) k_ssm_delta(const DeltaArgs a) {
-  __shared__ float qs[kMaxHeadDim], kn[kMaxHeadDim], o[kMaxHeadDim], red[kThreads / 32];
+  __shared__ float qs[kMaxHeadDim], kn[kMaxHeadDim], red[kThreads / 32];
   const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const int r0 = blockIdx.y * a.rows_per_cta, r1 = min(r0 + a.rows_per_cta, a.D);
   const int D = a.D, key_dim = a.nk * D;
   const int src = h / (a.nv / a.nk);
   const float* q = a.conv_out + (int64_t)src * D;
@@ -159,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) k_ssm_delta(const DeltaArgs a) {
   const float decay = expf(a.gate[h]), beta = a.beta[h];
   float* S = a.state + (int64_t)h * D * D;
   const int per = (D + 31) / 32;
-  for (int i = warp; i < D; i += nw) {
+  for (int i = r0 + warp; i < r1; i += nw) {
     float s[kMaxHeadDim / 32];
     float dot = 0.0f;
 #pragma unroll
@@ -178,10 +183,15 @@ __global__ void __launch_bounds__(kThreads) k_ssm_delta(const DeltaArgs a) {
         od += s[e] * qs[lane + 32 * e];
       }
     od = warp_sum(od);
-    if (lane == 0) o[i] = od;
+    if (lane == 0) a.obuf[(int64_t)h * D + i] = od;
   }
-  __syncthreads();
-  // gated RMSNorm (math.rs:53-63) times silu(z)
+}
+
+// Gated RMSNorm of each value head's o (math.rs:53-63) times silu(z); a CTA per head.
+__global__ void __launch_bounds__(kThreads) k_ssm_norm(const DeltaArgs a) {
+  __shared__ float red[kThreads / 32];
+  const int h = blockIdx.x, tid = threadIdx.x, D = a.D;
+  const float* o = a.obuf + (int64_t)h * D;
   float ss = 0.0f;
   for (int i = tid; i < D; i += blockDim.x) ss += o[i] * o[i];
   const float tot = block_sum(ss, red);
@@ -216,7 +226,7 @@ int ssm_dims(const AhSsmConfig* c, SsmDims* s) {
 }
 
 size_t ws_floats(const SsmDims& s) {
-  return (size_t)(2 * pad4(s.conv_dim) + 2 * pad4(s.value_dim) + 2 * pad4(s.nv));
+  return (size_t)(2 * pad4(s.conv_dim) + 3 * pad4(s.value_dim) + 2 * pad4(s.nv));
 }
 
 bool aligned16f(const float* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -265,6 +275,7 @@ int ah_ssm_forward(const AhSsmConfig* cfg, const AhSsmWeights* w, float* conv_st
   float* res = z + pad4(s.value_dim);
   float* beta = res + pad4(s.value_dim);
   float* gate = beta + pad4(s.nv);
+  float* obuf = gate + pad4(s.nv);
   // input projections, beta and the decay gate in one launch (ssm.rs:184-199)
   SsmGemvArgs g{};
   g.x = x;
@@ -289,13 +300,18 @@ int ah_ssm_forward(const AhSsmConfig* cfg, const AhSsmWeights* w, float* conv_st
   da.gate = gate;
   da.norm_w = w->norm;
   da.state = ssm_state;
+  da.obuf = obuf;
   da.result = res;
   da.D = (int)s.D;
   da.nk = (int)s.nk;
   da.nv = (int)s.nv;
+  da.rows_per_cta = 16;  // 2 rows per warp: the heads' rows spread over many SMs
   da.eps = cfg->rms_eps;
   da.scale = 1.0f / sqrtf((float)s.D);
-  k_ssm_delta<<<(int)s.nv, kThreads, 0, st>>>(da);
+  k_ssm_delta<<<dim3((unsigned)s.nv, (unsigned)((s.D + da.rows_per_cta - 1) / da.rows_per_cta)), kThreads, 0, st>>>(
+      da);
+  AH_LAUNCH_CHECK();
+  k_ssm_norm<<<(int)s.nv, kThreads, 0, st>>>(da);
   AH_LAUNCH_CHECK();
   // output projection (ssm.rs:295)
   SsmGemvArgs go{};

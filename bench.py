@@ -548,7 +548,67 @@ def secondary_measurements(K, dev, stream, peak, no_cpu=False):
                      "us_per_call": round(s * 1e6, 2), "shape": "4096x11008"}
     del q8, f, h
     out["dedup_load"] = dedup_load(K, dev, stream, peak, cpu=not no_cpu)
+    out["ssm_step"] = ssm_step(dev, stream, peak, cpu=not no_cpu)
     return out
+
+
+SSM_CFG = dict(n_embd=2048, d_state=128, n_group=16, dt_rank=32, d_inner=4096, d_conv=4, eps=1e-6)
+
+
+def ssm_step(dev, stream, peak, cpu=True, steps=200):
+    """One token through the gated delta-net SSM block (inference/ssm.rs:171-296)
+    at a Qwen3.5-like width: f32 weights (128 MB), the per-head state read and
+    written (2 x 2 MB) and the conv window per step.  Three weight copies
+    rotate (384 MB, larger than L2)."""
+    import torch
+    from agent_harness_b200.ssm import SsmBlock
+    cfg = SSM_CFG
+    rng = np.random.default_rng(13)
+    D, nv, ng, d = cfg["d_state"], cfg["dt_rank"], cfg["n_group"], cfg["n_embd"]
+    vd = cfg["d_inner"]
+    cd = 2 * ng * D + vd
+    shapes = {"wqkv": (cd, d), "wqkv_gate": (vd, d), "conv1d": (cd, cfg["d_conv"]), "dt_bias": (nv,), "a": (nv,),
+              "alpha": (nv, d), "beta": (nv, d), "norm": (D,), "out": (d, vd)}
+    blocks = []
+    for c in range(3):
+        w = {k: (rng.standard_normal(sh) * (0.02 if len(sh) == 2 and sh[1] == d or k == "out" else 0.5))
+             .astype(np.float32) for k, sh in shapes.items()}
+        w["a"] = -np.abs(w["a"])
+        blocks.append(SsmBlock(cfg, w, device=dev))
+    states = [b.new_state() for b in blocks]
+    x = torch.randn(d, device=dev)
+    out = torch.empty(d, device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(6):
+            blocks[i % 3].forward(x, states[i % 3], out=out)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(steps):
+            blocks[i % 3].forward(x, states[i % 3], out=out)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1e3 / steps
+    wbytes = sum(int(np.prod(sh)) * 4 for sh in shapes.values())
+    sbytes = 2 * nv * D * D * 4 + 2 * (cfg["d_conv"] - 1) * cd * 4
+    nbytes = wbytes + sbytes
+    res = {"config": "n_embd 2048, d_state 128, 16 k heads, 32 v heads, d_inner 4096, d_conv 4 (f32 weights)",
+           "us_per_token": round(sec * 1e6, 2), "gbs": round(nbytes / sec / 1e9, 1),
+           "frac_of_measured_peak": round(nbytes / sec / 1e9 / peak, 4), "bytes_per_token": nbytes,
+           "launches_per_token": 5, "finite": bool(torch.isfinite(out).all().item())}
+    if cpu:
+        from oracle import oracle as O
+        wc = {k: blocks[0].w[k].cpu().numpy() for k in O.SSM_WEIGHTS}
+        cs = np.zeros(((cfg["d_conv"] - 1), cd), np.float32)
+        ss = np.zeros((nv, D, D), np.float32)
+        xn = x.cpu().numpy()
+        t0 = time.perf_counter()
+        n = 3
+        for _ in range(n):
+            O.ssm_forward(cfg, wc, cs, ss, xn)
+        dt = (time.perf_counter() - t0) / n
+        res["cpu_baseline"] = {"us_per_token": round(dt * 1e6, 1), "cores": 1, "kind": "port",
+                               "sample": f"{n} tokens through the oracle restatement of ssm.rs:171-296"}
+    return res
 
 
 DEDUP_ROWS, DEDUP_COLS = 14336, 4096  # an 8B FFN gate/up matrix
@@ -630,7 +690,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode", "gemm", "tp", "load"],
+    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode", "gemm", "tp", "load", "ssm"],
                     help="decode / gemm / tp / load: only the 8B decode, the prefill GEMM, the 70B tensor-parallel "
                          "decode or the DedupCount load-path measurement (for profiling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -646,6 +706,15 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "ssm":
+        import torch
+        torch.cuda.set_device(0)
+        from agent_harness_b200 import _lib
+        _lib.check(_lib.lib().ah_device_init(0))
+        dev = torch.device("cuda", 0)
+        print(json.dumps({"workload": "ssm_step", **ssm_step(dev, torch.cuda.Stream(device=dev), peaks()[0],
+                                                             cpu=not args.no_cpu)}), flush=True)
+        return 0
     if args.workload == "load":
         import torch
         torch.cuda.set_device(0)
