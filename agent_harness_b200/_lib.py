@@ -50,6 +50,13 @@ SIGNATURES = {
     "ah_q4w_shape": (i32, [vp, C.POINTER(i64), C.POINTER(i64)]),
     "ah_q4w_weight_bytes": (i64, [vp]),
     "ah_q4w_gemv_host": (i32, [vp, vp, vp, i32, vp]),
+    "ah_arena_page_granularity": (i32, [C.POINTER(sz)]),
+    "ah_arena_create": (i32, [sz, sz, i64, C.POINTER(vp)]),
+    "ah_arena_destroy": (i32, [vp]),
+    "ah_arena_commit_page": (i32, [vp, i64]),
+    "ah_arena_evict_page": (i32, [vp, i64, i32, vp, vp]),
+    "ah_arena_page_state": (i32, [vp, i64, C.POINTER(i32), C.POINTER(vp)]),
+    "ah_arena_gemv_4bit": (i32, [vp, i64, vp, vp, vp, vp, i64, i64, i64, vp]),
     "ah_ssm_workspace_bytes": (i32, [vp, C.POINTER(sz)]),
     "ah_ssm_forward": (i32, [vp, vp, vp, vp, vp, vp, vp, sz, vp]),
     "ah_q4w_planes": (i32, [vp, C.POINTER(vp), C.POINTER(sz), C.POINTER(vp), C.POINTER(sz), C.POINTER(i32)]),

@@ -327,6 +327,37 @@ AH_API int ah_dedup_into_q4w(const AhDedupTable* t, const uint16_t* prefix_idx, 
                              const uint16_t* tail_idx, int64_t n_tail_idx, const uint8_t* sign_bits,
                              int64_t n_sign_bytes, AhQ4Weight* w, void* stream);
 
+/* ---- paged virtual tensor arena (memory_controller/virtual_tensor_arena.rs) ------------ */
+/* Page residency (PageResidency, virtual_tensor_arena.rs:5-10). */
+#define AH_PAGE_UNMAPPED 0
+#define AH_PAGE_GPU 1
+#define AH_PAGE_CPU 2
+typedef struct AhArena AhArena;
+/* Minimum page size (the device's physical allocation granularity). */
+AH_API int ah_arena_page_granularity(size_t* bytes);
+/* Replaces VirtualTensorArena::new (:34-68): a reserved virtual range of
+ * total_virtual_bytes on the current device in pages of page_bytes, all
+ * unmapped.  gpu_page_budget caps GPU-resident pages (-1: no cap); a commit
+ * past it is routed to the host as an out-of-memory commit is. */
+AH_API int ah_arena_create(size_t total_virtual_bytes, size_t page_bytes, int64_t gpu_page_budget, AhArena** out);
+AH_API int ah_arena_destroy(AhArena* a);
+/* Replaces commit_page (:70-140): maps physical GPU memory at the page's fixed
+ * address, or routes the page to the host pool on out-of-memory (:142-147);
+ * pages already committed are left as they are. */
+AH_API int ah_arena_commit_page(AhArena* a, int64_t page);
+/* Replaces evict_page (:149-212): move != 0 copies a GPU page's bytes into
+ * host_pool + page * page_bytes and marks it host resident; move == 0 drops
+ * it (unmapped).  Waits for the device first: nothing may still use the page. */
+AH_API int ah_arena_evict_page(AhArena* a, int64_t page, int move, void* host_pool, void* stream);
+/* The page's residency and, when GPU resident, its device address. */
+AH_API int ah_arena_page_state(const AhArena* a, int64_t page, int* residency, void** dev_ptr);
+/* Replaces execute_layer_math (:216-257): gemv_4bit_into (inference/math.rs:
+ * 255-295) with the page's bytes as `packed`, on the device either way: a GPU
+ * page through its address, a host page through host_pool (pinned) over the
+ * bus.  out, scales and x are device pointers; an unmapped page is AH_EINVAL. */
+AH_API int ah_arena_gemv_4bit(AhArena* a, int64_t page, const void* host_pool, float* out, const float* scales,
+                              const float* x, int64_t rows, int64_t cols, int64_t group_size, void* stream);
+
 /* ---- gated delta-net SSM block (inference/ssm.rs) ------------------------------------ */
 /* ModelConfig's SSM fields (inference/config.rs:31-39): head_k_dim = d_state,
  * num_k_heads = n_group, num_v_heads = dt_rank, head_v_dim = d_inner / dt_rank
