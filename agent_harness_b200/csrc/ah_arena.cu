@@ -244,8 +244,11 @@ int ah_arena_gemv_4bit(AhArena* a, int64_t page, const void* host_pool, float* o
   AH_REQUIRE(rows >= 0 && cols >= 0 && (size_t)((rows * cols + 1) / 2) <= a->page_bytes,
              "arena: a %lld x %lld packed matrix does not fit one page", (long long)rows, (long long)cols);
   const uint8_t* packed = nullptr;
+  // the lock is held through the (asynchronous) launch: an eviction takes it,
+  // then waits for the device before unmapping, so the page stays mapped for
+  // every GEMV enqueued on it
+  std::lock_guard<std::mutex> lk(a->mu);
   {
-    std::lock_guard<std::mutex> lk(a->mu);
     switch (a->residency[page]) {
       case AH_PAGE_UNMAPPED:  // virtual_tensor_arena.rs:231-232 panics
         return fail(AH_EINVAL, "arena: page %lld is unmapped", (long long)page);
