@@ -852,22 +852,6 @@ __global__ void k_rope_table(float2* t, int max_seq, int half, float base) {
   t[i] = make_float2(cs, sn);
 }
 
-template <typename... Args>
-int launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  AH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, args...));
-  return AH_OK;
-}
-
 }  // namespace
 }  // namespace ah
 

@@ -86,6 +86,25 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Host: launch with programmatic stream serialisation, so the kernel's CTAs may
+// start before the previous kernel on the stream completes; the kernel calls
+// pdl_wait() before it touches anything that kernel produces.
+template <typename... Args>
+int launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  AH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, args...));
+  return AH_OK;
+}
+
 // ---- thread-block clusters / distributed shared memory ----------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -1,25 +1,30 @@
 // ah_ssm.cu — the gated delta-net SSM block (inference/ssm.rs:171-296), one
 // token step on the device.
 //
-// Five launches per step, all on the caller's stream:
-//   k_ssm_gemv (4 segments)  qkv_mixed = Wqkv x; z = Wgate x;
+// Three launches per step, all on the caller's stream, each allowed to start
+// while the previous one drains (programmatic dependent launch):
+//   k_ssm_gemv (4 segments)  qkv_mixed = Wqkv x, each row's channel going
+//                            straight through the depthwise conv1d over the
+//                            (d_conv - 1)-step window, SiLU and the window shift
+//                            (math.rs:165-190); z = Wgate x;
 //                            beta = sigmoid(Wbeta x); gate = softplus(Walpha x + dt_bias) * a
-//   k_ssm_conv               depthwise conv1d over the (d_conv - 1)-step window,
-//                            SiLU, window shift (math.rs:165-190)
 //   k_ssm_delta              per value head and 16-row slice of its state: L2 norm
 //                            of q and k (their key head), S *= exp(gate); sk = S k;
-//                            delta = (v - sk) beta; S += delta k^T; o = S q / sqrt(d)
-//   k_ssm_norm               per value head: gated RMSNorm of o, times silu(z)
+//                            delta = (v - sk) beta; S += delta k^T; o = S q / sqrt(d);
+//                            the head's last slice to finish applies the gated
+//                            RMSNorm of o times silu(z)
 //   k_ssm_gemv (1 segment)   out = Wout result
 // The recurrence is row-parallel: row i of a head's state needs only k, q, v_i
 // and beta, so one warp owns each row and S streams through HBM once per step
 // (2 x 4 B per state element).  The projections are HBM-bound f32 GEMVs, a
-// warp per row.  Sums are warp trees rather than the reference's sequential
-// loops, so results agree to f32 rounding, not bit for bit; the state update
-// uses separately rounded multiply and add, as the Rust code does.
+// warp (or, for short wide matrices, a few warps) per row.  Sums are warp trees
+// rather than the reference's sequential loops, so results agree to f32
+// rounding, not bit for bit; the state update uses separately rounded multiply
+// and add, as the Rust code does.
 #include <algorithm>
 
 #include "ah_common.cuh"
+#include "ah_sm100.cuh"
 
 #define AH_TRY_SSM(expr)          \
   do {                            \
@@ -58,7 +63,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-enum SegEpi : int { kSegPlain = 0, kSegSigmoid = 1, kSegSoftplusGate = 2 };
+enum SegEpi : int { kSegPlain = 0, kSegSigmoid = 1, kSegSoftplusGate = 2, kSegConv = 3 };
 struct GemvSeg {
   const float* w;  // [rows][cols]
   float* y;        // [rows]
@@ -71,56 +76,95 @@ struct SsmGemvArgs {
   GemvSeg seg[4];
   int nseg;
   int cols;
-  int vec;  // float4 loads (cols % 4 == 0, 16-byte aligned rows and x)
+  int vec;    // float4 loads (cols % 4 == 0, 16-byte aligned rows and x)
+  int split;  // warps per row (1, 2, 4 or 8): each sums a contiguous share of the columns
   const float* x;
+  // kSegConv: conv_out[c] = silu(sum_k state[k][c] w[c][k] + y_c w[c][d_conv-1]),
+  // then the window moves one step (math.rs:165-190)
+  const float* conv_w;  // [channels][d_conv]
+  float* conv_state;    // [(d_conv - 1)][channels]
+  int d_conv;
+  int* zero;  // [nzero] set to 0 once the previous launch on the stream is complete
+  int nzero;
 };
 
-// A warp per output row over the concatenated segments.
-__global__ void __launch_bounds__(kThreads) k_ssm_gemv(const SsmGemvArgs a) {
-  const int lane = threadIdx.x & 31;
-  int total = 0;
-  for (int s = 0; s < a.nseg; ++s) total += a.seg[s].rows;
-  const int warps = gridDim.x * (blockDim.x >> 5);
-  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < total; r += warps) {
-    int s = 0, rr = r;
-    while (rr >= a.seg[s].rows) rr -= a.seg[s++].rows;
-    const GemvSeg& g = a.seg[s];
-    const float* row = g.w + (int64_t)rr * a.cols;
-    float acc = 0.0f;
-    if (a.vec) {
-      const float4* r4 = reinterpret_cast<const float4*>(row);
-      const float4* x4 = reinterpret_cast<const float4*>(a.x);
-#pragma unroll 4
-      for (int j = lane; j < a.cols / 4; j += 32) {
-        const float4 w = __ldg(r4 + j), x = __ldg(x4 + j);
-        acc += w.x * x.x + w.y * x.y + w.z * x.z + w.w * x.w;
-      }
-    } else {
-      for (int j = lane; j < a.cols; j += 32) acc += __ldg(row + j) * __ldg(a.x + j);
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) {
-      if (g.epi == kSegSigmoid) acc = sigmoid_ref(acc);
-      else if (g.epi == kSegSoftplusGate) acc = softplus_ref(acc + g.bias[rr]) * g.mul[rr];
-      g.y[rr] = acc;
-    }
-  }
+constexpr int kGemvBatch = 8;  // float4 loads in flight per lane
+
+__device__ __forceinline__ float4 ldg4_or0(const float4* p, int j, int hi) {
+  return j < hi ? __ldg(p + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 }
 
-// conv_out[c] = silu(sum_k state[k][c] w[c][k] + x[c] w[c][d_conv-1]); then
-// the window moves one step (math.rs:165-190).  A thread per channel.
-__global__ void __launch_bounds__(kThreads) k_ssm_conv(const float* __restrict__ qkv, const float* __restrict__ w,
-                                                       float* __restrict__ state, float* __restrict__ out, int channels,
-                                                       int d_conv) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= channels) return;
-  float sum = 0.0f;
-  for (int k = 0; k < d_conv - 1; ++k) sum += state[(int64_t)k * channels + c] * w[(int64_t)c * d_conv + k];
-  const float x = qkv[c];
-  sum += x * w[(int64_t)c * d_conv + (d_conv - 1)];
-  for (int k = 0; k + 1 < d_conv - 1; ++k) state[(int64_t)k * channels + c] = state[(int64_t)(k + 1) * channels + c];
-  if (d_conv > 1) state[(int64_t)(d_conv - 2) * channels + c] = x;
-  out[c] = silu_ssm(sum);
+// `split` warps per output row over the concatenated segments; a CTA covers
+// 8 / split rows.  Each lane issues kGemvBatch independent float4 weight loads
+// before it consumes them, and the first batch is fetched before the launch
+// waits for the previous kernel on the stream (weights do not change during
+// the step), so the weight stream starts while the producer of x drains.
+__global__ void __launch_bounds__(kThreads) k_ssm_gemv(const SsmGemvArgs a) {
+  __shared__ float part[kThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int S = a.split;
+  int total = 0;
+  for (int s = 0; s < a.nseg; ++s) total += a.seg[s].rows;
+  const int r = blockIdx.x * ((kThreads / 32) / S) + warp / S, piece = warp % S;
+  const bool live = r < total;
+  int s = 0, rr = r;
+  if (live)
+    while (rr >= a.seg[s].rows) rr -= a.seg[s++].rows;
+  const GemvSeg& g = a.seg[s];
+  const float* row = g.w + (int64_t)(live ? rr : 0) * a.cols;
+  float acc = 0.0f;
+  if (a.vec) {
+    const int n4 = a.cols / 4, share = (n4 + S - 1) / S;
+    const int lo = min(piece * share, n4), hi = live ? min(lo + share, n4) : lo;
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    float4 w[kGemvBatch];
+#pragma unroll
+    for (int u = 0; u < kGemvBatch; ++u) w[u] = ldg4_or0(r4, lo + lane + 32 * u, hi);
+    pdl_wait();
+    for (int j0 = lo + lane;;) {
+#pragma unroll
+      for (int u = 0; u < kGemvBatch; ++u) {
+        const float4 x = ldg4_or0(x4, j0 + 32 * u, hi);
+        acc += w[u].x * x.x + w[u].y * x.y + w[u].z * x.z + w[u].w * x.w;
+      }
+      j0 += 32 * kGemvBatch;
+      if (j0 >= hi) break;
+#pragma unroll
+      for (int u = 0; u < kGemvBatch; ++u) w[u] = ldg4_or0(r4, j0 + 32 * u, hi);
+    }
+  } else {
+    pdl_wait();
+    const int share = (a.cols + S - 1) / S;
+    const int lo = min(piece * share, a.cols), hi = live ? min(lo + share, a.cols) : lo;
+    for (int j = lo + lane; j < hi; j += 32) acc += __ldg(row + j) * __ldg(a.x + j);
+  }
+  pdl_launch_dependents();
+  if (a.zero && blockIdx.x == 0)
+    for (int i = threadIdx.x; i < a.nzero; i += blockDim.x) a.zero[i] = 0;
+  acc = warp_sum(acc);
+  if (S > 1) {  // the row's pieces in column order
+    if (lane == 0) part[warp] = acc;
+    __syncthreads();
+    if (piece != 0) return;
+    acc = part[warp];
+    for (int p = 1; p < S; ++p) acc += part[warp + p];
+  }
+  if (!live || lane != 0) return;
+  if (g.epi == kSegSigmoid) {
+    acc = sigmoid_ref(acc);
+  } else if (g.epi == kSegSoftplusGate) {
+    acc = softplus_ref(acc + g.bias[rr]) * g.mul[rr];
+  } else if (g.epi == kSegConv) {
+    const int c = rr, ch = g.rows, dc = a.d_conv;
+    float sum = 0.0f;
+    for (int k = 0; k < dc - 1; ++k) sum += a.conv_state[(int64_t)k * ch + c] * a.conv_w[(int64_t)c * dc + k];
+    sum += acc * a.conv_w[(int64_t)c * dc + (dc - 1)];
+    for (int k = 0; k + 1 < dc - 1; ++k) a.conv_state[(int64_t)k * ch + c] = a.conv_state[(int64_t)(k + 1) * ch + c];
+    if (dc > 1) a.conv_state[(int64_t)(dc - 2) * ch + c] = acc;
+    acc = silu_ssm(sum);
+  }
+  g.y[rr] = acc;
 }
 
 struct DeltaArgs {
@@ -132,18 +176,36 @@ struct DeltaArgs {
   float* state;           // [nv][D][D]
   float* obuf;            // [value_dim]: o = S q, before the gated norm
   float* result;          // [value_dim]
+  int* done;              // [nv]: row slices of the head finished this step (zeroed by the projection launch)
   int D, nk, nv, rows_per_cta;
   float eps, scale;
 };
 
+constexpr int kDeltaRowsPerWarp = 2;
+
 // CTA (h, c): value head h (its key head is h / (nv / nk)), state rows
-// [c * rows_per_cta, (c + 1) * rows_per_cta).
+// [c * rows_per_cta, (c + 1) * rows_per_cta), kDeltaRowsPerWarp rows per warp
+// at once.  The state rows are fetched first, so their HBM latency overlaps
+// the L2 norms of q and k.  The last CTA of a head to finish (a counter per
+// head, after a device-scope fence) applies the gated RMSNorm of the head's
+// o (math.rs:53-63) times silu(z).
 __global__ void __launch_bounds__(kThreads) k_ssm_delta(const DeltaArgs a) {
+  constexpr int E = kMaxHeadDim / 32, RW = kDeltaRowsPerWarp;
   __shared__ float qs[kMaxHeadDim], kn[kMaxHeadDim], red[kThreads / 32];
-  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  __shared__ int last;
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r0 = blockIdx.y * a.rows_per_cta, r1 = min(r0 + a.rows_per_cta, a.D);
   const int D = a.D, key_dim = a.nk * D;
   const int src = h / (a.nv / a.nk);
+  float* S = a.state + (int64_t)h * D * D;
+  pdl_wait();
+  const int row0 = r0 + warp * RW;
+  float s[RW][E];
+#pragma unroll
+  for (int t = 0; t < RW; ++t)
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      s[t][e] = (row0 + t < r1 && lane + 32 * e < D) ? S[(int64_t)(row0 + t) * D + lane + 32 * e] : 0.0f;
   const float* q = a.conv_out + (int64_t)src * D;
   const float* k = a.conv_out + key_dim + (int64_t)src * D;
   const float* v = a.conv_out + 2 * key_dim + (int64_t)h * D;
@@ -161,43 +223,48 @@ __global__ void __launch_bounds__(kThreads) k_ssm_delta(const DeltaArgs a) {
     kn[i] = k[i] * ik;
   }
   __syncthreads();
+  pdl_launch_dependents();
   const float decay = expf(a.gate[h]), beta = a.beta[h];
-  float* S = a.state + (int64_t)h * D * D;
-  const int per = (D + 31) / 32;
-  for (int i = r0 + warp; i < r1; i += nw) {
-    float s[kMaxHeadDim / 32];
+#pragma unroll
+  for (int t = 0; t < RW; ++t) {
+    const int i = row0 + t;
+    if (i >= r1) break;  // warp-uniform
     float dot = 0.0f;
 #pragma unroll
-    for (int e = 0; e < kMaxHeadDim / 32; ++e)
-      if (e < per && lane + 32 * e < D) {
-        s[e] = S[(int64_t)i * D + lane + 32 * e] * decay;
-        dot += s[e] * kn[lane + 32 * e];
+    for (int e = 0; e < E; ++e)
+      if (lane + 32 * e < D) {
+        s[t][e] *= decay;
+        dot += s[t][e] * kn[lane + 32 * e];
       }
     const float delta = (v[i] - warp_sum(dot)) * beta;
     float od = 0.0f;
 #pragma unroll
-    for (int e = 0; e < kMaxHeadDim / 32; ++e)
-      if (e < per && lane + 32 * e < D) {
-        s[e] = __fadd_rn(s[e], __fmul_rn(delta, kn[lane + 32 * e]));  // S += delta k^T, unfused like the reference
-        S[(int64_t)i * D + lane + 32 * e] = s[e];
-        od += s[e] * qs[lane + 32 * e];
+    for (int e = 0; e < E; ++e)
+      if (lane + 32 * e < D) {
+        s[t][e] = __fadd_rn(s[t][e], __fmul_rn(delta, kn[lane + 32 * e]));  // S += delta k^T, unfused like the reference
+        S[(int64_t)i * D + lane + 32 * e] = s[t][e];
+        od += s[t][e] * qs[lane + 32 * e];
       }
     od = warp_sum(od);
     if (lane == 0) a.obuf[(int64_t)h * D + i] = od;
   }
-}
-
-// Gated RMSNorm of each value head's o (math.rs:53-63) times silu(z); a CTA per head.
-__global__ void __launch_bounds__(kThreads) k_ssm_norm(const DeltaArgs a) {
-  __shared__ float red[kThreads / 32];
-  const int h = blockIdx.x, tid = threadIdx.x, D = a.D;
+  // the last row slice of head h to finish normalises the head
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(&a.done[h], 1) == (int)gridDim.y - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
   const float* o = a.obuf + (int64_t)h * D;
   float ss = 0.0f;
-  for (int i = tid; i < D; i += blockDim.x) ss += o[i] * o[i];
+  for (int i = tid; i < D; i += blockDim.x) {
+    const float oi = __ldcg(o + i);
+    ss += oi * oi;
+  }
   const float tot = block_sum(ss, red);
   const float inv = 1.0f / sqrtf(tot / (float)D + a.eps);
   for (int i = tid; i < D; i += blockDim.x)
-    a.result[(int64_t)h * D + i] = (o[i] * inv * a.norm_w[i]) * silu_ssm(a.z[(int64_t)h * D + i]);
+    a.result[(int64_t)h * D + i] = (__ldcg(o + i) * inv * a.norm_w[i]) * silu_ssm(a.z[(int64_t)h * D + i]);
 }
 
 struct SsmDims {
@@ -225,19 +292,25 @@ int ssm_dims(const AhSsmConfig* c, SsmDims* s) {
   return AH_OK;
 }
 
+// conv_out | z | result | obuf | beta | gate | per-head counters (int)
 size_t ws_floats(const SsmDims& s) {
-  return (size_t)(2 * pad4(s.conv_dim) + 3 * pad4(s.value_dim) + 2 * pad4(s.nv));
+  return (size_t)(pad4(s.conv_dim) + 3 * pad4(s.value_dim) + 3 * pad4(s.nv));
 }
 
 bool aligned16f(const float* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int launch_gemv(const SsmGemvArgs& g, int total_rows, cudaStream_t st) {
+// Warps per row: one while the rows alone give every SM two CTAs' worth of
+// warps, else up to 8, so that short, wide matrices still keep enough loads in
+// flight.
+int launch_gemv(SsmGemvArgs g, int total_rows, cudaStream_t st) {
   const int warps_per_cta = kThreads / 32;
-  int grid = (total_rows + warps_per_cta - 1) / warps_per_cta;
-  grid = std::min(grid, sm_count() * 8);
-  k_ssm_gemv<<<grid, kThreads, 0, st>>>(g);
-  AH_LAUNCH_CHECK();
-  return AH_OK;
+  const int want = 2 * sm_count() * warps_per_cta;
+  g.split = 1;
+  while (g.split < warps_per_cta && total_rows * g.split < want && g.cols / (4 * 32 * g.split) >= 2 * kGemvBatch)
+    g.split *= 2;
+  const int rows_per_cta = warps_per_cta / g.split;
+  return launch_pdl(k_ssm_gemv, dim3((unsigned)((total_rows + rows_per_cta - 1) / rows_per_cta)), dim3(kThreads), 0,
+                    st, g);
 }
 
 }  // namespace
@@ -269,29 +342,31 @@ int ah_ssm_forward(const AhSsmConfig* cfg, const AhSsmWeights* w, float* conv_st
              "ssm_forward: workspace of %zu bytes (16-byte aligned) required", ws_floats(s) * sizeof(float));
   cudaStream_t st = as_stream(stream);
   float* ws = static_cast<float*>(workspace);
-  float* qkv = ws;
-  float* cout = qkv + pad4(s.conv_dim);
+  float* cout = ws;
   float* z = cout + pad4(s.conv_dim);
   float* res = z + pad4(s.value_dim);
-  float* beta = res + pad4(s.value_dim);
+  float* obuf = res + pad4(s.value_dim);
+  float* beta = obuf + pad4(s.value_dim);
   float* gate = beta + pad4(s.nv);
-  float* obuf = gate + pad4(s.nv);
-  // input projections, beta and the decay gate in one launch (ssm.rs:184-199)
+  int* done = reinterpret_cast<int*>(gate + pad4(s.nv));
+  // input projections with the conv1d + SiLU + window shift fused into the
+  // qkv rows, beta and the decay gate, in one launch (ssm.rs:184-207)
   SsmGemvArgs g{};
   g.x = x;
   g.cols = (int)s.d;
   g.nseg = 4;
-  g.seg[0] = GemvSeg{w->wqkv, qkv, (int)s.conv_dim, kSegPlain, nullptr, nullptr};
+  g.seg[0] = GemvSeg{w->wqkv, cout, (int)s.conv_dim, kSegConv, nullptr, nullptr};
   g.seg[1] = GemvSeg{w->wqkv_gate, z, (int)s.value_dim, kSegPlain, nullptr, nullptr};
   g.seg[2] = GemvSeg{w->beta, beta, (int)s.nv, kSegSigmoid, nullptr, nullptr};
   g.seg[3] = GemvSeg{w->alpha, gate, (int)s.nv, kSegSoftplusGate, w->dt_bias, w->a};
   g.vec = s.d % 4 == 0 && aligned16f(x) && aligned16f(w->wqkv) && aligned16f(w->wqkv_gate) &&
           aligned16f(w->beta) && aligned16f(w->alpha);
+  g.conv_w = w->conv1d;
+  g.conv_state = conv_state;
+  g.d_conv = (int)s.d_conv;
+  g.zero = done;
+  g.nzero = (int)s.nv;
   AH_TRY_SSM(launch_gemv(g, (int)(s.conv_dim + s.value_dim + 2 * s.nv), st));
-  // conv1d + SiLU + window shift (ssm.rs:202-207)
-  k_ssm_conv<<<(int)((s.conv_dim + kThreads - 1) / kThreads), kThreads, 0, st>>>(qkv, w->conv1d, conv_state, cout,
-                                                                                 (int)s.conv_dim, (int)s.d_conv);
-  AH_LAUNCH_CHECK();
   // L2 norms, gated delta rule, gated RMSNorm (ssm.rs:216-292)
   DeltaArgs da{};
   da.conv_out = cout;
@@ -302,24 +377,22 @@ int ah_ssm_forward(const AhSsmConfig* cfg, const AhSsmWeights* w, float* conv_st
   da.state = ssm_state;
   da.obuf = obuf;
   da.result = res;
+  da.done = done;
   da.D = (int)s.D;
   da.nk = (int)s.nk;
   da.nv = (int)s.nv;
-  da.rows_per_cta = 16;  // 2 rows per warp: the heads' rows spread over many SMs
+  da.rows_per_cta = (kThreads / 32) * kDeltaRowsPerWarp;  // the heads' rows spread over many SMs
   da.eps = cfg->rms_eps;
   da.scale = 1.0f / sqrtf((float)s.D);
-  k_ssm_delta<<<dim3((unsigned)s.nv, (unsigned)((s.D + da.rows_per_cta - 1) / da.rows_per_cta)), kThreads, 0, st>>>(
-      da);
-  AH_LAUNCH_CHECK();
-  k_ssm_norm<<<(int)s.nv, kThreads, 0, st>>>(da);
-  AH_LAUNCH_CHECK();
+  AH_TRY_SSM(launch_pdl(k_ssm_delta, dim3((unsigned)s.nv, (unsigned)((s.D + da.rows_per_cta - 1) / da.rows_per_cta)),
+                        dim3(kThreads), 0, st, da));
   // output projection (ssm.rs:295)
   SsmGemvArgs go{};
   go.x = res;
   go.cols = (int)s.value_dim;
   go.nseg = 1;
   go.seg[0] = GemvSeg{w->out, out, (int)s.d, kSegPlain, nullptr, nullptr};
-  go.vec = s.value_dim % 4 == 0 && aligned16f(w->out);
+  go.vec = s.value_dim % 4 == 0 && aligned16f(w->out) && aligned16f(out);
   return launch_gemv(go, (int)s.d, st);
 }
 

@@ -594,7 +594,7 @@ def ssm_step(dev, stream, peak, cpu=True, steps=200):
     res = {"config": "n_embd 2048, d_state 128, 16 k heads, 32 v heads, d_inner 4096, d_conv 4 (f32 weights)",
            "us_per_token": round(sec * 1e6, 2), "gbs": round(nbytes / sec / 1e9, 1),
            "frac_of_measured_peak": round(nbytes / sec / 1e9 / peak, 4), "bytes_per_token": nbytes,
-           "launches_per_token": 5, "finite": bool(torch.isfinite(out).all().item())}
+           "launches_per_token": 3, "finite": bool(torch.isfinite(out).all().item())}
     if cpu:
         from oracle import oracle as O
         wc = {k: blocks[0].w[k].cpu().numpy() for k in O.SSM_WEIGHTS}

@@ -12,10 +12,12 @@ from test_ssm_cpu import SMALL, ssm_weights
 pytestmark = pytest.mark.gpu
 
 QWEN_LIKE = dict(n_embd=1024, d_state=128, n_group=4, dt_rank=8, d_inner=1024, d_conv=4, eps=1e-6)
+# a short, wide output projection (256 x 4096): several warps share each row
+WIDE_OUT = dict(n_embd=256, d_state=128, n_group=2, dt_rank=32, d_inner=4096, d_conv=4, eps=1e-6)
 
 
-@pytest.mark.parametrize("cfg", [SMALL, QWEN_LIKE, dict(SMALL, d_state=32, d_inner=128, d_conv=1)],
-                         ids=["small", "head128", "no_conv_window"])
+@pytest.mark.parametrize("cfg", [SMALL, QWEN_LIKE, dict(SMALL, d_state=32, d_inner=128, d_conv=1), WIDE_OUT],
+                         ids=["small", "head128", "no_conv_window", "wide_out_split_rows"])
 def test_ssm_forward_matches_oracle(cuda, oracle, cfg):
     from agent_harness_b200.ssm import SsmBlock
     w = ssm_weights(cfg, 3)
