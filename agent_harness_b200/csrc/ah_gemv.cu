@@ -611,14 +611,19 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4(co
 // fused QKV, the LM head): each CTA splits all of x into shared memory once,
 // then walks row tiles rt = blockIdx.x, +gridDim.x, ...; its eight warps take
 // the eight K-chunks of the tile and meet in local shared memory, so a tile
-// costs one CTA barrier instead of a cluster exchange.  The next tile's weights
-// are in flight while the current one is reduced.
+// costs one CTA barrier instead of a cluster exchange.  A tile's nibble and
+// scale planes are contiguous in HBM (KP x 512 B and KP x 8 scale entries), so
+// each arrives by two bulk copies into one of n_stages shared-memory stages,
+// completing on the stage's mbarrier: n_stages tiles per CTA are in flight
+// while earlier ones are multiplied and reduced, and the first n_stages are
+// requested before the kernel waits for its predecessor (weights do not
+// change).  A stage is refilled once every warp has read it.
 template <int NT, bool kF32, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4_rows(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs a) {
   constexpr int BM = 4 * NT;
   using SV = typename ScaleT<kF32>::V;
   constexpr int U = kGemvBatchPairs<NT>;  // block pairs per register batch
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int B = a.batch;
@@ -626,49 +631,71 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4_ro
   const int ppc = (int)a.pairs_per_chunk;  // pairs per warp = ceil(kp / 8)
   const int kbc = 2 * (int)KP;             // the whole K
   const int plane = kbc * 64 + 64;
-  uint8_t* xs = smem;                                                           // [2B][plane]
-  float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc+1]: rows padded
+  const int S = a.n_stages;
+  const uint32_t nib_bytes = (uint32_t)KP * 512u, scl_bytes = (uint32_t)KP * 8u * (uint32_t)sizeof(SV);
+  const uint32_t stage_bytes = nib_bytes + scl_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  uint8_t* base = smem + (size_t)S * stage_bytes + (((size_t)S * 8 + 15) & ~(size_t)15);
+  uint8_t* xs = base;                                                           // [2B][plane]
+  float4* blk_info = reinterpret_cast<float4*>(base + (size_t)2 * B * plane);  // [B][kbc+1]: rows padded
                                                                                 // so tokens hit different banks
   float* part = reinterpret_cast<float*>(blk_info + B * (kbc + 1));             // [warps][16][B]
   float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
   float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
-  int64_t rt = blockIdx.x;
   const int64_t p0 = (int64_t)warp * ppc;
   const int np = (int)max((int64_t)0, min(p0 + ppc, KP) - p0);
-  const uint4* nibp = a.w.nib + (rt * KP + p0) * 32 + lane;
-  const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + (rt * KP + p0) * 8 + g;
-  const int64_t tile_nib = KP * 32 * gridDim.x, tile_scl = KP * 8 * gridDim.x;
-  uint4 wa[U], wb[U];
-  SV sa[U], sb[U];
-  if (rt < r16) {
-    load_pairs<kF32, U>(wa, sa, nibp, sclp, 0, np);
-    load_pairs<kF32, U>(wb, sb, nibp, sclp, U, np);
+  const int64_t my_tiles = r16 > (int64_t)blockIdx.x ? (r16 - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  if (tid == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
   }
+  __syncthreads();
+  int64_t issued = 0;  // tiles requested (thread 0)
+  auto request = [&](int64_t i) {
+    const int s = (int)(i % S);
+    const int64_t rt = blockIdx.x + i * gridDim.x;
+    uint8_t* dst = smem + (size_t)s * stage_bytes;
+    mbar_arrive_expect_tx(&full[s], stage_bytes);
+    bulk_g2s(dst, a.w.nib + rt * KP * 32, nib_bytes, &full[s]);
+    bulk_g2s(dst + nib_bytes, reinterpret_cast<const SV*>(a.w.scales) + rt * KP * 8, scl_bytes, &full[s]);
+  };
+  if (tid == 0)
+    for (; issued < S && issued < my_tiles; ++issued) request(issued);
   if (a.early_trigger) pdl_launch_dependents();
   pdl_wait();
   rms_stats<BM, PRO>(a, wred, tok_inv, tid, lane, warp);
   split_x<PRO>(a, xs, blk_info, plane, kbc, 0, a.w.cols, tok_inv, tid, warp);
   __syncthreads();
   float* fin = wred;  // [16][B]
-  for (; rt < r16; rt += gridDim.x) {
+  int64_t k = 0;
+  for (; k < my_tiles; ++k) {
+    const int64_t rt = blockIdx.x + k * gridDim.x;
+    const int s = (int)(k % S);
+    const bool ok = mbar_wait_bounded(&full[s], (uint32_t)((k / S) & 1), a.err, 0x601);
+    if (__syncthreads_or(!ok)) break;
+    const uint4* snib = reinterpret_cast<const uint4*>(smem + (size_t)s * stage_bytes) + p0 * 32 + lane;
+    const SV* sscl = reinterpret_cast<const SV*>(smem + (size_t)s * stage_bytes + nib_bytes) + p0 * 8 + g;
     float tot[NT][4];
 #pragma unroll
     for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
-    for (int p = 0; p < np; p += 2 * U) {
-      mma_pairs<NT, kF32, U>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
-      if (p + 2 * U < np) load_pairs<kF32, U>(wa, sa, nibp, sclp, p + 2 * U, np);
-      mma_pairs<NT, kF32, U>(tot, wb, sb, p + U, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
-      if (p + 3 * U < np) load_pairs<kF32, U>(wb, sb, nibp, sclp, p + 3 * U, np);
+    for (int p = 0; p < np; p += U) {
+      uint4 w[U];
+      SV sv[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (p + u < np) {
+          w[u] = snib[(p + u) * 32];
+          sv[u] = sscl[(p + u) * 8];
+        }
+      mma_pairs<NT, kF32, U>(tot, w, sv, p, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
     }
-    const bool has_next = rt + gridDim.x < r16;
-    nibp += tile_nib;
-    sclp += tile_scl;
-    if (has_next) {
-      load_pairs<kF32, U>(wa, sa, nibp, sclp, 0, np);
-      load_pairs<kF32, U>(wb, sb, nibp, sclp, U, np);
-    } else if (!a.early_trigger) {
-      pdl_launch_dependents();
+    __syncthreads();  // stage s read by every warp: refill it
+    if (tid == 0 && issued < my_tiles) {
+      fence_proxy_async_smem();
+      request(issued);
+      ++issued;
     }
+    if (k + 1 == my_tiles && !a.early_trigger) pdl_launch_dependents();
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
       const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
@@ -709,8 +736,8 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4_ro
         fin[i] = h;
       }
       // peer slots: the stores reach the other GPUs before this grid completes
-        if (EPI == kEpiStore && a.n_peer > 0) __threadfence_system();
-        if (a.ss_out) {
+      if (EPI == kEpiStore && a.n_peer > 0) __threadfence_system();
+      if (a.ss_out) {
         __syncthreads();
         if (tid < B) {
           float q = 0.0f;
@@ -720,6 +747,9 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4_ro
       }
     }
   }
+  // A wait gave up: let the copies still in flight land (bounded) before exiting.
+  if (k < my_tiles && tid == 0)
+    for (int64_t j = k; j < issued; ++j) mbar_wait_bounded(&full[j % S], (uint32_t)((j / S) & 1), a.err, 0x602);
 }
 
 using GemvKernel = void (*)(const GemvArgs);
@@ -763,6 +793,19 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
   p.smem = (size_t)2 * batch * plane + (size_t)batch * (kbc + 1) * 16 + (size_t)kGemvWarps * 16 * batch * 4 +
            (size_t)kGemvMaxBatch * 4 + (size_t)kGemvWarps * (4 * p.nt) * 4 + (size_t)16 * batch * 4 + 16;
   if (!rows_mode) p.smem += (size_t)2 * kGemvCluster * 16 * batch * 4;  // DSMEM partial slots
+  p.smem_base = p.smem;
+  p.n_stages = 0;
+  if (rows_mode) {  // tile stages (nibbles + scales) and their mbarriers in front
+    const size_t stage = (size_t)w.kp * 512 + (size_t)w.kp * 8 * (w.f32_scales ? 16 : 8);
+    int n = 0;
+    while (n < kGemvMaxStages &&
+           (size_t)(n + 1) * stage + (((size_t)(n + 1) * 8 + 15) & ~(size_t)15) + p.smem_base <= (size_t)kGemvRowsCtaSmem)
+      ++n;
+    if (n >= 2) {
+      p.n_stages = n;
+      p.smem = (size_t)n * stage + (((size_t)n * 8 + 15) & ~(size_t)15) + p.smem_base;
+    }
+  }
   return p;
 }
 
@@ -836,8 +879,9 @@ int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
 }
 
 // Cluster mode for GEMVs whose row groups fit in one wave (one pass each);
-// rows mode for many-tile GEMVs whose full-K split fits comfortably in shared
-// memory (it is then amortised over several tiles per CTA).
+// rows mode for many-tile GEMVs whose full-K split of x fits comfortably in
+// shared memory beside at least two tile stages (it is then amortised over
+// several tiles per CTA).
 int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, GemvKernel* kern, int* cap) {
   GemvPlan pc = gemv_plan(w, batch, false);
   if (pc.smem > (size_t)kGemvSmemLimit)
@@ -849,7 +893,8 @@ int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, G
   AH_TRY_GEMV(kernel_setup(kc, pc, &ccap));
   const int64_t n_rg = (w.r16 + kGemvWarps - 1) / kGemvWarps;
   GemvPlan pr = gemv_plan(w, batch, true);
-  if (n_rg > ccap && pr.smem <= (size_t)kGemvRowsSmem) {
+  if (n_rg > ccap && pr.smem_base <= (size_t)kGemvRowsSmem && pr.n_stages >= 2 && aligned16(w.nib) &&
+      aligned16(w.scales)) {
     GemvKernel kr = select_kernel(pr, w.f32_scales, pro, epi);
     int rcap = 0;
     AH_TRY_GEMV(kernel_setup(kr, pr, &rcap));
@@ -922,6 +967,9 @@ int gemv_launch_one(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   int cap = 0;
   AH_TRY_GEMV(choose_plan(a.w, a.batch, pro, epi, &plan, &kern, &cap));
   a.pairs_per_chunk = plan.pairs_per_chunk;
+  a.n_stages = plan.n_stages;
+  a.err = device_error_word();
+  AH_REQUIRE(!plan.rows_mode || a.err, "gemv: device error word unavailable");
   cudaLaunchConfig_t cfg{};
   cfg.blockDim = dim3(kGemvThreads, 1, 1);
   cfg.dynamicSmemBytes = plan.smem;

@@ -47,7 +47,9 @@ constexpr int kGemvBatchPairs = NT >= 3 ? 2 : kGemvU;
 template <int NT>
 constexpr int kGemvMinBlocks = NT >= 3 ? 2 : 0;
 constexpr int kGemvSmemLimit = 200 * 1024;
-constexpr int kGemvRowsSmem = 96 * 1024;   // rows mode only while two CTAs fit per SM
+constexpr int kGemvRowsSmem = 96 * 1024;   // rows mode only while x's split takes at most this much
+constexpr int kGemvRowsCtaSmem = 112 * 1024;  // rows mode: two CTAs (16 warps) per SM
+constexpr int kGemvMaxStages = 4;          // rows mode: row tiles in flight per CTA
 
 struct Q4Tiled {
   const uint4* nib;    // [r16][kp][32]
@@ -80,6 +82,8 @@ struct GemvArgs {
   float* ss_out;
   int64_t pairs_per_chunk; // block pairs per K-chunk (cluster CTA)
   int early_trigger;       // set by the launcher: grid fits in one resident wave
+  int n_stages;            // rows mode: row tiles in flight in shared memory
+  int* err;                // device error word (a bounded wait that gave up)
   // Store epilogue scatter (tensor-parallel all-reduce over peer memory): with
   // n_peer > 0 every output element goes to peer_y[p] + row*peer_row + b for
   // p < n_peer (local and peer GPUs' receive buffers) instead of y: rows of

@@ -14,6 +14,8 @@ struct GemvPlan {
   int ksplit;               // always 1: a launch covers the full K
   size_t smem;              // dynamic shared memory bytes
   bool rows_mode;           // persistent full-K CTAs instead of clusters
+  size_t smem_base;         // rows mode: shared memory besides the tile stages
+  int n_stages;             // rows mode: row tiles in flight (0: rows mode unavailable)
 };
 
 GemvPlan gemv_plan(const Q4Tiled& w, int batch);
