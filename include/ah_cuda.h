@@ -374,7 +374,10 @@ typedef struct {
 typedef struct {
   const float *wqkv, *wqkv_gate, *conv1d, *dt_bias, *a, *alpha, *beta, *norm, *out;
 } AhSsmWeights;
-/* Device workspace one step needs (caller-allocated, 16-byte aligned). */
+/* Device workspace one step needs (caller-allocated, 16-byte aligned, any
+ * contents).  It holds the step's intermediates and per-head completion
+ * counters, so one workspace serves one step at a time: steps that share it run
+ * on one stream. */
 AH_API int ah_ssm_workspace_bytes(const AhSsmConfig* cfg, size_t* bytes);
 /* Replaces inference/ssm.rs:171-296 SsmBlock::forward(input, state, config):
  * one token, x [n_embd] -> out [n_embd], updating the state in place:
