@@ -96,3 +96,40 @@ def test_ssm_oracle_rejects_mismatched_head_dims(oracle):
     with pytest.raises(ValueError):
         O.ssm_forward(cfg, w, np.zeros((3, 192), np.float32), np.zeros(4 * 32 * 16, np.float32),
                       np.zeros(64, np.float32))
+
+
+def _pad4(n):
+    return (n + 3) // 4 * 4
+
+
+@pytest.mark.parametrize("cfg", [SMALL, dict(n_embd=2048, d_state=128, n_group=16, dt_rank=32, d_inner=4096,
+                                             d_conv=4, eps=1e-6)], ids=["small", "n2048"])
+def test_ssm_workspace_bytes_on_host(cfg):
+    # host arithmetic of the C-ABI, no device needed: the step's intermediates
+    # (conv output, z, the normed result, o) and beta, gate and the per-head
+    # completion counters
+    import ctypes as C
+    from agent_harness_b200 import _lib
+    from agent_harness_b200.ssm import _Cfg
+    c = _Cfg(cfg["n_embd"], cfg["d_state"], cfg["n_group"], cfg["dt_rank"], cfg["d_inner"], cfg["d_conv"],
+             cfg["eps"])
+    n = C.c_size_t()
+    _lib.call("ah_ssm_workspace_bytes", C.byref(c), C.byref(n))
+    conv_dim = 2 * cfg["n_group"] * cfg["d_state"] + cfg["d_inner"]
+    want = 4 * (_pad4(conv_dim) + 3 * _pad4(cfg["d_inner"]) + 3 * _pad4(cfg["dt_rank"]))
+    assert n.value == want
+
+
+@pytest.mark.parametrize("bad", [dict(d_inner=128),            # head_v_dim 32 != head_k_dim 16 (ssm.rs:239)
+                                 dict(dt_rank=3, d_inner=48),   # v heads not a multiple of k heads
+                                 dict(d_state=512, d_inner=2048),  # head dim above 256
+                                 dict(n_embd=0)], ids=["head_dims", "head_groups", "head_dim_max", "zero_dim"])
+def test_ssm_config_rejected_on_host(bad):
+    import ctypes as C
+    from agent_harness_b200 import _lib
+    from agent_harness_b200.ssm import _Cfg
+    cfg = dict(SMALL, **bad)
+    c = _Cfg(cfg["n_embd"], cfg["d_state"], cfg["n_group"], cfg["dt_rank"], cfg["d_inner"], cfg["d_conv"],
+             cfg["eps"])
+    with pytest.raises(_lib.AhError):
+        _lib.call("ah_ssm_workspace_bytes", C.byref(c), C.byref(C.c_size_t()))
