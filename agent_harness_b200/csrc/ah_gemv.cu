@@ -671,40 +671,43 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs
   for (; k < my_tiles; ++k) {
     const int64_t rt = blockIdx.x + k * gridDim.x;
     const int s = (int)(k % S);
-    const bool ok = mbar_wait_bounded(&full[s], (uint32_t)((k / S) & 1), a.err, 0x601);
-    if (__syncthreads_or(!ok)) break;
-    const uint4* snib = reinterpret_cast<const uint4*>(smem + (size_t)s * stage_bytes) + p0 * 32 + lane;
-    const SV* sscl = reinterpret_cast<const SV*>(smem + (size_t)s * stage_bytes + nib_bytes) + p0 * 8 + g;
-    float tot[NT][4];
+    // warp-uniform, so a warp runs its mma.sync with all lanes or not at all
+    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full[s], (uint32_t)((k / S) & 1), a.err, 0x601));
+    if (ok) {
+      const uint4* snib = reinterpret_cast<const uint4*>(smem + (size_t)s * stage_bytes) + p0 * 32 + lane;
+      const SV* sscl = reinterpret_cast<const SV*>(smem + (size_t)s * stage_bytes + nib_bytes) + p0 * 8 + g;
+      float tot[NT][4];
 #pragma unroll
-    for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
-    for (int p = 0; p < np; p += U) {
-      uint4 w[U];
-      SV sv[U];
+      for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
+      for (int p = 0; p < np; p += U) {
+        uint4 w[U];
+        SV sv[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (p + u < np) {
-          w[u] = snib[(p + u) * 32];
-          sv[u] = sscl[(p + u) * 8];
+        for (int u = 0; u < U; ++u)
+          if (p + u < np) {
+            w[u] = snib[(p + u) * 32];
+            sv[u] = sscl[(p + u) * 8];
+          }
+        mma_pairs<NT, kF32, U>(tot, w, sv, p, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
+      }
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
+        if (b < B) {
+          part[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
+          part[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
         }
-      mma_pairs<NT, kF32, U>(tot, w, sv, p, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
+      }
     }
-    __syncthreads();  // stage s read by every warp: refill it
+    // one barrier: stage s read by every warp (refill it), the partials are in
+    // place, and every wait succeeded
+    if (__syncthreads_or(!ok)) break;
     if (tid == 0 && issued < my_tiles) {
       fence_proxy_async_smem();
       request(issued);
       ++issued;
     }
     if (k + 1 == my_tiles && !a.early_trigger) pdl_launch_dependents();
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
-      if (b < B) {
-        part[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
-        part[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
-      }
-    }
-    __syncthreads();
     for (int i = tid; i < 16 * B; i += kGemvThreads) {
       float v = 0.0f;
 #pragma unroll
