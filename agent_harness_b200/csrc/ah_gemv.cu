@@ -623,7 +623,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs
   constexpr int BM = 4 * NT;
   using SV = typename ScaleT<kF32>::V;
   constexpr int U = kGemvBatchPairs<NT>;  // block pairs per register batch
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int B = a.batch;
@@ -642,6 +642,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs
   float* part = reinterpret_cast<float*>(blk_info + B * (kbc + 1));             // [warps][16][B]
   float* tok_inv = part + kGemvWarps * 16 * B;                                  // [16]
   float* wred = tok_inv + kGemvMaxBatch;                                        // [warps][BM], then [16][B]
+  float* part_odd = wred + kGemvWarps * BM + 16 * B;                            // partials of odd tiles
   const int64_t p0 = (int64_t)warp * ppc;
   const int np = (int)max((int64_t)0, min(p0 + ppc, KP) - p0);
   const int64_t my_tiles = r16 > (int64_t)blockIdx.x ? (r16 - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
@@ -690,12 +691,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs
           }
         mma_pairs<NT, kF32, U>(tot, w, sv, p, np, B, g, t, xs, blk_info, plane, kbc, (int)(2 * p0));
       }
+      float* pw = (k & 1) ? part_odd : part;
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
         const int b = 4 * j + t;  // columns 2t (hi) and 2t+1 (lo) of tile j
         if (b < B) {
-          part[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
-          part[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
+          pw[(warp * 16 + g) * B + b] = tot[j][0] + tot[j][1];
+          pw[(warp * 16 + g + 8) * B + b] = tot[j][2] + tot[j][3];
         }
       }
     }
@@ -708,46 +710,53 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs
       ++issued;
     }
     if (k + 1 == my_tiles && !a.early_trigger) pdl_launch_dependents();
-    for (int i = tid; i < 16 * B; i += kGemvThreads) {
-      float v = 0.0f;
+    // warp k % 8 reduces tile k and runs its epilogue while the other warps
+    // go on to tile k + 1 (partials alternate between two buffers; the next
+    // barrier waits for this warp)
+    if (warp == (int)(k & (kGemvWarps - 1))) {
+      const float* pk = (k & 1) ? part_odd : part;
+      for (int i = lane; i < 16 * B; i += 32) {
+        float v = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kGemvWarps; ++w) v += part[w * 16 * B + i];  // K-chunk order
-      fin[i] = v;
-    }
-    __syncthreads();
-    if (EPI == kEpiSwiglu) {
-      for (int i = tid; i < 8 * B; i += kGemvThreads) {
-        const int r = i / B, b = i - r * B;
-        const int64_t o = rt * 8 + r;
-        if (o < a.w.rows / 2) a.y[b * a.y_stride + o] = silu_ref(fin[r * B + b]) * fin[(r + 8) * B + b];
+        for (int w = 0; w < kGemvWarps; ++w) v += pk[w * 16 * B + i];  // K-chunk order
+        fin[i] = v;
       }
-    } else {
-      for (int i = tid; i < 16 * B; i += kGemvThreads) {
-        const int r = i / B, b = i - r * B;
-        const int64_t R = rt * 16 + r;
-        float h = 0.0f;
-        if (R < a.w.rows) {
-          if (EPI == kEpiStore && a.n_peer > 0) {
-            h = fin[i];
-            for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][R * a.peer_row + b] = h;  // NVLink stores
-          } else {
-            float* d = a.y + b * a.y_stride + R;
-            h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
-            *d = h;
+      __syncwarp();
+      if (EPI == kEpiSwiglu) {
+        for (int i = lane; i < 8 * B; i += 32) {
+          const int r = i / B, b = i - r * B;
+          const int64_t o = rt * 8 + r;
+          if (o < a.w.rows / 2) a.y[b * a.y_stride + o] = silu_ref(fin[r * B + b]) * fin[(r + 8) * B + b];
+        }
+      } else {
+        for (int i = lane; i < 16 * B; i += 32) {
+          const int r = i / B, b = i - r * B;
+          const int64_t R = rt * 16 + r;
+          float h = 0.0f;
+          if (R < a.w.rows) {
+            if (EPI == kEpiStore && a.n_peer > 0) {
+              h = fin[i];
+              for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][R * a.peer_row + b] = h;  // NVLink stores
+            } else {
+              float* d = a.y + b * a.y_stride + R;
+              h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
+              *d = h;
+            }
+          }
+          fin[i] = h;
+        }
+        // peer slots: the stores reach the other GPUs before this grid completes
+        if (EPI == kEpiStore && a.n_peer > 0) __threadfence_system();
+        if (a.ss_out) {
+          __syncwarp();
+          if (lane < B) {
+            float q = 0.0f;
+            for (int r = 0; r < 16; ++r) q = fmaf(fin[r * B + lane], fin[r * B + lane], q);
+            a.ss_out[lane * a.w.r16 + rt] = q;
           }
         }
-        fin[i] = h;
       }
-      // peer slots: the stores reach the other GPUs before this grid completes
-      if (EPI == kEpiStore && a.n_peer > 0) __threadfence_system();
-      if (a.ss_out) {
-        __syncthreads();
-        if (tid < B) {
-          float q = 0.0f;
-          for (int r = 0; r < 16; ++r) q = fmaf(fin[r * B + tid], fin[r * B + tid], q);
-          a.ss_out[tid * a.w.r16 + rt] = q;
-        }
-      }
+      __syncwarp();
     }
   }
   // A wait gave up: let the copies still in flight land (bounded) before exiting.
@@ -796,6 +805,7 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
   p.smem = (size_t)2 * batch * plane + (size_t)batch * (kbc + 1) * 16 + (size_t)kGemvWarps * 16 * batch * 4 +
            (size_t)kGemvMaxBatch * 4 + (size_t)kGemvWarps * (4 * p.nt) * 4 + (size_t)16 * batch * 4 + 16;
   if (!rows_mode) p.smem += (size_t)2 * kGemvCluster * 16 * batch * 4;  // DSMEM partial slots
+  if (rows_mode) p.smem += (size_t)kGemvWarps * 16 * batch * 4;  // partials of odd tiles
   p.smem_base = p.smem;
   p.n_stages = 0;
   if (rows_mode) {  // tile stages (nibbles + scales) and their mbarriers in front
