@@ -622,7 +622,7 @@ template <int NT, bool kF32, int PRO, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs a) {
   constexpr int BM = 4 * NT;
   using SV = typename ScaleT<kF32>::V;
-  constexpr int U = kGemvBatchPairs<NT>;  // block pairs per register batch
+  constexpr int U = kGemvBatchPairs<NT>;  // block pairs read from the stage per batch
   extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;

@@ -39,8 +39,8 @@ constexpr int kGemvU = 4;                 // block pairs per register batch (two
 // CTAs fit per SM.
 template <int NT>
 constexpr int kGemvBatchPairs = NT >= 3 ? 2 : kGemvU;
-// Minimum resident CTAs per SM for __launch_bounds__: 2 for wide batches (a
-// 128-register cap); 0 leaves narrow batches at the compiler's own choice
+// Minimum resident CTAs per SM for the cluster kernel's __launch_bounds__
+// (the rows kernel always asks for 2): 2 for wide batches (a 128-register cap); 0 leaves narrow batches at the compiler's own choice
 // (~128 registers for 1 tile, ~138 for 2).  An explicit 1 would let those
 // take 150-200 registers, i.e. one CTA per SM, which made batch-1 GEMVs up
 // to 1.9x slower.
