@@ -891,10 +891,11 @@ int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
   return AH_OK;
 }
 
-// Cluster mode for GEMVs whose row groups fit in one wave (one pass each);
-// rows mode for many-tile GEMVs whose full-K split of x fits comfortably in
-// shared memory beside at least two tile stages (it is then amortised over
-// several tiles per CTA).
+// Cluster mode for GEMVs whose row groups fit in one wave (one pass each) and
+// for those with fewer than two row tiles per resident rows-mode CTA; rows mode
+// for many-tile GEMVs whose full-K split of x fits comfortably in shared
+// memory beside at least two tile stages (it is then amortised over several
+// tiles per CTA).
 int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, GemvKernel* kern, int* cap) {
   GemvPlan pc = gemv_plan(w, batch, false);
   if (pc.smem > (size_t)kGemvSmemLimit)
@@ -911,7 +912,7 @@ int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, G
     GemvKernel kr = select_kernel(pr, w.f32_scales, pro, epi);
     int rcap = 0;
     AH_TRY_GEMV(kernel_setup(kr, pr, &rcap));
-    if (rcap > 0) {
+    if (rcap > 0 && w.r16 >= 2 * (int64_t)rcap) {  // the stages pay off from two tiles per CTA
       *plan = pr;
       *kern = kr;
       *cap = rcap;

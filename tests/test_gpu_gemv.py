@@ -161,10 +161,10 @@ def test_golden_gemv(cuda):
 
 
 @pytest.mark.parametrize("rows,cols,batch", [(1200, 96, 1), (1504, 4096 + 32, 1), (2048, 4096, 3),
-                                             (4096, 14336, 1), (1216, 1024, 2)])
+                                             (4096, 14336, 1), (1216, 1024, 2), (12800, 256, 1), (9600, 512, 2)])
 def test_many_row_tile_shapes(cuda, oracle, rows, cols, batch):
-    # 75 .. 256 row tiles (cluster and rows schedules), incl. K = 4096+32
-    # columns (65 block pairs) and K = 14336
+    # 75 .. 800 row tiles (cluster and rows schedules; rows mode from two tiles
+    # per resident CTA), incl. K = 4096+32 columns (65 block pairs) and K = 14336
     from agent_harness_b200 import kernels as K
     blocks, W = _q4_0_weight(K, rows, cols, rows + cols + batch, cuda)
     x = K.fill_normal(batch * cols, 0.0, 1.0, 7 + batch, device=cuda).reshape(batch, cols)
