@@ -12,6 +12,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libah_cuda.so")
 
 AH_OK, AH_EINVAL, AH_ENOMEM, AH_ECUDA, AH_ENCCL, AH_ETIMEOUT, AH_EUNSUPPORTED = 0, -1, -2, -3, -4, -5, -6
+AH_INJECT_ALLOC, AH_INJECT_NCCL, AH_INJECT_LAUNCH = 1, 2, 3
 
 vp = C.c_void_p
 i64 = C.c_int64
@@ -28,6 +29,9 @@ SIGNATURES = {
     "ah_version": (i32, []),
     "ah_device_init": (i32, [i32]),
     "ah_check_device_error": (i32, [vp]),
+    "ah_device_alloc_count": (i64, []),
+    "ah_debug_inject_failure": (i32, [i32, i64]),
+    "ah_debug_residual_add_peer": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, vp]),
     "ah_packed_bytes": (i64, [i64]),
     "ah_n_groups": (i64, [i64, i64]),
     "ah_quantized_bytes": (i64, [i64, i64]),

@@ -41,10 +41,23 @@ int sm_count();  // SM count of the current device (cached per device)
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Per-device error word (device memory, zero-initialised) that kernels with
-// bounded waits set when a wait gives up; read and cleared by
-// ah_check_device_error.  Allocated on first use for the current device.
+// Per-device error word (a zero-initialised __device__ variable of this
+// library's module) that kernels with bounded waits set when a wait gives up;
+// read and cleared by ah_check_device_error.  Looking it up allocates nothing.
 int* device_error_word();
+
+// Every device allocation of the library goes through here: counted for
+// ah_device_alloc_count, and failed on request by ah_debug_inject_failure.
+cudaError_t dev_malloc(void** p, size_t bytes);
+template <typename T>
+inline cudaError_t dev_malloc(T** p, size_t bytes) {
+  void* v = nullptr;
+  const cudaError_t e = dev_malloc(&v, bytes);
+  *p = static_cast<T*>(v);
+  return e;
+}
+// True when an armed injection of this AH_INJECT_* kind fires on this call.
+bool inject_failure(int kind);
 // Codes in the error word: 0x5xxx input indices a kernel found out of range
 // (AH_EINVAL); every other code is a bounded wait that gave up (AH_ETIMEOUT).
 constexpr int kDeviceIndexError = 0x5000;

@@ -910,7 +910,7 @@ struct AhModel {
 namespace {
 
 int dalloc(AhModel* m, void** p, size_t bytes) {
-  if (cudaMalloc(p, bytes) != cudaSuccess) {
+  if (ah::dev_malloc(p, bytes) != cudaSuccess) {
     cudaGetLastError();
     *p = nullptr;
     return fail(AH_ENOMEM, "model: cudaMalloc of %zu bytes failed", bytes);
@@ -1288,12 +1288,27 @@ int ah_model_create_tp(const AhModelConfig* cfg, int rank, int world, const void
   if (world > 1) {
     ncclUniqueId id;
     std::memcpy(&id, nccl_id, sizeof(id));
+    if (inject_failure(AH_INJECT_NCCL))
+      return fail(AH_ENCCL, "ncclCommInitRank(rank %d of %d) failed (injected)", rank, world);
     if (ncclCommInitRank(&comm, world, id, rank) != ncclSuccess)
       return fail(AH_ENCCL, "ncclCommInitRank(rank %d of %d) failed", rank, world);
   }
   const int rc = model_create(cfg, rank, world, comm, out);
   if (rc != AH_OK && comm) ncclCommDestroy(comm);
   return rc;
+}
+
+int ah_debug_residual_add_peer(float* hidden, const float* slots, int world, int batch, int d, float* ss,
+                               const unsigned* flags, const unsigned* seq, void* stream) {
+  AH_REQUIRE(hidden && slots && ss && flags && seq, "debug_residual_add_peer: null argument");
+  AH_REQUIRE(world >= 1 && world <= 8 && batch >= 1 && batch <= 16 && d > 0 && d % 16 == 0,
+             "debug_residual_add_peer: world 1..8, batch 1..16, d a positive multiple of 16");
+  int* err = device_error_word();
+  AH_REQUIRE(err != nullptr, "debug_residual_add_peer: device error word unavailable");
+  k_residual_add_peer<<<dim3((d + 255) / 256, batch), 256, 0, as_stream(stream)>>>(hidden, slots, world, batch, ss, d,
+                                                                                   flags, seq, err);
+  AH_LAUNCH_CHECK();
+  return AH_OK;
 }
 
 int ah_model_ipc_handle(AhModel* m, void* handle_out, size_t bytes) {
@@ -1414,7 +1429,7 @@ int load_projection(AhModel* m, int kind, int layer, const ProjSrc& src, cudaStr
     cudaFree(p);
     p = nullptr;
   }
-  if (!p && cudaMalloc(&p, proj_bytes(src.fmt, rows, d)) != cudaSuccess) {
+  if (!p && ah::dev_malloc(&p, proj_bytes(src.fmt, rows, d)) != cudaSuccess) {
     cudaGetLastError();
     p = nullptr;
     return fail(AH_ENOMEM, "model_load_tensor: staging of %zu bytes", proj_bytes(src.fmt, rows, d));
@@ -1534,7 +1549,7 @@ int ah_model_load_tensor_f32(AhModel* m, int kind, int layer, const float* data,
   const int64_t n = rows * cols;
   float* sc = nullptr;
   uint8_t* pk = nullptr;
-  if (cudaMalloc(&sc, (size_t)(n / 32) * 4) != cudaSuccess || cudaMalloc(&pk, (size_t)n / 2) != cudaSuccess) {
+  if (ah::dev_malloc(&sc, (size_t)(n / 32) * 4) != cudaSuccess || ah::dev_malloc(&pk, (size_t)n / 2) != cudaSuccess) {
     cudaGetLastError();
     if (sc) cudaFree(sc);
     return fail(AH_ENOMEM, "model_load_tensor_f32: quantization buffers of %lld elements", (long long)n);
@@ -1565,7 +1580,7 @@ int ah_model_init_random(AhModel* m, uint64_t seed, float w_std, float emb_std, 
   const int64_t max_cols = std::max<int64_t>({(int64_t)m->dq, (int64_t)m->nff, (int64_t)d});
   void* tmp = nullptr;
   const size_t tmp_bytes = (size_t)std::max<int64_t>(max_rows * (d / 32), (int64_t)d * (max_cols / 32)) * 18;
-  if (cudaMalloc(&tmp, tmp_bytes) != cudaSuccess) {
+  if (ah::dev_malloc(&tmp, tmp_bytes) != cudaSuccess) {
     cudaGetLastError();
     return fail(AH_ENOMEM, "model_init_random: staging of %zu bytes", tmp_bytes);
   }
@@ -1596,7 +1611,7 @@ int ah_model_init_random(AhModel* m, uint64_t seed, float w_std, float emb_std, 
   if (rc == AH_OK) {
     // the LM head is the largest tensor: generate this rank's rows in their own buffer
     void* lmb = nullptr;
-    if (cudaMalloc(&lmb, (size_t)m->nvoc * (d / 32) * 18) != cudaSuccess) {
+    if (ah::dev_malloc(&lmb, (size_t)m->nvoc * (d / 32) * 18) != cudaSuccess) {
       cudaGetLastError();
       rc = fail(AH_ENOMEM, "model_init_random: output.weight staging");
     } else {
@@ -1664,7 +1679,7 @@ int ah_model_generate(AhModel* m, const int32_t* prompt, int batch, int n_prompt
   AH_TRY(ah_model_reset(m, batch, stream));
   if (m->d_prompt) cudaFree(m->d_prompt);
   m->d_prompt = nullptr;
-  if (cudaMalloc(&m->d_prompt, (size_t)batch * n_prompt * 4) != cudaSuccess) {
+  if (ah::dev_malloc(&m->d_prompt, (size_t)batch * n_prompt * 4) != cudaSuccess) {
     cudaGetLastError();
     return fail(AH_ENOMEM, "model_generate: prompt buffer");
   }

@@ -344,7 +344,7 @@ int check_digits(int a, int b) {
 }
 
 int upload(AhDedupTable* t, float** dst, const std::vector<float>& src) {
-  if (cudaMalloc(dst, src.size() * sizeof(float)) != cudaSuccess) {
+  if (ah::dev_malloc(dst, src.size() * sizeof(float)) != cudaSuccess) {
     cudaGetLastError();
     *dst = nullptr;
     return fail(AH_ENOMEM, "dedup: cudaMalloc of %zu bytes failed", src.size() * sizeof(float));
@@ -606,10 +606,10 @@ int ah_host_dedup_decompress_all(const uint16_t* prefixes, int64_t n_prefix, con
   uint8_t* ds = nullptr;
   float* dout = nullptr;
   int rc = AH_OK;
-  if (cudaMalloc(&dp, std::max<int64_t>(n_pidx, 1) * 2) != cudaSuccess ||
-      cudaMalloc(&dt, std::max<int64_t>(n_tidx, 1) * 2) != cudaSuccess ||
-      cudaMalloc(&ds, std::max<int64_t>(n_sign, 1)) != cudaSuccess ||
-      cudaMalloc(&dout, (size_t)count * 4) != cudaSuccess) {
+  if (ah::dev_malloc(&dp, std::max<int64_t>(n_pidx, 1) * 2) != cudaSuccess ||
+      ah::dev_malloc(&dt, std::max<int64_t>(n_tidx, 1) * 2) != cudaSuccess ||
+      ah::dev_malloc(&ds, std::max<int64_t>(n_sign, 1)) != cudaSuccess ||
+      ah::dev_malloc(&dout, (size_t)count * 4) != cudaSuccess) {
     cudaGetLastError();
     rc = fail(AH_ENOMEM, "dedup_decompress_all: device allocation failed");
   }

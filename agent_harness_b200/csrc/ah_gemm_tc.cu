@@ -524,13 +524,18 @@ int gemm_launch(const GemmArgs& a, int64_t grid_x, int64_t grid_y, cudaStream_t 
   using L = GemmSmem<kHalves>;
   static_assert(L::kDynamic <= 227 * 1024, "shared memory budget");
   auto kern = k_gemm_q4_tc<kHalves, kF32>;
-  static int configured_device = -1;
+  // the shared-memory cap is set once per device, race-free across host threads
+  constexpr int kMaxDevices = 64;
+  static std::once_flag once[kMaxDevices];
+  static cudaError_t set_rc[kMaxDevices];
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    AH_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynamic));
-    configured_device = dev;
-  }
+  AH_CUDA_TRY(cudaGetDevice(&dev));
+  AH_REQUIRE(dev >= 0 && dev < kMaxDevices, "gemm: device %d out of range", dev);
+  std::call_once(once[dev], [&] {
+    set_rc[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::kDynamic);
+  });
+  if (set_rc[dev] != cudaSuccess)
+    return fail(AH_ECUDA, "gemm: cudaFuncSetAttribute: %s", cudaGetErrorString(set_rc[dev]));
   // programmatic dependent launch: the prologue (barriers, TMEM, the first
   // weight stages) overlaps the activation prep; A is read after pdl_wait()
   cudaLaunchConfig_t cfg{};

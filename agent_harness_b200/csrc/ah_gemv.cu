@@ -149,7 +149,7 @@ int q4w_alloc(int64_t rows, int64_t cols, bool engine, AhQ4Weight** out) {
   w->t.f32_scales = engine;
   const size_t nib_bytes = (size_t)w->t.r16 * w->t.kp * 32 * 16;
   const size_t sc_bytes = (size_t)w->t.r16 * w->t.kp * 8 * (engine ? 16 : 8);
-  if (cudaMalloc(&w->nib_alloc, nib_bytes) != cudaSuccess || cudaMalloc(&w->scale_alloc, sc_bytes) != cudaSuccess) {
+  if (ah::dev_malloc(&w->nib_alloc, nib_bytes) != cudaSuccess || ah::dev_malloc(&w->scale_alloc, sc_bytes) != cudaSuccess) {
     cudaGetLastError();
     if (w->nib_alloc) cudaFree(w->nib_alloc);
     if (w->scale_alloc) cudaFree(w->scale_alloc);
@@ -1010,6 +1010,7 @@ int gemv_launch_one(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   ++na;
   cfg.attrs = attr;
   cfg.numAttrs = na;
+  if (inject_failure(AH_INJECT_LAUNCH)) return fail(AH_ECUDA, "gemv: kernel launch failed (injected)");
   AH_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, a));
   return AH_OK;
 }
@@ -1108,7 +1109,7 @@ int ah_q4w_gemv_host(const AhQ4Weight* cw, const float* x_host, float* y_host, i
   std::lock_guard<std::mutex> lk(w->mu);
   const size_t x_max = ((size_t)kGemvMaxBatch * w->t.cols * 4 + 255) / 256 * 256;
   if (!w->stage) {
-    if (cudaMalloc(&w->stage, x_max + (size_t)kGemvMaxBatch * w->t.rows * 4) != cudaSuccess) {
+    if (ah::dev_malloc(&w->stage, x_max + (size_t)kGemvMaxBatch * w->t.rows * 4) != cudaSuccess) {
       cudaGetLastError();
       w->stage = nullptr;
       return fail(AH_ENOMEM, "q4w_gemv_host: staging allocation failed");

@@ -51,7 +51,7 @@ int stage_buf(int slot, size_t bytes, void** out) {
     if (t_stage.bufs[slot]) cudaFree(t_stage.bufs[slot]);
     t_stage.bufs[slot] = nullptr;
     t_stage.caps[slot] = 0;
-    if (cudaMalloc(&t_stage.bufs[slot], bytes) != cudaSuccess) {
+    if (ah::dev_malloc(&t_stage.bufs[slot], bytes) != cudaSuccess) {
       cudaGetLastError();
       return fail(AH_ENOMEM, "host staging: cudaMalloc of %zu bytes failed", bytes);
     }

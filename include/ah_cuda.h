@@ -59,6 +59,28 @@ AH_API int ah_device_init(int device);
  * (AH_ETIMEOUT when a wait gave up since the last call). */
 AH_API int ah_check_device_error(void* stream);
 
+/* ---- diagnostics (no reference counterpart) --------------------------------- */
+/* Device allocations (cudaMalloc) the library has made since it was loaded,
+ * over all threads and devices: a caller can check that an entry allocates
+ * nothing by reading it before and after the call. */
+AH_API int64_t ah_device_alloc_count(void);
+/* Host-side failure injection for tests: the nth library call of `kind` from
+ * now on (1 = the next one) fails as if the underlying call had failed, and
+ * its status travels to the caller as usual (ah_last_error names the
+ * injection); nth = 0 disarms.  Nothing is injected on the device. */
+#define AH_INJECT_ALLOC 1  /* a device allocation       -> AH_ENOMEM */
+#define AH_INJECT_NCCL 2   /* ncclCommInitRank          -> AH_ENCCL  */
+#define AH_INJECT_LAUNCH 3 /* a fused GEMV kernel launch -> AH_ECUDA  */
+AH_API int ah_debug_inject_failure(int kind, int64_t nth);
+/* Runs the tensor-parallel decoder's peer all-reduce step once on caller device
+ * buffers: waits (bounded, ~0.4 s) until flags[r] >= *seq for every rank r <
+ * world, then hidden[b][i] += sum_r slots[r][i][b] (rank order) and writes the
+ * per-16-row sums of squares ss[b][d/16].  A flag that never reaches *seq makes
+ * the wait give up: ah_check_device_error then returns AH_ETIMEOUT and hidden
+ * is left as it was.  For tests of the bounded wait on one GPU. */
+AH_API int ah_debug_residual_add_peer(float* hidden, const float* slots, int world, int batch, int d, float* ss,
+                                      const unsigned* flags, const unsigned* seq, void* stream);
+
 /* ---- sizes (models/quantization.rs:423-435) -------------------------------- */
 AH_API int64_t ah_packed_bytes(int64_t n_elements);
 AH_API int64_t ah_n_groups(int64_t n_elements, int64_t group_size);
@@ -172,7 +194,10 @@ AH_API int ah_q4w_gemm(const AhQ4Weight* w, const float* a_dev, int64_t lda, int
 /* No counterpart in the reference: ah_q4w_gemm without a caller workspace.  The
  * workspace lives in a fixed 8 MiB static device buffer per device (at 4096
  * columns: up to 768 tokens); larger requests return AH_EINVAL before any
- * launch.  Calls that overlap in time on one device race on that buffer. */
+ * launch.  Calls that overlap in time on one device race on that buffer.  The
+ * call allocates nothing, on its first call on a device (even before
+ * ah_device_init) as on later ones: the buffer and the device error word are
+ * module variables whose addresses are looked up, not allocated. */
 AH_API int ah_q4w_gemm_noalloc(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev,
                                int64_t ldc, void* stream);
 
