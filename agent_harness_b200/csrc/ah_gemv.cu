@@ -2,6 +2,7 @@
 // dequant+GEMV kernel (batch 1..16) with its prologue/epilogue variants, and
 // the C-ABI entry points built on it.  Layout and arithmetic: ah_gemv.cuh.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <utility>
@@ -21,6 +22,7 @@ struct AhQ4Weight {
   int64_t weight_bytes = 0;
   void* nib_alloc = nullptr;
   void* scale_alloc = nullptr;
+  void* combine_alloc = nullptr;  // streaming-GEMV boundary slots and counters
   // device staging for host-buffer calls (ah_q4w_gemv_host), allocated on the
   // first such call for the largest batch; mu serialises those calls
   void* stage = nullptr;
@@ -156,6 +158,22 @@ int q4w_alloc(int64_t rows, int64_t cols, bool engine, AhQ4Weight** out) {
     delete w;
     return fail(AH_ENOMEM, "q4w_create: cudaMalloc of %zu bytes failed", nib_bytes + sc_bytes);
   }
+  // boundary slots of the streaming GEMV: one per pair of neighbouring CTAs of
+  // a one-CTA-per-SM grid; the counters start (and stay, between launches) at 0
+  const int nbd = sm_count();
+  const size_t cmb_floats = (size_t)nbd * 2 * 16 * kStreamMaxBatch;
+  if (ah::dev_malloc(&w->combine_alloc, cmb_floats * 4 + (size_t)nbd * 4) != cudaSuccess ||
+      cudaMemset(w->combine_alloc, 0, cmb_floats * 4 + (size_t)nbd * 4) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(w->nib_alloc);
+    cudaFree(w->scale_alloc);
+    if (w->combine_alloc) cudaFree(w->combine_alloc);
+    delete w;
+    return fail(AH_ENOMEM, "q4w_create: cudaMalloc of the GEMV boundary slots failed");
+  }
+  w->t.combine = static_cast<float*>(w->combine_alloc);
+  w->t.combine_cnt = reinterpret_cast<int*>(w->t.combine + cmb_floats);
+  w->t.n_boundaries = nbd;
   w->t.nib = static_cast<const uint4*>(w->nib_alloc);
   w->t.scales = w->scale_alloc;
   w->weight_bytes = engine ? rows * ((cols + 1) / 2) + rows * nb * 4 : rows * nb * 18;
@@ -180,6 +198,7 @@ int q4w_create(const RowSource& src, bool engine, int64_t rows, int64_t cols, Ah
   if (e != cudaSuccess) {
     cudaFree(w->nib_alloc);
     cudaFree(w->scale_alloc);
+    cudaFree(w->combine_alloc);
     delete w;
     return fail(AH_ECUDA, "q4w_create: repack launch failed: %s", cudaGetErrorString(e));
   }
@@ -764,6 +783,309 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs
     for (int64_t j = k; j < issued; ++j) mbar_wait_bounded(&full[j % S], (uint32_t)((j / S) & 1), a.err, 0x602);
 }
 
+// One warp's epilogue of a finished row tile rt: fin[16][B] holds the tile's
+// full sums.  Writes y (store, residual add, or the SwiGLU pairs of an
+// interleaved gate/up tile), the tensor-parallel peer scatter, and the tile's
+// sum of squares for the next RMSNorm.
+template <int EPI>
+__device__ __forceinline__ void tile_epilogue_warp(const GemvArgs& a, int64_t rt, float* fin, int lane) {
+  const int B = a.batch;
+  if (EPI == kEpiSwiglu) {
+    // tile rows r < 8 are gate rows 8rt+r, rows r+8 the matching up rows
+    for (int i = lane; i < 8 * B; i += 32) {
+      const int r = i / B, b = i - r * B;
+      const int64_t o = rt * 8 + r;
+      if (o < a.w.rows / 2) a.y[b * a.y_stride + o] = silu_ref(fin[r * B + b]) * fin[(r + 8) * B + b];
+    }
+    __syncwarp();
+    return;
+  }
+  for (int i = lane; i < 16 * B; i += 32) {
+    const int r = i / B, b = i - r * B;
+    const int64_t R = rt * 16 + r;
+    float h = 0.0f;
+    if (R < a.w.rows) {
+      if (EPI == kEpiStore && a.n_peer > 0) {
+        h = fin[i];
+        for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][R * a.peer_row + b] = h;  // NVLink stores
+      } else {
+        float* d = a.y + b * a.y_stride + R;
+        h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
+        *d = h;
+      }
+    }
+    fin[i] = h;
+  }
+  // peer slots: the stores reach the other GPUs before this grid completes
+  if (EPI == kEpiStore && a.n_peer > 0) __threadfence_system();
+  if (a.ss_out) {
+    __syncwarp();
+    if (lane < B) {
+      float q = 0.0f;
+      for (int r = 0; r < 16; ++r) q = fmaf(fin[r * B + lane], fin[r * B + lane], q);
+      a.ss_out[lane * a.w.r16 + rt] = q;
+    }
+  }
+  __syncwarp();
+}
+
+// Walks a CTA's run of units as items: item k covers [s_k, e_k) with
+// e_k = min(s_k + P, end of the run, end of s_k's row tile), so items never
+// cross a tile.
+struct ItemWalk {
+  uint32_t s, tile, tile_end, u1, kp, p;
+  __device__ __forceinline__ void init(uint32_t u0, uint32_t u1_, uint32_t kp_, uint32_t p_) {
+    s = u0;
+    u1 = u1_;
+    kp = kp_;
+    p = p_;
+    tile = u0 / kp_;
+    tile_end = (tile + 1) * kp_;
+  }
+  // the next item's [start, end) and row tile; advances
+  __device__ __forceinline__ void take(uint32_t& is, uint32_t& ie, uint32_t& it) {
+    is = s;
+    it = tile;
+    ie = min(min(s + p, u1), tile_end);
+    s = ie;
+    if (s == tile_end) {
+      ++tile;
+      tile_end += kp;
+    }
+  }
+};
+
+// Streaming GEMV for batches of 1..4 tokens (one n8 tensor-core tile).  The
+// grid has at most one CTA per SM; with U = r16 * kp (row tile, block pair)
+// units in the tiled layout, CTA c owns the contiguous run [c*U/G, (c+1)*U/G),
+// so every CTA streams the same weight bytes to within one unit (576 B), and
+// every run holds at least one tile's worth.  A run is cut into items of at
+// most P units that never cross a row tile; round r gives item 8r + w to warp
+// w.  A round's units are contiguous in both planes and arrive by two bulk
+// copies into one of S shared-memory stages.  The first S rounds are requested
+// before the kernel waits for its predecessor, and the kernel lets its
+// dependents launch at once: the next GEMV's CTA, which fits on the SM beside
+// this one, streams its weights while this one computes.  After each round one
+// warp (rotating) adds the round's item partials in unit order to the open
+// tile's sum and finishes every tile that the run holds whole.  The first and
+// the last tile of a run may be shared with the neighbouring CTA: both CTAs
+// leave their partial in the weight's boundary slots at the end, and the
+// second to arrive adds left + right and runs the epilogue, so the result
+// does not depend on timing.
+template <bool kF32, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_stream(const GemvArgs a) {
+  constexpr int BM = kStreamMaxBatch;
+  using SV = typename ScaleT<kF32>::V;
+  constexpr int U = kGemvU;                      // units read from the stage per batch
+  constexpr uint32_t kSclB = 8u * sizeof(SV);    // scale bytes per unit
+  constexpr int kSlot = 16 * kStreamMaxBatch;    // floats per boundary slot
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int B = a.batch;
+  const uint32_t KP = (uint32_t)a.w.kp;
+  const uint32_t total = (uint32_t)(a.w.r16 * a.w.kp);
+  const uint32_t G = gridDim.x, c = blockIdx.x;
+  const uint32_t u0 = (uint32_t)((uint64_t)total * c / G), u1 = (uint32_t)((uint64_t)total * (c + 1) / G);
+  const uint32_t P = (uint32_t)a.pairs_per_chunk;
+  const int S = a.n_stages;
+  const uint32_t st_nib = 8u * P * 512u;
+  const uint32_t stage_bytes = 8u * P * (512u + kSclB);
+  const int kbc = 2 * (int)KP;
+  const int plane = kbc * 64 + 64;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
+  uint8_t* base = smem + (size_t)S * stage_bytes + (((size_t)S * 8 + 15) & ~(size_t)15);
+  uint8_t* xs = base;                                                            // [2B][plane]
+  float4* blk_info = reinterpret_cast<float4*>(base + (size_t)2 * B * plane);   // [B][kbc+1]
+  float* part = reinterpret_cast<float*>(blk_info + B * (kbc + 1));              // [2][warps][16][B]
+  float* acc = part + 2 * kGemvWarps * 16 * B;                                   // [16][B] open tile
+  float* acc_first = acc + 16 * B;                                               // [16][B] first tile
+  float* tok_inv = acc_first + 16 * B;                                           // [16]
+  float* wred = tok_inv + kGemvMaxBatch;                                         // [warps][BM]
+  int* open_tile = reinterpret_cast<int*>(wred + kGemvWarps * BM);
+
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+    *open_tile = -1;
+  }
+  // producer (thread 0): its own walk, S rounds ahead of the consumers
+  ItemWalk pw;
+  pw.init(u0, u1, KP, P);
+  uint32_t issued = 0;
+  auto issue = [&](uint32_t r) {
+    const uint32_t rs = pw.s;
+    uint32_t is, ie, it;
+#pragma unroll 1
+    for (int w = 0; w < kGemvWarps && pw.s < u1; ++w) pw.take(is, ie, it);
+    const uint32_t n = pw.s - rs;
+    uint8_t* dst = smem + (size_t)(r % S) * stage_bytes;
+    uint64_t* bar = &full[r % S];
+    mbar_arrive_expect_tx(bar, n * (512u + kSclB));
+    bulk_g2s(dst, a.w.nib + (size_t)rs * 32, n * 512u, bar);
+    bulk_g2s(dst + st_nib, reinterpret_cast<const SV*>(a.w.scales) + (size_t)rs * 8, n * kSclB, bar);
+  };
+  if (tid == 0)
+    for (; (int)issued < S && pw.s < u1; ++issued) issue(issued);
+  // weights do not depend on the predecessor; the dependents' weights do not
+  // depend on this kernel either
+  pdl_launch_dependents();
+  pdl_wait();
+  rms_stats<BM, PRO>(a, wred, tok_inv, tid, lane, warp);
+  split_x<PRO>(a, xs, blk_info, plane, kbc, 0, a.w.cols, tok_inv, tid, warp);
+  __syncthreads();
+
+  ItemWalk cw;  // consumers' walk (every thread keeps the same one)
+  cw.init(u0, u1, KP, P);
+  uint32_t r = 0;
+  int fin_warp = 0;
+  bool aborted = false;
+  for (; cw.s < u1; ++r) {
+    const uint32_t rs = cw.s;
+    uint32_t tiles8[kGemvWarps];
+    uint32_t ms = 0, me = 0, mt = 0;
+    int n_items = 0;
+#pragma unroll
+    for (int w = 0; w < kGemvWarps; ++w) {
+      tiles8[w] = 0;
+      if (cw.s < u1) {
+        uint32_t is, ie, it;
+        cw.take(is, ie, it);
+        tiles8[w] = it;
+        n_items = w + 1;
+        if (w == warp) {
+          ms = is;
+          me = ie;
+          mt = it;
+        }
+      }
+    }
+    const int st = (int)(r % (uint32_t)S);
+    const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full[st], (r / (uint32_t)S) & 1u, a.err, 0x611));
+    if (ok && warp < n_items) {
+      const uint8_t* stg = smem + (size_t)st * stage_bytes;
+      const uint4* snib = reinterpret_cast<const uint4*>(stg) + (size_t)(ms - rs) * 32 + lane;
+      const SV* sscl = reinterpret_cast<const SV*>(stg + st_nib) + (size_t)(ms - rs) * 8 + g;
+      const int np = (int)(me - ms);
+      const int kb0 = 2 * (int)(ms - mt * KP);
+      float tot[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+      for (int p = 0; p < np; p += U) {
+        uint4 w[U];
+        SV sv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (p + u < np) {
+            w[u] = snib[(p + u) * 32];
+            sv[u] = sscl[(p + u) * 8];
+          }
+        mma_pairs<1, kF32, U>(tot, w, sv, p, np, B, g, t, xs, blk_info, plane, kbc, kb0);
+      }
+      float* pr = part + (size_t)((r & 1u) * kGemvWarps + warp) * 16 * B;
+      if (t < B) {  // columns 2t (hi) and 2t+1 (lo) of token t
+        pr[g * B + t] = tot[0][0] + tot[0][1];
+        pr[(g + 8) * B + t] = tot[0][2] + tot[0][3];
+      }
+    }
+    // one barrier: the stage is read by every warp, the partials are in place,
+    // and every wait succeeded
+    if (__syncthreads_or(!ok)) {
+      aborted = true;
+      break;
+    }
+    if (tid == 0 && pw.s < u1) {
+      fence_proxy_async_smem();
+      issue(issued);
+      ++issued;
+    }
+    // warp r % 8 adds the round's items in unit order and finishes tiles
+    if (warp == (int)(r & (kGemvWarps - 1))) {
+      const float* pr = part + (size_t)(r & 1u) * kGemvWarps * 16 * B;
+      const int nv = 16 * B;
+      int ot = *open_tile;
+      float v0 = 0.0f, v1 = 0.0f;  // acc[lane], acc[lane + 32]
+      if (ot >= 0) {
+        if (lane < nv) v0 = acc[lane];
+        if (lane + 32 < nv) v1 = acc[lane + 32];
+      }
+#pragma unroll
+      for (int w = 0; w < kGemvWarps; ++w) {
+        if (w < n_items) {
+          const float p0 = lane < nv ? pr[w * nv + lane] : 0.0f;
+          const float p1 = lane + 32 < nv ? pr[w * nv + lane + 32] : 0.0f;
+          if ((int)tiles8[w] != ot) {
+            if (ot >= 0) {  // tile ot is complete in this run
+              if ((uint32_t)ot * KP < u0) {  // shared with the left neighbour: finished at the end
+                if (lane < nv) acc_first[lane] = v0;
+                if (lane + 32 < nv) acc_first[lane + 32] = v1;
+              } else {
+                if (lane < nv) acc[lane] = v0;
+                if (lane + 32 < nv) acc[lane + 32] = v1;
+                __syncwarp();
+                tile_epilogue_warp<EPI>(a, ot, acc, lane);
+              }
+            }
+            ot = (int)tiles8[w];
+            v0 = p0;
+            v1 = p1;
+          } else {
+            v0 += p0;
+            v1 += p1;
+          }
+        }
+      }
+      if (lane < nv) acc[lane] = v0;
+      if (lane + 32 < nv) acc[lane + 32] = v1;
+      if (lane == 0) *open_tile = ot;
+      __syncwarp();
+    }
+    fin_warp = (int)(r & (kGemvWarps - 1));
+  }
+  if (aborted) {
+    // let the copies still in flight land (bounded) before the CTA exits
+    if (tid == 0)
+      for (uint32_t j = r; j < issued; ++j) mbar_wait_bounded(&full[j % S], (j / (uint32_t)S) & 1u, a.err, 0x612);
+    fin_warp = 0;
+  }
+  // the run's last tile (open) and, if shared, its first tile
+  if (warp != fin_warp) return;
+  const int nv = 16 * B;
+  const bool right = (u1 % KP) != 0;  // last tile continues in CTA c + 1
+  const bool left = (u0 % KP) != 0;   // first tile began in CTA c - 1
+  const int ot = *open_tile;
+  if (!right && !aborted && ot >= 0) tile_epilogue_warp<EPI>(a, ot, acc, lane);
+  if (!right && !left) return;
+  float* slot_r = a.w.combine + ((size_t)c * 2 + 0) * kSlot;
+  float* slot_l = a.w.combine + ((size_t)(c - 1) * 2 + 1) * kSlot;
+  for (int i = lane; i < nv; i += 32) {
+    if (right) slot_r[i] = acc[i];
+    if (left) slot_l[i] = acc_first[i];
+  }
+  __threadfence();
+  __syncwarp();
+  int old_r = 0, old_l = 0;
+  if (lane == 0) {
+    if (right) old_r = atomicAdd(&a.w.combine_cnt[c], 1);
+    if (left) old_l = atomicAdd(&a.w.combine_cnt[c - 1], 1);
+  }
+  old_r = __shfl_sync(0xFFFFFFFFu, old_r, 0);
+  old_l = __shfl_sync(0xFFFFFFFFu, old_l, 0);
+  if (old_r == 1 || old_l == 1) __threadfence();
+  if (right && old_r == 1) {  // this CTA arrived second: left (this) + right (CTA c + 1)
+    const float* o = a.w.combine + ((size_t)c * 2 + 1) * kSlot;
+    for (int i = lane; i < nv; i += 32) acc[i] = acc[i] + __ldcg(o + i);
+    __syncwarp();
+    tile_epilogue_warp<EPI>(a, u1 / KP, acc, lane);
+    if (lane == 0) atomicExch(&a.w.combine_cnt[c], 0);
+  }
+  if (left && old_l == 1) {  // left (CTA c - 1) + right (this)
+    const float* o = a.w.combine + ((size_t)(c - 1) * 2 + 0) * kSlot;
+    for (int i = lane; i < nv; i += 32) acc_first[i] = __ldcg(o + i) + acc_first[i];
+    __syncwarp();
+    tile_epilogue_warp<EPI>(a, u0 / KP, acc_first, lane);
+    if (lane == 0) atomicExch(&a.w.combine_cnt[c - 1], 0);
+  }
+}
+
 using GemvKernel = void (*)(const GemvArgs);
 #define AH_TRY_GEMV(expr)         \
   do {                            \
@@ -790,6 +1112,21 @@ GemvKernel pick_format(int pro, int epi) {
 template <int NT, bool kRows>
 GemvKernel pick_kernel(bool f32s, int pro, int epi) {
   return f32s ? pick_format<NT, kRows, true>(pro, epi) : pick_format<NT, kRows, false>(pro, epi);
+}
+
+template <bool F>
+GemvKernel pick_stream_format(int pro, int epi) {
+  if (pro == kProPlain) {
+    if (epi == kEpiStore) return k_gemv_q4_stream<F, kProPlain, kEpiStore>;
+    if (epi == kEpiAdd) return k_gemv_q4_stream<F, kProPlain, kEpiAdd>;
+    return k_gemv_q4_stream<F, kProPlain, kEpiSwiglu>;
+  }
+  if (epi == kEpiStore) return k_gemv_q4_stream<F, kProRmsNorm, kEpiStore>;
+  if (epi == kEpiAdd) return k_gemv_q4_stream<F, kProRmsNorm, kEpiAdd>;
+  return k_gemv_q4_stream<F, kProRmsNorm, kEpiSwiglu>;
+}
+GemvKernel pick_stream_kernel(bool f32s, int pro, int epi) {
+  return f32s ? pick_stream_format<true>(pro, epi) : pick_stream_format<false>(pro, epi);
 }
 
 }  // namespace
@@ -823,6 +1160,78 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
 }
 
 GemvPlan gemv_plan(const Q4Tiled& w, int batch) { return gemv_plan(w, batch, false); }
+
+namespace {
+// Streaming kernel switch, read once: AH_GEMV_STREAM=0 turns it off (the
+// cluster / rows kernels serve every batch), 2 prefers one CTA per SM with
+// deeper stages over two co-resident CTAs; unset or 1 is the default.
+int stream_setting() {
+  static const int v = [] {
+    const char* e = getenv("AH_GEMV_STREAM");
+    return e ? atoi(e) : 1;
+  }();
+  return v;
+}
+constexpr size_t kStreamSmemTwo = 112 * 1024;  // two CTAs per SM (this GEMV and the next)
+constexpr size_t kStreamSmemOne = 220 * 1024;
+constexpr int kStreamMaxStages = 6;
+}  // namespace
+
+// Streaming-kernel plan for batches of 1..kStreamMaxBatch: the grid (at most
+// one CTA per SM, at least one row tile of units per CTA), items of P block
+// pairs and S stages of 8 items, in the largest stage ring that leaves room
+// for the co-resident next GEMV (or, failing that, for one CTA per SM).
+bool stream_plan(const Q4Tiled& w, int batch, GemvPlan* out) {
+  const int setting = stream_setting();
+  if (setting == 0 || batch < 1 || batch > kStreamMaxBatch || !w.combine || w.r16 < 1) return false;
+  if ((uint64_t)w.r16 * (uint64_t)w.kp >= (1ull << 31)) return false;
+  int64_t G = std::min<int64_t>(sm_count(), w.r16);
+  G = std::min<int64_t>(G, (int64_t)w.n_boundaries + 1);
+  const int64_t kbc = 2 * w.kp;
+  const int64_t plane = kbc * 64 + 64;
+  const size_t scl_b = (size_t)8 * (w.f32_scales ? 16 : 8);
+  const size_t base = (size_t)2 * batch * plane + (size_t)batch * (kbc + 1) * 16 +
+                      (size_t)2 * kGemvWarps * 16 * batch * 4 + (size_t)2 * 16 * batch * 4 +
+                      (size_t)kGemvMaxBatch * 4 + (size_t)kGemvWarps * kStreamMaxBatch * 4 + 16;
+  // rounds a CTA runs at most (items of P units, plus one short item per tile it touches)
+  const int64_t run = ((int64_t)w.r16 * w.kp + G - 1) / G;
+  const size_t budgets[2] = {setting == 2 ? kStreamSmemOne : kStreamSmemTwo,
+                             setting == 2 ? kStreamSmemTwo : kStreamSmemOne};
+  for (size_t budget : budgets) {
+    int best_p = 0, best_s = 0;
+    size_t best_inflight = 0;
+    for (int P : {8, 4}) {
+      const size_t stage = (size_t)8 * P * (512 + scl_b);
+      const int64_t rounds = (run / P + run / w.kp + 2 + kGemvWarps - 1) / kGemvWarps;
+      int S = 0;
+      while (S < kStreamMaxStages && S < rounds &&
+             (size_t)(S + 1) * stage + (((size_t)(S + 1) * 8 + 15) & ~(size_t)15) + base <= budget)
+        ++S;
+      if (S < 1 || (S < 2 && rounds > 1)) continue;
+      const size_t inflight = (size_t)S * stage;
+      if (inflight > best_inflight) {
+        best_inflight = inflight;
+        best_p = P;
+        best_s = S;
+      }
+    }
+    if (best_s > 0) {
+      GemvPlan p{};
+      p.nt = 1;
+      p.stream_mode = true;
+      p.grid = (int)G;
+      p.pairs_per_chunk = best_p;
+      p.n_stages = best_s;
+      p.ksplit = 1;
+      const size_t stage = (size_t)8 * best_p * (512 + scl_b);
+      p.smem = (size_t)best_s * stage + (((size_t)best_s * 8 + 15) & ~(size_t)15) + base;
+      p.smem_base = base;
+      *out = p;
+      return true;
+    }
+  }
+  return false;
+}
 
 namespace {
 GemvKernel select_kernel(const GemvPlan& plan, bool f32s, int pro, int epi) {
@@ -897,6 +1306,20 @@ int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
 // memory beside at least two tile stages (it is then amortised over several
 // tiles per CTA).
 int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, GemvKernel* kern, int* cap) {
+  GemvPlan ps;
+  if (stream_plan(w, batch, &ps) && aligned16(w.nib) && aligned16(w.scales)) {
+    GemvKernel ks = pick_stream_kernel(w.f32_scales, pro, epi);
+    ps.rows_mode = true;  // kernel_setup: plain (non-cluster) occupancy query
+    int scap = 0;
+    AH_TRY_GEMV(kernel_setup(ks, ps, &scap));
+    ps.rows_mode = false;
+    if (scap > 0) {
+      *plan = ps;
+      *kern = ks;
+      *cap = scap;
+      return AH_OK;
+    }
+  }
   GemvPlan pc = gemv_plan(w, batch, false);
   if (pc.smem > (size_t)kGemvSmemLimit)
     return fail(AH_EUNSUPPORTED, "gemv: batch %d x %lld columns needs %zu B of shared memory per CTA (limit %d)",
@@ -931,6 +1354,8 @@ namespace {
 // The largest token count (<= batch) whose split of x fits one CTA's shared
 // memory; larger batches run as several launches over token slices.
 int max_sub_batch(const Q4Tiled& w, int batch) {
+  GemvPlan ps;
+  if (stream_plan(w, batch, &ps)) return batch;
   for (int b = batch; b >= 1; --b)
     if (gemv_plan(w, b, false).smem <= (size_t)kGemvSmemLimit) return b;
   return 0;
@@ -990,7 +1415,11 @@ int gemv_launch_one(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if (plan.rows_mode) {
+  if (plan.stream_mode) {
+    AH_REQUIRE(a.err != nullptr, "gemv: device error word unavailable");
+    a.early_trigger = 1;
+    cfg.gridDim = dim3((unsigned)plan.grid, 1, 1);
+  } else if (plan.rows_mode) {
     const int64_t n = std::min<int64_t>(a.w.r16, cap);
     a.early_trigger = a.w.r16 <= cap ? 1 : 0;
     cfg.gridDim = dim3((unsigned)n, 1, 1);
@@ -1094,6 +1523,7 @@ int ah_q4w_destroy(AhQ4Weight* w) {
   cudaSetDevice(w->device);
   cudaFree(w->nib_alloc);
   cudaFree(w->scale_alloc);
+  if (w->combine_alloc) cudaFree(w->combine_alloc);
   if (w->stage) cudaFree(w->stage);
   if (w->host_graph) cudaGraphExecDestroy(w->host_graph);
   if (w->host_cap) cudaStreamDestroy(w->host_cap);

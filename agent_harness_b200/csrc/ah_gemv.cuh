@@ -57,7 +57,15 @@ struct Q4Tiled {
   int64_t rows, cols;  // logical shape
   int64_t r16, kp;     // tiles, block pairs
   bool f32_scales;
+  // streaming GEMV: a row tile whose K range two neighbouring CTAs share meets
+  // in slot pair [boundary][side] (side 0 = the left CTA's partial, 1 = the
+  // right one's; kStreamMaxBatch tokens x 16 rows each) and counter [boundary]
+  // (0 between launches; the second CTA to arrive sums and resets it)
+  float* combine;
+  int* combine_cnt;
+  int n_boundaries;    // combine slots allocated (grids of up to n_boundaries + 1 CTAs)
 };
+constexpr int kStreamMaxBatch = 4;  // tokens of the streaming kernel (one n8 tensor-core tile)
 
 // ---- epilogue / prologue selectors --------------------------------------------
 enum GemvPrologue : int { kProPlain = 0, kProRmsNorm = 1 };
