@@ -79,6 +79,13 @@ SIGNATURES = {
     "ah_q4w_gemm_noalloc": (i32, [vp, vp, i64, i64, vp, i64, vp]),
     "ah_gemv_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, i64, vp]),
     "ah_matvec_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, vp]),
+    "ah_gemv_4bit_rows": (i32, [vp, vp, vp, vp, i64, i64, i64, i64, vp]),
+    "ah_swiglu_4bit_into": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i64, i64, i64, vp, vp, vp, vp]),
+    "ah_q4w_from_engine_gate_up": (i32, [vp, vp, vp, vp, i64, i64, C.POINTER(vp), vp]),
+    "ah_q4w_from_q4_0_gate_up": (i32, [vp, vp, i64, i64, C.POINTER(vp), vp]),
+    "ah_q4w_swiglu": (i32, [vp, vp, vp, vp, vp, i32, vp]),
+    "ah_host_gemv_4bit_worker_scalar": (i32, [vp, vp, vp, vp, sz, sz, sz, sz]),
+    "ah_host_swiglu_4bit_into": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, sz, sz, sz, vp, vp, vp]),
     "ah_model_create": (i32, [vp, C.POINTER(vp)]),
     "ah_nccl_unique_id": (i32, [vp, C.c_size_t]),
     "ah_model_create_tp": (i32, [vp, i32, i32, vp, C.POINTER(vp)]),

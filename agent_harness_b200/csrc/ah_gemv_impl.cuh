@@ -18,6 +18,7 @@ struct GemvPlan {
   int n_stages;             // rows / stream mode: stages in flight (0: mode unavailable)
   bool stream_mode;         // streaming kernel: one CTA per SM, balanced unit runs
   int grid;                 // stream mode: CTAs
+  int threads;              // stream mode: threads per CTA (compute warps + the producer warp)
 };
 
 GemvPlan gemv_plan(const Q4Tiled& w, int batch);

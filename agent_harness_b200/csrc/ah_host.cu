@@ -8,6 +8,9 @@
 #include "ah_common.cuh"
 
 namespace ah {
+// the engine-format GEMV over a window of rows whose bytes start at byte0 (ah_gemv.cu)
+int gemv_rows_window(float* out, const float* scales, const uint8_t* packed, const float* x, int64_t rows,
+                     int64_t cols, int64_t gs, int64_t row0, int64_t byte0, cudaStream_t st);
 namespace {
 
 struct Staging {
@@ -106,6 +109,74 @@ int ah_host_gemv_4bit_into(float* out, const float* scales, const uint8_t* packe
   AH_TRY(ah_gemv_4bit_into(static_cast<float*>(dy), static_cast<const float*>(ds), static_cast<const uint8_t*>(dp),
                            static_cast<const float*>(dx), (int64_t)rows, (int64_t)cols, (int64_t)g, t_stage.stream));
   return finish_download(out, dy, rows * sizeof(float));
+}
+
+int ah_host_gemv_4bit_worker_scalar(float* out, const float* scales, const uint8_t* packed, const float* x,
+                                    size_t row_start, size_t row_end, size_t cols, size_t gs) {
+  AH_REQUIRE(row_end >= row_start, "host_gemv_4bit_worker_scalar: row_end < row_start");
+  const size_t rows = row_end - row_start;
+  if (rows == 0) return AH_OK;
+  AH_REQUIRE(out != nullptr, "host_gemv_4bit_worker_scalar: null out");
+  if (cols == 0) {
+    memset(out, 0, rows * sizeof(float));
+    return AH_OK;
+  }
+  AH_REQUIRE(scales && packed && x, "host_gemv_4bit_worker_scalar: null input");
+  const size_t g = gs < 1 ? 1 : gs;
+  const size_t n_gpr = (cols + g - 1) / g;
+  // only the rows the worker reads: their scales and the bytes holding their nibbles
+  const size_t b0 = (row_start * cols) >> 1, b1 = (row_end * cols + 1) >> 1;
+  AH_TRY(stage_ready());
+  void *ds, *dp, *dx, *dy;
+  AH_TRY(upload(0, scales + row_start * n_gpr, rows * n_gpr * sizeof(float), &ds));
+  AH_TRY(upload(1, packed + b0, b1 - b0, &dp));
+  AH_TRY(upload(2, x, cols * sizeof(float), &dx));
+  AH_TRY(stage_buf(3, rows * sizeof(float), &dy));
+  AH_TRY(gemv_rows_window(static_cast<float*>(dy), static_cast<const float*>(ds), static_cast<const uint8_t*>(dp),
+                          static_cast<const float*>(dx), (int64_t)rows, (int64_t)cols, (int64_t)g, (int64_t)row_start,
+                          (int64_t)b0, t_stage.stream));
+  return finish_download(out, dy, rows * sizeof(float));
+}
+
+int ah_host_swiglu_4bit_into(float* out, const float* input, const float* gate_scales, const uint8_t* gate_packed,
+                             const float* up_scales, const uint8_t* up_packed, const float* down_scales,
+                             const uint8_t* down_packed, size_t n_embd, size_t n_ff, size_t gs, float* scratch_gate,
+                             float* scratch_up, float* scratch_act) {
+  if (n_embd == 0 && n_ff == 0) return AH_OK;
+  AH_REQUIRE(n_embd == 0 || out != nullptr, "host_swiglu_4bit_into: null out");
+  AH_REQUIRE(n_ff == 0 || (scratch_gate && scratch_up && scratch_act), "host_swiglu_4bit_into: null scratch");
+  const size_t g = gs < 1 ? 1 : gs;
+  AH_TRY(stage_ready());
+  void *dgs = nullptr, *dgp = nullptr, *dus = nullptr, *dup = nullptr, *dds = nullptr, *ddp = nullptr, *dx = nullptr;
+  void *dout = nullptr, *dsg = nullptr, *dsu = nullptr, *dsa = nullptr;
+  const size_t ff_sc = n_ff * ((n_embd + g - 1) / g), dn_sc = n_embd * ((n_ff + g - 1) / g);
+  if (n_ff && n_embd) {
+    AH_REQUIRE(gate_scales && gate_packed && up_scales && up_packed && input, "host_swiglu_4bit_into: null input");
+    AH_TRY(upload(0, gate_scales, ff_sc * 4, &dgs));
+    AH_TRY(upload(1, gate_packed, (n_ff * n_embd + 1) / 2, &dgp));
+    AH_TRY(upload(2, up_scales, ff_sc * 4, &dus));
+    AH_TRY(upload(3, up_packed, (n_ff * n_embd + 1) / 2, &dup));
+    AH_TRY(upload(4, input, n_embd * 4, &dx));
+    AH_REQUIRE(down_scales && down_packed, "host_swiglu_4bit_into: null down weights");
+    AH_TRY(upload(5, down_scales, dn_sc * 4, &dds));
+    AH_TRY(upload(6, down_packed, (n_embd * n_ff + 1) / 2, &ddp));
+  }
+  AH_TRY(stage_buf(7, n_embd * 4, &dout));
+  AH_TRY(stage_buf(8, n_ff * 4, &dsg));
+  AH_TRY(stage_buf(9, n_ff * 4, &dsu));
+  AH_TRY(stage_buf(10, n_ff * 4, &dsa));
+  AH_TRY(ah_swiglu_4bit_into(static_cast<float*>(dout), static_cast<const float*>(dx), static_cast<const float*>(dgs),
+                             static_cast<const uint8_t*>(dgp), static_cast<const float*>(dus),
+                             static_cast<const uint8_t*>(dup), static_cast<const float*>(dds),
+                             static_cast<const uint8_t*>(ddp), (int64_t)n_embd, (int64_t)n_ff, (int64_t)g,
+                             static_cast<float*>(dsg), static_cast<float*>(dsu), static_cast<float*>(dsa),
+                             t_stage.stream));
+  if (n_ff) {
+    AH_CUDA_TRY(cudaMemcpyAsync(scratch_gate, dsg, n_ff * 4, cudaMemcpyDeviceToHost, t_stage.stream));
+    AH_CUDA_TRY(cudaMemcpyAsync(scratch_up, dsu, n_ff * 4, cudaMemcpyDeviceToHost, t_stage.stream));
+    AH_CUDA_TRY(cudaMemcpyAsync(scratch_act, dsa, n_ff * 4, cudaMemcpyDeviceToHost, t_stage.stream));
+  }
+  return finish_download(out, dout, n_embd * 4);
 }
 
 int ah_host_dequant_layer(const float* scales, const uint8_t* packed, float* result, size_t n, size_t gs) {

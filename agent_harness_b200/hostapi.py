@@ -6,7 +6,8 @@ through the synchronous ah_host_* entries of the C ABI.  No CPU fallback.
 
   models/quantization.rs : GROUP_SIZE, quantize, dequant_weight, dequant_layer,
                            packed_bytes, n_groups, quantized_bytes
-  inference/math.rs      : gemv_4bit_into, matvec_4bit_into
+  inference/math.rs      : gemv_4bit_into, matvec_4bit_into, gemv_4bit_parallel_worker_scalar
+  inference/ffn.rs       : swiglu_4bit_into
   models/avx512_kernel.rs: f16_bytes_to_f32, bf16_bytes_to_f32
   models/formats/gguf.rs : f16_to_f32, bf16_to_f32, dequantize_to_f32
 """
@@ -88,6 +89,34 @@ def gemv_4bit_into(out: np.ndarray, scales: np.ndarray, packed: np.ndarray, x: n
 def matvec_4bit_into(out, scales, packed, x, dim: int, group_size: int = GROUP_SIZE) -> None:
     """math.rs:205-214."""
     gemv_4bit_into(out, scales, packed, x, dim, dim, group_size)
+
+
+def gemv_4bit_parallel_worker_scalar(out: np.ndarray, global_scales: np.ndarray, global_packed: np.ndarray,
+                                     x: np.ndarray, row_start: int, row_end: int, cols: int,
+                                     group_size: int = GROUP_SIZE) -> None:
+    """math.rs:382-418: out[i - row_start] for rows [row_start, row_end) of the
+    full matrix (the row-range worker gemv_4bit_into hands to each thread)."""
+    if out.dtype != np.float32 or not out.flags.c_contiguous or out.size < row_end - row_start:
+        raise AhError(-1, "out must be a contiguous float32 array of row_end - row_start values")
+    s, p, xv = _c(global_scales, np.float32), _c(global_packed, np.uint8), _c(x, np.float32)
+    call("ah_host_gemv_4bit_worker_scalar", _p(out), _p(s), _p(p), _p(xv), row_start, row_end, cols, group_size)
+
+
+# --- inference/ffn.rs -----------------------------------------------------------------
+
+def swiglu_4bit_into(out: np.ndarray, input: np.ndarray, gate_scales, gate_packed, up_scales, up_packed, down_scales,
+                     down_packed, n_embd: int, n_ff: int, group_size: int, scratch_gate: np.ndarray,
+                     scratch_up: np.ndarray, scratch_act: np.ndarray) -> None:
+    """ffn.rs:155-174: gate/up GEMVs, act = silu(gate) * up, out = down . act;
+    the scratch slices receive the intermediates, as the reference's do."""
+    for a, n in ((out, n_embd), (scratch_gate, n_ff), (scratch_up, n_ff), (scratch_act, n_ff)):
+        if a.dtype != np.float32 or not a.flags.c_contiguous or a.size < n:
+            raise AhError(-1, "out and scratch slices must be contiguous float32 arrays of their lengths")
+    args = [_c(v, dt) for v, dt in ((input, np.float32), (gate_scales, np.float32), (gate_packed, np.uint8),
+                                     (up_scales, np.float32), (up_packed, np.uint8), (down_scales, np.float32),
+                                     (down_packed, np.uint8))]
+    call("ah_host_swiglu_4bit_into", _p(out), *[_p(a) for a in args], n_embd, n_ff, group_size, _p(scratch_gate),
+         _p(scratch_up), _p(scratch_act))
 
 
 # --- models/avx512_kernel.rs / models/formats/gguf.rs ---------------------------------

@@ -242,3 +242,60 @@ def gemv_4bit_into(out: torch.Tensor, scales: torch.Tensor, packed: torch.Tensor
     call("ah_gemv_4bit_into", _ptr(out), _ptr(scales), _ptr(packed), _ptr(x) if x.numel() else None, rows, cols,
          group_size, _stream(out.device))
     return out
+
+
+def gemv_4bit_rows(out: torch.Tensor, scales: torch.Tensor, packed: torch.Tensor, x: torch.Tensor, row_start: int,
+                   row_end: int, cols: int, group_size: int = GROUP_SIZE) -> torch.Tensor:
+    """inference/math.rs:382-418 gemv_4bit_parallel_worker_scalar on device
+    tensors: rows [row_start, row_end) of the full planes into out."""
+    call("ah_gemv_4bit_rows", _ptr(out), _ptr(scales), _ptr(packed), _ptr(x), row_start, row_end, cols, group_size,
+         _stream(out.device))
+    return out
+
+
+def swiglu_4bit_into(out: torch.Tensor, x: torch.Tensor, gate_scales, gate_packed, up_scales, up_packed,
+                     down_scales, down_packed, n_embd: int, n_ff: int, group_size: int, scratch_gate: torch.Tensor,
+                     scratch_up: torch.Tensor, scratch_act: torch.Tensor) -> torch.Tensor:
+    """inference/ffn.rs:155-174 on device tensors in the engine's own storage."""
+    call("ah_swiglu_4bit_into", _ptr(out), _ptr(x), _ptr(gate_scales), _ptr(gate_packed), _ptr(up_scales),
+         _ptr(up_packed), _ptr(down_scales), _ptr(down_packed), n_embd, n_ff, group_size, _ptr(scratch_gate),
+         _ptr(scratch_up), _ptr(scratch_act), _stream(out.device))
+    return out
+
+
+class SwigluBlock:
+    """The feed-forward block on resident tiled weights, as the decoder runs it:
+    gate and up interleaved in one weight (one GEMV whose epilogue writes
+    silu(gate) * up), then the down GEMV."""
+
+    def __init__(self, gate_up: C.c_void_p, down: Q4Weight, n_embd: int, n_ff: int):
+        self.gate_up = Q4Weight(gate_up, 2 * n_ff, n_embd, down.device)
+        self.down, self.n_embd, self.n_ff = down, n_embd, n_ff
+
+    @classmethod
+    def from_engine(cls, gate_scales, gate_packed, up_scales, up_packed, down_scales, down_packed, n_embd: int,
+                    n_ff: int) -> "SwigluBlock":
+        h = C.c_void_p()
+        call("ah_q4w_from_engine_gate_up", _ptr(gate_scales), _ptr(gate_packed), _ptr(up_scales), _ptr(up_packed),
+             n_ff, n_embd, C.byref(h), _stream(gate_packed.device))
+        return cls(h, Q4Weight.from_engine(down_scales, down_packed, n_embd, n_ff), n_embd, n_ff)
+
+    @classmethod
+    def from_q4_0(cls, gate_blocks, up_blocks, down_blocks, n_embd: int, n_ff: int) -> "SwigluBlock":
+        h = C.c_void_p()
+        call("ah_q4w_from_q4_0_gate_up", _ptr(gate_blocks), _ptr(up_blocks), n_ff, n_embd, C.byref(h),
+             _stream(gate_blocks.device))
+        return cls(h, Q4Weight.from_q4_0(down_blocks, n_embd, n_ff), n_embd, n_ff)
+
+    def __call__(self, x: torch.Tensor, act: torch.Tensor | None = None) -> torch.Tensor:
+        xb = x.reshape(-1, self.n_embd)
+        batch = xb.shape[0]
+        act = act if act is not None else torch.empty(batch, self.n_ff, dtype=torch.float32, device=x.device)
+        out = torch.empty(batch, self.n_embd, dtype=torch.float32, device=x.device)
+        call("ah_q4w_swiglu", self.gate_up.handle, self.down.handle, _ptr(xb), _ptr(act), _ptr(out), batch,
+             _stream(x.device))
+        return out.reshape(self.n_embd) if x.dim() == 1 else out
+
+    def close(self):
+        self.gate_up.close()
+        self.down.close()

@@ -210,6 +210,37 @@ AH_API int ah_gemv_4bit_into(float* out_dev, const float* scales_dev, const uint
 AH_API int ah_matvec_4bit_into(float* out_dev, const float* scales_dev, const uint8_t* packed_dev, const float* x_dev,
                         int64_t dim, int64_t group_size, void* stream);
 
+/* Reference: inference/math.rs:382-418 gemv_4bit_parallel_worker_scalar(out,
+ * global_scales, global_packed, x, row_start, row_end, cols, gs): rows
+ * [row_start, row_end) of the engine-format matrix whose full planes are
+ * scales_dev / packed_dev; out_dev holds row_end - row_start values. */
+AH_API int ah_gemv_4bit_rows(float* out_dev, const float* scales_dev, const uint8_t* packed_dev, const float* x_dev,
+                             int64_t row_start, int64_t row_end, int64_t cols, int64_t group_size, void* stream);
+
+/* ---- SwiGLU feed-forward block ------------------------------------------------------ */
+/* Reference: inference/ffn.rs:155-174 swiglu_4bit_into (the quantized branch of
+ * FfnBlock::forward, ffn.rs:72-111), device pointers, engine format as stored,
+ * any group size: scratch_gate = gate.input, scratch_up = up.input (one fused
+ * pass over input), scratch_act = silu(gate) * up, out = down.scratch_act.
+ * gate/up: [n_ff][n_embd]; down: [n_embd][n_ff]. */
+AH_API int ah_swiglu_4bit_into(float* out_dev, const float* input_dev, const float* gate_scales_dev,
+                               const uint8_t* gate_packed_dev, const float* up_scales_dev,
+                               const uint8_t* up_packed_dev, const float* down_scales_dev,
+                               const uint8_t* down_packed_dev, int64_t n_embd, int64_t n_ff, int64_t group_size,
+                               float* scratch_gate_dev, float* scratch_up_dev, float* scratch_act_dev, void* stream);
+/* The same block on resident tiled weights, as the decoder runs it: gate and up
+ * interleaved in one weight (8 rows of each per 16-row tile) so one fused GEMV
+ * writes act = silu(gate) * up straight from its epilogue, then the down GEMV.
+ * Built from the engine format (group 32) or Q4_0 blocks; n_ff % 8 == 0.
+ * x [batch][n_embd] -> act [batch][n_ff] -> out [batch][n_embd], batch <= 16. */
+AH_API int ah_q4w_from_engine_gate_up(const float* gate_scales_dev, const uint8_t* gate_packed_dev,
+                                      const float* up_scales_dev, const uint8_t* up_packed_dev, int64_t n_ff,
+                                      int64_t n_embd, AhQ4Weight** out, void* stream);
+AH_API int ah_q4w_from_q4_0_gate_up(const void* gate_blocks_dev, const void* up_blocks_dev, int64_t n_ff,
+                                    int64_t n_embd, AhQ4Weight** out, void* stream);
+AH_API int ah_q4w_swiglu(const AhQ4Weight* gate_up, const AhQ4Weight* down, const float* x_dev, float* act_dev,
+                         float* out_dev, int batch, void* stream);
+
 /* ---- Llama-shaped decoder ----------------------------------------------------------- */
 /* Reference: inference/config.rs:6-58 ModelConfig (the fields the decoder uses;
  * rope sections default to [head_dim/2, 0, 0, 0] as config.rs:170-172 does). */
@@ -422,6 +453,17 @@ AH_API int ah_host_dedup_decompress_all(const uint16_t* prefixes, int64_t n_pref
 /* Reference: inference/math.rs:255-295 gemv_4bit_into(out, scales, packed, x, rows, cols, gs). */
 AH_API int ah_host_gemv_4bit_into(float* out, const float* scales, const uint8_t* packed, const float* x, size_t rows,
                            size_t cols, size_t group_size);
+/* Reference: inference/math.rs:382-418 gemv_4bit_parallel_worker_scalar(out, global_scales,
+ * global_packed, x, row_start, row_end, cols, gs); out[row_end - row_start]. */
+AH_API int ah_host_gemv_4bit_worker_scalar(float* out, const float* scales, const uint8_t* packed, const float* x,
+                                           size_t row_start, size_t row_end, size_t cols, size_t group_size);
+/* Reference: inference/ffn.rs:155-174 swiglu_4bit_into(out, input, gate_scales, gate_packed,
+ * up_scales, up_packed, down_scales, down_packed, n_embd, n_ff, gs, scratch_gate, scratch_up,
+ * scratch_act); the three scratch slices receive the reference's intermediates. */
+AH_API int ah_host_swiglu_4bit_into(float* out, const float* input, const float* gate_scales,
+                                    const uint8_t* gate_packed, const float* up_scales, const uint8_t* up_packed,
+                                    const float* down_scales, const uint8_t* down_packed, size_t n_embd, size_t n_ff,
+                                    size_t group_size, float* scratch_gate, float* scratch_up, float* scratch_act);
 /* Reference: models/quantization.rs:439-454 dequant_layer(scales, packed, result, gs). */
 AH_API int ah_host_dequant_layer(const float* scales, const uint8_t* packed, float* result, size_t n, size_t group_size);
 /* Reference: models/quantization.rs:369-404 quantize(weights, gs) -> (scales, packed). */

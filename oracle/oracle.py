@@ -177,6 +177,26 @@ def gemv_4bit_into(scales, packed, x, rows, cols, group_size=32) -> np.ndarray:
     return out
 
 
+def gemv_4bit_worker_scalar(scales, packed, x, row_start, row_end, cols, group_size=32) -> np.ndarray:
+    """inference/math.rs:382-418 on rows [row_start, row_end) of the full planes."""
+    out = np.zeros(max(row_end - row_start, 0), np.float32)
+    x = _c(x, np.float32)
+    lib().or_gemv_4bit_worker_scalar(out if out.size else np.zeros(1, np.float32), _c(scales, np.float32),
+                                     _c(packed, np.uint8), x if x.size else np.zeros(1, np.float32),
+                                     row_start, row_end, cols, group_size)
+    return out
+
+
+def swiglu_4bit_into(inp, g_s, g_p, u_s, u_p, d_s, d_p, n_embd, n_ff, group_size=32):
+    """inference/ffn.rs:155-174 -> (out, scratch_gate, scratch_up, scratch_act)."""
+    out = np.zeros(max(n_embd, 1), np.float32)
+    sg, su, sa = (np.zeros(max(n_ff, 1), np.float32) for _ in range(3))
+    lib().or_swiglu_4bit_into(out, _c(inp, np.float32), _c(g_s, np.float32), _c(g_p, np.uint8), _c(u_s, np.float32),
+                              _c(u_p, np.uint8), _c(d_s, np.float32), _c(d_p, np.uint8), n_embd, n_ff, group_size,
+                              sg, su, sa)
+    return out[:n_embd], sg[:n_ff], su[:n_ff], sa[:n_ff]
+
+
 def gemv_q4_0(blocks, x, rows, cols) -> np.ndarray:
     out = np.empty(rows, np.float32)
     lib().or_gemv_q4_0(out, _c(blocks, np.uint8), _c(x, np.float32), rows, cols)
