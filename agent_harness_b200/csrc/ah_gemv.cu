@@ -2,7 +2,6 @@
 // dequant+GEMV kernel (batch 1..16) with its prologue/epilogue variants, and
 // the C-ABI entry points built on it.  Layout and arithmetic: ah_gemv.cuh.
 #include <algorithm>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <utility>
@@ -22,7 +21,6 @@ struct AhQ4Weight {
   int64_t weight_bytes = 0;
   void* nib_alloc = nullptr;
   void* scale_alloc = nullptr;
-  void* combine_alloc = nullptr;  // streaming-GEMV boundary slots and counters
   // device staging for host-buffer calls (ah_q4w_gemv_host), allocated on the
   // first such call for the largest batch; mu serialises those calls
   void* stage = nullptr;
@@ -158,22 +156,6 @@ int q4w_alloc(int64_t rows, int64_t cols, bool engine, AhQ4Weight** out) {
     delete w;
     return fail(AH_ENOMEM, "q4w_create: cudaMalloc of %zu bytes failed", nib_bytes + sc_bytes);
   }
-  // boundary slots of the streaming GEMV: one per pair of neighbouring CTAs of
-  // a one-CTA-per-SM grid; the counters start (and stay, between launches) at 0
-  const int nbd = sm_count();
-  const size_t cmb_floats = (size_t)nbd * 2 * 16 * kStreamMaxBatch;
-  if (ah::dev_malloc(&w->combine_alloc, cmb_floats * 4 + (size_t)nbd * 4) != cudaSuccess ||
-      cudaMemset(w->combine_alloc, 0, cmb_floats * 4 + (size_t)nbd * 4) != cudaSuccess) {
-    cudaGetLastError();
-    cudaFree(w->nib_alloc);
-    cudaFree(w->scale_alloc);
-    if (w->combine_alloc) cudaFree(w->combine_alloc);
-    delete w;
-    return fail(AH_ENOMEM, "q4w_create: cudaMalloc of the GEMV boundary slots failed");
-  }
-  w->t.combine = static_cast<float*>(w->combine_alloc);
-  w->t.combine_cnt = reinterpret_cast<int*>(w->t.combine + cmb_floats);
-  w->t.n_boundaries = nbd;
   w->t.nib = static_cast<const uint4*>(w->nib_alloc);
   w->t.scales = w->scale_alloc;
   w->weight_bytes = engine ? rows * ((cols + 1) / 2) + rows * nb * 4 : rows * nb * 18;
@@ -198,7 +180,6 @@ int q4w_create(const RowSource& src, bool engine, int64_t rows, int64_t cols, Ah
   if (e != cudaSuccess) {
     cudaFree(w->nib_alloc);
     cudaFree(w->scale_alloc);
-    cudaFree(w->combine_alloc);
     delete w;
     return fail(AH_ECUDA, "q4w_create: repack launch failed: %s", cudaGetErrorString(e));
   }
@@ -783,461 +764,6 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv_q4_rows(const GemvArgs
     for (int64_t j = k; j < issued; ++j) mbar_wait_bounded(&full[j % S], (uint32_t)((j / S) & 1), a.err, 0x602);
 }
 
-// One warp's epilogue of a finished row tile rt: fin[16][B] holds the tile's
-// full sums.  Writes y (store, residual add, or the SwiGLU pairs of an
-// interleaved gate/up tile), the tensor-parallel peer scatter, and the tile's
-// sum of squares for the next RMSNorm.
-template <int EPI>
-__device__ __forceinline__ void tile_epilogue_warp(const GemvArgs& a, int64_t rt, float* fin, int lane) {
-  const int B = a.batch;
-  if constexpr (EPI == kEpiSwiglu) {
-    // tile rows r < 8 are gate rows 8rt+r, rows r+8 the matching up rows
-    for (int i = lane; i < 8 * B; i += 32) {
-      const int r = i / B, b = i - r * B;
-      const int64_t o = rt * 8 + r;
-      if (o < a.w.rows / 2) a.y[b * a.y_stride + o] = silu_ref(fin[r * B + b]) * fin[(r + 8) * B + b];
-    }
-    __syncwarp();
-    return;
-  }
-  for (int i = lane; i < 16 * B; i += 32) {
-    const int r = i / B, b = i - r * B;
-    const int64_t R = rt * 16 + r;
-    float h = 0.0f;
-    if (R < a.w.rows) {
-      if (EPI == kEpiStore && a.n_peer > 0) {
-        h = fin[i];
-        for (int p = 0; p < a.n_peer; ++p) a.peer_y[p][R * a.peer_row + b] = h;  // NVLink stores
-      } else {
-        float* d = a.y + b * a.y_stride + R;
-        h = (EPI == kEpiAdd) ? *d + fin[i] : fin[i];  // residual: hidden[i] += out[i]
-        *d = h;
-      }
-    }
-    fin[i] = h;
-  }
-  // peer slots: the stores reach the other GPUs before this grid completes
-  if (EPI == kEpiStore && a.n_peer > 0) __threadfence_system();
-  if (a.ss_out) {
-    __syncwarp();
-    if (lane < B) {
-      float q = 0.0f;
-      for (int r = 0; r < 16; ++r) q = fmaf(fin[r * B + lane], fin[r * B + lane], q);
-      a.ss_out[lane * a.w.r16 + rt] = q;
-    }
-  }
-  __syncwarp();
-}
-
-// Splits x for the streaming kernel in one pass: per (token, 32-column block)
-// the values are scaled by 2^s so the block's max |x| lands in [2^14, 2^15)
-// and stored as f16 hi + lo (~22 significant bits; k-step-1 columns stored /16
-// to meet the 16x larger A values) in the planes [2*BT][plane] (plane j =
-// token j/2, hi or lo).  Per block, bias[b][kb] = {bh, bl, bh, bl} holds
-// -8 * 2^-24 * the block's sum of hi (lo) values, the accumulator start value
-// that applies the nibble offset inside the tensor core, and ex[b][kb] =
-// 2^(24 - s) undoes both scalings.  Eight consecutive threads share a block
-// (four values each); every thread issues all its loads before converting.
-template <int BT, int PRO, int NTH>
-__device__ __forceinline__ void split_x_stream(const GemvArgs& a, uint8_t* xs, float4* bias, float* ex, int plane,
-                                               int kbc, const float* tok_inv, int tid) {
-  constexpr int kBatch = 8;  // float4 loads in flight per thread
-  const int B = a.batch;
-  const int64_t K = a.w.cols;
-  const bool vec_ok = ((a.x_stride & 3) == 0) && ((reinterpret_cast<uintptr_t>(a.x) & 15u) == 0);
-  const int per_tok = kbc * 8;          // float4 slots per token (padded blocks)
-  const int total = B * per_tok;
-  const int J = (total + NTH - 1) / NTH;
-  const int sub = tid & 7;
-  const int e0 = sub * 4;
-  const int stp = e0 >> 4, reg = (e0 & 15) >> 3;
-  const int tA = ((e0 & 15) >> 1) & 3;
-  const int halfA = tA * 4 + stp * 2 + reg;
-  const float pre = stp ? 0.0625f : 1.0f;
-  const float wsum = stp ? 16.0f : 1.0f;
-  for (int jb = 0; jb < J; jb += kBatch) {
-    float v[kBatch][4];
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.0f;
-      const int i = (jb + u) * NTH + tid;
-      if (jb + u < J && i < total) {
-        const int b = i / per_tok;
-        const int64_t k = (int64_t)(i - b * per_tok) * 4;
-        const float* xr = a.x + b * a.x_stride;
-        if (vec_ok && k + 3 < K) {
-          const float4 f = __ldg(reinterpret_cast<const float4*>(xr + k));
-          v[u][0] = f.x; v[u][1] = f.y; v[u][2] = f.z; v[u][3] = f.w;
-        } else {
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (k + q < K) v[u][q] = xr[k + q];
-        }
-        if (PRO == kProRmsNorm) {
-          const float inv = tok_inv[b];
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            if (k + q < K) v[u][q] = (v[u][q] * inv) * __half2float(__ushort_as_half(a.norm_w[k + q]));
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      if (jb + u >= J) break;  // uniform
-      const int i = (jb + u) * NTH + tid;
-      const bool live = i < total;  // uniform over each group of eight lanes
-      float m = fmaxf(fmaxf(fabsf(v[u][0]), fabsf(v[u][1])), fmaxf(fabsf(v[u][2]), fabsf(v[u][3])));
-      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 1));
-      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 2));
-      m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, 4));
-      const int eb = (int)((__float_as_uint(m) >> 23) & 0xFFu);
-      const int sc = (m == 0.0f || m != m) ? 0 : min(max(14 - (eb - 127), -100), 100);
-      const float up = __uint_as_float((uint32_t)(127 + sc) << 23) * pre;
-      const float2 s01 = make_float2(v[u][0] * up, v[u][1] * up), s23 = make_float2(v[u][2] * up, v[u][3] * up);
-      const __half2 h01 = __float22half2_rn(s01), h23 = __float22half2_rn(s23);
-      const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-      const __half2 l01 = __float22half2_rn(make_float2(s01.x - f01.x, s01.y - f01.y));
-      const __half2 l23 = __float22half2_rn(make_float2(s23.x - f23.x, s23.y - f23.y));
-      const float2 g01 = __half22float2(l01), g23 = __half22float2(l23);
-      float shi = ((f01.x + f01.y) + (f23.x + f23.y)) * wsum;
-      float slo = ((g01.x + g01.y) + (g23.x + g23.y)) * wsum;
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        shi += __shfl_xor_sync(0xFFFFFFFFu, shi, o);
-        slo += __shfl_xor_sync(0xFFFFFFFFu, slo, o);
-      }
-      if (live) {
-        const int b = i / per_tok;
-        const int kb = (i - b * per_tok) >> 3;
-        __half2* ph = reinterpret_cast<__half2*>(xs + (2 * b) * plane) + kb * 16 + halfA;
-        __half2* pl = reinterpret_cast<__half2*>(xs + (2 * b + 1) * plane) + kb * 16 + halfA;
-        ph[0] = h01;
-        ph[4] = h23;
-        pl[0] = l01;
-        pl[4] = l23;
-        if (sub == 0) {
-          const float c = -8.0f * 5.9604644775390625e-8f;  // -8 * 2^-24
-          bias[b * kbc + kb] = make_float4(c * shi, c * slo, c * shi, c * slo);
-          ex[b * kbc + kb] = __uint_as_float((uint32_t)(127 + 24 - sc) << 23);
-        }
-      }
-    }
-  }
-}
-
-// One (row tile, block pair) unit: 16 rows x 64 columns against the split x,
-// two blocks of two m16n8k16 products each; the block sums, scaled by the
-// block's weight scale and x exponent, go to t0..t3 (rows g, g+8 x hi, lo).
-template <bool kF32>
-__device__ __forceinline__ void stream_unit(const uint4& w, const typename ScaleT<kF32>::V& sv, const uint8_t* xk,
-                                            const float4* bk, const float* ek, float& t0, float& t1, float& t2,
-                                            float& t3) {
-#pragma unroll
-  for (int blk = 0; blk < 2; ++blk) {
-    const uint4 bf = *reinterpret_cast<const uint4*>(xk + blk * 64);
-    const float4 cq = bk[blk];
-    const float e = ek[blk];
-    const uint32_t w0 = blk ? w.z : w.x;  // row g
-    const uint32_t w8 = blk ? w.w : w.y;  // row g+8
-    const uint32_t w0s = w0 >> 8, w8s = w8 >> 8;
-    float acc4[4] = {cq.x, cq.y, cq.z, cq.w};
-    mma16816(acc4, w0 & 0x000F000Fu, w8 & 0x000F000Fu, w0s & 0x000F000Fu, w8s & 0x000F000Fu, bf.x, bf.y, acc4);
-    mma16816(acc4, w0 & 0x00F000F0u, w8 & 0x00F000F0u, w0s & 0x00F000F0u, w8s & 0x00F000F0u, bf.z, bf.w, acc4);
-    float dg, dg8;
-    ScaleT<kF32>::get(sv, blk, dg, dg8);
-    const float de = dg * e, d8e = dg8 * e;
-    t0 = fmaf(de, acc4[0], t0);
-    t1 = fmaf(de, acc4[1], t1);
-    t2 = fmaf(d8e, acc4[2], t2);
-    t3 = fmaf(d8e, acc4[3], t3);
-  }
-}
-
-// Streaming GEMV for batches of 1..BT tokens (BT = 1 or 4: one n8
-// tensor-core tile holds hi and lo columns of four tokens), with NW compute
-// warps and one producer warp per CTA.  The grid has at most one CTA per SM;
-// with U = r16 * kp (row tile, block pair) units in the tiled layout, CTA c
-// owns the contiguous run of q or q + 1 units that starts at c*q + min(c, U
-// mod G) (q = U / G, at least one tile's worth), so every CTA streams the same
-// weight bytes to within one unit (576 B).  Units are grouped into cells of P
-// pairs of one tile (cell j of tile t: pairs [jP, min(jP + P, kp))); the run's
-// items are the cells it meets, clipped to the run, and round r gives item
-// NW*r + w to compute warp w.  A round's units are contiguous in both planes
-// and arrive by two bulk copies into one of S shared-memory stages (mbarrier
-// `full`).  The producer requests the first S rounds before the kernel waits
-// for its predecessor, and the kernel lets its dependents launch at once: the
-// next GEMV's CTA, which fits on the SM beside this one, streams its weights
-// while this one computes.  Compute warps never meet at a CTA barrier: each
-// leaves its item's partial in the stage's partial slots and arrives on the
-// stage's `empty` mbarrier; the producer warp waits for it, adds the round's
-// partials in unit order to the open tile's sum (in registers), finishes every
-// tile the run holds whole (epilogue), and refills the stage.  A run's first
-// tile may have begun in CTA c - 1 and its last may continue in CTA c + 1:
-// the right-hand CTA publishes its share of the shared tile as soon as it is
-// complete (its first tile; slot plus a release flag), and the left-hand CTA,
-// which reaches that tile last, adds left + right and runs the epilogue, so
-// the result does not depend on timing.
-template <int BT, int NW, bool kF32, int PRO, int EPI>
-__global__ void __launch_bounds__((NW + 1) * 32, 2) k_gemv_q4_stream(const GemvArgs a) {
-  using SV = typename ScaleT<kF32>::V;
-  constexpr int U = kGemvU;                    // units per unguarded batch
-  constexpr uint32_t kSclB = 8u * sizeof(SV);  // scale bytes per unit
-  constexpr int kSlot = 16 * kStreamMaxBatch;  // floats per boundary slot
-  constexpr uint32_t kFlagWait = 1u << 22;     // x ~100 ns sleeps: ~0.4 s
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t = lane & 3;
-  const int B = a.batch;
-  const uint32_t KP = (uint32_t)a.w.kp;
-  const uint32_t total = (uint32_t)(a.w.r16 * a.w.kp);
-  const uint32_t G = gridDim.x, c = blockIdx.x;
-  const uint32_t q = total / G, rem = total - q * G;
-  const uint32_t u0 = c * q + min(c, rem), u1 = u0 + q + (c < rem ? 1u : 0u);
-  const uint32_t ps = (uint32_t)a.pairs_per_chunk;  // log2 of the cell's pairs P
-  const uint32_t P = 1u << ps, CPT = a.cpt;
-  const int S = a.n_stages;
-  const uint32_t st_nib = (uint32_t)NW * P * 512u;
-  const uint32_t stage_bytes = (uint32_t)NW * P * (512u + kSclB);
-  const int kbc = 2 * (int)KP;
-  const int plane = kbc * 64 + 64;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * stage_bytes);
-  uint64_t* empty = full + S;
-  uint8_t* base = smem + (size_t)S * stage_bytes + (((size_t)S * 16 + 15) & ~(size_t)15);
-  uint8_t* xs = base;                                                          // [2BT][plane]
-  float4* bias = reinterpret_cast<float4*>(base + (size_t)2 * BT * plane);    // [BT][kbc]
-  float* ex = reinterpret_cast<float*>(bias + BT * kbc);                       // [BT][kbc]
-  float* part = ex + BT * kbc;                                                 // [S][NW][16][B]
-  float* tok_inv = part + (size_t)S * NW * 16 * BT;                            // [16]
-  float* wred = tok_inv + kGemvMaxBatch;                                       // [NW + 1][4]
-  float* fin = wred + (NW + 1) * kStreamMaxBatch;                              // [16][B] a finished tile
-  float* fin_r = fin + 16 * BT;                                                // [16][B] CTA c + 1's share
-  const bool producer = warp == NW;
-
-  // cells and items: tile of cell cc, unit range of round r
-  auto cell_tile = [&](uint32_t cc) -> uint32_t { return CPT == 1 ? cc : __umulhi(cc, a.cpt_magic); };
-  auto cell_start = [&](uint32_t cc) -> uint32_t {
-    const uint32_t tt = cell_tile(cc);
-    return tt * KP + ((cc - tt * CPT) << ps);
-  };
-  const uint32_t tile0 = u0 / KP, tile1 = (u1 - 1) / KP;
-  const uint32_t c0 = tile0 * CPT + ((u0 - tile0 * KP) >> ps);
-  const uint32_t c1 = tile1 * CPT + ((u1 - 1 - tile1 * KP) >> ps);
-  const uint32_t n_items = c1 - c0 + 1;
-  const uint32_t n_rounds = (n_items + NW - 1) / NW;
-  auto round_start = [&](uint32_t r) -> uint32_t {
-    return r == 0 ? u0 : (r >= n_rounds ? u1 : cell_start(c0 + r * NW));
-  };
-  auto issue = [&](uint32_t r) {
-    const uint32_t rs = round_start(r), n = round_start(r + 1) - rs;
-    uint8_t* dst = smem + (size_t)(r % S) * stage_bytes;
-    uint64_t* bar = &full[r % S];
-    mbar_arrive_expect_tx(bar, n * (512u + kSclB));
-    bulk_g2s(dst, a.w.nib + (size_t)rs * 32, n * 512u, bar);
-    bulk_g2s(dst + st_nib, reinterpret_cast<const SV*>(a.w.scales) + (size_t)rs * 8, n * kSclB, bar);
-  };
-  if (producer && lane == 0) {
-    for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], NW);
-    }
-    fence_mbar_init();
-    for (uint32_t r = 0; (int)r < S && r < n_rounds; ++r) issue(r);
-  }
-  pdl_wait();
-  // RMSNorm statistics (inference/math.rs:53-63) from the producer's partial
-  // sums of squares; then the split of x (compute warps)
-  if (PRO == kProRmsNorm) {
-    float ss[kStreamMaxBatch];
-#pragma unroll
-    for (int b = 0; b < kStreamMaxBatch; ++b) {
-      ss[b] = 0.0f;
-      if (b < B)
-        for (int i = tid; i < a.n_ss_in; i += (NW + 1) * 32) ss[b] += a.ss_in[b * a.n_ss_in + i];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss[b] += __shfl_xor_sync(0xFFFFFFFFu, ss[b], o);
-    }
-    if (lane == 0)
-#pragma unroll
-      for (int b = 0; b < kStreamMaxBatch; ++b) wred[warp * kStreamMaxBatch + b] = ss[b];
-    __syncthreads();
-    if (tid < B) {
-      float s_tot = 0.0f;
-      for (int w = 0; w <= NW; ++w) s_tot += wred[w * kStreamMaxBatch + tid];
-      tok_inv[tid] = __fdiv_rn(1.0f, sqrtf(__fdiv_rn(s_tot, (float)a.w.cols) + a.eps));  // inference/math.rs:59
-    }
-    __syncthreads();
-  }
-  if (!producer) split_x_stream<BT, PRO, NW * 32>(a, xs, bias, ex, plane, kbc, tok_inv, tid);
-  __syncthreads();
-  // x is in shared memory: let the dependents launch and stream their weights
-  // under this kernel's products (earlier, their copies would queue ahead of
-  // the loads of x in the SM's memory pipe)
-  pdl_launch_dependents();
-
-  if (!producer) {
-    // ---- compute warps: one item per round, partial into the stage's slot ----
-    const int col = (g < 2 * B) ? g : (g & 1);  // columns past the batch read token 0's planes
-    const int tok = t < B ? t : 0;
-    const uint8_t* xl = xs + (size_t)col * plane + t * 16;
-    const float4* bl = bias + (size_t)tok * kbc;
-    const float* el = ex + (size_t)tok * kbc;
-    for (uint32_t r = 0; r < n_rounds; ++r) {
-      const int st = (int)(r % (uint32_t)S);
-      const uint32_t k = r * NW + warp;
-      const bool ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(&full[st], (r / (uint32_t)S) & 1u, a.err, 0x611));
-      if (ok && k < n_items) {
-        const uint32_t rs = round_start(r);
-        const uint32_t cc = c0 + k;
-        const uint32_t mt = cell_tile(cc);
-        const uint32_t cs = mt * KP + ((cc - mt * CPT) << ps);
-        const uint32_t ms = k == 0 ? u0 : cs;
-        const uint32_t me = min(min(cs + P, (mt + 1) * KP), u1);
-        const uint8_t* stg = smem + (size_t)st * stage_bytes;
-        const uint4* snib = reinterpret_cast<const uint4*>(stg) + (size_t)(ms - rs) * 32 + lane;
-        const SV* sscl = reinterpret_cast<const SV*>(stg + st_nib) + (size_t)(ms - rs) * 8 + g;
-        const int np = (int)(me - ms);
-        const int kb0 = 2 * (int)(ms - mt * KP);
-        const uint8_t* xk = xl + (size_t)kb0 * 64;
-        const float4* bk = bl + kb0;
-        const float* ek = el + kb0;
-        float t0 = 0.0f, t1 = 0.0f, t2 = 0.0f, t3 = 0.0f;
-        int p = 0;
-        for (; p + U <= np; p += U) {  // full batches: no guards, so the units overlap
-          uint4 w[U];
-          SV sv[U];
-#pragma unroll
-          for (int u = 0; u < U; ++u) {
-            w[u] = snib[(p + u) * 32];
-            sv[u] = sscl[(p + u) * 8];
-          }
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-            stream_unit<kF32>(w[u], sv[u], xk + (p + u) * 128, bk + 2 * (p + u), ek + 2 * (p + u), t0, t1, t2, t3);
-        }
-        for (; p < np; ++p) {  // the short tail of a clipped item
-          const uint4 w = snib[p * 32];
-          const SV sv = sscl[p * 8];
-          stream_unit<kF32>(w, sv, xk + p * 128, bk + 2 * p, ek + 2 * p, t0, t1, t2, t3);
-        }
-        float* pr = part + ((size_t)st * NW + warp) * 16 * B;
-        if (t < B) {  // columns 2t (hi) and 2t+1 (lo) of token t
-          pr[g * B + t] = t0 + t1;
-          pr[(g + 8) * B + t] = t2 + t3;
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      if (!ok) return;
-    }
-    return;
-  }
-
-  // ---- producer warp: reduce each round in unit order, finish tiles, refill ----
-  const int nv = 16 * B;  // [16 rows][B tokens]: lanes hold values lane and lane + 32
-  int ot = -1;
-  float v0 = 0.0f, v1 = 0.0f;
-  bool ok = true;
-  uint32_t r = 0;
-  auto to_fin = [&](float f0, float f1) {
-    if (lane < nv) fin[lane] = f0;
-    if (lane + 32 < nv) fin[lane + 32] = f1;
-    __syncwarp();
-  };
-  const bool right = (u1 % KP) != 0;  // the last tile continues in CTA c + 1
-  int got = 0;
-  for (; r < n_rounds; ++r) {
-    const int st = (int)(r % (uint32_t)S);
-    if (right && r + 1 == n_rounds) {
-      // while the compute warps run the last round: take CTA c + 1's share of
-      // the last tile (published when that CTA finished its first tile)
-      if (lane == 0) {
-        for (uint32_t it = 0; it < kFlagWait; ++it) {
-          if (ld_acquire_gpu(&a.w.combine_cnt[c]) != 0) {
-            got = 1;
-            break;
-          }
-          __nanosleep(100);
-        }
-        if (got) {
-          const float* slot = a.w.combine + (size_t)c * kSlot;
-          for (int i = 0; i < nv; ++i) fin_r[i] = slot[i];
-          a.w.combine_cnt[c] = 0;  // consumed: the flag is clear for the next launch
-        } else {
-          atomicExch(a.err, 0x614);
-        }
-      }
-      got = __shfl_sync(0xFFFFFFFFu, got, 0);
-      __syncwarp();
-    }
-    ok = __all_sync(0xFFFFFFFFu, mbar_wait_bounded(&empty[st], (r / (uint32_t)S) & 1u, a.err, 0x613));
-    if (!ok) break;
-    const float* pr = part + (size_t)st * NW * 16 * B;
-    float p0[NW], p1[NW];
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      p0[w] = lane < nv ? pr[w * nv + lane] : 0.0f;
-      p1[w] = lane + 32 < nv ? pr[w * nv + lane + 32] : 0.0f;
-    }
-    __syncwarp();
-    // the stage's weights and partials are consumed: refill it now, so the
-    // copies run under the reduction
-    if (lane == 0 && r + S < n_rounds) {
-      fence_proxy_async_smem();
-      issue(r + S);
-    }
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const uint32_t kk = r * NW + w;
-      if (kk < n_items) {
-        const int tw = (int)cell_tile(c0 + kk);
-        if (tw != ot) {
-          if (ot >= 0) {  // tile ot is complete in this run
-            to_fin(v0, v1);
-            if ((uint32_t)ot * KP < u0) {
-              // began in CTA c - 1: publish this share for it (slot, then a release flag)
-              if (lane == 0) {
-                float* slot = a.w.combine + (size_t)(c - 1) * kSlot;
-                for (int i = 0; i < nv; ++i) slot[i] = fin[i];
-                st_release_gpu(&a.w.combine_cnt[c - 1], 1);
-              }
-              __syncwarp();
-            } else {
-              tile_epilogue_warp<EPI>(a, ot, fin, lane);
-            }
-          }
-          ot = tw;
-          v0 = p0[w];
-          v1 = p1[w];
-        } else {
-          v0 += p0[w];
-          v1 += p1[w];
-        }
-      }
-    }
-  }
-  if (!ok) {
-    // a wait gave up: let the copies still in flight land (bounded) first
-    if (lane == 0)
-      for (uint32_t j = r; j < n_rounds && j < r + (uint32_t)S; ++j)
-        mbar_wait_bounded(&full[j % S], (j / (uint32_t)S) & 1u, a.err, 0x612);
-    return;
-  }
-  // the run's last tile: whole here, or continued in CTA c + 1, whose share
-  // arrived through slot c
-  if (ot < 0) return;
-  if (!right) {
-    to_fin(v0, v1);
-    tile_epilogue_warp<EPI>(a, ot, fin, lane);
-    return;
-  }
-  if (!got) return;
-  // left (this CTA) + right (CTA c + 1)
-  if (lane < nv) fin[lane] = v0 + fin_r[lane];
-  if (lane + 32 < nv) fin[lane + 32] = v1 + fin_r[lane + 32];
-  __syncwarp();
-  tile_epilogue_warp<EPI>(a, ot, fin, lane);
-}
-
 using GemvKernel = void (*)(const GemvArgs);
 #define AH_TRY_GEMV(expr)         \
   do {                            \
@@ -1264,22 +790,6 @@ GemvKernel pick_format(int pro, int epi) {
 template <int NT, bool kRows>
 GemvKernel pick_kernel(bool f32s, int pro, int epi) {
   return f32s ? pick_format<NT, kRows, true>(pro, epi) : pick_format<NT, kRows, false>(pro, epi);
-}
-
-template <int BT, bool F>
-GemvKernel pick_stream_format(int pro, int epi) {
-  if (pro == kProPlain) {
-    if (epi == kEpiStore) return k_gemv_q4_stream<BT, kStreamWarps, F, kProPlain, kEpiStore>;
-    if (epi == kEpiAdd) return k_gemv_q4_stream<BT, kStreamWarps, F, kProPlain, kEpiAdd>;
-    return k_gemv_q4_stream<BT, kStreamWarps, F, kProPlain, kEpiSwiglu>;
-  }
-  if (epi == kEpiStore) return k_gemv_q4_stream<BT, kStreamWarps, F, kProRmsNorm, kEpiStore>;
-  if (epi == kEpiAdd) return k_gemv_q4_stream<BT, kStreamWarps, F, kProRmsNorm, kEpiAdd>;
-  return k_gemv_q4_stream<BT, kStreamWarps, F, kProRmsNorm, kEpiSwiglu>;
-}
-GemvKernel pick_stream_kernel(int bt, bool f32s, int pro, int epi) {
-  if (bt == 1) return f32s ? pick_stream_format<1, true>(pro, epi) : pick_stream_format<1, false>(pro, epi);
-  return f32s ? pick_stream_format<4, true>(pro, epi) : pick_stream_format<4, false>(pro, epi);
 }
 
 }  // namespace
@@ -1313,81 +823,6 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
 }
 
 GemvPlan gemv_plan(const Q4Tiled& w, int batch) { return gemv_plan(w, batch, false); }
-
-namespace {
-// Streaming kernel switch, read once: AH_GEMV_STREAM=0 turns it off (the
-// cluster / rows kernels serve every batch), 2 prefers one CTA per SM with
-// deeper stages over two co-resident CTAs; unset or 1 is the default.
-int stream_setting() {
-  static const int v = [] {
-    const char* e = getenv("AH_GEMV_STREAM");
-    return e ? atoi(e) : 1;
-  }();
-  return v;
-}
-constexpr size_t kStreamSmemTwo = 112 * 1024;  // two CTAs per SM (this GEMV and the next)
-constexpr size_t kStreamSmemOne = 220 * 1024;
-constexpr int kStreamMaxStages = 6;
-}  // namespace
-
-// Streaming-kernel plan for batches of 1..kStreamMaxBatch: the grid (at most
-// one CTA per SM, at least one row tile of units per CTA), items of P block
-// pairs and S stages of 8 items, in the largest stage ring that leaves room
-// for the co-resident next GEMV (or, failing that, for one CTA per SM).
-bool stream_plan(const Q4Tiled& w, int batch, GemvPlan* out) {
-  const int setting = stream_setting();
-  if (setting == 0 || batch < 1 || batch > kStreamMaxBatch || !w.combine || w.r16 < 1) return false;
-  if ((uint64_t)w.r16 * (uint64_t)w.kp >= (1ull << 30)) return false;
-  const int bt = batch == 1 ? 1 : kStreamMaxBatch;  // instantiated token counts
-  int64_t G = std::min<int64_t>(sm_count(), w.r16);
-  G = std::min<int64_t>(G, (int64_t)w.n_boundaries + 1);
-  const int64_t kbc = 2 * w.kp;
-  const int64_t plane = kbc * 64 + 64;
-  const size_t scl_b = (size_t)8 * (w.f32_scales ? 16 : 8);
-  const size_t base = (size_t)2 * bt * plane + (size_t)bt * kbc * 20 + (size_t)kGemvMaxBatch * 4 +
-                      (size_t)(kStreamWarps + 1) * kStreamMaxBatch * 4 + (size_t)2 * 16 * bt * 4 + 16;
-  const size_t per_stage_extra = 16 + (size_t)kStreamWarps * 16 * bt * 4;  // mbarriers + partial slots
-  const int64_t run = ((int64_t)w.r16 * w.kp + G - 1) / G;  // units of the longest run
-  const size_t budgets[2] = {setting == 2 ? kStreamSmemOne : kStreamSmemTwo,
-                             setting == 2 ? kStreamSmemTwo : kStreamSmemOne};
-  for (size_t budget : budgets) {
-    int best_p = 0, best_s = 0;
-    size_t best_inflight = 0;
-    for (int P : {8, 4}) {
-      const int64_t cpt = (w.kp + P - 1) / P;
-      // cells x cpt must stay below 2^32 for the division by multiply-high
-      if ((uint64_t)w.r16 * (uint64_t)cpt * (uint64_t)cpt >= (1ull << 32)) continue;
-      const size_t stage = (size_t)kStreamWarps * P * (512 + scl_b);
-      const int64_t items = run / P + run / w.kp + 3;  // cells a run meets, at most
-      const int64_t rounds = (items + kStreamWarps - 1) / kStreamWarps;
-      int S = 0;
-      while (S < kStreamMaxStages && S < rounds && (size_t)(S + 1) * (stage + per_stage_extra) + base <= budget) ++S;
-      if (S < 1 || (S < 2 && rounds > 1)) continue;
-      const size_t inflight = (size_t)S * stage;
-      if (inflight > best_inflight) {
-        best_inflight = inflight;
-        best_p = P;
-        best_s = S;
-      }
-    }
-    if (best_s > 0) {
-      GemvPlan p{};
-      p.nt = bt;
-      p.stream_mode = true;
-      p.grid = (int)G;
-      p.pairs_per_chunk = best_p;
-      p.n_stages = best_s;
-      p.ksplit = 1;
-      const size_t stage = (size_t)kStreamWarps * best_p * (512 + scl_b);
-      p.smem = (size_t)best_s * (stage + per_stage_extra) + base;
-      p.threads = (kStreamWarps + 1) * 32;
-      p.smem_base = base;
-      *out = p;
-      return true;
-    }
-  }
-  return false;
-}
 
 namespace {
 GemvKernel select_kernel(const GemvPlan& plan, bool f32s, int pro, int epi) {
@@ -1435,8 +870,7 @@ int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
   }
   int n = 0;
   if (plan.rows_mode) {
-    AH_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, plan.threads > 0 ? plan.threads : kGemvThreads,
-                                                              plan.smem));
+    AH_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, plan.smem));
     n *= sm_count();
   } else {
     cudaLaunchConfig_t q{};
@@ -1463,20 +897,6 @@ int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
 // memory beside at least two tile stages (it is then amortised over several
 // tiles per CTA).
 int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, GemvKernel* kern, int* cap) {
-  GemvPlan ps;
-  if (stream_plan(w, batch, &ps) && aligned16(w.nib) && aligned16(w.scales)) {
-    GemvKernel ks = pick_stream_kernel(ps.nt, w.f32_scales, pro, epi);
-    ps.rows_mode = true;  // kernel_setup: plain (non-cluster) occupancy query
-    int scap = 0;
-    AH_TRY_GEMV(kernel_setup(ks, ps, &scap));
-    ps.rows_mode = false;
-    if (scap > 0) {
-      *plan = ps;
-      *kern = ks;
-      *cap = scap;
-      return AH_OK;
-    }
-  }
   GemvPlan pc = gemv_plan(w, batch, false);
   if (pc.smem > (size_t)kGemvSmemLimit)
     return fail(AH_EUNSUPPORTED, "gemv: batch %d x %lld columns needs %zu B of shared memory per CTA (limit %d)",
@@ -1511,8 +931,6 @@ namespace {
 // The largest token count (<= batch) whose split of x fits one CTA's shared
 // memory; larger batches run as several launches over token slices.
 int max_sub_batch(const Q4Tiled& w, int batch) {
-  GemvPlan ps;
-  if (stream_plan(w, batch, &ps)) return batch;
   for (int b = batch; b >= 1; --b)
     if (gemv_plan(w, b, false).smem <= (size_t)kGemvSmemLimit) return b;
   return 0;
@@ -1572,15 +990,7 @@ int gemv_launch_one(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if (plan.stream_mode) {
-    AH_REQUIRE(a.err != nullptr, "gemv: device error word unavailable");
-    a.early_trigger = 1;
-    a.cpt = (uint32_t)((a.w.kp + plan.pairs_per_chunk - 1) / plan.pairs_per_chunk);
-    a.cpt_magic = a.cpt > 1 ? (uint32_t)((1ull << 32) / a.cpt + 1) : 0u;
-    a.pairs_per_chunk = plan.pairs_per_chunk == 8 ? 3 : 2;  // the kernel takes log2 of the cell's pairs
-    cfg.gridDim = dim3((unsigned)plan.grid, 1, 1);
-    cfg.blockDim = dim3((unsigned)plan.threads, 1, 1);
-  } else if (plan.rows_mode) {
+  if (plan.rows_mode) {
     const int64_t n = std::min<int64_t>(a.w.r16, cap);
     a.early_trigger = a.w.r16 <= cap ? 1 : 0;
     cfg.gridDim = dim3((unsigned)n, 1, 1);
@@ -1730,7 +1140,6 @@ int ah_q4w_destroy(AhQ4Weight* w) {
   cudaSetDevice(w->device);
   cudaFree(w->nib_alloc);
   cudaFree(w->scale_alloc);
-  if (w->combine_alloc) cudaFree(w->combine_alloc);
   if (w->stage) cudaFree(w->stage);
   if (w->host_graph) cudaGraphExecDestroy(w->host_graph);
   if (w->host_cap) cudaStreamDestroy(w->host_cap);

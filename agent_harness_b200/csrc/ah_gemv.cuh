@@ -57,16 +57,7 @@ struct Q4Tiled {
   int64_t rows, cols;  // logical shape
   int64_t r16, kp;     // tiles, block pairs
   bool f32_scales;
-  // streaming GEMV: a row tile whose K range two neighbouring CTAs share meets
-  // in slot pair [boundary][side] (side 0 = the left CTA's partial, 1 = the
-  // right one's; kStreamMaxBatch tokens x 16 rows each) and counter [boundary]
-  // (0 between launches; the second CTA to arrive sums and resets it)
-  float* combine;
-  int* combine_cnt;
-  int n_boundaries;    // combine slots allocated (grids of up to n_boundaries + 1 CTAs)
 };
-constexpr int kStreamMaxBatch = 4;  // tokens of the streaming kernel (one n8 tensor-core tile)
-constexpr int kStreamWarps = 8;     // compute warps of the streaming kernel (plus one producer warp)
 
 // ---- epilogue / prologue selectors --------------------------------------------
 enum GemvPrologue : int { kProPlain = 0, kProRmsNorm = 1 };
@@ -91,8 +82,7 @@ struct GemvArgs {
   float* ss_out;
   int64_t pairs_per_chunk; // block pairs per K-chunk (cluster CTA)
   int early_trigger;       // set by the launcher: grid fits in one resident wave
-  int n_stages;            // rows / stream mode: stages in flight in shared memory
-  uint32_t cpt, cpt_magic; // stream mode: item cells per row tile and floor(2^32 / cpt) + 1
+  int n_stages;            // rows mode: row tiles in flight in shared memory
   int* err;                // device error word (a bounded wait that gave up)
   // Store epilogue scatter (tensor-parallel all-reduce over peer memory): with
   // n_peer > 0 every output element goes to peer_y[p] + row*peer_row + b for

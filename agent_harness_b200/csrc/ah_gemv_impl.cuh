@@ -15,10 +15,7 @@ struct GemvPlan {
   size_t smem;              // dynamic shared memory bytes
   bool rows_mode;           // persistent full-K CTAs instead of clusters
   size_t smem_base;         // rows mode: shared memory besides the tile stages
-  int n_stages;             // rows / stream mode: stages in flight (0: mode unavailable)
-  bool stream_mode;         // streaming kernel: one CTA per SM, balanced unit runs
-  int grid;                 // stream mode: CTAs
-  int threads;              // stream mode: threads per CTA (compute warps + the producer warp)
+  int n_stages;             // rows mode: row tiles in flight (0: rows mode unavailable)
 };
 
 GemvPlan gemv_plan(const Q4Tiled& w, int batch);

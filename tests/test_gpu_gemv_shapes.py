@@ -1,11 +1,9 @@
-"""GPU parity of the streaming GEMV schedule (batches of 1..4 tokens): one CTA
-per SM, each streaming a balanced contiguous run of (row tile, block pair)
-units, with the row tiles that two neighbouring CTAs share summed through the
-weight's boundary slots.  Against the oracle's scalar gemv (inference/math.rs:
-382-418) at the north-star tolerance, on shapes that put run boundaries in the
-middle of tiles, that give fewer tiles than SMs, odd block-pair counts and
-ragged rows; and repeated calls must give bit-identical results (the
-boundary counters return to zero after every launch)."""
+"""GPU parity of the fused Q4 GEMV (batches of 1..4 tokens) on shapes that
+stress its schedules: the benchmark shape, the 8B decoder's projections, an
+odd block-pair count, ragged rows, fewer row tiles than SMs, a single padded
+tile.  Against the oracle's scalar gemv (inference/math.rs:382-418) at the
+north-star tolerance, and repeated calls on the same input must give
+bit-identical results (no state carried between launches)."""
 import numpy as np
 import pytest
 import torch
@@ -20,18 +18,18 @@ def relerr(y, ref):
 
 
 @pytest.mark.parametrize("rows,cols,batch", [
-    (4096, 4096, 1),        # the benchmark shape: 148 runs of 110-111 units over 256 tiles
+    (4096, 4096, 1),        # the benchmark shape
     (4096, 4096, 4),
     (6144, 4096, 1),        # fused QKV of the 8B shape
-    (4096, 14336, 1),       # down projection: 224 pairs per tile, two-stage ring
+    (4096, 14336, 1),       # down projection: 224 block pairs per tile
     (4096 + 16, 4096 + 32, 2),  # 65 block pairs (odd), one extra tile
-    (1000, 2048, 3),        # ragged rows, 63 tiles: fewer tiles than SMs (one run per tile)
+    (1000, 2048, 3),        # ragged rows, 63 tiles: fewer tiles than SMs
     (2368, 1024, 1),        # 148 tiles exactly
-    (2384, 1024, 1),        # 149 tiles: every run boundary inside a tile
+    (2384, 1024, 1),        # 149 tiles
     (7, 64, 1),             # a single padded tile
     (3000, 96, 4),          # 2 block pairs per tile, 188 tiles
 ])
-def test_stream_shapes_match_oracle(cuda, oracle, rows, cols, batch):
+def test_shapes_match_oracle(cuda, oracle, rows, cols, batch):
     from agent_harness_b200 import kernels as K
     blocks = K.synth_q4_0(rows, cols, 0.02, rows * 3 + cols + batch, device=cuda)
     W = K.Q4Weight.from_q4_0(blocks, rows, cols)
@@ -47,7 +45,7 @@ def test_stream_shapes_match_oracle(cuda, oracle, rows, cols, batch):
             assert err <= TOL, (rows, cols, batch, b, err)
             assert err < 1e-5, err  # f32-grade split-f16 products
         outs.append((x, y))
-    # the same input again: bit-identical (deterministic boundary sums)
+    # the same input again: bit-identical
     x, y = outs[0]
     y2 = W.gemv(x).cpu().numpy().reshape(batch, rows)
     assert np.array_equal(y.view(np.uint32), y2.view(np.uint32))
@@ -57,7 +55,7 @@ def test_stream_shapes_match_oracle(cuda, oracle, rows, cols, batch):
     W.close()
 
 
-def test_stream_engine_format(cuda, oracle):
+def test_engine_format_ragged_tiles(cuda, oracle):
     from agent_harness_b200 import kernels as K
     rng = np.random.default_rng(71)
     rows, cols = 2384, 2048
@@ -72,10 +70,9 @@ def test_stream_engine_format(cuda, oracle):
     W.close()
 
 
-def test_stream_back_to_back_weights_share_nothing(cuda, oracle):
-    # launches on different weights queued back to back (the next one's
-    # weights stream while the previous one computes) and on the same weight
-    # twice in a row
+def test_back_to_back_weights_share_nothing(cuda, oracle):
+    # launches on different weights queued back to back (each prefetches its
+    # weights under the previous one's tail) and on the same weight twice in a row
     from agent_harness_b200 import kernels as K
     shapes = [(4096, 4096), (2384, 1024), (4096, 4096), (1000, 2048)]
     ws, bs = [], []
