@@ -71,10 +71,19 @@ __global__ void __launch_bounds__(kThreads) k_half_to_f32_scalar(const uint8_t* 
   }
 }
 
+template <class F>
+int launch_dequant_blocks(const void* blocks, float* out, int64_t n, cudaStream_t st);
+template <bool kBf16>
+struct HalfFmt;
+
+// The bulk-copy ring for 16-byte aligned buffers of at least one tile; the
+// register-batched kernel and the byte-addressed one cover the rest.
 template <bool kBf16>
 int launch_half_to_f32(const void* src, float* dst, int64_t n, cudaStream_t st) {
   if (n == 0) return AH_OK;
   AH_REQUIRE(src && dst && n > 0, "half_to_f32: null pointer or negative n");
+  if (aligned16(src) && aligned16(dst) && n >= (int64_t)HalfFmt<kBf16>::kTileBlocks * 32)
+    return launch_dequant_blocks<HalfFmt<kBf16>>(src, dst, n, st);
   int64_t done = 0;
   if (aligned16(src) && aligned16(dst)) {
     int64_t n8 = n / 8;
@@ -172,6 +181,26 @@ struct Q4Fmt {  // formats/gguf.rs:480-502, types/dtype.rs:69-75
     const uint32_t byte = bp[2 + (i >> 1)];
     const uint32_t nib = (i & 1) ? (byte >> 4) : (byte & 0xFu);
     return x86_mul(f16_bits_to_f32(dbits), (float)(int)nib - 8.0f);
+  }
+};
+
+// f16 / bf16 as a "block" format of 32 halves (64 bytes): the conversion then
+// streams through the same bulk-copy ring as the quantised blocks.
+template <bool kBf16>
+struct HalfFmt {
+  static constexpr int kBlockBytes = 64;
+  static constexpr int kTileBlocks = 128;  // 8 KB in, 16 KB out
+  static __device__ __forceinline__ float4 unpack(const uint8_t* tile, int f) {
+    const uint2 h = *reinterpret_cast<const uint2*>(tile + f * 8);
+    float4 v;
+    v.x = half_bits_to_f32<kBf16>(h.x & 0xFFFFu);
+    v.y = half_bits_to_f32<kBf16>(h.x >> 16);
+    v.z = half_bits_to_f32<kBf16>(h.y & 0xFFFFu);
+    v.w = half_bits_to_f32<kBf16>(h.y >> 16);
+    return v;
+  }
+  static __device__ __forceinline__ float element(const uint8_t* src, int64_t e) {
+    return half_bits_to_f32<kBf16>((uint32_t)src[2 * e] | ((uint32_t)src[2 * e + 1] << 8));
   }
 };
 

@@ -36,10 +36,19 @@ N_COPIES = 64
 GEMV_BYTES = ROWS * (COLS // 32) * 18 + COLS * 4 + ROWS * 4  # 9,469,952
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum per GEMV launch, from the ncu
-# capture summarised in profiles/gemv_q4_0_4096x4096_batch1.md (read 9,492,480 B,
-# write 0 B: y stays in L2 at kernel end).
-NCU_TRAFFIC_PER_LAUNCH = 9492480
+PROFILE_GEMV = os.path.join(ROOT, "profiles", "gemv_q4_0_4096x4096_batch1.md")
+
+
+def ncu_traffic_per_launch():
+    """dram__bytes_read.sum + dram__bytes_write.sum of one headline GEMV launch,
+    as the ncu summary of this kernel records it ("traffic_bytes_per_launch:"),
+    or None when no capture is recorded."""
+    import re
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9,]+)", open(PROFILE_GEMV).read())
+        return int(m.group(1).replace(",", "")) if m else None
+    except OSError:
+        return None
 
 
 def peaks():
@@ -311,6 +320,25 @@ def run_gpu(args):
     if not args.quick and not args.no_tp:
         extra["decode_70b_tp"] = decode_70b_tp(dev, rank, world, args.tp_prompt, args.tp_new,
                                                allreduce=args.tp_allreduce)
+    if rank == 0 and not args.no_cpu and not args.quick:
+        if "decode_8b" in extra:
+            sh8 = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096),
+                   (4096, 14336)]
+            step, nt, layer = cpu_decode_baseline(sh8, 32, (128256, 4096), 1)
+            extra["decode_8b"]["cpu_baseline"] = {
+                "value": round(1.0 / step, 3), "unit": "tokens/s", "cores": nt, "kind": "port",
+                "sample": f"extrapolated: one layer's 7 projection GEMVs ({layer * 1e3:.1f} ms) x 32 + the LM head "
+                          "through the AVX-512 gemv_4bit_into restatement (the engine forward's weight streaming, "
+                          "inference/mod.rs:411-538); attention and norms not included"}
+        if "decode_70b_tp" in extra:
+            sh70 = [(8192, 8192), (1024, 8192), (1024, 8192), (8192, 8192), (28672, 8192), (28672, 8192),
+                    (8192, 28672)]
+            step, nt, layer = cpu_decode_baseline(sh70, 80, (128256, 8192), TP_BATCH)
+            extra["decode_70b_tp"]["cpu_baseline"] = {
+                "value": round(TP_BATCH / step, 4), "unit": "tokens/s", "cores": nt, "kind": "port",
+                "sample": f"extrapolated: one layer's 7 projection GEMVs ({layer * 1e3:.1f} ms per token) x 80 + "
+                          f"the LM head, x {TP_BATCH} sequences, through the AVX-512 gemv_4bit_into restatement "
+                          "(the reference decodes one token per forward); attention and norms not included"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = time_cpu_gemv(seconds=args.cpu_seconds)
@@ -329,7 +357,8 @@ def run_gpu(args):
             "pct_of_8tbs": round(100.0 * achieved / NOMINAL_HBM_GBS, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "traffic": NCU_TRAFFIC_PER_LAUNCH,
+                         "traffic": ncu_traffic_per_launch(),
+                         "traffic_source": "profiles/gemv_q4_0_4096x4096_batch1.md (ncu, this kernel)",
                          "kernel": "k_gemv_q4<1,false,0,0>", "bytes_per_launch": GEMV_BYTES,
                          "avg_launch_us": round(per_launch_s * 1e6, 4)},
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "h2d_bytes_per_step": N_COPIES * COLS * 4,
@@ -358,10 +387,37 @@ DECODE_PROMPT, DECODE_NEW = 2048, 256
 DECODE_BYTES_PER_TOKEN_WEIGHTS = 4221370368  # all Q4_0 projections + LM head of the 8B shape
 
 
-TP_PROMPT, TP_NEW, TP_BATCH = 128, 64, 16
+TP_PROMPT, TP_NEW, TP_BATCH = 2048, 128, 16
 # all Q4_0 projections + LM head of the 70B shape (80 x (q 8192^2 + k,v 1024x8192
 # + o 8192^2 + gate,up,down 3 x 28672x8192) + 128256x8192) x 18/32 bytes
 DECODE70_WEIGHT_BYTES = 39094714368
+
+
+def cpu_decode_baseline(layer_shapes, n_layer, head_shape, tokens, min_s=0.3):
+    """The reference's decode on the host cores: its engine forward spends its
+    time in gemv_4bit_into (the AVX-512 worker, inference/math.rs:255-380) once
+    per projection, layer and token.  Each projection shape of one layer and the
+    LM head is timed on engine-format weights (random bytes: the timing does
+    not depend on the values); the step is layer x n_layer + head, times the
+    tokens of a step.  Attention, norms and sampling are left out (they are a
+    few per cent of the weight streaming at these shapes), so this is an
+    extrapolated lower bound on the reference's step time."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    nt = cpu_threads()
+    per = {}
+    for rows, cols in list(layer_shapes) + [head_shape]:
+        if (rows, cols) in per:
+            continue
+        sc = (rng.random(rows * cols // 32) * 0.004).astype(np.float32)
+        pk = rng.integers(0, 256, rows * cols // 2, dtype=np.uint8)
+        x = rng.standard_normal(cols).astype(np.float32)
+        y = np.empty(rows, np.float32)
+        per[(rows, cols)] = _cpu_seconds(lambda: O.avx_gemv_4bit_into(y, sc, pk, x, rows, cols, nt), min_s=min_s,
+                                         max_calls=10)
+    layer = sum(per[sh] for sh in layer_shapes)
+    step = (layer * n_layer + per[head_shape]) * tokens
+    return step, nt, layer
 
 
 def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_BATCH, allreduce="peer"):
@@ -406,12 +462,32 @@ def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_B
     first = toks[1, :4].cpu().numpy().tolist()
     m.close()
     per_step = ms / 1e3 / n_new
+    split = {}
+    if world > 1:
+        # the step's collective alone: 2 all-reduces per layer of the block
+        # output [batch, d_model] f32 (NCCL), timed on the device, max over ranks
+        import torch.distributed as dist
+        buf = torch.zeros(batch, cfg.n_embd, device=dev)
+        for _ in range(20):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize(dev)
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(st)
+        for _ in range(2 * cfg.n_layer):
+            dist.all_reduce(buf)
+        c1.record(st)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([c0.elapsed_time(c1)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        split = {"allreduce_alone_ms_per_step": round(float(t.item()), 3),
+                 "allreduce_note": f"{2 * cfg.n_layer} ncclAllReduce of [{batch}, {cfg.n_embd}] f32 timed alone; "
+                                   "the rest of the step streams weights"}
     return {"tokens_per_s": round(batch * n_new / (ms / 1e3), 1), "ms_per_step": round(per_step * 1e3, 3),
             "batch": batch, "n_prompt": n_prompt, "n_new": n_new, "tp": world,
             "block_allreduce": (allreduce if world > 1 else "none"),
             "weight_gbs_per_gpu": round(DECODE70_WEIGHT_BYTES / world / per_step / 1e9, 1),
             "prefill_tokens_per_s_token_by_token": round(batch * (n_prompt - 1) / prefill_s, 1),
-            "first_tokens_seq0_3": first,
+            "first_tokens_seq0_3": first, **split,
             "note": "tensor parallel over the job's ranks: row/column-sharded projections, one all-reduce per "
                     "attention/MLP block (peer: GEMV epilogue stores into every rank's slots over NVLink + flag; "
                     "nccl: ncclAllReduce), argmax-candidate all-gather; steps replayed as CUDA graphs"}
@@ -518,35 +594,100 @@ def prefill_gemm(K, dev, iters=20, cpu_tokens=0):
     return out
 
 
-def secondary_measurements(K, dev, stream, peak, no_cpu=False):
-    """Config-1 dequant and f16->f32 throughput (each launch > L2), and the
-    DedupCount load path."""
+def _gpu_seconds(fn, stream, iters=20):
+    """Device time per call (CUDA events on `stream`, after 3 warm-up calls)."""
     import torch
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            fn()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / iters
+
+
+def _cpu_seconds(fn, min_s=0.5, max_calls=20):
+    fn()  # first touch of the output pages
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls:
+        fn()
+        n += 1
+        if time.perf_counter() - t0 >= min_s:
+            break
+    return (time.perf_counter() - t0) / n
+
+
+def secondary_measurements(K, dev, stream, peak, no_cpu=False):
+    """Config-1 conversions and dequantisation (every launch > L2: 206-271 MB
+    moved), each with the reference's CPU implementation of the same call timed
+    on the host beside it, and the DedupCount load path and SSM step."""
+    import torch
+    from agent_harness_b200 import _lib
     out = {}
     n = 4096 * 11008
     w = K.fill_normal(n, 0.0, 0.02, 0, device=dev)
     q8 = K.quantize_q8_0(w)
+    q4 = K.quantize_q4_0(w)
+    sc, pk = K.quantize_q4(w, 32)
     del w
     f = torch.empty(n, dtype=torch.float32, device=dev)
     h = K.f32_to_f16(K.fill_normal(n, 0.0, 1.0, 1, device=dev))
-    for name, fn, nbytes in (("dequant_q8_0", lambda: K.dequant_q8_0(q8, n, out=f), q8.numel() + 4 * n),
-                             ("f16_to_f32", lambda: K.f16_to_f32(h), 2 * n + 4 * n)):
-        with torch.cuda.stream(stream):
-            for _ in range(3):
-                fn()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            iters = 20
-            e0.record(stream)
-            for _ in range(iters):
-                fn()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        s = e0.elapsed_time(e1) / 1e3 / iters
+    st = C.c_void_p(stream.cuda_stream)
+    L = _lib.lib()
+    rows = (
+        ("dequant_q8_0", lambda: K.dequant_q8_0(q8, n, out=f), q8.numel() + 4 * n,
+         "Q8_0 blocks {f16 d; i8 q[32]} (gguf.rs:459-479)"),
+        ("dequant_q4_0", lambda: K.dequant_q4_0(q4, n, out=f), q4.numel() + 4 * n,
+         "Q4_0 blocks {f16 d; u8 q[16]} (gguf.rs:480-502)"),
+        ("dequant_layer", lambda: L.ah_dequant_layer(C.c_void_p(sc.data_ptr()), C.c_void_p(pk.data_ptr()),
+                                                     C.c_void_p(f.data_ptr()), n, 32, st),
+         pk.numel() + 4 * sc.numel() + 4 * n, "engine format, f32 group-32 scales (quantization.rs:439-454)"),
+        ("f16_to_f32", lambda: L.ah_f16_to_f32(C.c_void_p(h.data_ptr()), C.c_void_p(f.data_ptr()), n, st),
+         2 * n + 4 * n, "f16 bits N(0,1) seed 1 (gguf.rs:93-120)"),
+    )
+    for name, fn, nbytes, what in rows:
+        s = _gpu_seconds(fn, stream)
         gbs = nbytes / s / 1e9
         out[name] = {"gbs": round(gbs, 2), "pct_of_8tbs": round(100 * gbs / NOMINAL_HBM_GBS, 2),
                      "frac_of_measured_peak": round(gbs / peak, 4), "bytes_per_call": nbytes,
-                     "us_per_call": round(s * 1e6, 2), "shape": "4096x11008"}
-    del q8, f, h
+                     "us_per_call": round(s * 1e6, 2), "shape": "4096x11008", "input": what}
+    if not no_cpu:
+        from oracle import oracle as O
+        OL = O.lib()
+        q8h, q4h, sch, pkh, hh = (t.cpu().numpy() for t in (q8, q4, sc, pk, h))
+        # the AVX-512 restatement keeps the reference's read of 4 halves past the
+        # end (avx512_kernel.rs:147): give it a padded copy
+        hu8 = np.zeros(2 * n + 64, np.uint8)
+        hu8[: 2 * n] = hh.view(np.uint8)
+        dst = np.empty(n, np.float32)
+        cpu = {
+            "dequant_q8_0": [("scalar gguf.rs:459-479 restated", 1,
+                              lambda: OL.or_dequantize_to_f32(q8h, q8h.size, 8, n, dst))],
+            "dequant_q4_0": [("scalar gguf.rs:480-502 restated", 1,
+                              lambda: OL.or_dequantize_to_f32(q4h, q4h.size, 2, n, dst))],
+            "dequant_layer": [("dequant_layer_avx512 as-is (quantization.rs:456-530)", 1,
+                               lambda: OL.or_avx_dequant_layer(sch, pkh, dst, n)),
+                              ("scalar branch quantization.rs:444-452", 1,
+                               lambda: OL.or_dequant_layer(sch, pkh, dst, n, 32))],
+            "f16_to_f32": [("f16_bytes_to_f32 AVX-512 as-is (avx512_kernel.rs:212-232)", 1,
+                            lambda: OL.or_avx_f16_bytes_to_f32(hu8, 2 * n, dst)),
+                           ("scalar gguf::f16_to_f32 per element (gguf.rs:93-120)", 1,
+                            lambda: OL.or_f16_array_to_f32(hh.view(np.uint16), dst, n))],
+        }
+        for name, legs in cpu.items():
+            nbytes = out[name]["bytes_per_call"]
+            res = []
+            for what, cores, fn in legs:
+                sec = _cpu_seconds(fn)
+                res.append({"value": round(nbytes / sec / 1e9, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                            "sample": f"the whole 4096x11008 call, {what}, {sec * 1e3:.1f} ms per call"})
+            out[name]["cpu_baseline"] = res[0]
+            if len(res) > 1:
+                out[name]["cpu_baseline_alt"] = res[1]
+    del q8, q4, sc, pk, f, h
     out["dedup_load"] = dedup_load(K, dev, stream, peak, cpu=not no_cpu)
     out["ssm_step"] = ssm_step(dev, stream, peak, cpu=not no_cpu)
     return out

@@ -111,6 +111,44 @@ def test_8b_width_two_layers(cuda, oracle):
     m.close()
 
 
+def test_8b_full_depth(cuda, oracle):
+    # The full 8B decode configuration (32 layers, d 4096, FFN 14336, 32/8
+    # heads x 128, vocab 128256, theta 5e5, weights seed 6): a 4-token prompt
+    # with the logits of every step against the oracle, then 4 greedy tokens
+    # through the graph-replayed generate path against the oracle's greedy
+    # continuation (errors that grow with depth, or a layer-indexing slip past
+    # the first layers, would show here).
+    from agent_harness_b200.model import LLAMA_8B, Model, ModelConfig
+    cfg = ModelConfig(**{**LLAMA_8B.__dict__, "max_seq": 16, "max_batch": 1})
+    m = Model(cfg)
+    m.init_random(6)
+    W = oracle_weights(cfg, 6, cuda)
+    o = oracle_model(oracle, cfg, W)
+    prompt = np.array([[128000, 17, 40000, 91234]], np.int32)
+    m.reset(1)
+    worst = 0.0
+    for t in range(prompt.shape[1]):
+        lg = m.forward(prompt[:, t]).cpu().numpy()[0]
+        ref = o.forward(int(prompt[0, t]), t)
+        err = relerr(lg, ref)
+        worst = max(worst, err)
+        assert err <= TOL, (t, err)
+        assert int(np.argmax(lg)) == oracle.argmax(ref), t
+    new = m.generate(prompt, 4)[:, 0].tolist()
+    toks, pos = [], prompt.shape[1]
+    for _ in range(4):
+        top2 = np.sort(ref)[-2:]
+        if top2[1] - top2[0] < 1e-3 * np.max(np.abs(ref)):
+            break  # a near tie: the tokens may legitimately differ from here on
+        nxt = oracle.argmax(ref)
+        toks.append(nxt)
+        ref = o.forward(nxt, pos)
+        pos += 1
+    assert len(toks) >= 1 and new[: len(toks)] == toks, (new, toks)
+    m.close()
+    print(f"8B full depth: worst logits error {worst:.2e}, tokens {new}")
+
+
 @pytest.mark.parametrize("shape", ["hd64_g2_batch2", "hd128_g8"])
 def test_long_context_attention_splits(cuda, oracle, shape):
     # Contexts long enough for the attention to split the cached positions over
