@@ -104,6 +104,7 @@ SIGNATURES = {
     "ah_model_forward": (i32, [vp, vp, vp, vp]),
     "ah_model_decode": (i32, [vp, i32, vp, vp]),
     "ah_model_position": (i32, [vp, C.POINTER(i32)]),
+    "ah_model_set_prefill": (i32, [vp, i32]),
     "ah_host_gemv_4bit_into": (i32, [vp, vp, vp, vp, sz, sz, sz]),
     "ah_host_dequant_layer": (i32, [vp, vp, vp, sz, sz]),
     "ah_host_quantize": (i32, [vp, sz, sz, vp, vp]),

@@ -32,6 +32,7 @@
 #include <nccl.h>
 
 #include "ah_gemv_impl.cuh"
+#include "ah_prefill.cuh"
 #include "ah_tma.cuh"
 
 using namespace ah;
@@ -842,6 +843,12 @@ __global__ void k_advance(int* pos, int* tok, const int* prompt, int n_prompt, i
   if (threadIdx.x == 0) *pos = p;
 }
 
+// After a prefill of positions 0 .. p-1: position p next, with prompt token p.
+__global__ void k_prefill_state(int* pos, int* tok, const int* prompt, int n_prompt, int p, int batch) {
+  if (threadIdx.x < batch) tok[threadIdx.x] = prompt[threadIdx.x * n_prompt + p];
+  if (threadIdx.x == 0) *pos = p;
+}
+
 __global__ void k_rope_table(float2* t, int max_seq, int half, float base) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= max_seq * half) return;
@@ -905,6 +912,12 @@ struct AhModel {
   const int* g_prompt[2] = {nullptr, nullptr};
   int g_nprompt[2] = {0, 0};
   std::vector<void*> allocs;
+  // prompt prefill through the GEMMs (allocated on first use for kPrefillRows rows)
+  int pf_mode = 1;  // 0: token by token, as the reference; 1: GEMM prefill from kPrefillMinTokens
+  float *pf_h = nullptr, *pf_x = nullptr, *pf_qkv = nullptr, *pf_attn = nullptr, *pf_part = nullptr;
+  float *pf_gu = nullptr, *pf_act = nullptr;
+  void* pf_ws = nullptr;
+  size_t pf_ws_bytes = 0;
 };
 
 namespace {
@@ -1086,6 +1099,82 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     }
   }
   AH_TRY(launch_pdl(k_advance, dim3(1), dim3(32), 0, st, m->d_pos, m->d_tok, prompt, n_prompt, B));
+  return AH_OK;
+}
+
+// ---- prompt prefill through the GEMMs ---------------------------------------------
+// The decoder's only state between steps is the KV cache and the position, so
+// the prefill writes the cache for prompt positions 0 .. P-1 of every sequence
+// and leaves the position at P with prompt token P next: exactly the state the
+// token-by-token prefill (inference/mod.rs:550) leaves.  Positions go in chunks
+// of up to kPrefillRows rows (sequences x positions); per chunk and layer the
+// projections run as tcgen05 GEMMs and the row kernels of ah_prefill.cu do
+// norms, RoPE + KV append, causal attention, SwiGLU and residual adds.  The
+// last layer stops after its KV append (its outputs feed nothing cached).
+constexpr int kPrefillRows = 2048;
+constexpr int kPrefillMinTokens = 8;
+
+int prefill_buffers(AhModel* m) {
+  if (m->pf_h) return AH_OK;
+  const AhModelConfig& c = m->c;
+  const size_t R = kPrefillRows, d = c.n_embd;
+  int rc = AH_OK;
+  auto A = [&](void** p, size_t bytes) {
+    if (rc == AH_OK) rc = dalloc(m, p, bytes);
+  };
+  A((void**)&m->pf_h, R * d * 4);
+  A((void**)&m->pf_x, R * d * 4);
+  A((void**)&m->pf_qkv, R * (size_t)(m->dq + 2 * m->dkv) * 4);
+  A((void**)&m->pf_attn, R * (size_t)m->dq * 4);
+  A((void**)&m->pf_part, R * d * 4);
+  A((void**)&m->pf_gu, R * (size_t)2 * m->nff * 4);
+  A((void**)&m->pf_act, R * (size_t)m->nff * 4);
+  size_t ws = 0;
+  for (const AhQ4Weight* w : {m->wqkv[0], m->wo[0], m->wgu[0], m->wd[0]})
+    ws = std::max(ws, gemm_workspace_bytes(q4w_tiled(w), (int64_t)R));
+  A(&m->pf_ws, ws + 1024);
+  m->pf_ws_bytes = ws;
+  return rc;
+}
+
+int prefill_gemm(AhModel* m, const int* prompt, int n_prompt, int P, cudaStream_t st) {
+  const AhModelConfig& c = m->c;
+  const int B = m->batch, d = c.n_embd, L = c.n_layer, hd = c.head_dim;
+  const int ldq = m->dq + 2 * m->dkv;
+  AH_TRY(prefill_buffers(m));
+  void* ws = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(m->pf_ws) + 1023) & ~uintptr_t(1023));
+  const int C = std::max(1, kPrefillRows / B);
+  const float scale = 1.0f / sqrtf((float)hd);  // mod.rs:478
+  for (int p0 = 0; p0 < P; p0 += C) {
+    const PrefillRows pr{B, std::min(C, P - p0), p0, n_prompt};
+    const int64_t rows = (int64_t)B * pr.cnt;
+    AH_TRY(prefill_embed(m->tok_embd, prompt, pr, d, c.vocab_size, m->pf_h, st));
+    for (int l = 0; l < L; ++l) {
+      AH_TRY(prefill_rmsnorm(m->pf_h, m->attn_norm + (size_t)l * d, c.rms_eps, rows, d, m->pf_x, st));
+      AH_TRY(gemm_run(q4w_tiled(m->wqkv[l]), m->pf_x, d, rows, m->pf_qkv, ldq, ws, m->pf_ws_bytes, st));
+      AH_TRY(prefill_rope_append(m->pf_qkv, ldq, m->rope, m->kc, m->vc, l, L, m->nh, m->nkv, hd, c.max_seq, pr, st));
+      if (l + 1 == L) break;
+      AH_TRY(prefill_attention(m->pf_qkv, ldq, m->kc, m->vc, l, L, m->nh, m->nkv, hd, c.max_seq, scale, pr,
+                               m->pf_attn, m->dq, st));
+      AH_TRY(gemm_run(q4w_tiled(m->wo[l]), m->pf_attn, m->dq, rows, m->pf_part, d, ws, m->pf_ws_bytes, st));
+      if (m->tp_world > 1 &&
+          ncclAllReduce(m->pf_part, m->pf_part, (size_t)rows * d, ncclFloat, ncclSum, m->comm, st) != ncclSuccess)
+        return fail(AH_ENCCL, "prefill: all-reduce of the attention block output failed");
+      AH_TRY(prefill_add(m->pf_h, m->pf_part, rows * d, st));
+      AH_TRY(prefill_rmsnorm(m->pf_h, m->ffn_norm + (size_t)l * d, c.rms_eps, rows, d, m->pf_x, st));
+      AH_TRY(gemm_run(q4w_tiled(m->wgu[l]), m->pf_x, d, rows, m->pf_gu, 2 * (int64_t)m->nff, ws, m->pf_ws_bytes,
+                      st));
+      AH_TRY(prefill_swiglu(m->pf_gu, rows, m->nff, m->pf_act, st));
+      AH_TRY(gemm_run(q4w_tiled(m->wd[l]), m->pf_act, m->nff, rows, m->pf_part, d, ws, m->pf_ws_bytes, st));
+      if (m->tp_world > 1 &&
+          ncclAllReduce(m->pf_part, m->pf_part, (size_t)rows * d, ncclFloat, ncclSum, m->comm, st) != ncclSuccess)
+        return fail(AH_ENCCL, "prefill: all-reduce of the MLP block output failed");
+      AH_TRY(prefill_add(m->pf_h, m->pf_part, rows * d, st));
+    }
+  }
+  k_prefill_state<<<1, 32, 0, st>>>(m->d_pos, m->d_tok, prompt, n_prompt, P, B);
+  AH_LAUNCH_CHECK();
+  m->pos = P;
   return AH_OK;
 }
 
@@ -1637,6 +1726,12 @@ int ah_model_reset(AhModel* m, int batch, void* stream) {
   return AH_OK;
 }
 
+int ah_model_set_prefill(AhModel* m, int mode) {
+  AH_REQUIRE(m && (mode == 0 || mode == 1), "model_set_prefill: mode must be 0 or 1");
+  m->pf_mode = mode;
+  return AH_OK;
+}
+
 int ah_model_position(const AhModel* m, int* pos) {
   AH_REQUIRE(m && pos, "model_position: null argument");
   *pos = m->pos;
@@ -1689,8 +1784,14 @@ int ah_model_generate(AhModel* m, const int32_t* prompt, int batch, int n_prompt
   for (int b = 0; b < batch; ++b) first[b] = prompt[(size_t)b * n_prompt];
   AH_CUDA_TRY(cudaMemcpyAsync(m->d_tok, first.data(), (size_t)batch * 4, cudaMemcpyHostToDevice, st));
   AH_CUDA_TRY(cudaStreamSynchronize(st));
-  for (int p = 0; p + 1 < n_prompt; ++p) AH_TRY(run_step_graph(m, 0, m->d_prompt, n_prompt, st));
-  if (n_new == 0) return AH_OK;
+  if (m->pf_mode == 1 && n_prompt - 1 >= kPrefillMinTokens)
+    AH_TRY(prefill_gemm(m, m->d_prompt, n_prompt, n_prompt - 1, st));  // positions 0 .. n_prompt-2
+  else
+    for (int p = 0; p + 1 < n_prompt; ++p) AH_TRY(run_step_graph(m, 0, m->d_prompt, n_prompt, st));
+  if (n_new == 0) {
+    AH_CUDA_TRY(cudaStreamSynchronize(st));
+    return AH_OK;
+  }
   AH_TRY(run_step_graph(m, 1, nullptr, 0, st));  // last prompt token: logits -> first new token
   for (int i = 1; i < n_new; ++i) AH_TRY(run_step_graph(m, 1, nullptr, 0, st));
   if (out)

@@ -28,6 +28,12 @@ int gemv_launch(GemvArgs a, int prologue, int epilogue, cudaStream_t st, bool pd
 // prologue, epilogue) without launching, so a later launch can be captured.
 int gemv_prepare(const Q4Tiled& w, int batch, int prologue, int epilogue);
 
+// The tcgen05 GEMM c[m][ldc] = a[m][lda] . W^T (ah_gemm_tc.cu) and the
+// workspace it needs for m rows (1024-byte aligned).
+size_t gemm_workspace_bytes(const Q4Tiled& w, int64_t m);
+int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c, int64_t ldc, void* ws,
+             size_t ws_bytes, cudaStream_t st);
+
 const Q4Tiled& q4w_tiled(const AhQ4Weight* w);
 // An uninitialised tiled weight of the given shape (f32 scales when `engine`);
 // its planes are filled by the caller's kernel.

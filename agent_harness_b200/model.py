@@ -154,6 +154,11 @@ class Model:
              out.ctypes.data_as(C.c_void_p), self._stream())
         return out
 
+    def set_prefill(self, mode: int):
+        """1 (default): long prompts through the prefill GEMMs; 0: one forward()
+        per prompt token, as the reference (inference/mod.rs:550)."""
+        call("ah_model_set_prefill", self._h, mode)
+
     @property
     def position(self) -> int:
         v = C.c_int(0)

@@ -385,6 +385,7 @@ def run_gpu(args):
 
 DECODE_PROMPT, DECODE_NEW = 2048, 256
 DECODE_BYTES_PER_TOKEN_WEIGHTS = 4221370368  # all Q4_0 projections + LM head of the 8B shape
+DECODE_PROJ_WEIGHTS = 32 * (4096 * 6144 + 4096 * 4096 + 3 * 14336 * 4096)  # per token, without the LM head
 
 
 TP_PROMPT, TP_NEW, TP_BATCH = 2048, 128, 16
@@ -446,7 +447,7 @@ def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_B
         m.enable_peer_allreduce(allgather)
     prompt = np.random.default_rng(9).integers(0, cfg.vocab_size, (batch, n_prompt)).astype(np.int32)
     t0 = time.perf_counter()
-    m.generate(prompt, 1)  # token-by-token prefill (inference/mod.rs:550) + first token
+    m.generate(prompt, 1)  # prompt through the prefill GEMMs + first token
     prefill_s = time.perf_counter() - t0
     st = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -486,7 +487,8 @@ def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_B
             "batch": batch, "n_prompt": n_prompt, "n_new": n_new, "tp": world,
             "block_allreduce": (allreduce if world > 1 else "none"),
             "weight_gbs_per_gpu": round(DECODE70_WEIGHT_BYTES / world / per_step / 1e9, 1),
-            "prefill_tokens_per_s_token_by_token": round(batch * (n_prompt - 1) / prefill_s, 1),
+            "prefill_tokens_per_s": round(batch * (n_prompt - 1) / prefill_s, 1),
+            "prefill_s": round(prefill_s, 2),
             "first_tokens_seq0_3": first, **split,
             "note": "tensor parallel over the job's ranks: row/column-sharded projections, one all-reduce per "
                     "attention/MLP block (peer: GEMV epilogue stores into every rank's slots over NVLink + flag; "
@@ -504,8 +506,10 @@ def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW):
     m = Model(cfg, device=dev)
     m.init_random(6, w_std=0.02, emb_std=1.0, norm_std=0.02)
     prompt = np.random.default_rng(7).integers(0, cfg.vocab_size, (1, n_prompt)).astype(np.int32)
+    first = m.generate(prompt[:, :64], 1)  # warm-up: buffers, graphs
+    torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
-    first = m.generate(prompt, 1)  # token-by-token prefill (inference/mod.rs:550) + first token
+    first = m.generate(prompt, 1)  # prompt through the prefill GEMMs + first token
     prefill_s = time.perf_counter() - t0
     st = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -515,13 +519,28 @@ def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW):
     torch.cuda.synchronize(dev)
     ms = e0.elapsed_time(e1)
     tk = toks.cpu().numpy().ravel()
-    # replay check: the same prompt decodes to the same tokens
-    again = m.generate(prompt[:, :64], 8)
-    again2 = m.generate(prompt[:, :64], 8)
+    # replay check: the same prompt decodes to the same tokens; and the GEMM
+    # prefill agrees with the reference's token-by-token prefill on a prefix
+    again = m.generate(prompt[:, :256], 8)
+    again2 = m.generate(prompt[:, :256], 8)
+    m.set_prefill(0)
+    t1 = time.perf_counter()
+    tokwise = m.generate(prompt[:, :256], 8)
+    tok_s = time.perf_counter() - t1
+    m.set_prefill(1)
     m.close()
     per_tok = ms / 1e3 / n_new
+    gemm_flop = 2.0 * (n_prompt - 1) * DECODE_PROJ_WEIGHTS
+    peak_tf, _ = tensor_peak()
     return {"tokens_per_s": round(n_new / (ms / 1e3), 2), "ms_per_token": round(per_tok * 1e3, 4),
-            "prefill_tokens_per_s_token_by_token": round((n_prompt - 1) / prefill_s, 1),
+            "prefill_tokens_per_s": round((n_prompt - 1) / prefill_s, 1),
+            "prefill": {"path": "tcgen05 GEMM prefill (projections) + causal attention over the f16 KV cache, "
+                                "chunks of 2048 rows; wall clock incl. the first decode step",
+                        "ms": round(prefill_s * 1e3, 2),
+                        "projection_tflops": round(gemm_flop / prefill_s / 1e12, 1),
+                        "projection_frac_of_peak": round(gemm_flop / prefill_s / 1e12 / peak_tf, 4),
+                        "token_by_token_tokens_per_s": round(255 / tok_s, 1),
+                        "agrees_with_token_by_token": bool(np.array_equal(tokwise, again))},
             "weight_gbs": round(DECODE_BYTES_PER_TOKEN_WEIGHTS / per_tok / 1e9, 1),
             "n_prompt": n_prompt, "n_new": n_new, "first_tokens": [int(first[0, 0])] + [int(v) for v in tk[1:6]],
             "deterministic": bool(np.array_equal(again, again2)),

@@ -321,11 +321,20 @@ AH_API int ah_model_init_random(AhModel* m, uint64_t seed, float w_std, float em
 AH_API uint64_t ah_model_tensor_seed(uint64_t seed, int kind, int layer);
 /* Reference: inference/mod.rs:547-562 generate with temperature 0 (greedy,
  * sampling.rs:4-14 argmax), for `batch` sequences in lock step.  `prompt` is
- * [batch][n_prompt] host int32; prefill runs forward() token by token as the
- * reference does (mod.rs:550), then `n_new` greedy steps write their tokens to
+ * [batch][n_prompt] host int32; the prompt is consumed as ah_model_set_prefill
+ * selects (GEMM prefill by default, or forward() token by token as the
+ * reference does, mod.rs:550), then `n_new` greedy steps write their tokens to
  * `out_tokens` [n_new][batch] (host).  Resets the KV cache. */
 AH_API int ah_model_generate(AhModel* m, const int32_t* prompt, int batch, int n_prompt, int n_new,
                              int32_t* out_tokens, void* stream);
+/* How ah_model_generate consumes the prompt (no reference counterpart: the
+ * reference always runs one forward() per prompt token, inference/mod.rs:550).
+ * mode 1 (default): prompts of 9 tokens or more go through the prefill GEMMs
+ * (tcgen05) in chunks of up to 2048 rows (sequences x positions) with a causal
+ * attention over the f16 KV cache, and the last prompt token through the
+ * decode step; mode 0: token by token, as the reference.  Both leave the same
+ * state (KV cache, position) up to rounding. */
+AH_API int ah_model_set_prefill(AhModel* m, int mode);
 /* Lower-level stepping (same semantics): reset, feed one token per sequence
  * (forward(), inference/mod.rs:333-545) and read the logits [batch][vocab]. */
 AH_API int ah_model_reset(AhModel* m, int batch, void* stream);
