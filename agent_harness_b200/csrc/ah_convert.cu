@@ -204,18 +204,50 @@ struct HalfFmt {
   }
 };
 
+// The engine's SoA format (quantization.rs:365-404, group 32): "blocks" of
+// 16 nibble bytes, with the group's f32 scale in a second array staged beside
+// them (kAuxBytes per block).
+struct EngineFmt {
+  static constexpr int kBlockBytes = 16;
+  static constexpr int kAuxBytes = 4;
+  static constexpr int kTileBlocks = 256;  // 4 KB nibbles + 1 KB scales in, 32 KB out
+  static __device__ __forceinline__ float4 unpack(const uint8_t* tile, const uint8_t* aux, int f) {
+    const float s = reinterpret_cast<const float*>(aux)[f >> 3];
+    const uint32_t b = *reinterpret_cast<const uint16_t*>(tile + (f >> 3) * 16 + (f & 7) * 2);
+    float4 v;  // element 2i in the low nibble of byte i (quantization.rs:444-452)
+    v.x = x86_mul(s, (float)(int)(b & 0xFu) - 8.0f);
+    v.y = x86_mul(s, (float)(int)((b >> 4) & 0xFu) - 8.0f);
+    v.z = x86_mul(s, (float)(int)((b >> 8) & 0xFu) - 8.0f);
+    v.w = x86_mul(s, (float)(int)((b >> 12) & 0xFu) - 8.0f);
+    return v;
+  }
+};
+
+template <class F, class = void>
+struct AuxOf {
+  static constexpr int kBytes = 0;
+};
+template <class F>
+struct AuxOf<F, decltype((void)F::kAuxBytes)> {
+  static constexpr int kBytes = F::kAuxBytes;
+};
+
 // Persistent CTAs walk whole tiles t = blockIdx.x + k*gridDim.x.  Thread 0
 // keeps kStages bulk copies in flight; every thread unpacks the tile in shared
 // memory and streams its float4s out.
 template <class F>
 __global__ void __launch_bounds__(kThreads) k_dequant_blocks_tma(const uint8_t* __restrict__ blocks,
                                                                  float* __restrict__ out, int64_t n_tiles,
-                                                                 int* __restrict__ err) {
+                                                                 int* __restrict__ err,
+                                                                 const void* __restrict__ aux_src = nullptr) {
   constexpr int kTileBytes = F::kTileBlocks * F::kBlockBytes;
+  constexpr int kAuxTile = F::kTileBlocks * AuxOf<F>::kBytes;  // second source per tile (0: none)
   constexpr int kF4PerTile = F::kTileBlocks * 8;
-  static_assert(kTileBytes % 16 == 0, "bulk copies move 16-byte multiples");
+  static_assert(kTileBytes % 16 == 0 && kAuxTile % 16 == 0, "bulk copies move 16-byte multiples");
   __shared__ __align__(128) uint8_t buf[kStages][kTileBytes];
+  __shared__ __align__(128) uint8_t aux[kStages][kAuxTile > 0 ? kAuxTile : 16];
   __shared__ __align__(8) uint64_t full[kStages];
+  const uint8_t* auxg = static_cast<const uint8_t*>(aux_src);
   const int tid = threadIdx.x;
   const int64_t my_tiles =
       n_tiles > (int64_t)blockIdx.x ? (n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
@@ -228,8 +260,9 @@ __global__ void __launch_bounds__(kThreads) k_dequant_blocks_tma(const uint8_t* 
   if (tid == 0) {
     for (; issued < kStages && issued < my_tiles; ++issued) {
       const int64_t t = blockIdx.x + issued * gridDim.x;
-      mbar_arrive_expect_tx(&full[issued], kTileBytes);
+      mbar_arrive_expect_tx(&full[issued], kTileBytes + kAuxTile);
       bulk_g2s(buf[issued], blocks + t * kTileBytes, kTileBytes, &full[issued]);
+      if (kAuxTile > 0) bulk_g2s(aux[issued], auxg + t * kAuxTile, kAuxTile, &full[issued]);
     }
   }
   int64_t k = 0;
@@ -243,14 +276,18 @@ __global__ void __launch_bounds__(kThreads) k_dequant_blocks_tma(const uint8_t* 
 #pragma unroll
     for (int j = 0; j < kF4PerTile / kThreads; ++j) {
       const int f = tid + j * kThreads;
-      st_cs_f4(o + f, F::unpack(buf[s], f));
+      if constexpr (kAuxTile > 0)
+        st_cs_f4(o + f, F::unpack(buf[s], aux[s], f));
+      else
+        st_cs_f4(o + f, F::unpack(buf[s], f));
     }
     __syncthreads();  // stage s fully consumed
     if (tid == 0 && issued < my_tiles) {
       const int64_t tn = blockIdx.x + issued * gridDim.x;
       fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&full[s], kTileBytes);
+      mbar_arrive_expect_tx(&full[s], kTileBytes + kAuxTile);
       bulk_g2s(buf[s], blocks + tn * kTileBytes, kTileBytes, &full[s]);
+      if (kAuxTile > 0) bulk_g2s(aux[s], auxg + tn * kAuxTile, kAuxTile, &full[s]);
       ++issued;
     }
   }
@@ -410,14 +447,27 @@ int ah_dequant_layer(const float* scales, const uint8_t* packed, float* out, int
   AH_REQUIRE(scales && packed && out && n > 0 && gs > 0, "dequant_layer: bad arguments");
   cudaStream_t st = as_stream(stream);
   int64_t done = 0;
-  if (gs == 32 && (reinterpret_cast<uintptr_t>(packed) & 3u) == 0 && aligned16(out)) {
-    const int64_t n8 = n / 8;
+  if (gs == 32 && aligned16(packed) && aligned16(scales) && aligned16(out) &&
+      n >= (int64_t)EngineFmt::kTileBlocks * 32) {
+    // whole tiles through the bulk-copy ring (nibbles and scales on one mbarrier)
+    const int64_t n_tiles = n / ((int64_t)EngineFmt::kTileBlocks * 32);
+    int64_t g = (int64_t)sm_count() * 4;
+    if (g > n_tiles) g = n_tiles;
+    int* err = device_error_word();
+    AH_REQUIRE(err != nullptr, "dequant_layer: device error word unavailable");
+    k_dequant_blocks_tma<EngineFmt><<<(int)g, kThreads, 0, st>>>(packed, out, n_tiles, err, scales);
+    AH_LAUNCH_CHECK();
+    done = n_tiles * EngineFmt::kTileBlocks * 32;
+  }
+  if (done < n && gs == 32 && (reinterpret_cast<uintptr_t>(packed) & 3u) == 0 && aligned16(out)) {
+    const int64_t n8 = (n - done) / 8;  // done is a multiple of 32: groups stay whole
     if (n8 > 0) {
-      k_dequant_engine_gs32<<<grid_for(n8), kThreads, 0, st>>>(scales, reinterpret_cast<const uint32_t*>(packed),
-                                                               reinterpret_cast<float4*>(out), n8);
+      k_dequant_engine_gs32<<<grid_for(n8), kThreads, 0, st>>>(scales + done / 32,
+                                                               reinterpret_cast<const uint32_t*>(packed + done / 2),
+                                                               reinterpret_cast<float4*>(out + done), n8);
       AH_LAUNCH_CHECK();
     }
-    done = n8 * 8;
+    done += n8 * 8;
   }
   if (done < n) {
     k_dequant_engine_any<<<grid_for(n - done), kThreads, 0, st>>>(scales, packed, out, done, n, gs);

@@ -484,8 +484,9 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4(co
 
   // Weights do not depend on the previous kernel: start streaming them now
   // (two batches of kGemvU pairs in flight per lane).
-  const int64_t p0 = (int64_t)crank * ppc;
-  const int np = (int)max((int64_t)0, min(p0 + ppc, KP) - p0);
+  const int64_t PE = a.pair_end > 0 ? a.pair_end : KP;  // this launch's K window [pair_begin, PE)
+  const int64_t p0 = a.pair_begin + (int64_t)crank * ppc;
+  const int np = (int)max((int64_t)0, min(p0 + ppc, PE) - p0);
   const uint4* nibp = a.w.nib + (rt * KP + p0) * 32 + lane;
   const SV* sclp = reinterpret_cast<const SV*>(a.w.scales) + (rt * KP + p0) * 8 + g;
   const int64_t tile_nib = KP * 32 * kGemvWarps * n_cl;  // uint4 stride to the next row group of this CTA
@@ -503,7 +504,8 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4(co
 
   const int64_t K = a.w.cols;
   rms_stats<BM, PRO>(a, wred, tok_inv, tid, lane, warp);
-  split_x<PRO>(a, xs, blk_info, plane, kbc, p0 * 64, min(p0 * 64 + (int64_t)ppc * 64, K), tok_inv, tid, warp);
+  split_x<PRO>(a, xs, blk_info, plane, kbc, p0 * 64, min(min(p0 * 64 + (int64_t)ppc * 64, PE * 64), K), tok_inv, tid,
+               warp);
   __syncthreads();
 
   // ---- row groups: main loop (local), DSMEM reduction, epilogue ------------------
@@ -794,11 +796,12 @@ GemvKernel pick_kernel(bool f32s, int pro, int epi) {
 
 }  // namespace
 
-GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
+GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode, int64_t kp_window) {
   GemvPlan p{};
   p.nt = (batch + 3) / 4;
   p.rows_mode = rows_mode;
-  p.pairs_per_chunk = (w.kp + kGemvCluster - 1) / kGemvCluster;  // one K-chunk per warp (rows) or cluster CTA
+  const int64_t kp = kp_window > 0 ? kp_window : w.kp;
+  p.pairs_per_chunk = (kp + kGemvCluster - 1) / kGemvCluster;  // one K-chunk per warp (rows) or cluster CTA
   p.ksplit = 1;
   const int64_t kbc = rows_mode ? 2 * w.kp : 2 * p.pairs_per_chunk;
   const int64_t plane = kbc * 64 + 64;
@@ -822,7 +825,7 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode) {
   return p;
 }
 
-GemvPlan gemv_plan(const Q4Tiled& w, int batch) { return gemv_plan(w, batch, false); }
+GemvPlan gemv_plan(const Q4Tiled& w, int batch) { return gemv_plan(w, batch, false, 0); }
 
 namespace {
 GemvKernel select_kernel(const GemvPlan& plan, bool f32s, int pro, int epi) {
@@ -896,8 +899,9 @@ int kernel_setup(GemvKernel kern, const GemvPlan& plan, int* capacity) {
 // for many-tile GEMVs whose full-K split of x fits comfortably in shared
 // memory beside at least two tile stages (it is then amortised over several
 // tiles per CTA).
-int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, GemvKernel* kern, int* cap) {
-  GemvPlan pc = gemv_plan(w, batch, false);
+int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, GemvKernel* kern, int* cap,
+                int64_t kp_window = 0) {
+  GemvPlan pc = gemv_plan(w, batch, false, kp_window);
   if (pc.smem > (size_t)kGemvSmemLimit)
     return fail(AH_EUNSUPPORTED, "gemv: batch %d x %lld columns needs %zu B of shared memory per CTA (limit %d)",
                 batch, (long long)w.cols, pc.smem, kGemvSmemLimit);
@@ -907,7 +911,7 @@ int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, G
   AH_TRY_GEMV(kernel_setup(kc, pc, &ccap));
   const int64_t n_rg = (w.r16 + kGemvWarps - 1) / kGemvWarps;
   GemvPlan pr = gemv_plan(w, batch, true);
-  if (n_rg > ccap && pr.smem_base <= (size_t)kGemvRowsSmem && pr.n_stages >= 2 && aligned16(w.nib) &&
+  if (kp_window == 0 && n_rg > ccap && pr.smem_base <= (size_t)kGemvRowsSmem && pr.n_stages >= 2 && aligned16(w.nib) &&
       aligned16(w.scales)) {
     GemvKernel kr = select_kernel(pr, w.f32_scales, pro, epi);
     int rcap = 0;
@@ -938,6 +942,21 @@ int max_sub_batch(const Q4Tiled& w, int batch) {
 int gemv_launch_one(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl);
 }  // namespace
 
+namespace {
+// K windows for a batch whose split of x does not fit one CTA: the fewest
+// windows (each launch then covers kp_window block pairs) whose plan fits, or 0.
+// Only for epilogues that can accumulate (store, then residual adds) into a
+// local y; SwiGLU and the peer scatter need the whole sum and take token slices.
+int64_t k_window(const Q4Tiled& w, int batch, int epi, int n_peer) {
+  if (epi == kEpiSwiglu || n_peer > 0) return 0;
+  for (int64_t nw = 2; nw <= 16; ++nw) {
+    const int64_t win = (w.kp + nw - 1) / nw;
+    if (gemv_plan(w, batch, false, win).smem <= (size_t)kGemvSmemLimit) return win;
+  }
+  return 0;
+}
+}  // namespace
+
 int gemv_prepare(const Q4Tiled& w, int batch, int pro, int epi) {
   AH_REQUIRE(batch >= 1 && batch <= kGemvMaxBatch, "gemv: batch must be 1..16");
   const int sb = max_sub_batch(w, batch);
@@ -945,6 +964,15 @@ int gemv_prepare(const Q4Tiled& w, int batch, int pro, int epi) {
   GemvPlan plan;
   GemvKernel kern;
   int cap;
+  if (sb < batch) {
+    // the peer scatter never combines with windows; the decoder's o / down
+    // GEMVs under tensor parallelism take token slices, prepared below
+    const int64_t win = k_window(w, batch, epi, 0);
+    if (win > 0) {
+      AH_TRY_GEMV(choose_plan(w, batch, pro, epi, &plan, &kern, &cap, win));
+      AH_TRY_GEMV(choose_plan(w, batch, pro, kEpiAdd, &plan, &kern, &cap, win));
+    }
+  }
   AH_TRY_GEMV(choose_plan(w, sb, pro, epi, &plan, &kern, &cap));
   if (batch % sb) AH_TRY_GEMV(choose_plan(w, batch % sb, pro, epi, &plan, &kern, &cap));
   return AH_OK;
@@ -955,6 +983,20 @@ int gemv_launch(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   const int sb = max_sub_batch(a.w, a.batch);
   AH_REQUIRE(sb >= 1, "gemv: %lld columns do not fit one CTA even for one token", (long long)a.w.cols);
   if (sb == a.batch) return gemv_launch_one(a, pro, epi, st, pdl);
+  const int64_t win = k_window(a.w, a.batch, epi, a.n_peer);
+  if (win > 0) {
+    // K windows: every weight byte is read once; the first window stores (or
+    // adds, for a residual epilogue) and the later ones add into y; the last
+    // writes the sums of squares of the final values
+    for (int64_t pb = 0, i = 0; pb < a.w.kp; pb += win, ++i) {
+      GemvArgs s = a;
+      s.pair_begin = pb;
+      s.pair_end = std::min(pb + win, a.w.kp);
+      if (s.pair_end < a.w.kp) s.ss_out = nullptr;
+      AH_TRY_GEMV(gemv_launch_one(s, pro, i == 0 ? epi : kEpiAdd, st, pdl));
+    }
+    return AH_OK;
+  }
   // token slices: every per-token operand moves by the slice start
   for (int b0 = 0; b0 < a.batch; b0 += sb) {
     GemvArgs s = a;
@@ -979,7 +1021,8 @@ int gemv_launch_one(GemvArgs a, int pro, int epi, cudaStream_t st, bool pdl) {
   GemvPlan plan;
   GemvKernel kern;
   int cap = 0;
-  AH_TRY_GEMV(choose_plan(a.w, a.batch, pro, epi, &plan, &kern, &cap));
+  const int64_t kp_window = a.pair_end > 0 ? a.pair_end - a.pair_begin : 0;
+  AH_TRY_GEMV(choose_plan(a.w, a.batch, pro, epi, &plan, &kern, &cap, kp_window));
   a.pairs_per_chunk = plan.pairs_per_chunk;
   a.n_stages = plan.n_stages;
   a.err = device_error_word();

@@ -83,6 +83,10 @@ struct GemvArgs {
   int64_t pairs_per_chunk; // block pairs per K-chunk (cluster CTA)
   int early_trigger;       // set by the launcher: grid fits in one resident wave
   int n_stages;            // rows mode: row tiles in flight in shared memory
+  // cluster mode: the block pairs [pair_begin, pair_end) of K this launch
+  // covers (pair_end 0: all of K); a GEMV whose split of x would not fit runs
+  // as launches over K windows, the later ones adding into y
+  int64_t pair_begin, pair_end;
   int* err;                // device error word (a bounded wait that gave up)
   // Store epilogue scatter (tensor-parallel all-reduce over peer memory): with
   // n_peer > 0 every output element goes to peer_y[p] + row*peer_row + b for

@@ -19,7 +19,8 @@ struct GemvPlan {
 };
 
 GemvPlan gemv_plan(const Q4Tiled& w, int batch);
-GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode);
+// kp_window > 0: a cluster-mode launch over a window of that many block pairs
+GemvPlan gemv_plan(const Q4Tiled& w, int batch, bool rows_mode, int64_t kp_window = 0);
 // Launches the fused GEMV with the given prologue/epilogue; `pdl` enables
 // programmatic dependent launch (weights are prefetched before the kernel waits
 // for its predecessor's output).

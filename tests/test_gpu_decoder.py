@@ -149,6 +149,27 @@ def test_8b_full_depth(cuda, oracle):
     print(f"8B full depth: worst logits error {worst:.2e}, tokens {new}")
 
 
+def test_batch16_wide_ffn_k_windows(cuda, oracle):
+    # batch 16 with a 28672-wide FFN: the down projection's split of x does not
+    # fit one CTA, so it runs as launches over K windows (residual add, RMSNorm
+    # partials from the last window); every sequence's logits against the oracle
+    from agent_harness_b200.model import Model, ModelConfig
+    cfg = ModelConfig(n_layer=1, n_embd=256, n_ff=28672, n_head=4, n_head_kv=2, head_dim=64, vocab_size=512,
+                      max_seq=16, max_batch=16, rope_freq_base=10000.0, rms_eps=1e-5)
+    m = Model(cfg)
+    m.init_random(31)
+    W = oracle_weights(cfg, 31, cuda)
+    prompt = np.random.default_rng(4).integers(0, cfg.vocab_size, (16, 3)).astype(np.int32)
+    om = [oracle_model(oracle, cfg, W) for _ in range(16)]
+    m.reset(16)
+    for t in range(prompt.shape[1]):
+        lg = m.forward(prompt[:, t]).cpu().numpy()
+        for b in range(16):
+            ref = om[b].forward(int(prompt[b, t]), t)
+            assert relerr(lg[b], ref) <= TOL, (t, b, relerr(lg[b], ref))
+    m.close()
+
+
 @pytest.mark.parametrize("shape", ["hd64_g2_batch2", "hd128_g8"])
 def test_long_context_attention_splits(cuda, oracle, shape):
     # Contexts long enough for the attention to split the cached positions over
