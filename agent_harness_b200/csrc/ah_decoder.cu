@@ -358,7 +358,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attention_tc(const __grid_cons
   pdl_wait();
   const int pos = *a.pos;
   const int n_ctx = pos + 1;
-  const int n_split = min(kAttnSplits, (n_ctx + 63) / 64);
+  int n_split = min(kAttnSplits, (n_ctx + 63) / 64);
+  // many sequences x kv heads (batched decode): fewer, longer splits (up to
+  // the tile's kAttnMaxChunk rows) halve the per-item fixed costs
+  if (a.batch * a.n_kv * n_split > 4 * (int)gridDim.x)
+    n_split = max(1, min(n_split, (n_ctx + kAttnMaxChunk - 1) / kAttnMaxChunk));
   const int chunk = (n_ctx + n_split - 1) / n_split;  // <= kAttnMaxChunk (max_seq is checked at creation)
   const int kw = (chunk + 63) >> 6;                   // 16-position k-steps per warp (1 or 2)
   const int n_items = a.batch * a.n_kv * n_split;

@@ -170,6 +170,26 @@ def test_batch16_wide_ffn_k_windows(cuda, oracle):
     m.close()
 
 
+def test_batch16_long_context_attention(cuda, oracle):
+    # batch 16 x 8 kv heads at a 640-position context: the tensor-core
+    # attention takes the long (128-position) splits of batched decode
+    from agent_harness_b200.model import Model, ModelConfig
+    cfg = ModelConfig(n_layer=1, n_embd=512, n_ff=512, n_head=8, n_head_kv=8, head_dim=64, vocab_size=512,
+                      max_seq=700, max_batch=16, rope_freq_base=10000.0, rms_eps=1e-5)
+    m = Model(cfg)
+    m.init_random(41)
+    W = oracle_weights(cfg, 41, cuda)
+    prompt = np.random.default_rng(8).integers(0, cfg.vocab_size, (16, 640)).astype(np.int32)
+    m.generate(prompt, 0)  # positions 0 .. 638
+    lg = m.forward(prompt[:, -1]).cpu().numpy()
+    for b in (0, 15):
+        o = oracle_model(oracle, cfg, W)
+        for t, tok in enumerate(prompt[b]):
+            ref = o.forward(int(tok), t)
+        assert relerr(lg[b], ref) <= TOL, (b, relerr(lg[b], ref))
+    m.close()
+
+
 @pytest.mark.parametrize("shape", ["hd64_g2_batch2", "hd128_g8"])
 def test_long_context_attention_splits(cuda, oracle, shape):
     # Contexts long enough for the attention to split the cached positions over
