@@ -16,6 +16,8 @@ pytestmark = pytest.mark.gpu
 SMALL = dict(n_layer=2, n_embd=256, n_ff=512, n_head=4, n_head_kv=2, head_dim=64, vocab_size=1000, max_seq=64,
              max_batch=2, rope_freq_base=10000.0, rms_eps=1e-5)
 PROMPT = np.array([[3, 14, 159, 265, 358, 979], [2, 71, 828, 182, 845, 904]], np.int32)
+# long enough for the prefill GEMMs (with an all-reduce of the block outputs)
+LONG = (np.arange(2 * 40, dtype=np.int32).reshape(2, 40) * 37 + 11) % 1000
 
 
 def _free_port():
@@ -48,10 +50,13 @@ def _rank(rank, world, port, q, p2p=False):
         m.reset(2)
         logits = [m.forward(PROMPT[:, t]).cpu().numpy() for t in range(PROMPT.shape[1])]
         gen = m.generate(PROMPT, 8)
+        gen_long = m.generate(LONG, 6)
+        m.generate(LONG, 0)
+        last = m.forward(LONG[:, -1]).cpu().numpy()
         torch.cuda.synchronize()
         err = _lib.lib().ah_check_device_error(None)
         m.close()
-        q.put((rank, logits, gen, err))
+        q.put((rank, logits, (gen, gen_long, last), err))
     finally:
         dist.destroy_process_group()
 
@@ -85,6 +90,13 @@ def test_tp2_matches_single_gpu(cuda, p2p):
         err = np.max(np.abs(full - ref)) / np.max(np.abs(ref))
         assert err <= 1e-3, (t, err)
     gen1 = m.generate(PROMPT, 8)
+    gen1_long = m.generate(LONG, 6)
+    m.generate(LONG, 0)
+    last1 = m.forward(LONG[:, -1]).cpu().numpy()
     m.close()
-    assert np.array_equal(res[0][1], res[1][1])
-    assert np.array_equal(res[0][1], gen1)
+    (g0, gl0, la0), (g1, gl1, la1) = res[0][1], res[1][1]
+    assert np.array_equal(g0, g1) and np.array_equal(g0, gen1)
+    # the long prompt went through the tensor-parallel prefill GEMMs
+    assert np.array_equal(gl0, gl1) and np.array_equal(gl0, gen1_long)
+    full = np.concatenate([la0, la1], axis=1)
+    assert np.max(np.abs(full - last1)) / np.max(np.abs(last1)) <= 1e-3
