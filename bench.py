@@ -421,14 +421,15 @@ def cpu_decode_baseline(layer_shapes, n_layer, head_shape, tokens, min_s=0.3):
     return step, nt, layer
 
 
-def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_BATCH, allreduce="peer"):
+def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_BATCH, allreduce="peer", n_layer=None):
     """70B-shape greedy decode, batch 16, tensor-parallel over the job's ranks
     (80 layers, d 8192, FFN 28672, 64/8 heads x 128, vocab 128256; Q4_0
     N(0,0.02) seed 8; prompts of uniform ids seed 9).  Decode steps are timed
     with CUDA events on every rank; the max over ranks is reported."""
     import torch
     from agent_harness_b200.model import LLAMA_70B, Model, ModelConfig, nccl_unique_id
-    cfg = ModelConfig(**{**LLAMA_70B.__dict__, "max_seq": n_prompt + n_new + 8, "max_batch": batch})
+    cfg = ModelConfig(**{**LLAMA_70B.__dict__, "max_seq": n_prompt + n_new + 8, "max_batch": batch,
+                         "n_layer": n_layer or LLAMA_70B.n_layer})
     nid = None
     if world > 1:
         import torch.distributed as dist
@@ -484,7 +485,7 @@ def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_B
                  "allreduce_note": f"{2 * cfg.n_layer} ncclAllReduce of [{batch}, {cfg.n_embd}] f32 timed alone; "
                                    "the rest of the step streams weights"}
     return {"tokens_per_s": round(batch * n_new / (ms / 1e3), 1), "ms_per_step": round(per_step * 1e3, 3),
-            "batch": batch, "n_prompt": n_prompt, "n_new": n_new, "tp": world,
+            "batch": batch, "n_prompt": n_prompt, "n_new": n_new, "tp": world, "n_layer": cfg.n_layer,
             "block_allreduce": (allreduce if world > 1 else "none"),
             "weight_gbs_per_gpu": round(DECODE70_WEIGHT_BYTES / world / per_step / 1e9, 1),
             "prefill_tokens_per_s": round(batch * (n_prompt - 1) / prefill_s, 1),
@@ -495,14 +496,15 @@ def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_B
                     "nccl: ncclAllReduce), argmax-candidate all-gather; steps replayed as CUDA graphs"}
 
 
-def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW):
+def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW, n_layer=None):
     """8B-shape greedy decode, batch 1: 32 layers, d 4096, FFN 14336, 32/8 heads
     x 128, vocab 128256, theta 5e5; Q4_0 projections N(0,0.02) seed 6, f16
     embeddings/norms, f16 KV; prompt of uniform token ids (seed 7)."""
     import torch
     from agent_harness_b200.model import LLAMA_8B, Model
-    cfg = LLAMA_8B
-    cfg.max_seq = n_prompt + n_new + 8
+    from agent_harness_b200.model import ModelConfig
+    cfg = ModelConfig(**{**LLAMA_8B.__dict__, "max_seq": max(n_prompt, 256) + n_new + 16,
+                         "n_layer": n_layer or LLAMA_8B.n_layer})
     m = Model(cfg, device=dev)
     m.init_random(6, w_std=0.02, emb_std=1.0, norm_std=0.02)
     prompt = np.random.default_rng(7).integers(0, cfg.vocab_size, (1, n_prompt)).astype(np.int32)
@@ -542,7 +544,7 @@ def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW):
                         "token_by_token_tokens_per_s": round(255 / tok_s, 1),
                         "agrees_with_token_by_token": bool(np.array_equal(tokwise, again))},
             "weight_gbs": round(DECODE_BYTES_PER_TOKEN_WEIGHTS / per_tok / 1e9, 1),
-            "n_prompt": n_prompt, "n_new": n_new, "first_tokens": [int(first[0, 0])] + [int(v) for v in tk[1:6]],
+            "n_prompt": n_prompt, "n_new": n_new, "n_layer": cfg.n_layer, "first_tokens": [int(first[0, 0])] + [int(v) for v in tk[1:6]],
             "deterministic": bool(np.array_equal(again, again2)),
             "note": "decode steps replayed as one CUDA graph each (5 fused kernels per layer + head + argmax)"}
 
@@ -858,9 +860,11 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
     ap.add_argument("--decode-prompt", type=int, default=DECODE_PROMPT)
     ap.add_argument("--decode-new", type=int, default=DECODE_NEW)
+    ap.add_argument("--decode-layers", type=int, default=None, help="fewer 8B-shape layers (profiling only)")
     ap.add_argument("--no-tp", action="store_true", help="skip the 70B tensor-parallel decode measurement")
     ap.add_argument("--tp-prompt", type=int, default=TP_PROMPT)
     ap.add_argument("--tp-new", type=int, default=TP_NEW)
+    ap.add_argument("--tp-layers", type=int, default=None, help="fewer 70B-shape layers (profiling only)")
     ap.add_argument("--tp-allreduce", default="peer", choices=["peer", "nccl"],
                     help="block all-reduce of the tensor-parallel decoder")
     args = ap.parse_args()
@@ -891,7 +895,7 @@ def main():
         from agent_harness_b200 import _lib
         _lib.check(_lib.lib().ah_device_init(0))
         print(json.dumps({"workload": "decode_8b", **decode_8b(torch.device("cuda", 0), args.decode_prompt,
-                                                               args.decode_new)}), flush=True)
+                                                               args.decode_new, args.decode_layers)}), flush=True)
         return 0
     if args.workload == "tp":
         import torch
@@ -905,7 +909,7 @@ def main():
         from agent_harness_b200 import _lib
         _lib.check(_lib.lib().ah_device_init(local))
         r = decode_70b_tp(torch.device("cuda", local), rank, world, args.tp_prompt, args.tp_new,
-                          allreduce=args.tp_allreduce)
+                          allreduce=args.tp_allreduce, n_layer=args.tp_layers)
         if rank == 0:
             print(json.dumps({"workload": "decode_70b_tp", **r}), flush=True)
         if world > 1:
