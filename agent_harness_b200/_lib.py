@@ -77,6 +77,8 @@ SIGNATURES = {
     "ah_q4w_gemm_workspace_bytes": (i32, [vp, i64, C.POINTER(C.c_size_t)]),
     "ah_q4w_gemm": (i32, [vp, vp, i64, i64, vp, i64, vp, C.c_size_t, vp]),
     "ah_q4w_gemm_noalloc": (i32, [vp, vp, i64, i64, vp, i64, vp]),
+    "ah_q4w_gemv_tc_workspace_bytes": (i32, [vp, C.POINTER(C.c_size_t)]),
+    "ah_q4w_gemv_tc": (i32, [vp, vp, i64, i32, vp, i64, i32, vp, C.c_size_t, vp]),
     "ah_gemv_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, i64, vp]),
     "ah_matvec_4bit_into": (i32, [vp, vp, vp, vp, i64, i64, vp]),
     "ah_gemv_4bit_rows": (i32, [vp, vp, vp, vp, i64, i64, i64, i64, vp]),
@@ -105,6 +107,7 @@ SIGNATURES = {
     "ah_model_decode": (i32, [vp, i32, vp, vp]),
     "ah_model_position": (i32, [vp, C.POINTER(i32)]),
     "ah_model_set_prefill": (i32, [vp, i32]),
+    "ah_model_set_batched_gemv": (i32, [vp, i32]),
     "ah_host_gemv_4bit_into": (i32, [vp, vp, vp, vp, sz, sz, sz]),
     "ah_host_dequant_layer": (i32, [vp, vp, vp, sz, sz]),
     "ah_host_quantize": (i32, [vp, sz, sz, vp, vp]),

@@ -869,6 +869,9 @@ __global__ void k_rope_table(float2* t, int max_seq, int half, float base) {
 // ---------------------------------------------------------------------------
 // Model object
 // ---------------------------------------------------------------------------
+// Smallest batch whose decode GEMVs run on the tcgen05 batched GEMV by default.
+constexpr int kBgemvMinBatchDefault = 9;
+
 struct AhModel {
   AhModelConfig c{};  // the full (unsharded) model
   int device = 0;
@@ -922,6 +925,11 @@ struct AhModel {
   float *pf_gu = nullptr, *pf_act = nullptr;
   void* pf_ws = nullptr;
   size_t pf_ws_bytes = 0;
+  // decode steps of at least bg_min_batch sequences run their GEMVs on the
+  // tcgen05 batched GEMV (17: never); its workspace is allocated on first use
+  int bg_min_batch = kBgemvMinBatchDefault;
+  void* bg_ws = nullptr;
+  size_t bg_ws_bytes = 0;
 };
 
 namespace {
@@ -1017,6 +1025,8 @@ int launch_attention(AhModel* m, const AttnArgs& at, size_t attn_smem, cudaStrea
                     p);
 }
 
+int step_gemv(AhModel* m, const GemvArgs& a, int pro, int epi, cudaStream_t st);
+
 // Enqueues one decoder step (all layers; with_head adds LM head + argmax).
 int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cudaStream_t st) {
   const AhModelConfig& c = m->c;
@@ -1031,7 +1041,7 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     q.eps = c.rms_eps;
     q.ss_in = m->ss;
     q.n_ss_in = d / 16;
-    AH_TRY(gemv_launch(q, kProRmsNorm, kEpiStore, st, true));
+    AH_TRY(step_gemv(m, q, kProRmsNorm, kEpiStore, st));
     AttnArgs at{};
     at.qkv = m->qkv;
     at.kc = m->kc;
@@ -1054,34 +1064,34 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     if (tp && m->p2p) {
       GemvArgs o = gemv_args(m->wo[l], m->attn, m->dq, m->part, d, B);
       set_peer_scatter(m, o, 0);
-      AH_TRY(gemv_launch(o, kProPlain, kEpiStore, st, true));
+      AH_TRY(step_gemv(m, o, kProPlain, kEpiStore, st));
       AH_TRY(reduce_residual_peer(m, 0, st));
     } else if (tp) {
-      AH_TRY(gemv_launch(gemv_args(m->wo[l], m->attn, m->dq, m->part, d, B), kProPlain, kEpiStore, st, true));
+      AH_TRY(step_gemv(m, gemv_args(m->wo[l], m->attn, m->dq, m->part, d, B), kProPlain, kEpiStore, st));
       AH_TRY(reduce_residual(m, st));
     } else {
       GemvArgs o = gemv_args(m->wo[l], m->attn, m->dq, m->hidden, d, B);
       o.ss_out = m->ss;
-      AH_TRY(gemv_launch(o, kProPlain, kEpiAdd, st, true));
+      AH_TRY(step_gemv(m, o, kProPlain, kEpiAdd, st));
     }
     GemvArgs gu = gemv_args(m->wgu[l], m->hidden, d, m->act, m->nff, B);
     gu.norm_w = m->ffn_norm + (size_t)l * d;
     gu.eps = c.rms_eps;
     gu.ss_in = m->ss;
     gu.n_ss_in = d / 16;
-    AH_TRY(gemv_launch(gu, kProRmsNorm, kEpiSwiglu, st, true));
+    AH_TRY(step_gemv(m, gu, kProRmsNorm, kEpiSwiglu, st));
     if (tp && m->p2p) {
       GemvArgs dn = gemv_args(m->wd[l], m->act, m->nff, m->part, d, B);
       set_peer_scatter(m, dn, 1);
-      AH_TRY(gemv_launch(dn, kProPlain, kEpiStore, st, true));
+      AH_TRY(step_gemv(m, dn, kProPlain, kEpiStore, st));
       AH_TRY(reduce_residual_peer(m, 1, st));
     } else if (tp) {
-      AH_TRY(gemv_launch(gemv_args(m->wd[l], m->act, m->nff, m->part, d, B), kProPlain, kEpiStore, st, true));
+      AH_TRY(step_gemv(m, gemv_args(m->wd[l], m->act, m->nff, m->part, d, B), kProPlain, kEpiStore, st));
       AH_TRY(reduce_residual(m, st));
     } else {
       GemvArgs dn = gemv_args(m->wd[l], m->act, m->nff, m->hidden, d, B);
       dn.ss_out = m->ss;
-      AH_TRY(gemv_launch(dn, kProPlain, kEpiAdd, st, true));
+      AH_TRY(step_gemv(m, dn, kProPlain, kEpiAdd, st));
     }
   }
   if (with_head) {
@@ -1090,7 +1100,7 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     h.eps = c.rms_eps;
     h.ss_in = m->ss;
     h.n_ss_in = d / 16;
-    AH_TRY(gemv_launch(h, kProRmsNorm, kEpiStore, st, true));
+    AH_TRY(step_gemv(m, h, kProRmsNorm, kEpiStore, st));
     ArgPair* pair = tp ? static_cast<ArgPair*>(m->am_pair) : nullptr;
     AH_TRY(launch_pdl(k_argmax, dim3(kArgmaxChunks, B), dim3(256), 0, st, (const float*)m->logits, m->nvoc, m->am_v,
                       m->am_i, m->am_cnt, m->d_tok, m->tok_log, (const int*)m->d_pos, B, pair,
@@ -1182,10 +1192,34 @@ int prefill_gemm(AhModel* m, const int* prompt, int n_prompt, int P, cudaStream_
   return AH_OK;
 }
 
+bool use_bgemv(const AhModel* m) { return m->batch >= m->bg_min_batch; }
+
+// One decode-step GEMV: the tcgen05 batched GEMV for wide enough batches,
+// else the mma.sync GEMV.
+int step_gemv(AhModel* m, const GemvArgs& a, int pro, int epi, cudaStream_t st) {
+  if (use_bgemv(m)) {
+    void* ws = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(m->bg_ws) + 1023) & ~uintptr_t(1023));
+    return bgemv_launch(a, pro, epi, ws, m->bg_ws_bytes, st, true);
+  }
+  return gemv_launch(a, pro, epi, st, true);
+}
+
 // Kernel attributes and occupancy are resolved before a capture starts.
 int prepare_step(AhModel* m) {
   const AhModelConfig& c = m->c;
   const int B = m->batch;
+  if (use_bgemv(m)) {
+    if (!m->bg_ws) {
+      size_t ws = 0;
+      for (const AhQ4Weight* w : {m->lm, m->wqkv[0], m->wo[0], m->wgu[0], m->wd[0]})
+        ws = std::max(ws, bgemv_workspace_bytes(q4w_tiled(w)));
+      AH_TRY(dalloc(m, &m->bg_ws, ws + 1024));
+      m->bg_ws_bytes = ws;
+    }
+    AH_TRY(bgemv_prepare(q4w_tiled(m->lm), kEpiStore));
+    AH_TRY(bgemv_prepare(q4w_tiled(m->lm), kEpiAdd));
+    AH_TRY(bgemv_prepare(q4w_tiled(m->lm), kEpiSwiglu));
+  }
   AH_TRY(gemv_prepare(q4w_tiled(m->lm), B, kProRmsNorm, kEpiStore));
   AH_TRY(gemv_prepare(q4w_tiled(m->wqkv[0]), B, kProRmsNorm, kEpiStore));
   const int ro = m->tp_world > 1 ? kEpiStore : kEpiAdd;
@@ -1727,6 +1761,19 @@ int ah_model_reset(AhModel* m, int batch, void* stream) {
   m->batch = batch;
   m->pos = 0;
   AH_CUDA_TRY(cudaMemsetAsync(m->d_pos, 0, 4, st));
+  return AH_OK;
+}
+
+int ah_model_set_batched_gemv(AhModel* m, int min_batch) {
+  AH_REQUIRE(m && min_batch >= 1 && min_batch <= kGemvMaxBatch + 1,
+             "model_set_batched_gemv: min_batch must be 1..17");
+  if (m->bg_min_batch == min_batch) return AH_OK;
+  m->bg_min_batch = min_batch;
+  // the captured steps hold the other GEMV: capture again on the next step
+  for (int i = 0; i < 2; ++i) {
+    if (m->g_step[i]) cudaGraphExecDestroy(m->g_step[i]);
+    m->g_step[i] = nullptr;
+  }
   return AH_OK;
 }
 

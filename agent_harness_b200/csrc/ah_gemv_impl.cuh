@@ -35,6 +35,16 @@ size_t gemm_workspace_bytes(const Q4Tiled& w, int64_t m);
 int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c, int64_t ldc, void* ws,
              size_t ws_bytes, cudaStream_t st);
 
+// The tcgen05 batched GEMV (ah_bgemv_tc.cu): the same products as
+// gemv_launch for 1..16 tokens, weights dequantised into tensor memory, work
+// split stream-K over persistent CTAs.  Needs a 1024-byte aligned workspace of
+// bgemv_workspace_bytes(w); bgemv_prepare sets kernel attributes ahead of a
+// graph capture.  K windows (pair_end) are not supported.
+size_t bgemv_workspace_bytes(const Q4Tiled& w);
+int bgemv_prepare(const Q4Tiled& w, int epilogue);
+int bgemv_launch(const GemvArgs& a, int prologue, int epilogue, void* ws, size_t ws_bytes, cudaStream_t st,
+                 bool pdl);
+
 const Q4Tiled& q4w_tiled(const AhQ4Weight* w);
 // An uninitialised tiled weight of the given shape (f32 scales when `engine`);
 // its planes are filled by the caller's kernel.

@@ -224,6 +224,31 @@ class Q4Weight:
              C.c_void_p(aligned), need, _stream(a.device))
         return out
 
+    def gemv_tc_workspace_bytes(self) -> int:
+        n = C.c_size_t()
+        call("ah_q4w_gemv_tc_workspace_bytes", self._h, C.byref(n))
+        return n.value
+
+    def gemv_tc(self, x: torch.Tensor, out: torch.Tensor | None = None, accumulate: bool = False,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """y = W x for 1..16 token rows x [batch, cols] f32 through the tcgen05
+        batched GEMV (f16 operands, f32 accumulation); accumulate adds into out."""
+        assert x.dtype == torch.float32 and x.dim() == 2 and x.shape[1] == self.cols and x.stride(1) == 1
+        b = x.shape[0]
+        if out is None:
+            assert not accumulate
+            out = torch.empty(b, self.rows, dtype=torch.float32, device=x.device)
+        need = self.gemv_tc_workspace_bytes()
+        if workspace is None or workspace.numel() < need + 1024:
+            workspace = torch.empty(need + 1024, dtype=torch.uint8, device=x.device)
+        base = workspace.data_ptr()
+        aligned = (base + 1023) // 1024 * 1024
+        assert x.is_cuda and out.is_cuda and out.dim() == 2 and out.stride(1) == 1 and out.shape[0] == b
+        # row-strided views are fine: the entry point takes the row strides
+        call("ah_q4w_gemv_tc", self._h, C.c_void_p(x.data_ptr()), x.stride(0), b, C.c_void_p(out.data_ptr()),
+             out.stride(0), int(bool(accumulate)), C.c_void_p(aligned), need, _stream(x.device))
+        return out
+
     def close(self):
         if self._h:
             lib().ah_q4w_destroy(self._h)

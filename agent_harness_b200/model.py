@@ -159,6 +159,11 @@ class Model:
         per prompt token, as the reference (inference/mod.rs:550)."""
         call("ah_model_set_prefill", self._h, mode)
 
+    def set_batched_gemv(self, min_batch: int):
+        """Decode steps of at least min_batch sequences (default 9) run their
+        GEMVs on the tcgen05 batched GEMV; 1 always, 17 never."""
+        call("ah_model_set_batched_gemv", self._h, min_batch)
+
     @property
     def position(self) -> int:
         v = C.c_int(0)

@@ -394,6 +394,14 @@ TP_PROMPT, TP_NEW, TP_BATCH = 2048, 128, 16
 DECODE70_WEIGHT_BYTES = 39094714368
 
 
+def decode70_weight_bytes(n_layer):
+    """Q4_0 bytes (18 per 32 weights) one 70B-shape decode step streams: the
+    q|k|v, o, gate|up and down projections of n_layer layers plus the LM head."""
+    d, ff, kv, vocab = 8192, 28672, 1024, 128256
+    per_layer = d * (d + 2 * kv) + d * d + 2 * ff * d + d * ff
+    return (per_layer * n_layer + vocab * d) * 18 // 32
+
+
 def cpu_decode_baseline(layer_shapes, n_layer, head_shape, tokens, min_s=0.3):
     """The reference's decode on the host cores: its engine forward spends its
     time in gemv_4bit_into (the AVX-512 worker, inference/math.rs:255-380) once
@@ -487,7 +495,7 @@ def decode_70b_tp(dev, rank, world, n_prompt=TP_PROMPT, n_new=TP_NEW, batch=TP_B
     return {"tokens_per_s": round(batch * n_new / (ms / 1e3), 1), "ms_per_step": round(per_step * 1e3, 3),
             "batch": batch, "n_prompt": n_prompt, "n_new": n_new, "tp": world, "n_layer": cfg.n_layer,
             "block_allreduce": (allreduce if world > 1 else "none"),
-            "weight_gbs_per_gpu": round(DECODE70_WEIGHT_BYTES / world / per_step / 1e9, 1),
+            "weight_gbs_per_gpu": round(decode70_weight_bytes(cfg.n_layer) / world / per_step / 1e9, 1),
             "prefill_tokens_per_s": round(batch * (n_prompt - 1) / prefill_s, 1),
             "prefill_s": round(prefill_s, 2),
             "first_tokens_seq0_3": first, **split,

@@ -201,6 +201,20 @@ AH_API int ah_q4w_gemm(const AhQ4Weight* w, const float* a_dev, int64_t lda, int
 AH_API int ah_q4w_gemm_noalloc(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev,
                                int64_t ldc, void* stream);
 
+/* Replaces, for 1..16 tokens at once, the reference's gemv_4bit_into
+ * (inference/math.rs:255-295) per token, like ah_q4w_gemv, on the 5th-
+ * generation tensor cores: y_dev[b][y_stride] (+)= W . x_dev[b][x_stride] for
+ * b < batch.  W is dequantised as d*(q-8) rounded once to f16 and each x row is
+ * scaled by a power of two and rounded to f16 (the ah_q4w_gemm precision); f32
+ * accumulation.  accumulate != 0 adds into y instead of storing.
+ * `workspace_dev` (1024-byte aligned, at least ah_q4w_gemv_tc_workspace_bytes(w)
+ * bytes) holds the converted tokens and the partial sums of row blocks that
+ * several CTAs share; calls on different streams need different workspaces. */
+AH_API int ah_q4w_gemv_tc_workspace_bytes(const AhQ4Weight* w, size_t* bytes);
+AH_API int ah_q4w_gemv_tc(const AhQ4Weight* w, const float* x_dev, int64_t x_stride, int batch, float* y_dev,
+                          int64_t y_stride, int accumulate, void* workspace_dev, size_t workspace_bytes,
+                          void* stream);
+
 /* Reference: inference/math.rs:255-295 gemv_4bit_into on the engine format as
  * stored (f32 scales [rows][ceil(cols/gs)], linear nibbles), device pointers, any
  * group size; empty input -> zero output (math.rs:264-267). */
@@ -335,6 +349,11 @@ AH_API int ah_model_generate(AhModel* m, const int32_t* prompt, int batch, int n
  * decode step; mode 0: token by token, as the reference.  Both leave the same
  * state (KV cache, position) up to rounding. */
 AH_API int ah_model_set_prefill(AhModel* m, int mode);
+/* Which GEMV the decode steps use (no reference counterpart): steps of at
+ * least `min_batch` sequences (default 9) run every projection on the tcgen05
+ * batched GEMV (ah_q4w_gemv_tc precision: f16 operands, f32 accumulation),
+ * smaller ones on the mma.sync GEMV (ah_q4w_gemv).  1 always, 17 never. */
+AH_API int ah_model_set_batched_gemv(AhModel* m, int min_batch);
 /* Lower-level stepping (same semantics): reset, feed one token per sequence
  * (forward(), inference/mod.rs:333-545) and read the logits [batch][vocab]. */
 AH_API int ah_model_reset(AhModel* m, int batch, void* stream);

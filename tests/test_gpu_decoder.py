@@ -190,6 +190,47 @@ def test_batch16_long_context_attention(cuda, oracle):
     m.close()
 
 
+@pytest.mark.parametrize("tp_like", [False, True])
+def test_batch16_tensor_core_gemv_path(cuda, oracle, tp_like):
+    # the batched decode GEMVs (tcgen05, default from 9 sequences) against the
+    # oracle and against the mma.sync GEMVs (min_batch 17) on the same model:
+    # logits within 1e-3 of each other, greedy tokens identical.  tp_like has
+    # an odd block-pair count in the down projection (FFN 1088), head_dim 128
+    # with 4 query heads per kv head, and a partial last row block in the LM
+    # head (vocab 1000).
+    from agent_harness_b200.model import Model, ModelConfig
+    if tp_like:
+        cfg = ModelConfig(n_layer=2, n_embd=1024, n_ff=1088, n_head=8, n_head_kv=2, head_dim=128, vocab_size=1000,
+                          max_seq=32, max_batch=16, rope_freq_base=10000.0, rms_eps=1e-5)
+    else:
+        cfg = ModelConfig(n_layer=2, n_embd=512, n_ff=1536, n_head=8, n_head_kv=4, head_dim=64, vocab_size=2048,
+                          max_seq=32, max_batch=16, rope_freq_base=10000.0, rms_eps=1e-5)
+    m = Model(cfg)
+    m.init_random(53)
+    W = oracle_weights(cfg, 53, cuda)
+    prompt = np.random.default_rng(9).integers(0, cfg.vocab_size, (16, 4)).astype(np.int32)
+    om = [oracle_model(oracle, cfg, W) for _ in range(16)]
+    runs = {}
+    for mb in (9, 17):
+        m.set_batched_gemv(mb)
+        m.reset(16)
+        lgs = []
+        for t in range(prompt.shape[1]):
+            lgs.append(m.forward(prompt[:, t]).cpu().numpy())
+        runs[mb] = lgs
+    for t in range(prompt.shape[1]):
+        for b in range(16):
+            ref = om[b].forward(int(prompt[b, t]), t)
+            assert relerr(runs[9][t][b], ref) <= TOL, (t, b, relerr(runs[9][t][b], ref))
+            assert relerr(runs[9][t][b], runs[17][t][b]) <= TOL
+    m.set_batched_gemv(9)
+    g_tc = m.generate(prompt, 6)
+    m.set_batched_gemv(17)
+    g_ms = m.generate(prompt, 6)
+    assert np.array_equal(g_tc, g_ms)
+    m.close()
+
+
 @pytest.mark.parametrize("shape", ["hd64_g2_batch2", "hd128_g8"])
 def test_long_context_attention_splits(cuda, oracle, shape):
     # Contexts long enough for the attention to split the cached positions over
