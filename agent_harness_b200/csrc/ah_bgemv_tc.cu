@@ -13,8 +13,9 @@
 //               scales per step into a 12-stage raw ring (~110 KB in flight)
 //   warp 1      token producer: 2-D TMA of the 16 x 128 f16 token tile
 //               (128-byte swizzle) into a 16-slot ring
-//   warp 2      TMEM owner + MMA issuer: tcgen05.mma M=128 N=16 K=16 with A in
-//               tensor memory (kind::f16, f32 accumulators)
+//   warps 2, 15 TMEM owner (warp 2) and two MMA issuers taking alternate
+//               steps: tcgen05.mma M=128 N=16 K=16 with A in tensor memory
+//               (kind::f16, f32 accumulators, one per issuer)
 //   warps 3..10 dequant d*(q-8) (one RNE rounding to f16) from the raw ring
 //               into tensor memory with tcgen05.st.16x256b: that store's
 //               register layout is the m16n8 fragment layout the tiled Q4
@@ -87,20 +88,26 @@ constexpr int kBgBPair = kBgN * 64 * 2;               // 2048: 16 tokens x 64 f1
 constexpr int kBgBStep = kBgPairs * kBgBPair;         // 4096: one step's token tile
 constexpr int kBgBSlot = kBgBGroup * kBgBStep;        // 16384
 constexpr uint32_t kBgTmemCols = 512;
-// The MMAs of a step rotate over kBgAccSets accumulators (MMAs into one
-// accumulator run one after another); the epilogue adds the sets in order.
-constexpr int kBgAccSets = 4;
-constexpr int kBgAccStride = kBgAccSets * kBgN;       // columns per accumulator buffer (two buffers)
-constexpr int kBgACol0 = 2 * kBgAccStride;            // A stage a at columns kBgACol0 + 64a
+// kBgIssuers MMA issuer threads (in different warps) take the steps in turn,
+// each into its own accumulator (columns ((segment & 1) * kBgIssuers + t) * 16):
+// an MMA issue blocks while the previous MMA runs (M=128, K=16: ~56 ns
+// whatever N up to 128), so one issuer's barrier waits and bookkeeping would
+// leave the tensor core idle; the other's MMAs fill those gaps.  The epilogue
+// adds the accumulators.  Measured on the 70B gate/up (57344 x 8192, batch
+// 16): one issuer 172 us, two 111 us, three 126 us, four 124 us.
+constexpr int kBgIssuers = 2;
+constexpr int kBgACol0 = 2 * kBgIssuers * kBgN;       // A stage a at columns kBgACol0 + 64a
 constexpr int kBgACols = kBgPairs * 32;               // 64 columns per stage
 static_assert(kBgACol0 + kBgAStages * kBgACols <= (int)kBgTmemCols, "TMEM budget");
-static_assert(kBgPairs * 4 >= kBgAccSets, "every accumulator set takes an MMA in a step");
 static_assert(kBgRawStages % 2 == 0 && kBgAStages % 2 == 0, "stage parity selects the dequant group");
 static_assert(kBgBGroup * kBgBSlots >= kBgRawStages, "token tiles are requested ahead of their weights");
-static_assert((kBgBGroup & (kBgBGroup - 1)) == 0 && (kBgBSlots & (kBgBSlots - 1)) == 0, "powers of two");
+static_assert((kBgBSlots & (kBgBSlots - 1)) == 0, "a power of two");
+static_assert(kBgBGroup % kBgIssuers == 0, "every issuer takes the same number of steps of a token slot");
 constexpr int kBgDequantWarp0 = 3;
 constexpr int kBgEpiWarp0 = 11;
-constexpr int kBgThreads = 15 * 32;
+// issuer 0 is warp 2 (the TMEM owner), issuers 1.. are warps 15..
+constexpr int kBgIssuerWarp1 = 15;
+constexpr int kBgThreads = (kBgIssuerWarp1 + kBgIssuers - 1) * 32;
 constexpr uint32_t kBgWait = 1u << 24;
 constexpr uint32_t kBgIdesc = idesc_f16(kBgM, kBgN);
 constexpr int kBgPrepThreads = 256;
@@ -217,6 +224,19 @@ __global__ void __launch_bounds__(kBgPrepThreads) k_bgemv_prep(const GemvArgs a,
 
 __device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
   if (mbar_wait_bounded(bar, parity, err, AH_ETIMEOUT, kBgWait)) return true;
+  *abort_flag = 1;
+  return false;
+}
+
+// Wait with a short sleep after each failed poll, for the producers and the
+// dequant warps: their spinning would take issue slots and barrier-unit cycles
+// from the MMA issuers sharing their SM sub-partitions.
+__device__ __forceinline__ bool bg_wait_nap(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
+  for (uint32_t it = 0; it < (kBgWait >> 2); ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(32);
+  }
+  if (err) atomicExch(err, AH_ETIMEOUT);
   *abort_flag = 1;
   return false;
 }
@@ -375,13 +395,13 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemv_tc(const __grid_constan
     }
     for (int i = 0; i < kBgBSlots; ++i) {
       mbar_init(&b_full[i], 1);
-      mbar_init(&b_empty[i], 1);
+      mbar_init(&b_empty[i], kBgIssuers);  // each issuer commits after its last step of the slot
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_full[i], kBgIssuers);
       mbar_init(&acc_empty[i], 4);  // the four epilogue warps
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, kBgIssuers);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -401,7 +421,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemv_tc(const __grid_constan
       for (int i = 0; i < n; ++i) {
         const int r = i % kBgRawStages;
         if (*abort_flag) break;
-        if (i >= kBgRawStages && !bg_wait(&raw_empty[r], (uint32_t)((i / kBgRawStages - 1) & 1), err, abort_flag))
+        if (i >= kBgRawStages && !bg_wait_nap(&raw_empty[r], (uint32_t)((i / kBgRawStages - 1) & 1), err, abort_flag))
           break;
         uint8_t* dst = smem + BgSmem::kRaw + r * kBgRawStride;
         mbar_arrive_expect_tx(&raw_full[r], kTx);
@@ -431,7 +451,8 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemv_tc(const __grid_constan
       for (int gi = 0; gi < ng; ++gi) {
         const int bs = gi & (kBgBSlots - 1);
         if (*abort_flag) break;
-        if (gi >= kBgBSlots && !bg_wait(&b_empty[bs], (uint32_t)((gi / kBgBSlots - 1) & 1), err, abort_flag)) break;
+        if (gi >= kBgBSlots && !bg_wait_nap(&b_empty[bs], (uint32_t)((gi / kBgBSlots - 1) & 1), err, abort_flag))
+          break;
         const int cnt = n - gi * kBgBGroup < kBgBGroup ? n - gi * kBgBGroup : kBgBGroup;
         uint8_t* dst = smem + BgSmem::kB + bs * kBgBSlot;
         mbar_arrive_expect_tx(&b_full[bs], (uint32_t)(cnt * kBgBStep));
@@ -447,45 +468,54 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemv_tc(const __grid_constan
           mbar_wait_bounded(&b_full[gi & (kBgBSlots - 1)], (uint32_t)((gi / kBgBSlots) & 1), err, AH_ETIMEOUT,
                             kBgWait);
     }
-  } else if (warp == 2) {
-    // ---- MMA issuer: one thread; its loop is the kernel's critical path ----
+  } else if (warp == 2 || warp >= kBgIssuerWarp1) {
+    // ---- MMA issuers: issuer t takes the steps i with i % kBgIssuers == t ----
     if (lane == 0) {
-      int seg = 0, a = 0;
-      uint32_t a_ph = 0;
-      int64_t ks = start % S;
+      const int t = warp == 2 ? 0 : warp - kBgIssuerWarp1 + 1;
       const uint64_t bdesc0 = sw128_desc(smem_u32(smem + BgSmem::kB));
-      for (int i = 0; i < n; ++i) {
-        const bool first = i == 0 || ks == 0;
-        const bool last = i == n - 1 || ks == S - 1;
-        const int gi = i / kBgBGroup, bs = gi & (kBgBSlots - 1);
-        if (*abort_flag) break;
+      int64_t ks0 = start % S;
+      bool ok = true;
+      for (int i0 = 0, seg = 0; ok && i0 < n; ++seg) {
+        const int len = (int)(S - ks0 < (int64_t)(n - i0) ? S - ks0 : (int64_t)(n - i0));
         // the epilogue has read this accumulator buffer's previous segment
-        if (first && seg >= 2 && !bg_wait(&acc_empty[seg & 1], (uint32_t)(((seg >> 1) - 1) & 1), err, abort_flag))
-          break;
-        if ((i & (kBgBGroup - 1)) == 0 && !bg_wait(&b_full[bs], (uint32_t)((gi / kBgBSlots) & 1), err, abort_flag))
-          break;
-        if (!bg_wait(&a_full[a], a_ph, err, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t acc = tmem + (uint32_t)((seg & 1) * kBgAccStride);
-        const uint32_t ta = tmem + (uint32_t)(kBgACol0 + a * kBgACols);
-        // descriptor start addresses count 16-byte units
-        const uint64_t bd = bdesc0 + (uint64_t)((bs * kBgBSlot + (i & (kBgBGroup - 1)) * kBgBStep) >> 4);
+        if (seg >= 2 && !bg_wait(&acc_empty[seg & 1], (uint32_t)(((seg >> 1) - 1) & 1), err, abort_flag)) break;
+        const uint32_t acc = tmem + (uint32_t)(((seg & 1) * kBgIssuers + t) * kBgN);
+        bool first = true;
+        for (int i = i0 + (t - i0 % kBgIssuers + kBgIssuers) % kBgIssuers; i < i0 + len; i += kBgIssuers) {
+          const int a = i % kBgAStages;
+          const int gi = i / kBgBGroup, bs = gi & (kBgBSlots - 1);
+          // another role's give-up also shows as this thread's own bounded wait failing
+          if ((i & 15) < kBgIssuers && *abort_flag) {
+            ok = false;
+            break;
+          }
+          // the slot's token tiles: waited for at this issuer's first step of the slot
+          if (i % kBgBGroup < kBgIssuers && !bg_wait(&b_full[bs], (uint32_t)((gi / kBgBSlots) & 1), err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (!bg_wait(&a_full[a], (uint32_t)((i / kBgAStages) & 1), err, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ta = tmem + (uint32_t)(kBgACol0 + a * kBgACols);
+          // descriptor start addresses count 16-byte units
+          const uint64_t bd = bdesc0 + (uint64_t)((bs * kBgBSlot + (i % kBgBGroup) * kBgBStep) >> 4);
 #pragma unroll
-        for (int m = 0; m < kBgPairs * 4; ++m)
-          mma_f16_ts(acc + (uint32_t)((m % kBgAccSets) * kBgN), ta + (uint32_t)((m >> 2) * 32 + (m & 3) * 8),
-                     bd + (uint64_t)(((m >> 2) * kBgBPair + (m & 3) * 32) >> 4), kBgIdesc,
-                     (!first || m >= kBgAccSets) ? 1u : 0u);
-        mma_commit(&a_empty[a]);
-        if ((i & (kBgBGroup - 1)) == kBgBGroup - 1 || i == n - 1) mma_commit(&b_empty[bs]);
-        if (last) {
-          mma_commit(&acc_full[seg & 1]);
-          ++seg;
+          for (int m = 0; m < kBgPairs * 4; ++m)
+            mma_f16_ts(acc, ta + (uint32_t)((m >> 2) * 32 + (m & 3) * 8),
+                       bd + (uint64_t)(((m >> 2) * kBgBPair + (m & 3) * 32) >> 4), kBgIdesc,
+                       (!first || m > 0) ? 1u : 0u);
+          first = false;
+          mma_commit(&a_empty[a]);
+          // this issuer's last step of the slot (or of the CTA's range)
+          if (i % kBgBGroup == kBgBGroup - kBgIssuers + t || i + kBgIssuers >= n) mma_commit(&b_empty[bs]);
         }
-        if (++a == kBgAStages) {
-          a = 0;
-          a_ph ^= 1u;
-        }
-        if (++ks == S) ks = 0;
+        // arrives once this issuer's MMAs of the segment are done (at once if it had none)
+        mma_commit(&acc_full[seg & 1]);
+        i0 += len;
+        ks0 = 0;
       }
       // completes when every MMA above has (also on abort, so TMEM can be freed)
       mma_commit(mma_done);
@@ -503,9 +533,10 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemv_tc(const __grid_constan
         if (*abort_flag) {
           ok = false;
         } else {
-          ok = bg_wait(&raw_full[r], (uint32_t)((i / kBgRawStages) & 1), err, abort_flag);
+          ok = bg_wait_nap(&raw_full[r], (uint32_t)((i / kBgRawStages) & 1), err, abort_flag);
           // the MMAs that read this A stage last time have completed
-          if (ok && i >= kBgAStages) ok = bg_wait(&a_empty[a], (uint32_t)((i / kBgAStages - 1) & 1), err, abort_flag);
+          if (ok && i >= kBgAStages)
+            ok = bg_wait_nap(&a_empty[a], (uint32_t)((i / kBgAStages - 1) & 1), err, abort_flag);
         }
       }
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
@@ -564,7 +595,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemv_tc(const __grid_constan
         mbar_arrive(&a_full[a]);
       }
     }
-  } else {
+  } else if (warp < kBgEpiWarp0 + 4) {
     // ---- epilogue: accumulator -> outputs (or a stream-K partial) ----
     const int q = warp & 3;
     pdl_wait();  // row_inv, the counters and y follow the preceding grids
@@ -582,13 +613,17 @@ __global__ void __launch_bounds__(kBgThreads, 1) k_bgemv_tc(const __grid_constan
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
       tc_fence_after();
+      // issuer t has a step in the segment [i, i + len) iff (t - i) mod
+      // kBgIssuers < len; the accumulators are added in issuer order
       float v[kBgN];
-      const uint32_t tacc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((seg & 1) * kBgAccStride);
-      tmem_ld16(tacc, v);
 #pragma unroll
-      for (int j = 1; j < kBgAccSets; ++j) {
+      for (int b = 0; b < kBgN; ++b) v[b] = 0.0f;
+      const uint32_t tacc = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((seg & 1) * kBgIssuers * kBgN);
+#pragma unroll
+      for (int t = 0; t < kBgIssuers; ++t) {
+        if ((t - i % kBgIssuers + kBgIssuers) % kBgIssuers >= len) continue;  // warp-uniform
         float w[kBgN];
-        tmem_ld16(tacc + (uint32_t)(j * kBgN), w);
+        tmem_ld16(tacc + (uint32_t)(t * kBgN), w);
 #pragma unroll
         for (int b = 0; b < kBgN; ++b) v[b] += w[b];
       }

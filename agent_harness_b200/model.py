@@ -160,8 +160,9 @@ class Model:
         call("ah_model_set_prefill", self._h, mode)
 
     def set_batched_gemv(self, min_batch: int):
-        """Decode steps of at least min_batch sequences (default 9) run their
-        GEMVs on the tcgen05 batched GEMV; 1 always, 17 never."""
+        """Decode steps of at least min_batch sequences (default 9) run each
+        projection on the tcgen05 batched GEMV where it is the faster one
+        (large enough weights for the batch); 1: every projection, 17: never."""
         call("ah_model_set_batched_gemv", self._h, min_batch)
 
     @property

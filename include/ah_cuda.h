@@ -349,10 +349,13 @@ AH_API int ah_model_generate(AhModel* m, const int32_t* prompt, int batch, int n
  * decode step; mode 0: token by token, as the reference.  Both leave the same
  * state (KV cache, position) up to rounding. */
 AH_API int ah_model_set_prefill(AhModel* m, int mode);
-/* Which GEMV the decode steps use (no reference counterpart): steps of at
- * least `min_batch` sequences (default 9) run every projection on the tcgen05
- * batched GEMV (ah_q4w_gemv_tc precision: f16 operands, f32 accumulation),
- * smaller ones on the mma.sync GEMV (ah_q4w_gemv).  1 always, 17 never. */
+/* Which GEMV the decode steps use (no reference counterpart): in steps of at
+ * least `min_batch` sequences (default 9) a projection runs on the tcgen05
+ * batched GEMV (ah_q4w_gemv_tc precision: f16 operands, f32 accumulation)
+ * where that is the faster one -- from 20 MB of Q4 weights at 9-10 sequences,
+ * 11 MB at 11-12, 5 MB at 13-16 -- and on the mma.sync GEMV (ah_q4w_gemv)
+ * otherwise.  1: every projection of every step on the tcgen05 GEMV; 17:
+ * never. */
 AH_API int ah_model_set_batched_gemv(AhModel* m, int min_batch);
 /* Lower-level stepping (same semantics): reset, feed one token per sequence
  * (forward(), inference/mod.rs:333-545) and read the logits [batch][vocab]. */

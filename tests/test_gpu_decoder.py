@@ -192,8 +192,9 @@ def test_batch16_long_context_attention(cuda, oracle):
 
 @pytest.mark.parametrize("tp_like", [False, True])
 def test_batch16_tensor_core_gemv_path(cuda, oracle, tp_like):
-    # the batched decode GEMVs (tcgen05, default from 9 sequences) against the
-    # oracle and against the mma.sync GEMVs (min_batch 17) on the same model:
+    # the batched decode GEMVs (tcgen05; min_batch 1 forces them for every
+    # projection) against the oracle and against the mma.sync GEMVs (min_batch
+    # 17) on the same model:
     # logits within 1e-3 of each other, greedy tokens identical.  tp_like has
     # an odd block-pair count in the down projection (FFN 1088), head_dim 128
     # with 4 query heads per kv head, and a partial last row block in the LM
@@ -211,7 +212,7 @@ def test_batch16_tensor_core_gemv_path(cuda, oracle, tp_like):
     prompt = np.random.default_rng(9).integers(0, cfg.vocab_size, (16, 4)).astype(np.int32)
     om = [oracle_model(oracle, cfg, W) for _ in range(16)]
     runs = {}
-    for mb in (9, 17):
+    for mb in (1, 17):
         m.set_batched_gemv(mb)
         m.reset(16)
         lgs = []
@@ -221,13 +222,33 @@ def test_batch16_tensor_core_gemv_path(cuda, oracle, tp_like):
     for t in range(prompt.shape[1]):
         for b in range(16):
             ref = om[b].forward(int(prompt[b, t]), t)
-            assert relerr(runs[9][t][b], ref) <= TOL, (t, b, relerr(runs[9][t][b], ref))
-            assert relerr(runs[9][t][b], runs[17][t][b]) <= TOL
-    m.set_batched_gemv(9)
+            assert relerr(runs[1][t][b], ref) <= TOL, (t, b, relerr(runs[1][t][b], ref))
+            assert relerr(runs[1][t][b], runs[17][t][b]) <= TOL
+    m.set_batched_gemv(1)
     g_tc = m.generate(prompt, 6)
     m.set_batched_gemv(17)
     g_ms = m.generate(prompt, 6)
-    assert np.array_equal(g_tc, g_ms)
+    # greedy paths may part only at a near-tie: replay the mma.sync trajectory
+    # and check, at each sequence's first divergence, that the two candidates'
+    # logits are within 2e-3 of max|logit|
+    m.reset(16)
+    for t in range(prompt.shape[1]):
+        lg = m.forward(prompt[:, t]).cpu().numpy()
+    logs = [lg]
+    for j in range(g_ms.shape[0] - 1):
+        logs.append(m.forward(g_ms[j]).cpu().numpy())
+    diverged = 0
+    for b in range(16):
+        diff = np.nonzero(g_tc[:, b] != g_ms[:, b])[0]
+        if diff.size == 0:
+            continue
+        diverged += 1
+        j = int(diff[0])
+        l = logs[j][b]
+        assert g_ms[j, b] == int(np.argmax(l))
+        gap = float(l[g_ms[j, b]] - l[g_tc[j, b]])
+        assert 0.0 <= gap <= 2e-3 * float(np.max(np.abs(l))), (b, j, gap)
+    assert diverged <= 4, diverged
     m.close()
 
 
