@@ -100,3 +100,77 @@ def test_tp2_matches_single_gpu(cuda, p2p):
     assert np.array_equal(gl0, gl1) and np.array_equal(gl0, gen1_long)
     full = np.concatenate([la0, la1], axis=1)
     assert np.max(np.abs(full - last1)) / np.max(np.abs(last1)) <= 1e-3
+
+
+# batch 16 with every projection on the tcgen05 batched GEMV (min_batch 1):
+# the o / down projections' peer-store epilogue (nvlink_peer) or their NCCL
+# all-reduce, at widths whose row blocks several CTAs share (stream-K)
+WIDE = dict(n_layer=2, n_embd=1024, n_ff=2048, n_head=8, n_head_kv=2, head_dim=128, vocab_size=1000, max_seq=32,
+            max_batch=16, rope_freq_base=10000.0, rms_eps=1e-5)
+PROMPT16 = (np.arange(16 * 5, dtype=np.int32).reshape(16, 5) * 53 + 7) % 1000
+
+
+def _rank16(rank, world, port, q, p2p):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from agent_harness_b200 import _lib
+        from agent_harness_b200.model import Model, ModelConfig, nccl_unique_id
+        _lib.check(_lib.lib().ah_device_init(rank))
+        ids = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(ids, src=0)
+        m = Model(ModelConfig(**WIDE), device=f"cuda:{rank}", tp_rank=rank, tp_world=world, nccl_id=ids[0])
+        m.init_random(77)
+        m.set_batched_gemv(1)
+        if p2p:
+            def allgather(blob):
+                out = [None] * world
+                dist.all_gather_object(out, blob)
+                return out
+            m.enable_peer_allreduce(allgather)
+        m.reset(16)
+        logits = [m.forward(PROMPT16[:, t]).cpu().numpy() for t in range(PROMPT16.shape[1])]
+        gen = m.generate(PROMPT16, 4)
+        torch.cuda.synchronize()
+        err = _lib.lib().ah_check_device_error(None)
+        m.close()
+        q.put((rank, logits, gen, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "nvlink_peer"])
+def test_tp2_batch16_tensor_core_gemv(cuda, p2p):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank16, args=(r, 2, port, q, p2p)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r, lg, gen, err = q.get(timeout=600)
+        res[r] = (lg, gen, err)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res[0][2] == 0 and res[1][2] == 0
+    from agent_harness_b200.model import Model, ModelConfig
+    m = Model(ModelConfig(**WIDE), device="cuda:0")
+    m.init_random(77)
+    m.set_batched_gemv(1)
+    m.reset(16)
+    for t in range(PROMPT16.shape[1]):
+        ref = m.forward(PROMPT16[:, t]).cpu().numpy()
+        full = np.concatenate([res[0][0][t], res[1][0][t]], axis=1)
+        for b in range(16):
+            err = np.max(np.abs(full[b] - ref[b])) / np.max(np.abs(ref[b]))
+            assert err <= 1e-3, (t, b, err)
+    m.close()
+    # the ranks merge their argmax candidates: identical tokens on both
+    assert np.array_equal(res[0][1], res[1][1])
