@@ -110,7 +110,8 @@ constexpr int kBgIssuerWarp1 = 15;
 constexpr int kBgThreads = (kBgIssuerWarp1 + kBgIssuers - 1) * 32;
 constexpr uint32_t kBgWait = 1u << 24;
 constexpr uint32_t kBgIdesc = idesc_f16(kBgM, kBgN);
-constexpr int kBgPrepThreads = 256;
+constexpr int kBgPrepThreads = 512;
+constexpr int64_t kBgPrepStageMaxK = 50176;           // f32 row staging: 196 KB of shared memory
 
 struct BgSmem {
   static constexpr int kRaw = 0;
@@ -146,8 +147,13 @@ __host__ __device__ __forceinline__ int bg_kperm(int km) {
 
 // ---- token prep: f32 rows (optionally RMSNorm'ed) -> scaled, pair-permuted f16 ----
 // grid 16 (one CTA per token row; rows past the batch are zero).  Also zeroes
-// the stream-K counters of the GEMV that follows.
-template <int PRO>
+// the stream-K counters of the GEMV that follows.  kStage: the row is read once
+// (16-byte loads, several in flight per thread), normalised into shared memory
+// as f32, and the permuted f16 tiles are written from there; rows longer than
+// kBgPrepStageMaxK are read twice from global memory instead.  The GEMV's MMAs
+// wait for this grid, so its latency is on every decode GEMV's critical path
+// (the first, scalar version took ~12 us per call at K = 8192).
+template <int PRO, bool kStage>
 __global__ void __launch_bounds__(kBgPrepThreads) k_bgemv_prep(const GemvArgs a, int64_t kp, uint8_t* __restrict__ xt,
                                                                 float* __restrict__ row_inv, int* __restrict__ counter,
                                                                 int n_counter) {
@@ -155,10 +161,11 @@ __global__ void __launch_bounds__(kBgPrepThreads) k_bgemv_prep(const GemvArgs a,
   pdl_launch_dependents();
   // x, the sums of squares, xt and the counters belong to earlier kernels
   pdl_wait();
+  extern __shared__ float stage[];  // kStage: [kp * 64] normalised row
   const int b = blockIdx.x, tid = threadIdx.x;
   for (int i = b * kBgPrepThreads + tid; i < n_counter; i += kBgN * kBgPrepThreads) counter[i] = 0;
   const bool live = b < a.batch;
-  const int64_t K = a.w.cols;
+  const int64_t K = a.w.cols, kpad = kp * 64;
   const float* row = a.x + (live ? b : 0) * a.x_stride;
   __shared__ float red[kBgPrepThreads / 32];
   __shared__ float s_inv;
@@ -187,10 +194,41 @@ __global__ void __launch_bounds__(kBgPrepThreads) k_bgemv_prep(const GemvArgs a,
     return v;
   };
   float amax = 0.0f;
-  for (int64_t k = tid; k < K; k += kBgPrepThreads) amax = fmaxf(amax, fabsf(xv(k)));
+  if (kStage) {
+    const bool vec = live && (reinterpret_cast<uintptr_t>(row) & 15) == 0 && (K & 3) == 0 &&
+                     (PRO != kProRmsNorm || (reinterpret_cast<uintptr_t>(a.norm_w) & 7) == 0);
+    if (vec) {
+      float4* st4 = reinterpret_cast<float4*>(stage);
+#pragma unroll 4
+      for (int64_t c = tid; c < kpad / 4; c += kBgPrepThreads) {
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (c * 4 < K) {
+          v = __ldg(reinterpret_cast<const float4*>(row) + c);
+          if (PRO == kProRmsNorm) {
+            const uint2 nw = __ldg(reinterpret_cast<const uint2*>(a.norm_w) + c);
+            v.x = (v.x * inv) * __half2float(__ushort_as_half((unsigned short)(nw.x & 0xFFFFu)));
+            v.y = (v.y * inv) * __half2float(__ushort_as_half((unsigned short)(nw.x >> 16)));
+            v.z = (v.z * inv) * __half2float(__ushort_as_half((unsigned short)(nw.y & 0xFFFFu)));
+            v.w = (v.w * inv) * __half2float(__ushort_as_half((unsigned short)(nw.y >> 16)));
+          }
+        }
+        amax = fmaxf(fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+        st4[c] = v;
+      }
+    } else {
+#pragma unroll 4
+      for (int64_t k = tid; k < kpad; k += kBgPrepThreads) {
+        const float v = xv(k);
+        amax = fmaxf(amax, fabsf(v));
+        stage[k] = v;
+      }
+    }
+  } else {
+    for (int64_t k = tid; k < K; k += kBgPrepThreads) amax = fmaxf(amax, fabsf(xv(k)));
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-  __syncthreads();  // red[] is reused
+  __syncthreads();  // red[] is reused; the staged row is complete
   if ((tid & 31) == 0) red[tid >> 5] = amax;
   __syncthreads();
   amax = red[0];
@@ -214,8 +252,9 @@ __global__ void __launch_bounds__(kBgPrepThreads) k_bgemv_prep(const GemvArgs a,
     uint32_t h[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const __half2 v = __floats2half2_rn(xv(base + bg_kperm(km0 + 2 * i)) * scale,
-                                          xv(base + bg_kperm(km0 + 2 * i + 1)) * scale);
+      const int64_t k0 = base + bg_kperm(km0 + 2 * i), k1 = base + bg_kperm(km0 + 2 * i + 1);
+      const float v0 = kStage ? stage[k0] : xv(k0), v1 = kStage ? stage[k1] : xv(k1);
+      const __half2 v = __floats2half2_rn(v0 * scale, v1 * scale);
       h[i] = *reinterpret_cast<const uint32_t*>(&v);
     }
     out[c] = make_uint4(h[0], h[1], h[2], h[3]);
@@ -693,7 +732,28 @@ int bg_attr_epi(bool f32) {
   return f32 ? bg_attr<EPI, true>() : bg_attr<EPI, false>();
 }
 
+// The staged prep kernels' shared-memory cap (the row as f32), once per device.
+int bg_prep_attr() {
+  constexpr int kMaxDevices = 64;
+  static std::once_flag once[kMaxDevices];
+  static cudaError_t set_rc[kMaxDevices];
+  int dev = 0;
+  AH_CUDA_TRY(cudaGetDevice(&dev));
+  AH_REQUIRE(dev >= 0 && dev < kMaxDevices, "bgemv: device %d out of range", dev);
+  std::call_once(once[dev], [&] {
+    const int bytes = (int)(kBgPrepStageMaxK * 4);
+    set_rc[dev] = cudaFuncSetAttribute(k_bgemv_prep<kProPlain, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (set_rc[dev] == cudaSuccess)
+      set_rc[dev] =
+          cudaFuncSetAttribute(k_bgemv_prep<kProRmsNorm, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
+  if (set_rc[dev] != cudaSuccess)
+    return fail(AH_ECUDA, "bgemv: prep cudaFuncSetAttribute: %s", cudaGetErrorString(set_rc[dev]));
+  return AH_OK;
+}
+
 int bg_attr_any(int epi, bool f32) {
+  AH_TRY_BG(bg_prep_attr());
   if (epi == kEpiStore) return bg_attr_epi<kEpiStore>(f32);
   if (epi == kEpiAdd) return bg_attr_epi<kEpiAdd>(f32);
   return bg_attr_epi<kEpiSwiglu>(f32);
@@ -745,10 +805,16 @@ int bgemv_launch(const GemvArgs& a, int pro, int epi, void* ws, size_t ws_bytes,
   int64_t kp = a.w.kp;
   int n_counter = L.n_counter;
   void* prep_params[] = {&g, &kp, &xt, &row_inv, &counter, &n_counter};
-  const void* prep = pro == kProRmsNorm ? reinterpret_cast<const void*>(k_bgemv_prep<kProRmsNorm>)
-                                        : reinterpret_cast<const void*>(k_bgemv_prep<kProPlain>);
+  const bool stage = kp * 64 <= kBgPrepStageMaxK;
+  const void* prep =
+      pro == kProRmsNorm
+          ? (stage ? reinterpret_cast<const void*>(k_bgemv_prep<kProRmsNorm, true>)
+                   : reinterpret_cast<const void*>(k_bgemv_prep<kProRmsNorm, false>))
+          : (stage ? reinterpret_cast<const void*>(k_bgemv_prep<kProPlain, true>)
+                   : reinterpret_cast<const void*>(k_bgemv_prep<kProPlain, false>));
+  const size_t prep_smem = stage ? (size_t)kp * 64 * 4 : 0;
   if (inject_failure(AH_INJECT_LAUNCH)) return fail(AH_ECUDA, "bgemv: kernel launch failed (injected)");
-  AH_TRY_BG(launch_ex(prep, dim3(kBgN), dim3(kBgPrepThreads), 0, st, pdl, prep_params));
+  AH_TRY_BG(launch_ex(prep, dim3(kBgN), dim3(kBgPrepThreads), prep_smem, st, pdl, prep_params));
 
   alignas(64) BgArgs p{};
   p.g = g;
