@@ -32,6 +32,7 @@ SIGNATURES = {
     "ah_device_alloc_count": (i64, []),
     "ah_debug_inject_failure": (i32, [i32, i64]),
     "ah_debug_residual_add_peer": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, vp]),
+    "ah_debug_tc_mma_rate": (i32, [i32, i32, vp]),
     "ah_packed_bytes": (i64, [i64]),
     "ah_n_groups": (i64, [i64, i64]),
     "ah_quantized_bytes": (i64, [i64, i64]),

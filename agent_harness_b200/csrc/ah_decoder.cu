@@ -1197,17 +1197,15 @@ bool use_bgemv(const AhModel* m) { return m->batch >= m->bg_min_batch; }
 // Whether a decode GEMV of this weight runs on the tcgen05 batched GEMV.  Its
 // time is set by the MMA rate (a 128-row x 16-column tile per ~56 ns per SM,
 // whatever the batch), the mma.sync GEMV's grows with the batch: measured on
-// the 70B projections and their tensor-parallel slices, the tcgen05 kernel
-// wins from 20 MB of Q4 weights at 9-10 sequences (K >= 4096), 11 MB at 11-12
-// (K >= 4096) and 5 MB at 13-16 (K >= 2048; shorter rows leave too few steps
-// per row block).  min_batch 1 forces it for every GEMV.
+// the 70B projections and their tensor-parallel slices (bench.py --workload
+// bgemv), the tcgen05 kernel wins from 20 MB of Q4 weights at 9-12 sequences
+// (K >= 4096) and from 5 MB at 13-16 (K >= 2048; shorter rows leave too few
+// steps per row block).  min_batch 1 forces it for every GEMV.
 bool bgemv_pays(const AhModel* m, const Q4Tiled& w) {
   if (!use_bgemv(m)) return false;
   if (m->bg_min_batch <= 1) return true;
   const double mb = (double)w.rows * (double)w.cols * 18.0 / 32.0 / 1e6;
-  const int B = m->batch;
-  if (B >= 13) return mb >= 5.0 && w.cols >= 2048;
-  if (B >= 11) return mb >= 11.0 && w.cols >= 4096;
+  if (m->batch >= 13) return mb >= 5.0 && w.cols >= 2048;
   return mb >= 20.0 && w.cols >= 4096;
 }
 

@@ -853,6 +853,74 @@ def dedup_cpu_baseline(n=1 << 21):
             "sample": f"{n} elements: oracle compress(pd 2, 2 rounds), then decompress_all + quantize timed"}
 
 
+def mma_rate():
+    """Cost of one tcgen05.mma (kind::f16, K = 16) by N and form, from 256
+    back-to-back MMAs on one SM (ah_debug_tc_mma_rate)."""
+    import ctypes as C
+    from agent_harness_b200 import _lib
+    rows = []
+    names = {0: "1-CTA, A in shared memory, M=64", 1: "1-CTA, A in tensor memory, M=128",
+             2: "CTA pair, A in tensor memory, M=256"}
+    for mode, ns in ((1, (16, 32, 64, 128, 256)), (0, (16, 64, 256)), (2, (32, 64, 128, 256))):
+        for n in ns:
+            out = (C.c_longlong * 3)()
+            for _ in range(3):
+                _lib.call("ah_debug_tc_mma_rate", mode, n, C.cast(out, C.c_void_p))
+            rows.append({"form": names[mode], "n": n, "issue_cycles": round(out[0] / 256, 1),
+                         "complete_cycles": round(out[1] / 256, 1), "ns_per_mma": round(out[2] / 256, 1),
+                         "sm_mhz": round(1e3 * out[1] / max(out[2], 1))})
+    return rows
+
+
+def bgemv_shapes(dev):
+    """The batched tcgen05 GEMV (ah_q4w_gemv_tc) against the mma.sync GEMV
+    (ah_q4w_gemv) on the 70B projections and their tensor-parallel slices at
+    batches 9, 12 and 16: per-call device time over back-to-back calls on
+    rotating weight copies (>= 600 MB streamed per pass, larger than L2)."""
+    import torch
+    from agent_harness_b200 import kernels as K
+    shapes = []
+    for tp in (1, 2, 4, 8):
+        shapes += [(tp, "qkv", 10240 // tp, 8192), (tp, "o", 8192, 8192 // tp), (tp, "gate_up", 57344 // tp, 8192),
+                   (tp, "down", 8192, 28672 // tp), (tp, "lm_head", 128256 // tp, 8192)]
+    rows = []
+    for tp, name, r, c in shapes:
+        blocks = K.synth_q4_0(r, c, 0.02, 1, device=dev)
+        ncopy = max(1, 600_000_000 // (r * c * 9 // 16))
+        Ws = [K.Q4Weight.from_q4_0(blocks, r, c) for _ in range(ncopy)]
+        del blocks
+        wb = Ws[0].weight_bytes
+        ws = torch.empty(Ws[0].gemv_tc_workspace_bytes() + 1024, dtype=torch.uint8, device=dev)
+        for B in (16, 12, 9):
+            x = K.fill_normal(B * c, 0.0, 1.0, 2, device=dev).reshape(B, c)
+            y = torch.empty(B, r, device=dev)
+            t = {}
+            for impl in ("tc", "mma"):
+                def run(W):
+                    if impl == "tc":
+                        W.gemv_tc(x, out=y, workspace=ws)
+                    else:
+                        W.gemv(x, out=y)
+                for W in Ws:
+                    run(W)
+                torch.cuda.synchronize()
+                reps = max(1, 40 // ncopy)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    for W in Ws:
+                        run(W)
+                e1.record()
+                torch.cuda.synchronize()
+                t[impl] = e0.elapsed_time(e1) * 1e3 / (reps * ncopy)
+            rows.append({"tp": tp, "weight": name, "rows": r, "cols": c, "batch": B, "tc_us": round(t["tc"], 1),
+                         "mma_us": round(t["mma"], 1), "tc_gbs": round(wb / t["tc"] / 1e3),
+                         "mma_gbs": round(wb / t["mma"] / 1e3)})
+        for W in Ws:
+            W.close()
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -860,9 +928,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only")
-    ap.add_argument("--workload", default="gemv", choices=["gemv", "decode", "gemm", "tp", "load", "ssm"],
+    ap.add_argument("--workload", default="gemv",
+                    choices=["gemv", "decode", "gemm", "tp", "load", "ssm", "bgemv", "mma-rate"],
                     help="decode / gemm / tp / load: only the 8B decode, the prefill GEMM, the 70B tensor-parallel "
-                         "decode or the DedupCount load-path measurement (for profiling)")
+                         "decode or the DedupCount load-path measurement (for profiling); bgemv: the batched "
+                         "decode GEMVs on the 70B shapes; mma-rate: the tcgen05.mma cost table")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
@@ -878,6 +948,15 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload in ("bgemv", "mma-rate"):
+        import torch
+        torch.cuda.set_device(0)
+        from agent_harness_b200 import _lib
+        _lib.check(_lib.lib().ah_device_init(0))
+        rows = mma_rate() if args.workload == "mma-rate" else bgemv_shapes(torch.device("cuda", 0))
+        for r in rows:
+            print(json.dumps({"workload": args.workload, **r}), flush=True)
+        return 0
     if args.workload == "ssm":
         import torch
         torch.cuda.set_device(0)

@@ -80,6 +80,13 @@ AH_API int ah_debug_inject_failure(int kind, int64_t nth);
  * is left as it was.  For tests of the bounded wait on one GPU. */
 AH_API int ah_debug_residual_add_peer(float* hidden, const float* slots, int world, int batch, int d, float* ss,
                                       const unsigned* flags, const unsigned* seq, void* stream);
+/* Diagnostic (no reference counterpart): times 256 back-to-back tcgen05.mma
+ * (kind::f16, K = 16, one accumulator) on one SM -- mode 0: A from shared
+ * memory, M = 64; mode 1: A from tensor memory, M = 128; mode 2: the CTA-pair
+ * form, M = 256 over two SMs (N a multiple of 32).  out_host[0] = issue
+ * cycles, [1] = cycles to completion, [2] = nanoseconds to completion.  The
+ * batched decode GEMV's design rests on these costs. */
+AH_API int ah_debug_tc_mma_rate(int mode, int n, long long* out_host);
 
 /* ---- sizes (models/quantization.rs:423-435) -------------------------------- */
 AH_API int64_t ah_packed_bytes(int64_t n_elements);
@@ -352,8 +359,8 @@ AH_API int ah_model_set_prefill(AhModel* m, int mode);
 /* Which GEMV the decode steps use (no reference counterpart): in steps of at
  * least `min_batch` sequences (default 9) a projection runs on the tcgen05
  * batched GEMV (ah_q4w_gemv_tc precision: f16 operands, f32 accumulation)
- * where that is the faster one -- from 20 MB of Q4 weights at 9-10 sequences,
- * 11 MB at 11-12, 5 MB at 13-16 -- and on the mma.sync GEMV (ah_q4w_gemv)
+ * where that is the faster one -- from 20 MB of Q4 weights at 9-12 sequences,
+ * 5 MB at 13-16 -- and on the mma.sync GEMV (ah_q4w_gemv)
  * otherwise.  1: every projection of every step on the tcgen05 GEMV; 17:
  * never. */
 AH_API int ah_model_set_batched_gemv(AhModel* m, int min_batch);

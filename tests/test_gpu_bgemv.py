@@ -151,3 +151,21 @@ def test_no_device_timeouts_recorded(cuda):
     from agent_harness_b200._lib import lib
     torch.cuda.synchronize()
     assert lib().ah_check_device_error(None) == 0
+
+
+def test_mma_rate_probe(cuda):
+    # the diagnostic behind the kernel's design: an M=128 MMA with A in tensor
+    # memory costs the same for N = 16 and N = 128 (within 10%), and issue
+    # waits for completion (issue time >= 80% of completion time)
+    import ctypes as C
+    from agent_harness_b200._lib import AhError, call
+    t = {}
+    for n in (16, 128):
+        out = (C.c_longlong * 3)()
+        call("ah_debug_tc_mma_rate", 1, n, C.cast(out, C.c_void_p))
+        assert out[0] > 0 and out[1] >= out[0] and out[2] > 0
+        assert out[0] >= 0.8 * out[1]
+        t[n] = out[1]
+    assert abs(t[16] - t[128]) <= 0.1 * t[128]
+    with pytest.raises(AhError):
+        call("ah_debug_tc_mma_rate", 2, 16, C.cast((C.c_longlong * 3)(), C.c_void_p))  # the pair form needs N >= 32
