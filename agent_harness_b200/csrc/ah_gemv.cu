@@ -454,20 +454,12 @@ __device__ __forceinline__ void split_x(const GemvArgs& a, uint8_t* xs, float4* 
   }
 }
 
-// kStage (batches of up to 4 tokens, one row group per CTA): thread 0
-// bulk-copies the CTA's whole weight share -- each row tile's np pairs of
-// nibbles and scales are contiguous runs -- into shared memory at launch, and
-// the main loop reads it from there.  Without the register-resident batches
-// the kernel fits 4 CTAs per SM, so the next GEMV's grid is resident, and its
-// weights in flight, while this one still runs: a 256-CTA grid at 2 CTAs per
-// SM left most of the next grid's CTAs to start (and request their weights)
-// only after this one had finished.
-template <int NT, bool kF32, int PRO, int EPI, bool kStage = false>
-__global__ void __launch_bounds__(kGemvThreads, kStage ? 4 : kGemvMinBlocks<NT>) k_gemv_q4(const GemvArgs a) {
+template <int NT, bool kF32, int PRO, int EPI>
+__global__ void __launch_bounds__(kGemvThreads, kGemvMinBlocks<NT>) k_gemv_q4(const GemvArgs a) {
   constexpr int BM = 4 * NT;  // tokens this instantiation can hold
   using SV = typename ScaleT<kF32>::V;
   constexpr int U = kGemvBatchPairs<NT>;  // block pairs per register batch
-  extern __shared__ __align__(16) uint8_t smem_all[];
+  extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int B = a.batch;
@@ -481,11 +473,6 @@ __global__ void __launch_bounds__(kGemvThreads, kStage ? 4 : kGemvMinBlocks<NT>)
   const int ppc = (int)a.pairs_per_chunk;
   const int kbc = 2 * ppc;          // blocks per chunk
   const int plane = kbc * 64 + 64;  // bytes per x plane (64 B pad staggers banks)
-  constexpr int kScB = kF32 ? 128 : 64;  // scale bytes per (row tile, pair)
-  // staged: [warps][ppc] x 512 B nibbles, then [warps][ppc] x kScB scales, then the mbarrier
-  const size_t wbytes = kStage ? (size_t)kGemvWarps * ppc * (512 + kScB) : 0;
-  uint8_t* smem = smem_all + (kStage ? wbytes + 16 : 0);
-  uint64_t* wbar = reinterpret_cast<uint64_t*>(smem_all + wbytes);
   uint8_t* xs = smem;                                                           // [2B][plane]
   float4* blk_info = reinterpret_cast<float4*>(smem + (size_t)2 * B * plane);  // [B][kbc+1]: rows padded
                                                                                 // so tokens hit different banks
@@ -506,23 +493,7 @@ __global__ void __launch_bounds__(kGemvThreads, kStage ? 4 : kGemvMinBlocks<NT>)
   const int64_t tile_scl = KP * 8 * kGemvWarps * n_cl;
   uint4 wa[U], wb[U];
   SV sa[U], sb[U];
-  if constexpr (kStage) {
-    if (tid == 0) {
-      mbar_init(wbar, 1);
-      fence_mbar_init();
-      uint32_t bytes = 0;
-      for (int w = 0; w < kGemvWarps; ++w)
-        if (rg * kGemvWarps + w < a.w.r16) bytes += (uint32_t)np * (512 + kScB);
-      mbar_arrive_expect_tx(wbar, bytes);
-      for (int w = 0; w < kGemvWarps; ++w) {
-        const int64_t rtw = rg * kGemvWarps + w;
-        if (rtw >= a.w.r16 || np == 0) continue;
-        bulk_g2s(smem_all + (size_t)w * ppc * 512, a.w.nib + (rtw * KP + p0) * 32, (uint32_t)np * 512, wbar);
-        bulk_g2s(smem_all + (size_t)kGemvWarps * ppc * 512 + (size_t)w * ppc * kScB,
-                 static_cast<const uint8_t*>(a.w.scales) + (rtw * KP + p0) * kScB, (uint32_t)np * kScB, wbar);
-      }
-    }
-  } else if (warp_live) {
+  if (warp_live) {
     load_pairs<kF32, U>(wa, sa, nibp, sclp, 0, np);
     load_pairs<kF32, U>(wb, sb, nibp, sclp, U, np);
   }
@@ -543,30 +514,11 @@ __global__ void __launch_bounds__(kGemvThreads, kStage ? 4 : kGemvMinBlocks<NT>)
 #pragma unroll
     for (int j = 0; j < NT; ++j) tot[j][0] = tot[j][1] = tot[j][2] = tot[j][3] = 0.0f;
     if (warp_live) {
-      if constexpr (kStage) {
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait_bounded(wbar, 0, a.err, 0x603);
-        if (__shfl_sync(0xFFFFFFFFu, ok, 0)) {
-          const uint8_t* wn = smem_all + (size_t)warp * ppc * 512 + lane * 16;
-          const SV* wsc =
-              reinterpret_cast<const SV*>(smem_all + (size_t)kGemvWarps * ppc * 512 + (size_t)warp * ppc * kScB) + g;
-          for (int p = 0; p < np; p += U) {
-#pragma unroll
-            for (int u = 0; u < U; ++u)
-              if (p + u < np) {
-                wa[u] = *reinterpret_cast<const uint4*>(wn + (size_t)(p + u) * 512);
-                sa[u] = wsc[(p + u) * 8];
-              }
-            mma_pairs<NT, kF32, U>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, 0);
-          }
-        }
-      } else {
-        for (int p = 0; p < np; p += 2 * U) {
-          mma_pairs<NT, kF32, U>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, 0);
-          if (p + 2 * U < np) load_pairs<kF32, U>(wa, sa, nibp, sclp, p + 2 * U, np);
-          mma_pairs<NT, kF32, U>(tot, wb, sb, p + U, np, B, g, t, xs, blk_info, plane, kbc, 0);
-          if (p + 3 * U < np) load_pairs<kF32, U>(wb, sb, nibp, sclp, p + 3 * U, np);
-        }
+      for (int p = 0; p < np; p += 2 * U) {
+        mma_pairs<NT, kF32, U>(tot, wa, sa, p, np, B, g, t, xs, blk_info, plane, kbc, 0);
+        if (p + 2 * U < np) load_pairs<kF32, U>(wa, sa, nibp, sclp, p + 2 * U, np);
+        mma_pairs<NT, kF32, U>(tot, wb, sb, p + U, np, B, g, t, xs, blk_info, plane, kbc, 0);
+        if (p + 3 * U < np) load_pairs<kF32, U>(wb, sb, nibp, sclp, p + 3 * U, np);
       }
     }
     // prefetch the next row group's first two batches while this one is reduced
@@ -575,7 +527,7 @@ __global__ void __launch_bounds__(kGemvThreads, kStage ? 4 : kGemvMinBlocks<NT>)
     const bool next_live = rg_next < n_rg && rt_next < a.w.r16;
     nibp += tile_nib;
     sclp += tile_scl;
-    if (!kStage && next_live) {
+    if (next_live) {
       load_pairs<kF32, U>(wa, sa, nibp, sclp, 0, np);
       load_pairs<kF32, U>(wb, sb, nibp, sclp, U, np);
     }
@@ -655,9 +607,6 @@ __global__ void __launch_bounds__(kGemvThreads, kStage ? 4 : kGemvMinBlocks<NT>)
     warp_live = next_live;
     ++iter;
   }
-  // staged: the bulk copies have landed before the CTA exits (also after a give-up)
-  if constexpr (kStage)
-    if (tid == 0) mbar_wait_bounded(wbar, 0, a.err, 0x603);
 }
 
 // Persistent full-K CTAs for GEMVs with many row tiles (FFN gate/up, the
@@ -826,20 +775,6 @@ using GemvKernel = void (*)(const GemvArgs);
 
 // Every prologue / epilogue for both scale formats: Q4_0 blocks (f16 scales)
 // and the engine format of quantize() (f32 scales).
-template <bool F>
-GemvKernel pick_staged(int pro, int epi) {
-#define AH_KS(P, E) k_gemv_q4<1, F, P, E, true>
-  if (pro == kProPlain) {
-    if (epi == kEpiStore) return AH_KS(kProPlain, kEpiStore);
-    if (epi == kEpiAdd) return AH_KS(kProPlain, kEpiAdd);
-    return AH_KS(kProPlain, kEpiSwiglu);
-  }
-  if (epi == kEpiStore) return AH_KS(kProRmsNorm, kEpiStore);
-  if (epi == kEpiAdd) return AH_KS(kProRmsNorm, kEpiAdd);
-  return AH_KS(kProRmsNorm, kEpiSwiglu);
-#undef AH_KS
-}
-
 template <int NT, bool kRows, bool F>
 GemvKernel pick_format(int pro, int epi) {
 #define AH_K(P, E) (kRows ? k_gemv_q4_rows<NT, F, P, E> : k_gemv_q4<NT, F, P, E>)
@@ -894,7 +829,6 @@ GemvPlan gemv_plan(const Q4Tiled& w, int batch) { return gemv_plan(w, batch, fal
 
 namespace {
 GemvKernel select_kernel(const GemvPlan& plan, bool f32s, int pro, int epi) {
-  if (plan.staged) return f32s ? pick_staged<true>(pro, epi) : pick_staged<false>(pro, epi);
   if (plan.rows_mode) {
     switch (plan.nt) {
       case 1: return pick_kernel<1, true>(f32s, pro, epi);
@@ -976,23 +910,6 @@ int choose_plan(const Q4Tiled& w, int batch, int pro, int epi, GemvPlan* plan, G
   int ccap = 0;
   AH_TRY_GEMV(kernel_setup(kc, pc, &ccap));
   const int64_t n_rg = (w.r16 + kGemvWarps - 1) / kGemvWarps;
-  // staged cluster mode: one n8 tile (batch <= 4), no K window, the CTA's
-  // share of at most kGemvStageMaxPairs block pairs, every row group in one wave
-  if (kp_window == 0 && pc.nt == 1 && pc.pairs_per_chunk <= kGemvStageMaxPairs && aligned16(w.nib) &&
-      aligned16(w.scales)) {
-    GemvPlan ps = pc;
-    ps.staged = true;
-    ps.smem = pc.smem + (size_t)kGemvWarps * pc.pairs_per_chunk * (512 + (w.f32_scales ? 128 : 64)) + 16;
-    GemvKernel ks = select_kernel(ps, w.f32_scales, pro, epi);
-    int scap = 0;
-    AH_TRY_GEMV(kernel_setup(ks, ps, &scap));
-    if (scap > 0 && n_rg <= scap) {
-      *plan = ps;
-      *kern = ks;
-      *cap = scap;
-      return AH_OK;
-    }
-  }
   GemvPlan pr = gemv_plan(w, batch, true);
   if (kp_window == 0 && n_rg > ccap && pr.smem_base <= (size_t)kGemvRowsSmem && pr.n_stages >= 2 && aligned16(w.nib) &&
       aligned16(w.scales)) {

@@ -50,10 +50,6 @@ constexpr int kGemvSmemLimit = 200 * 1024;
 constexpr int kGemvRowsSmem = 96 * 1024;   // rows mode only while x's split takes at most this much
 constexpr int kGemvRowsCtaSmem = 112 * 1024;  // rows mode: two CTAs (16 warps) per SM
 constexpr int kGemvMaxStages = 4;          // rows mode: row tiles in flight per CTA
-// Staged cluster mode: batches of up to 4 tokens whose per-CTA K-chunk is at
-// most this many block pairs (<= 46 KB of weights) copy the CTA's whole weight
-// share into shared memory at launch and run 4 CTAs per SM.
-constexpr int kGemvStageMaxPairs = 10;
 
 struct Q4Tiled {
   const uint4* nib;    // [r16][kp][32]

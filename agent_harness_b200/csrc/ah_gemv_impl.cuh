@@ -16,7 +16,6 @@ struct GemvPlan {
   bool rows_mode;           // persistent full-K CTAs instead of clusters
   size_t smem_base;         // rows mode: shared memory besides the tile stages
   int n_stages;             // rows mode: row tiles in flight (0: rows mode unavailable)
-  bool staged = false;      // cluster mode with each CTA's weight share bulk-copied into shared memory
 };
 
 GemvPlan gemv_plan(const Q4Tiled& w, int batch);
