@@ -33,6 +33,7 @@
 
 #include "ah_gemv_impl.cuh"
 #include "ah_prefill.cuh"
+#include "ah_sample.cuh"
 #include "ah_tma.cuh"
 
 using namespace ah;
@@ -967,6 +968,13 @@ struct AhModel {
   int bg_min_batch = kBgemvMinBatchDefault;
   void* bg_ws = nullptr;
   size_t bg_ws_bytes = 0;
+  // next-token choice: greedy (temperature 0, the default) or temperature +
+  // top-k sampling (inference/sampling.rs:17-64) seeded per (seed, position, sequence)
+  float samp_temp = 0.0f;
+  int samp_k = 40;
+  uint64_t samp_seed = 0;
+  SampleCand* samp_cand = nullptr;  // [max_batch][kSampleMaxK] this rank's candidates
+  SampleCand* samp_all = nullptr;   // [world][max_batch][kSampleMaxK] all ranks' (tensor parallel)
 };
 
 namespace {
@@ -1138,6 +1146,25 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     h.ss_in = m->ss;
     h.n_ss_in = d / 16;
     AH_TRY(step_gemv(m, h, kProRmsNorm, kEpiStore, st));
+  }
+  if (with_head && m->samp_temp > 0.0f) {
+    // temperature + top-k sampling (mod.rs:552-553): one kernel on one GPU;
+    // under tensor parallelism each rank's top-k of its vocab slice, an
+    // all-gather, and the same merge and draw on every rank
+    const int K = m->samp_k;
+    if (!tp) {
+      AH_TRY(sample_launch(m->logits, m->nvoc, B, m->nvoc, K, 0, m->samp_temp, m->samp_seed, 0, m->d_pos, nullptr,
+                           m->d_tok, m->tok_log, st, true));
+    } else {
+      AH_TRY(sample_launch(m->logits, m->nvoc, B, m->nvoc, K, (int64_t)m->tp_rank * m->nvoc, m->samp_temp,
+                           m->samp_seed, 0, m->d_pos, m->samp_cand, nullptr, nullptr, st, true));
+      if (ncclAllGather(m->samp_cand, m->samp_all, (size_t)B * K * sizeof(SampleCand), ncclUint8, m->comm, st) !=
+          ncclSuccess)
+        return fail(AH_ENCCL, "model: all-gather of the sampling candidates failed");
+      AH_TRY(sample_merge_launch(m->samp_all, m->tp_world, B, K, m->samp_temp, m->samp_seed, m->d_pos, m->d_tok,
+                                 m->tok_log, st));
+    }
+  } else if (with_head) {
     ArgPair* pair = tp ? static_cast<ArgPair*>(m->am_pair) : nullptr;
     AH_TRY(launch_pdl(k_argmax, dim3(kArgmaxChunks, B), dim3(256), 0, st, (const float*)m->logits, m->nvoc, m->am_v,
                       m->am_i, m->am_cnt, m->d_tok, m->tok_log, (const int*)m->d_pos, B, pair,
@@ -1813,6 +1840,27 @@ int ah_model_reset(AhModel* m, int batch, void* stream) {
   m->batch = batch;
   m->pos = 0;
   AH_CUDA_TRY(cudaMemsetAsync(m->d_pos, 0, 4, st));
+  return AH_OK;
+}
+
+int ah_model_set_sampling(AhModel* m, float temperature, int top_k, uint64_t seed) {
+  AH_REQUIRE(m, "model_set_sampling: null model");
+  AH_REQUIRE(!(temperature > 0.0f) || (top_k >= 1 && top_k <= kSampleMaxK),
+             "model_set_sampling: top_k must be 1..%d", kSampleMaxK);
+  AH_REQUIRE(m->tp_world <= kSampleMaxRanks, "model_set_sampling: more than %d ranks", kSampleMaxRanks);
+  if (temperature > 0.0f && !m->samp_cand) {
+    const size_t per = (size_t)m->c.max_batch * kSampleMaxK * sizeof(SampleCand);
+    AH_TRY(dalloc(m, (void**)&m->samp_cand, per));
+    AH_TRY(dalloc(m, (void**)&m->samp_all, per * m->tp_world));
+  }
+  m->samp_temp = temperature > 0.0f ? temperature : 0.0f;
+  m->samp_k = top_k;
+  m->samp_seed = seed;
+  // the captured steps hold the other head: capture again on the next step
+  for (int i = 0; i < 2; ++i) {
+    if (m->g_step[i]) cudaGraphExecDestroy(m->g_step[i]);
+    m->g_step[i] = nullptr;
+  }
   return AH_OK;
 }
 

@@ -288,6 +288,27 @@ def swiglu_4bit_into(out: torch.Tensor, x: torch.Tensor, gate_scales, gate_packe
     return out
 
 
+def sample_logits(logits: torch.Tensor, temperature: float, top_k: int = 40, seed: int = 0, step: int = 0,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """inference/sampling.rs:17-64 sample(row, temperature, top_k) for each row
+    of a [batch, vocab] f32 device tensor; the draw of row b is
+    sample_uniform(seed, step, b).  Returns int32 tokens [batch]."""
+    if logits.dim() == 1:
+        logits = logits.unsqueeze(0)
+    assert logits.dtype == torch.float32 and logits.stride(1) == 1
+    batch, vocab = logits.shape
+    if out is None:
+        out = torch.empty(batch, dtype=torch.int32, device=logits.device)
+    call("ah_sample_logits", _ptr(logits), logits.stride(0), batch, vocab, temperature, top_k, seed, step, _ptr(out),
+         _stream(logits.device))
+    return out
+
+
+def sample_uniform(seed: int, step: int, seq: int) -> float:
+    """The draw in [0, 1) that sample_logits uses for sequence seq at step."""
+    return lib().ah_sample_uniform(seed, step, seq)
+
+
 class SwigluBlock:
     """The feed-forward block on resident tiled weights, as the decoder runs it:
     gate and up interleaved in one weight (one GEMV whose epilogue writes

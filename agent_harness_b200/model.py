@@ -165,6 +165,13 @@ class Model:
         (large enough weights for the batch); 1: every projection, 17: never."""
         call("ah_model_set_batched_gemv", self._h, min_batch)
 
+    def set_sampling(self, temperature: float, top_k: int = 40, seed: int = 0):
+        """Next-token choice of generate/decode: temperature 0 is greedy
+        (sampling.rs:4-14); above 0 temperature + top-k sampling
+        (inference/mod.rs:552-553, sampling.rs:17-64) with the draw of
+        sequence b at position p = kernels.sample_uniform(seed, p, b)."""
+        call("ah_model_set_sampling", self._h, temperature, top_k, seed)
+
     @property
     def position(self) -> int:
         v = C.c_int(0)

@@ -538,6 +538,15 @@ def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW, n_layer=None):
     tokwise = m.generate(prompt[:, :256], 8)
     tok_s = time.perf_counter() - t1
     m.set_prefill(1)
+    # the same decode with temperature 0.8 + top-k 40 sampling in place of the argmax
+    m.set_sampling(0.8, 40, 1)
+    m.generate(prompt, 1)
+    e0.record(st)
+    m.decode(n_new + 1, 1)
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms_sampled = e0.elapsed_time(e1)
+    m.set_sampling(0.0)
     m.close()
     per_tok = ms / 1e3 / n_new
     gemm_flop = 2.0 * (n_prompt - 1) * DECODE_PROJ_WEIGHTS
@@ -554,6 +563,7 @@ def decode_8b(dev, n_prompt=DECODE_PROMPT, n_new=DECODE_NEW, n_layer=None):
             "weight_gbs": round(DECODE_BYTES_PER_TOKEN_WEIGHTS / per_tok / 1e9, 1),
             "n_prompt": n_prompt, "n_new": n_new, "n_layer": cfg.n_layer, "first_tokens": [int(first[0, 0])] + [int(v) for v in tk[1:6]],
             "deterministic": bool(np.array_equal(again, again2)),
+            "sampled_tokens_per_s": round(n_new / (ms_sampled / 1e3), 2),
             "note": "decode steps replayed as one CUDA graph each (5 fused kernels per layer + head + argmax)"}
 
 
@@ -872,6 +882,31 @@ def mma_rate():
     return rows
 
 
+def sample_rate(dev):
+    """Temperature + top-k sampling (ah_sample_logits, T 0.8, top-k 40) per
+    call over [batch][vocab] f32 logits: device time of back-to-back calls."""
+    import torch
+    from agent_harness_b200 import kernels as K
+    rows = []
+    for vocab in (128256, 32000):
+        for batch in (1, 16):
+            lg = K.fill_normal(batch * vocab, 0.0, 2.0, 3, device=dev).reshape(batch, vocab)
+            out = torch.empty(batch, dtype=torch.int32, device=dev)
+            for s in range(5):
+                K.sample_logits(lg, 0.8, 40, seed=1, step=s, out=out)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 200
+            e0.record()
+            for s in range(reps):
+                K.sample_logits(lg, 0.8, 40, seed=1, step=s, out=out)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            rows.append({"vocab": vocab, "batch": batch, "top_k": 40, "us_per_call": round(us, 2),
+                         "logit_gbs": round(batch * vocab * 4 / us / 1e3, 1)})
+    return rows
+
+
 def bgemv_shapes(dev):
     """The batched tcgen05 GEMV (ah_q4w_gemv_tc) against the mma.sync GEMV
     (ah_q4w_gemv) on the 70B projections and their tensor-parallel slices at
@@ -929,10 +964,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="headline only")
     ap.add_argument("--workload", default="gemv",
-                    choices=["gemv", "decode", "gemm", "tp", "load", "ssm", "bgemv", "mma-rate"],
+                    choices=["gemv", "decode", "gemm", "tp", "load", "ssm", "bgemv", "mma-rate", "sample"],
                     help="decode / gemm / tp / load: only the 8B decode, the prefill GEMM, the 70B tensor-parallel "
                          "decode or the DedupCount load-path measurement (for profiling); bgemv: the batched "
-                         "decode GEMVs on the 70B shapes; mma-rate: the tcgen05.mma cost table")
+                         "decode GEMVs on the 70B shapes; mma-rate: the tcgen05.mma cost table; sample: "
+                         "temperature + top-k sampling per call")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-decode", action="store_true", help="skip the 8B decode measurement")
@@ -948,12 +984,14 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload in ("bgemv", "mma-rate"):
+    if args.workload in ("bgemv", "mma-rate", "sample"):
         import torch
         torch.cuda.set_device(0)
         from agent_harness_b200 import _lib
         _lib.check(_lib.lib().ah_device_init(0))
-        rows = mma_rate() if args.workload == "mma-rate" else bgemv_shapes(torch.device("cuda", 0))
+        dev = torch.device("cuda", 0)
+        rows = (mma_rate() if args.workload == "mma-rate" else
+                sample_rate(dev) if args.workload == "sample" else bgemv_shapes(dev))
         for r in rows:
             print(json.dumps({"workload": args.workload, **r}), flush=True)
         return 0

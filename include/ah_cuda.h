@@ -364,6 +364,14 @@ AH_API int ah_model_set_prefill(AhModel* m, int mode);
  * otherwise.  1: every projection of every step on the tcgen05 GEMV; 17:
  * never. */
 AH_API int ah_model_set_batched_gemv(AhModel* m, int min_batch);
+/* Next-token choice of the decode steps.  temperature 0 (the default): greedy,
+ * sampling.rs:4-14.  temperature > 0: inference/mod.rs:552-553 with top_k
+ * (the reference passes 40; 1..64 here): the top_k logits of each sequence,
+ * then sampling.rs:17-64's exp / sum / CDF scan in the reference's order, with
+ * the uniform r = ah_sample_uniform(seed, position, sequence) in place of the
+ * reference's clock-seeded xorshift (sampling.rs:67-86), so runs repeat.
+ * Under tensor parallelism every rank picks the same token. */
+AH_API int ah_model_set_sampling(AhModel* m, float temperature, int top_k, uint64_t seed);
 /* Lower-level stepping (same semantics): reset, feed one token per sequence
  * (forward(), inference/mod.rs:333-545) and read the logits [batch][vocab]. */
 AH_API int ah_model_reset(AhModel* m, int batch, void* stream);
@@ -374,6 +382,18 @@ AH_API int ah_model_forward(AhModel* m, const int32_t* tokens_dev, float* logits
 AH_API int ah_model_decode(AhModel* m, int n, int32_t* out_tokens_dev, void* stream);
 /* Current position (tokens consumed per sequence). */
 AH_API int ah_model_position(const AhModel* m, int* pos);
+
+/* ---- Sampling (inference/sampling.rs) ----------------------------------------------
+ * Replaces sampling.rs:17-64 sample(logits, temperature, top_k) for `batch`
+ * rows of logits_dev [batch][ld] (device f32, vocab <= ld): out_dev[b] (device
+ * int32) = the token that sample() returns for row b when its rand_val() draw
+ * is ah_sample_uniform(seed, step, b).  top_k in 1..64; temperature > 0.
+ * Candidates are ranked by logit, ties by lower index. */
+AH_API int ah_sample_logits(const float* logits_dev, int64_t ld, int batch, int64_t vocab, float temperature,
+                            int top_k, uint64_t seed, int64_t step, int32_t* out_dev, void* stream);
+/* The uniform draw in [0, 1) (24 bits, as sampling.rs:84-85 maps its xorshift
+ * state) of sequence `seq` at step `step`: a counter-based hash of the three. */
+AH_API float ah_sample_uniform(uint64_t seed, int64_t step, int seq);
 
 /* ---- DedupCount weight decoding (models/dedup/) --------------------------------------
  * A decode table holds one tensor's lookups flattened to f32 values on the

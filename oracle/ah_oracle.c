@@ -477,6 +477,51 @@ OR_API uint32_t or_argmax(const float* logits, int64_t n) {
     return best;
 }
 
+/* inference/sampling.rs:17-64 `sample` with the uniform draw r given (the
+ * reference draws it from a clock-seeded xorshift): p_i = exp((v_i - max) /
+ * T) over every logit, the top_k indices by p (descending; equal p in index
+ * order, which the reference's unstable selection leaves unspecified), the
+ * sum over them in that order, then the CDF scan.  top_k >= 1. */
+static const float* or_sample_p;
+static int or_sample_cmp(const void* a, const void* b) {
+    const int64_t ia = *(const int64_t*)a, ib = *(const int64_t*)b;
+    const float pa = or_sample_p[ia], pb = or_sample_p[ib];
+    if (pa > pb) return -1;
+    if (pa < pb) return 1;
+    return ia < ib ? -1 : (ia > ib ? 1 : 0);
+}
+OR_API uint32_t or_sample(const float* logits, int64_t n, float temperature, int64_t top_k, float r) {
+    if (n == 0) return 0;
+    float max_logit = -INFINITY;
+    for (int64_t i = 0; i < n; ++i) max_logit = fmaxf(max_logit, logits[i]);
+    const float inv_temp = 1.0f / temperature;
+    float* probs = (float*)malloc(sizeof(float) * (size_t)n);
+    int64_t* idx = (int64_t*)malloc(sizeof(int64_t) * (size_t)n);
+    for (int64_t i = 0; i < n; ++i) {
+        probs[i] = expf((logits[i] - max_logit) * inv_temp);
+        idx[i] = i;
+    }
+    const int64_t k = top_k < n ? top_k : n;
+    or_sample_p = probs;
+    qsort(idx, (size_t)n, sizeof(int64_t), or_sample_cmp);
+    float sum = 0.0f;
+    for (int64_t j = 0; j < k; ++j) sum += probs[idx[j]];
+    uint32_t pick = (uint32_t)idx[k - 1];
+    if (sum == 0.0f) {
+        pick = (uint32_t)idx[0];
+    } else {
+        const float inv = 1.0f / sum;
+        float cdf = 0.0f;
+        for (int64_t j = 0; j < k; ++j) {
+            cdf += probs[idx[j]] * inv;
+            if (r < cdf) { pick = (uint32_t)idx[j]; break; }
+        }
+    }
+    free(probs);
+    free(idx);
+    return pick;
+}
+
 /* inference/ffn.rs:155-174 `swiglu_4bit_into` on the engine INT4 format. */
 OR_API void or_swiglu_4bit_into(float* out, const float* input,
                                 const float* gs_, const uint8_t* gp, const float* us, const uint8_t* up,

@@ -62,6 +62,7 @@ def lib():
         L.or_softmax.argtypes = [f32p, i64]
         L.or_rope_multi.argtypes = [f32p, i64, i64, np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS"), C.c_float]
         L.or_argmax.argtypes = [f32p, i64]; L.or_argmax.restype = C.c_uint32
+        L.or_sample.argtypes = [f32p, i64, C.c_float, i64, C.c_float]; L.or_sample.restype = C.c_uint32
         L.or_swiglu_4bit_into.argtypes = [f32p, f32p, f32p, u8p, f32p, u8p, f32p, u8p, i64, i64, i64, f32p, f32p, f32p]
         L.or_model_forward.argtypes = [C.c_void_p, C.c_int32, i64, f32p]; L.or_model_forward.restype = C.c_int
         # AVX-512 as-is restatements (timing only)
@@ -224,6 +225,27 @@ def rope_head(x, pos, freq_base, sections=None):
         sections = np.array([x.size // 2, 0, 0, 0], np.int32)
     lib().or_rope_multi(x, x.size, pos, _c(sections, np.int32), freq_base)
     return x
+
+
+def sample(logits, temperature: float, top_k: int, r: float) -> int:
+    """inference/sampling.rs:17-64 with the uniform draw r given."""
+    logits = _c(logits, np.float32)
+    return int(lib().or_sample(logits, logits.size, float(temperature), int(top_k), float(r)))
+
+
+def sample_uniform(seed: int, step: int, seq: int) -> float:
+    """The device sampler's draw for (seed, step, sequence): 24 bits of a
+    splitmix64-style hash, mapped to [0, 1) as the reference maps its draw."""
+    M = (1 << 64) - 1
+
+    def mix(x):
+        x = (x + 0x9E3779B97F4A7C15) & M
+        x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & M
+        x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & M
+        return x ^ (x >> 31)
+
+    x = mix((seed ^ mix((step * 0x100000001B3 + seq) & M)) & M)
+    return float(np.float32(x & 0xFFFFFF) / np.float32(16777216.0))
 
 
 def argmax(logits) -> int:

@@ -53,16 +53,22 @@ def _rank(rank, world, port, q, p2p=False):
         gen_long = m.generate(LONG, 6)
         m.generate(LONG, 0)
         last = m.forward(LONG[:, -1]).cpu().numpy()
+        # temperature + top-k: per-rank candidates, all-gathered and merged
+        m.set_sampling(0.8, 40, 99)
+        m.reset(2)
+        s_last = [m.forward(PROMPT[:, t]).cpu().numpy() for t in range(PROMPT.shape[1])][-1]
+        s_tok = m.decode(1, 2).cpu().numpy()[0]
+        s_gen = m.generate(PROMPT, 8)
         torch.cuda.synchronize()
         err = _lib.lib().ah_check_device_error(None)
         m.close()
-        q.put((rank, logits, (gen, gen_long, last), err))
+        q.put((rank, logits, (gen, gen_long, last, s_last, s_tok, s_gen), err))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "nvlink_peer"])
-def test_tp2_matches_single_gpu(cuda, p2p):
+def test_tp2_matches_single_gpu(cuda, oracle, p2p):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -94,12 +100,19 @@ def test_tp2_matches_single_gpu(cuda, p2p):
     m.generate(LONG, 0)
     last1 = m.forward(LONG[:, -1]).cpu().numpy()
     m.close()
-    (g0, gl0, la0), (g1, gl1, la1) = res[0][1], res[1][1]
+    (g0, gl0, la0, sl0, st0, sg0), (g1, gl1, la1, sl1, st1, sg1) = res[0][1], res[1][1]
     assert np.array_equal(g0, g1) and np.array_equal(g0, gen1)
     # the long prompt went through the tensor-parallel prefill GEMMs
     assert np.array_equal(gl0, gl1) and np.array_equal(gl0, gen1_long)
     full = np.concatenate([la0, la1], axis=1)
     assert np.max(np.abs(full - last1)) / np.max(np.abs(last1)) <= 1e-3
+    # sampling: both ranks pick the same tokens, sample() of the full logits
+    # (the ranks' slices concatenated) with the draw for (99, position 5, b)
+    assert np.array_equal(st0, st1) and np.array_equal(sg0, sg1) and np.array_equal(sg0[0], st0)
+    full = np.concatenate([sl0, sl1], axis=1)
+    for b in range(2):
+        r = oracle.sample_uniform(99, PROMPT.shape[1] - 1, b)
+        assert st0[b] == oracle.sample(full[b], 0.8, 40, r), b
 
 
 # batch 16 with every projection on the tcgen05 batched GEMV (min_batch 1):

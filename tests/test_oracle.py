@@ -242,6 +242,69 @@ def test_argmax_first_max_wins(oracle):
     assert oracle.argmax(np.array([np.nan, -1, np.nan], np.float32)) == 1
 
 
+# --- sampling.rs:17-64 with the uniform draw given ----------------------------------
+
+def _sample_f64(logits, temperature, top_k, r):
+    """An independent restatement in float64 with a stable sort: the pick and
+    the distance of r from the nearest CDF boundary."""
+    x = np.asarray(logits, np.float64)
+    p = np.exp((x - x.max()) / temperature)
+    order = sorted(range(x.size), key=lambda i: (-p[i], i))[:min(top_k, x.size)]
+    cdf = np.cumsum(p[order]) / p[order].sum()
+    j = int(np.searchsorted(cdf, r, side="right"))
+    return order[min(j, len(order) - 1)], float(np.min(np.abs(cdf - r)))
+
+
+def test_sample_matches_restatement(oracle):
+    rng = np.random.default_rng(31)
+    for n, temp, k in ((1000, 1.0, 40), (300, 0.5, 5), (64, 2.0, 64), (7, 1.0, 40), (500, 0.8, 1)):
+        logits = (rng.standard_normal(n) * 3).astype(np.float32)
+        for r in rng.random(60).astype(np.float32):
+            got = oracle.sample(logits, temp, k, float(r))
+            want, margin = _sample_f64(logits, temp, k, float(r))
+            assert got == want or margin < 1e-5, (n, temp, k, r, got, want)
+
+
+def test_sample_edge_cases(oracle):
+    lg = np.array([1, 3, 3, 2], np.float32)
+    assert oracle.sample(lg, 1.0, 1, 0.99) == 1  # top-1 is the first maximum
+    assert oracle.sample(lg, 1.0, 40, 0.0) == 1  # r = 0: the first candidate
+    assert oracle.sample(lg, 1.0, 2, 0.75) == 2  # the tie's second member
+    # tiny temperature: only the two maxima keep weight, half each
+    assert [oracle.sample(lg, 1e-30, 40, r) for r in (0.3, 0.49, 0.51, 0.999)] == [1, 1, 2, 2]
+    # masked logits carry no weight
+    masked = np.array([-np.inf, 0.0, -np.inf, 0.0], np.float32)
+    assert {oracle.sample(masked, 1.0, 40, r) for r in (0.1, 0.6)} == {1, 3}
+
+
+def test_sample_frequencies(oracle):
+    # over many draws the picks follow the renormalised top-k softmax
+    rng = np.random.default_rng(4)
+    logits = (rng.standard_normal(200) * 1.5).astype(np.float32)
+    k, temp, n = 8, 0.9, 20000
+    picks = np.array([oracle.sample(logits, temp, k, oracle.sample_uniform(11, s, 0)) for s in range(n)])
+    top = np.argsort(-logits, kind="stable")[:k]
+    p = np.exp((logits[top] - logits.max()) / temp)
+    p /= p.sum()
+    assert set(np.unique(picks)) <= set(top.tolist())
+    for i, pi in zip(top, p):
+        f = np.mean(picks == i)
+        assert abs(f - pi) <= 5 * np.sqrt(pi * (1 - pi) / n) + 1e-3, (i, f, pi)
+
+
+def test_sample_uniform_matches_library(oracle):
+    # the draw the device sampler uses (a host function of the C-ABI library,
+    # no GPU needed) equals the oracle's restatement bit for bit
+    from agent_harness_b200 import kernels as K
+    O = oracle
+    for seed, step, seq in ((0, 0, 0), (1, 5, 3), (2**63 + 17, 123456, 15), (42, 2**40, 7)):
+        a, b = K.sample_uniform(seed, step, seq), O.sample_uniform(seed, step, seq)
+        assert a == b, (seed, step, seq, a, b)
+        assert 0.0 <= a < 1.0
+    vals = np.array([O.sample_uniform(9, s, q) for s in range(200) for q in range(16)])
+    assert abs(vals.mean() - 0.5) < 0.02 and vals.min() >= 0.0 and vals.max() < 1.0
+
+
 # --- the reference's AVX-512 kernels, restated as-is for timing, diverge as documented --
 
 def test_avx512_dequant_lane_permutation(oracle):
