@@ -110,7 +110,8 @@ SIGNATURES = {
     "ah_model_set_prefill": (i32, [vp, i32]),
     "ah_model_set_batched_gemv": (i32, [vp, i32]),
     "ah_model_set_sampling": (i32, [vp, f32, i32, u64]),
-    "ah_sample_logits": (i32, [vp, i64, i32, i64, f32, i32, u64, i64, vp, vp]),
+    "ah_sample_workspace_bytes": (sz, [i32, i64]),
+    "ah_sample_logits": (i32, [vp, i64, i32, i64, f32, i32, u64, i64, vp, vp, sz, vp]),
     "ah_sample_uniform": (f32, [u64, i64, i32]),
     "ah_host_gemv_4bit_into": (i32, [vp, vp, vp, vp, sz, sz, sz]),
     "ah_host_dequant_layer": (i32, [vp, vp, vp, sz, sz]),

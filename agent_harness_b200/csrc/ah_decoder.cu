@@ -975,6 +975,8 @@ struct AhModel {
   uint64_t samp_seed = 0;
   SampleCand* samp_cand = nullptr;  // [max_batch][kSampleMaxK] this rank's candidates
   SampleCand* samp_all = nullptr;   // [world][max_batch][kSampleMaxK] all ranks' (tensor parallel)
+  void* samp_ws = nullptr;          // the split top-k's slice candidates
+  size_t samp_ws_bytes = 0;
 };
 
 namespace {
@@ -1154,10 +1156,11 @@ int enqueue_step(AhModel* m, bool with_head, const int* prompt, int n_prompt, cu
     const int K = m->samp_k;
     if (!tp) {
       AH_TRY(sample_launch(m->logits, m->nvoc, B, m->nvoc, K, 0, m->samp_temp, m->samp_seed, 0, m->d_pos, nullptr,
-                           m->d_tok, m->tok_log, st, true));
+                           m->d_tok, m->tok_log, m->samp_ws, m->samp_ws_bytes, st));
     } else {
       AH_TRY(sample_launch(m->logits, m->nvoc, B, m->nvoc, K, (int64_t)m->tp_rank * m->nvoc, m->samp_temp,
-                           m->samp_seed, 0, m->d_pos, m->samp_cand, nullptr, nullptr, st, true));
+                           m->samp_seed, 0, m->d_pos, m->samp_cand, nullptr, nullptr, m->samp_ws, m->samp_ws_bytes,
+                           st));
       if (ncclAllGather(m->samp_cand, m->samp_all, (size_t)B * K * sizeof(SampleCand), ncclUint8, m->comm, st) !=
           ncclSuccess)
         return fail(AH_ENCCL, "model: all-gather of the sampling candidates failed");
@@ -1852,6 +1855,8 @@ int ah_model_set_sampling(AhModel* m, float temperature, int top_k, uint64_t see
     const size_t per = (size_t)m->c.max_batch * kSampleMaxK * sizeof(SampleCand);
     AH_TRY(dalloc(m, (void**)&m->samp_cand, per));
     AH_TRY(dalloc(m, (void**)&m->samp_all, per * m->tp_world));
+    m->samp_ws_bytes = sample_workspace_bytes(m->c.max_batch, m->nvoc);
+    if (m->samp_ws_bytes) AH_TRY(dalloc(m, &m->samp_ws, m->samp_ws_bytes));
   }
   m->samp_temp = temperature > 0.0f ? temperature : 0.0f;
   m->samp_k = top_k;

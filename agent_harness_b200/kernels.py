@@ -288,19 +288,35 @@ def swiglu_4bit_into(out: torch.Tensor, x: torch.Tensor, gate_scales, gate_packe
     return out
 
 
+def sample_workspace_bytes(batch: int, vocab: int) -> int:
+    return int(lib().ah_sample_workspace_bytes(batch, vocab))
+
+
 def sample_logits(logits: torch.Tensor, temperature: float, top_k: int = 40, seed: int = 0, step: int = 0,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                  split: bool = True) -> torch.Tensor:
     """inference/sampling.rs:17-64 sample(row, temperature, top_k) for each row
     of a [batch, vocab] f32 device tensor; the draw of row b is
-    sample_uniform(seed, step, b).  Returns int32 tokens [batch]."""
+    sample_uniform(seed, step, b).  Returns int32 tokens [batch].  Rows are
+    split over CTAs through a workspace (allocated here unless given);
+    split=False walks each row with one CTA."""
     if logits.dim() == 1:
         logits = logits.unsqueeze(0)
-    assert logits.dtype == torch.float32 and logits.stride(1) == 1
+    if not logits.is_cuda or logits.dtype != torch.float32 or logits.stride(1) != 1:
+        raise AhError(-1, "expected a CUDA f32 tensor with unit-stride rows")
     batch, vocab = logits.shape
     if out is None:
         out = torch.empty(batch, dtype=torch.int32, device=logits.device)
-    call("ah_sample_logits", _ptr(logits), logits.stride(0), batch, vocab, temperature, top_k, seed, step, _ptr(out),
-         _stream(logits.device))
+    ws, nbytes = None, 0
+    if split:
+        nbytes = sample_workspace_bytes(batch, vocab)
+        if workspace is None and nbytes:
+            workspace = torch.empty(nbytes, dtype=torch.uint8, device=logits.device)
+        if nbytes:
+            ws = _ptr(workspace)
+            nbytes = workspace.numel() * workspace.element_size()
+    call("ah_sample_logits", C.c_void_p(logits.data_ptr()), logits.stride(0), batch, vocab, temperature, top_k, seed,
+         step, _ptr(out), ws, nbytes, _stream(logits.device))
     return out
 
 

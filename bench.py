@@ -884,26 +884,41 @@ def mma_rate():
 
 def sample_rate(dev):
     """Temperature + top-k sampling (ah_sample_logits, T 0.8, top-k 40) per
-    call over [batch][vocab] f32 logits: device time of back-to-back calls."""
+    call over [batch][vocab] f32 logits: device time of back-to-back calls
+    captured in one CUDA graph (no host launch cost), rows split over slice
+    CTAs and walked by one CTA each."""
     import torch
     from agent_harness_b200 import kernels as K
     rows = []
+    reps = 100
     for vocab in (128256, 32000):
-        for batch in (1, 16):
+        for batch in (1, 16, 64):
             lg = K.fill_normal(batch * vocab, 0.0, 2.0, 3, device=dev).reshape(batch, vocab)
             out = torch.empty(batch, dtype=torch.int32, device=dev)
-            for s in range(5):
-                K.sample_logits(lg, 0.8, 40, seed=1, step=s, out=out)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            reps = 200
-            e0.record()
-            for s in range(reps):
-                K.sample_logits(lg, 0.8, 40, seed=1, step=s, out=out)
-            e1.record()
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / reps
-            rows.append({"vocab": vocab, "batch": batch, "top_k": 40, "us_per_call": round(us, 2),
-                         "logit_gbs": round(batch * vocab * 4 / us / 1e3, 1)})
+            ws = torch.empty(max(K.sample_workspace_bytes(batch, vocab), 16), dtype=torch.uint8, device=dev)
+            row = {"vocab": vocab, "batch": batch, "top_k": 40}
+            for split in (True, False):
+                st = torch.cuda.Stream(device=dev)
+                with torch.cuda.stream(st):
+                    for s in range(3):
+                        K.sample_logits(lg, 0.8, 40, seed=1, step=s, out=out, workspace=ws, split=split)
+                st.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=st):
+                    for s in range(reps):
+                        K.sample_logits(lg, 0.8, 40, seed=1, step=s, out=out, workspace=ws, split=split)
+                g.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(st):
+                    e0.record(st)
+                    g.replay()
+                    e1.record(st)
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / reps
+                row["split_us" if split else "one_cta_per_row_us"] = round(us, 2)
+                del g
+            rows.append(row)
     return rows
 
 

@@ -388,9 +388,16 @@ AH_API int ah_model_position(const AhModel* m, int* pos);
  * rows of logits_dev [batch][ld] (device f32, vocab <= ld): out_dev[b] (device
  * int32) = the token that sample() returns for row b when its rand_val() draw
  * is ah_sample_uniform(seed, step, b).  top_k in 1..64; temperature > 0.
- * Candidates are ranked by logit, ties by lower index. */
+ * Candidates are ranked by logit, ties by lower index.  With a device
+ * workspace of ah_sample_workspace_bytes(batch, vocab) bytes (16-byte
+ * aligned; any contents; one per stream) rows of 8192 logits or more are
+ * split over CTAs of 4096 logits (0 bytes: no split at this vocabulary); with
+ * workspace null, one CTA takes each row (large batches).  Both give the same
+ * tokens. */
+AH_API size_t ah_sample_workspace_bytes(int batch, int64_t vocab);
 AH_API int ah_sample_logits(const float* logits_dev, int64_t ld, int batch, int64_t vocab, float temperature,
-                            int top_k, uint64_t seed, int64_t step, int32_t* out_dev, void* stream);
+                            int top_k, uint64_t seed, int64_t step, int32_t* out_dev, void* workspace,
+                            size_t workspace_bytes, void* stream);
 /* The uniform draw in [0, 1) (24 bits, as sampling.rs:84-85 maps its xorshift
  * state) of sequence `seq` at step `step`: a counter-based hash of the three. */
 AH_API float ah_sample_uniform(uint64_t seed, int64_t step, int seq);

@@ -39,8 +39,10 @@ def test_matches_oracle(cuda, oracle, batch, vocab, temp, k):
     logits = (rng.standard_normal((batch, vocab)) * 2.5).astype(np.float32)
     d = torch.from_numpy(logits).to(cuda)
     for step in (0, 1, 977):
-        got = K.sample_logits(d, temp, k, seed=5, step=step).cpu().numpy()
-        _check(oracle, logits, temp, k, 5, step, got)
+        got = K.sample_logits(d, temp, k, seed=5, step=step)
+        _check(oracle, logits, temp, k, 5, step, got.cpu().numpy())
+        # rows split over slice CTAs and rows walked by one CTA pick the same
+        assert torch.equal(K.sample_logits(d, temp, k, seed=5, step=step, split=False), got)
 
 
 def test_ties_and_masks(cuda, oracle):
@@ -64,8 +66,9 @@ def test_ties_and_masks(cuda, oracle):
     d = torch.from_numpy(logits).to(cuda)
     for k in (1, 39, 40, 64):
         for step in range(4):
-            got = K.sample_logits(d, 1.0, k, seed=17, step=step).cpu().numpy()
-            _check(oracle, logits, 1.0, k, 17, step, got)
+            got = K.sample_logits(d, 1.0, k, seed=17, step=step)
+            _check(oracle, logits, 1.0, k, 17, step, got.cpu().numpy())
+            assert torch.equal(K.sample_logits(d, 1.0, k, seed=17, step=step, split=False), got)
     # the constant row at top-k 40: one of the first 40 indices
     got = np.array([K.sample_logits(d[1:2], 1.0, 40, seed=s).item() for s in range(32)])
     assert got.min() >= 0 and got.max() < 40 and len(set(got.tolist())) > 10
@@ -108,6 +111,12 @@ def test_bad_arguments_refused(cuda):
     for temp, k in ((0.0, 40), (-1.0, 40), (1.0, 0), (1.0, 65)):
         with pytest.raises(AhError):
             K.sample_logits(d, temp, k)
+    # a split row with a short workspace
+    big = torch.zeros(2, 20000, device=cuda)
+    need = K.sample_workspace_bytes(2, 20000)
+    assert need > 0 and K.sample_workspace_bytes(2, 8191) == 0
+    with pytest.raises(AhError):
+        K.sample_logits(big, 1.0, 64, workspace=torch.empty(need - 16, dtype=torch.uint8, device=cuda))
 
 
 def test_decoder_samples_its_own_logits(cuda, oracle):
