@@ -960,7 +960,7 @@ struct AhModel {
   // prompt prefill through the GEMMs (allocated on first use for kPrefillRows rows)
   int pf_mode = 1;  // 0: token by token, as the reference; 1: GEMM prefill from kPrefillMinTokens
   float *pf_h = nullptr, *pf_x = nullptr, *pf_qkv = nullptr, *pf_attn = nullptr, *pf_part = nullptr;
-  float *pf_gu = nullptr, *pf_act = nullptr;
+  float* pf_act = nullptr;
   void* pf_ws = nullptr;
   size_t pf_ws_bytes = 0;
   // decode steps of at least bg_min_batch sequences run their GEMVs on the
@@ -1207,8 +1207,7 @@ int prefill_buffers(AhModel* m) {
   A((void**)&m->pf_x, R * d * 4);
   A((void**)&m->pf_qkv, R * (size_t)(m->dq + 2 * m->dkv) * 4);
   A((void**)&m->pf_attn, R * (size_t)m->dq * 4);
-  A((void**)&m->pf_part, R * d * 4);
-  A((void**)&m->pf_gu, R * (size_t)2 * m->nff * 4);
+  if (m->tp_world > 1) A((void**)&m->pf_part, R * d * 4);
   A((void**)&m->pf_act, R * (size_t)m->nff * 4);
   size_t ws = 0;
   for (const AhQ4Weight* w : {m->wqkv[0], m->wo[0], m->wgu[0], m->wd[0]})
@@ -1216,6 +1215,18 @@ int prefill_buffers(AhModel* m) {
   A(&m->pf_ws, ws + 1024);
   m->pf_ws_bytes = ws;
   return rc;
+}
+
+// A block's output projection added into the hidden rows (pf_h += a . W^T).
+int block_out(AhModel* m, const AhQ4Weight* w, const float* a, int64_t lda, int64_t rows, void* ws, cudaStream_t st,
+              const char* what) {
+  const int d = m->c.n_embd;
+  if (m->tp_world == 1)
+    return gemm_run(q4w_tiled(w), a, lda, rows, m->pf_h, d, ws, m->pf_ws_bytes, st, kGemmEpiAdd);
+  AH_TRY(gemm_run(q4w_tiled(w), a, lda, rows, m->pf_part, d, ws, m->pf_ws_bytes, st));
+  if (ncclAllReduce(m->pf_part, m->pf_part, (size_t)rows * d, ncclFloat, ncclSum, m->comm, st) != ncclSuccess)
+    return fail(AH_ENCCL, "prefill: all-reduce of the %s block output failed", what);
+  return prefill_add(m->pf_h, m->pf_part, rows * d, st);
 }
 
 int prefill_gemm(AhModel* m, const int* prompt, int n_prompt, int P, cudaStream_t st) {
@@ -1237,20 +1248,13 @@ int prefill_gemm(AhModel* m, const int* prompt, int n_prompt, int P, cudaStream_
       if (l + 1 == L) break;
       AH_TRY(prefill_attention(m->pf_qkv, ldq, m->kc, m->vc, l, L, m->nh, m->nkv, hd, c.max_seq, scale, pr,
                                m->pf_attn, m->dq, st));
-      AH_TRY(gemm_run(q4w_tiled(m->wo[l]), m->pf_attn, m->dq, rows, m->pf_part, d, ws, m->pf_ws_bytes, st));
-      if (m->tp_world > 1 &&
-          ncclAllReduce(m->pf_part, m->pf_part, (size_t)rows * d, ncclFloat, ncclSum, m->comm, st) != ncclSuccess)
-        return fail(AH_ENCCL, "prefill: all-reduce of the attention block output failed");
-      AH_TRY(prefill_add(m->pf_h, m->pf_part, rows * d, st));
+      // one GPU: the o and down GEMMs add into the hidden rows in their
+      // epilogue; tensor parallel: partial sums, all-reduce, then the add
+      AH_TRY(block_out(m, m->wo[l], m->pf_attn, m->dq, rows, ws, st, "attention"));
       AH_TRY(prefill_rmsnorm(m->pf_h, m->ffn_norm + (size_t)l * d, c.rms_eps, rows, d, m->pf_x, st));
-      AH_TRY(gemm_run(q4w_tiled(m->wgu[l]), m->pf_x, d, rows, m->pf_gu, 2 * (int64_t)m->nff, ws, m->pf_ws_bytes,
-                      st));
-      AH_TRY(prefill_swiglu(m->pf_gu, rows, m->nff, m->pf_act, st));
-      AH_TRY(gemm_run(q4w_tiled(m->wd[l]), m->pf_act, m->nff, rows, m->pf_part, d, ws, m->pf_ws_bytes, st));
-      if (m->tp_world > 1 &&
-          ncclAllReduce(m->pf_part, m->pf_part, (size_t)rows * d, ncclFloat, ncclSum, m->comm, st) != ncclSuccess)
-        return fail(AH_ENCCL, "prefill: all-reduce of the MLP block output failed");
-      AH_TRY(prefill_add(m->pf_h, m->pf_part, rows * d, st));
+      AH_TRY(gemm_run(q4w_tiled(m->wgu[l]), m->pf_x, d, rows, m->pf_act, m->nff, ws, m->pf_ws_bytes, st,
+                      kGemmEpiSwiglu));
+      AH_TRY(block_out(m, m->wd[l], m->pf_act, m->nff, rows, ws, st, "MLP"));
     }
   }
   k_prefill_state<<<1, 32, 0, st>>>(m->d_pos, m->d_tok, prompt, n_prompt, P, B);

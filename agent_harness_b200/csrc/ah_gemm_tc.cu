@@ -65,6 +65,7 @@ constexpr int kDequantWarps = 8;  // >= 4: the first four cover the TMEM lane qu
 constexpr int kGemmThreads = (3 + kDequantWarps) * 32;
 constexpr uint32_t kWaitLimit = 1u << 24;
 constexpr int kStageStride = kBN + 4;  // f32 per staged C row: 848 B, 16-byte stores conflict-free
+constexpr int kGluStride = kBN / 2 + 4;  // the same for a SwiGLU row (104 outputs): 432 B
 
 constexpr uint32_t kIdesc = idesc_f16(kTokTile, kBN);
 
@@ -74,8 +75,10 @@ struct GemmSmem {
   static constexpr int kB = kA + kStages * kHalves * kATileBytes;
   static constexpr int kRaw = kB + kStages * kBBytes;
   static constexpr int kBars = kRaw + kRawStages * kRawBytes;
-  // the epilogue stages 128 rows of C over the (then idle) operand rings
+  // the epilogue stages 128 rows of C over the (then idle) operand rings (a
+  // SwiGLU epilogue: both token halves at once)
   static_assert(kTokTile * kStageStride * 4 <= kBars, "C staging must fit below the barriers");
+  static_assert(2 * kTokTile * kGluStride * 4 <= kBars, "SwiGLU staging must fit below the barriers");
   static constexpr int kNumBars = 3 * kStages + 2 * kRawStages + 1;
   static constexpr int kMisc = kBars + kNumBars * 8;
   static constexpr int kTotal = kMisc + 16;
@@ -93,6 +96,7 @@ struct GemmArgs {
   int64_t ldc;
   int64_t m;
   int* err;
+  int epi;     // GemmEpilogue
   bool c_vec;  // ldc % 4 == 0 and c 16-byte aligned
 };
 
@@ -385,12 +389,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(const __grid_con
     // epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its token rows).
     // Each thread stages its row segment (208 columns, scaled by 2^-s) in the
     // now idle operand rings and writes it with one bulk copy, so C leaves the
-    // SM as whole 832-byte row runs instead of 16-byte pieces of 32 rows.
-    // Where the bulk copy cannot address C (unaligned, ragged by a non
-    // multiple of 4 columns), threads store their 16-column pieces directly.
-    // Dequant warps past the first four have no epilogue work.
+    // SM as whole 832-byte row runs instead of 16-byte pieces of 32 rows (the
+    // residual-add epilogue adds the run into C with one bulk reduce).  Where
+    // the bulk copy cannot address C (unaligned, ragged by a non multiple of 4
+    // columns), threads store their 16-column pieces directly.  Dequant warps
+    // past the first four have no epilogue work, except under the SwiGLU
+    // epilogue: there warps 3..6 take token half 0 and warps 7..10 half 1.
+    // Its 16-column TMEM chunks are whole weight tiles (8 gate rows, then the
+    // 8 up rows of the same outputs), so each yields 8 outputs
+    // silu(g * 2^-s) * (u * 2^-s).
+    const bool glu = g.epi == kGemmEpiSwiglu;
+    const int h_first = glu && wd >= 4 ? 1 : 0;
+    const int h_step = glu ? 2 : 1;
+    const bool epi_warp = glu ? (wd < 4 || kHalves == 2) : wd < 4;
     const bool have =
-        __all_sync(0xffffffffu, wd < 4 && mbar_wait_bounded(acc_full, 0, g.err, AH_ETIMEOUT, kWaitLimit));
+        __all_sync(0xffffffffu, epi_warp && mbar_wait_bounded(acc_full, 0, g.err, AH_ETIMEOUT, kWaitLimit));
     tc_fence_after();
     pdl_wait();  // row_inv comes from the preceding prep grid
     if (have && !*abort_flag) {
@@ -398,17 +411,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(const __grid_con
       const int64_t n0 = rt0 * 16;
       const int64_t n_rows = g.w.rows;
       const int ncols = (int)(n_rows - n0 < kBN ? n_rows - n0 : kBN);
-      const bool bulk = g.c_vec && (ncols % 4) == 0;
-      float* stage = reinterpret_cast<float*>(smem) + (q * 32 + lane) * kStageStride;
-      for (int h = 0; h < kHalves; ++h) {
+      const int64_t o0 = glu ? n0 / 2 : n0;            // first output column
+      const int64_t n_out = glu ? n_rows / 2 : n_rows;  // output columns of C
+      const int ocols = glu ? ncols / 2 : ncols;
+      const bool bulk = g.c_vec && (ocols % 4) == 0;
+      float* stage = glu ? reinterpret_cast<float*>(smem) + (h_first * kTokTile + q * 32 + lane) * kGluStride
+                         : reinterpret_cast<float*>(smem) + (q * 32 + lane) * kStageStride;
+      for (int h = h_first; h < kHalves; h += h_step) {
         const int64_t m = (mt0 + h) * kTokTile + q * 32 + lane;
         const float inv = m < g.m ? g.row_inv[m] : 0.0f;
         float* crow = g.c + m * g.ldc;
-        if (bulk && h > 0) bulk_wait_read0();  // the previous row's copy has read the stage
+        if (bulk && h > h_first) bulk_wait_read0();  // the previous row's copy has read the stage
 #pragma unroll 1
         for (int c0 = 0; c0 < kBN; c0 += 16) {
           float v[16];
           tmem_ld16(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * kAccColStride + c0), v);
+          if (glu) {
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = silu_ref(v[i] * inv) * (v[i + 8] * inv);
+            if (bulk) {
+              *reinterpret_cast<float4*>(stage + c0 / 2) = make_float4(o[0], o[1], o[2], o[3]);
+              *reinterpret_cast<float4*>(stage + c0 / 2 + 4) = make_float4(o[4], o[5], o[6], o[7]);
+              continue;
+            }
+            if (m >= g.m) continue;
+            const int64_t n = o0 + c0 / 2;
+            if (g.c_vec && n + 8 <= n_out) {
+              st_cs_f4(reinterpret_cast<float4*>(crow + n), make_float4(o[0], o[1], o[2], o[3]));
+              st_cs_f4(reinterpret_cast<float4*>(crow + n + 4), make_float4(o[4], o[5], o[6], o[7]));
+            } else {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                if (n + i < n_out) crow[n + i] = o[i];
+            }
+            continue;
+          }
           if (bulk) {
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
@@ -418,7 +456,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(const __grid_con
           }
           if (m >= g.m) continue;
           const int64_t n = n0 + c0;
-          if (g.c_vec && n + 16 <= n_rows) {
+          if (g.epi == kGemmEpiAdd) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (n + i < n_rows) crow[n + i] += v[i] * inv;  // residual: hidden[i] += out[i]
+          } else if (g.c_vec && n + 16 <= n_rows) {
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
               st_cs_f4(reinterpret_cast<float4*>(crow + n + i),
@@ -431,7 +473,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm_q4_tc(const __grid_con
         }
         if (bulk && m < g.m) {
           fence_proxy_async_smem();
-          bulk_s2g(crow + n0, smem_u32(stage), (uint32_t)ncols * 4u);
+          if (g.epi == kGemmEpiAdd)
+            bulk_s2g_add_f32(crow + o0, smem_u32(stage), (uint32_t)ocols * 4u);
+          else
+            bulk_s2g(crow + o0, smem_u32(stage), (uint32_t)ocols * 4u);
           bulk_commit();
         }
       }
@@ -526,11 +571,14 @@ size_t gemm_workspace_bytes(const Q4Tiled& w, int64_t m) {
 }
 
 int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c, int64_t ldc, void* ws,
-             size_t ws_bytes, cudaStream_t st) {
+             size_t ws_bytes, cudaStream_t st, int epi) {
   AH_REQUIRE(m >= 0, "gemm: negative M");
   if (m == 0) return AH_OK;
   AH_REQUIRE(a != nullptr && c != nullptr && ws != nullptr, "gemm: null pointer");
-  AH_REQUIRE(lda >= w.cols && ldc >= w.rows, "gemm: lda must be >= cols and ldc >= rows");
+  AH_REQUIRE(epi == kGemmEpiStore || epi == kGemmEpiSwiglu || epi == kGemmEpiAdd, "gemm: unknown epilogue %d", epi);
+  AH_REQUIRE(epi != kGemmEpiSwiglu || w.rows % 16 == 0, "gemm: a SwiGLU epilogue needs whole 16-row tiles");
+  AH_REQUIRE(lda >= w.cols && ldc >= (epi == kGemmEpiSwiglu ? w.rows / 2 : w.rows),
+             "gemm: lda must be >= cols and ldc >= the output columns");
   AH_REQUIRE(ws_bytes >= gemm_workspace_bytes(w, m), "gemm: workspace of %zu bytes is below the %zu needed",
              ws_bytes, gemm_workspace_bytes(w, m));
   AH_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 1023) == 0, "gemm: workspace must be 1024-byte aligned");
@@ -548,6 +596,7 @@ int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c,
   g.ldc = ldc;
   g.m = m;
   g.err = device_error_word();
+  g.epi = epi;
   g.c_vec = (ldc % 4 == 0) && aligned16(c);
   // weight planes as uint32 rows of 16-row tiles; activations as f16 rows
   int rc = encode_2d(&g.tm_nib, w.nib, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)w.kp * 128, (uint64_t)w.r16, 128,

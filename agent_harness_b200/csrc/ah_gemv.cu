@@ -258,11 +258,6 @@ struct ScaleT<true> {  // engine format: four f32 scales
   }
 };
 
-__device__ __forceinline__ float silu_ref(float x) {  // inference/math.rs:83-95
-  const float sg = x >= 0.0f ? __fdiv_rn(1.0f, 1.0f + expf(-x)) : __fdiv_rn(expf(x), 1.0f + expf(x));
-  return x * sg;
-}
-
 // ---------------------------------------------------------------------------
 // The fused GEMV.  A thread-block cluster of kGemvCluster CTAs walks row groups
 // of kGemvWarps 16-row tiles (128 rows) over the full K; cluster CTA c takes

@@ -30,6 +30,14 @@
 
 namespace ah {
 
+// inference/math.rs:83-95 silu (the GEMV and GEMM SwiGLU epilogues, the
+// prefill row kernels)
+__device__ __forceinline__ float silu_ref(float x) {
+  const float sg = x >= 0.0f ? __fdiv_rn(1.0f, 1.0f + expf(-x)) : __fdiv_rn(expf(x), 1.0f + expf(x));
+  return x * sg;
+}
+
+
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kGemvMaxBatch = 16;

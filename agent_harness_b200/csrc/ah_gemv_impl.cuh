@@ -30,10 +30,14 @@ int gemv_launch(GemvArgs a, int prologue, int epilogue, cudaStream_t st, bool pd
 int gemv_prepare(const Q4Tiled& w, int batch, int prologue, int epilogue);
 
 // The tcgen05 GEMM c[m][ldc] = a[m][lda] . W^T (ah_gemm_tc.cu) and the
-// workspace it needs for m rows (1024-byte aligned).
+// workspace it needs for m rows (1024-byte aligned).  Epilogues: store;
+// SwiGLU over an interleaved gate/up weight (16-row tiles of 8 gate rows,
+// then the 8 up rows of the same outputs; c gets rows/2 columns
+// silu(gate) * up); residual add (c += a . W^T).
+enum GemmEpilogue { kGemmEpiStore = 0, kGemmEpiSwiglu = 1, kGemmEpiAdd = 2 };
 size_t gemm_workspace_bytes(const Q4Tiled& w, int64_t m);
 int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c, int64_t ldc, void* ws,
-             size_t ws_bytes, cudaStream_t st);
+             size_t ws_bytes, cudaStream_t st, int epi = kGemmEpiStore);
 
 // The tcgen05 batched GEMV (ah_bgemv_tc.cu): the same products as
 // gemv_launch for 1..16 tokens, weights dequantised into tensor memory, work

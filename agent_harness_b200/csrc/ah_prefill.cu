@@ -14,11 +14,6 @@
 namespace ah {
 namespace {
 
-__device__ __forceinline__ float silu_f(float x) {  // inference/math.rs:83-95
-  const float sg = x >= 0.0f ? __fdiv_rn(1.0f, 1.0f + expf(-x)) : __fdiv_rn(expf(x), 1.0f + expf(x));
-  return x * sg;
-}
-
 __global__ void __launch_bounds__(256) k_embed_rows(const uint16_t* __restrict__ emb, const int* __restrict__ prompt,
                                                     PrefillRows pr, int d, int vocab, float* __restrict__ hidden) {
   const int64_t r = blockIdx.y;
@@ -90,17 +85,6 @@ __global__ void __launch_bounds__(128) k_rope_append_rows(float* __restrict__ qk
 __global__ void __launch_bounds__(256) k_add_rows(float* __restrict__ h, const float* __restrict__ p, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     h[i] += p[i];  // residual: hidden[i] += out[i]
-}
-
-__global__ void __launch_bounds__(256) k_swiglu_rows(const float* __restrict__ gu, int64_t rows, int nff,
-                                                     float* __restrict__ act) {
-  const int64_t n = rows * nff;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = e / nff;
-    const int i = (int)(e - r * nff);
-    const float* g = gu + r * (2 * (int64_t)nff) + (i >> 3) * 16 + (i & 7);
-    act[e] = silu_f(g[0]) * g[8];
-  }
 }
 
 // Causal attention of a chunk's queries over the f16 KV cache, f32 arithmetic
@@ -582,12 +566,5 @@ int prefill_add(float* hidden, const float* part, int64_t n, cudaStream_t st) {
   return AH_OK;
 }
 
-int prefill_swiglu(const float* gu, int64_t rows, int nff, float* act, cudaStream_t st) {
-  const int64_t n = rows * nff;
-  const int64_t g = std::min<int64_t>((n + 255) / 256, (int64_t)sm_count() * 8);
-  k_swiglu_rows<<<(unsigned)g, 256, 0, st>>>(gu, rows, nff, act);
-  AH_LAUNCH_CHECK();
-  return AH_OK;
-}
 
 }  // namespace ah

@@ -32,8 +32,5 @@ int prefill_attention(const float* qkv, int ld, const uint16_t* kc, const uint16
                       int ld_out, cudaStream_t st);
 // hidden += part
 int prefill_add(float* hidden, const float* part, int64_t n, cudaStream_t st);
-// act[r][i] = silu(gate_i) * up_i from the interleaved gate/up rows (8 gate
-// rows, then the matching 8 up rows, per 16) (inference/ffn.rs:155-174)
-int prefill_swiglu(const float* gu, int64_t rows, int nff, float* act, cudaStream_t st);
 
 }  // namespace ah
