@@ -199,3 +199,35 @@ def test_world2_matches_unsharded_and_oracle(oracle):
         full = np.concatenate([np.asarray(res[0][0][step]), np.asarray(res[1][0][step])])
         ref = lg1[step]
         assert np.max(np.abs(full - ref)) <= 1e-4 * np.max(np.abs(ref)), step
+
+
+def _topk_sorted(values, idx, k):
+    """The k largest by (value desc, index asc), as (value, index) pairs."""
+    order = sorted(range(len(values)), key=lambda i: (-values[i], idx[i]))[:k]
+    return [(values[i], idx[i]) for i in order]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sampling_candidate_merge_equals_global(oracle, world):
+    # the tensor-parallel sampler's plan: each rank's top-k of its vocab slice
+    # (global indices), the W*k candidates merged by (value desc, index asc),
+    # then sample() over the merged top-k -- the same pick as sample() over
+    # the full row, for every draw, including tied logits across ranks
+    rng = np.random.default_rng(world)
+    vocab, k, temp = 512, 40, 0.8
+    for trial in range(6):
+        row = (rng.standard_normal(vocab) * 2).astype(np.float32)
+        if trial % 2:
+            row = np.round(row * 2).astype(np.float32) / 2  # ties within and across slices
+        per = vocab // world
+        cands = []
+        for r in range(world):
+            sl = row[r * per:(r + 1) * per]
+            cands += _topk_sorted(list(sl), list(range(r * per, (r + 1) * per)), k)
+        merged = _topk_sorted([c[0] for c in cands], [c[1] for c in cands], k)
+        glob = _topk_sorted(list(row), list(range(vocab)), k)
+        assert [c[1] for c in merged] == [c[1] for c in glob]
+        sub = np.array([c[0] for c in merged], np.float32)
+        for r in rng.random(20).astype(np.float32):
+            pick = merged[oracle.sample(sub, temp, k, float(r))][1]
+            assert pick == oracle.sample(row, temp, k, float(r))
