@@ -959,7 +959,7 @@ struct AhModel {
   std::vector<void*> allocs;
   // prompt prefill through the GEMMs (allocated on first use for kPrefillRows rows)
   int pf_mode = 1;  // 0: token by token, as the reference; 1: GEMM prefill from kPrefillMinTokens
-  float *pf_h = nullptr, *pf_x = nullptr, *pf_qkv = nullptr, *pf_attn = nullptr, *pf_part = nullptr;
+  float *pf_h = nullptr, *pf_qkv = nullptr, *pf_attn = nullptr, *pf_part = nullptr;
   float* pf_act = nullptr;
   void* pf_ws = nullptr;
   size_t pf_ws_bytes = 0;
@@ -1204,7 +1204,6 @@ int prefill_buffers(AhModel* m) {
     if (rc == AH_OK) rc = dalloc(m, p, bytes);
   };
   A((void**)&m->pf_h, R * d * 4);
-  A((void**)&m->pf_x, R * d * 4);
   A((void**)&m->pf_qkv, R * (size_t)(m->dq + 2 * m->dkv) * 4);
   A((void**)&m->pf_attn, R * (size_t)m->dq * 4);
   if (m->tp_world > 1) A((void**)&m->pf_part, R * d * 4);
@@ -1242,8 +1241,9 @@ int prefill_gemm(AhModel* m, const int* prompt, int n_prompt, int P, cudaStream_
     const int64_t rows = (int64_t)B * pr.cnt;
     AH_TRY(prefill_embed(m->tok_embd, prompt, pr, d, c.vocab_size, m->pf_h, st));
     for (int l = 0; l < L; ++l) {
-      AH_TRY(prefill_rmsnorm(m->pf_h, m->attn_norm + (size_t)l * d, c.rms_eps, rows, d, m->pf_x, st));
-      AH_TRY(gemm_run(q4w_tiled(m->wqkv[l]), m->pf_x, d, rows, m->pf_qkv, ldq, ws, m->pf_ws_bytes, st));
+      // RMSNorm inside each GEMM's activation prep
+      AH_TRY(gemm_run(q4w_tiled(m->wqkv[l]), m->pf_h, d, rows, m->pf_qkv, ldq, ws, m->pf_ws_bytes, st,
+                      kGemmEpiStore, m->attn_norm + (size_t)l * d, c.rms_eps));
       AH_TRY(prefill_rope_append(m->pf_qkv, ldq, m->rope, m->kc, m->vc, l, L, m->nh, m->nkv, hd, c.max_seq, pr, st));
       if (l + 1 == L) break;
       AH_TRY(prefill_attention(m->pf_qkv, ldq, m->kc, m->vc, l, L, m->nh, m->nkv, hd, c.max_seq, scale, pr,
@@ -1251,9 +1251,8 @@ int prefill_gemm(AhModel* m, const int* prompt, int n_prompt, int P, cudaStream_
       // one GPU: the o and down GEMMs add into the hidden rows in their
       // epilogue; tensor parallel: partial sums, all-reduce, then the add
       AH_TRY(block_out(m, m->wo[l], m->pf_attn, m->dq, rows, ws, st, "attention"));
-      AH_TRY(prefill_rmsnorm(m->pf_h, m->ffn_norm + (size_t)l * d, c.rms_eps, rows, d, m->pf_x, st));
-      AH_TRY(gemm_run(q4w_tiled(m->wgu[l]), m->pf_x, d, rows, m->pf_act, m->nff, ws, m->pf_ws_bytes, st,
-                      kGemmEpiSwiglu));
+      AH_TRY(gemm_run(q4w_tiled(m->wgu[l]), m->pf_h, d, rows, m->pf_act, m->nff, ws, m->pf_ws_bytes, st,
+                      kGemmEpiSwiglu, m->ffn_norm + (size_t)l * d, c.rms_eps));
       AH_TRY(block_out(m, m->wd[l], m->pf_act, m->nff, rows, ws, st, "MLP"));
     }
   }

@@ -139,8 +139,32 @@ __device__ __forceinline__ void prep_store8(uint8_t* out_row, int64_t c, const f
   *reinterpret_cast<uint4*>(out_row + c * 16) = make_uint4(h[0], h[1], h[2], h[3]);
 }
 
+// Block-wide sum (kPrepThreads threads) through red[]; every thread gets it.
+__device__ __forceinline__ float prep_block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();  // red[] may still be read by a previous reduction
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = red[0];
+#pragma unroll
+  for (int i = 1; i < kPrepThreads / 32; ++i) t += red[i];
+  return t;
+}
+
+// With norm_w: the row is RMS-normalised first (inference/math.rs:53-63:
+// x * 1/sqrt(mean(x^2) + eps) * w, w f16), so a GEMM can take the hidden rows
+// directly.
+__device__ __forceinline__ void prep_norm8(float (&v)[8], int64_t k0, int64_t k_cols, float inv,
+                                           const uint16_t* __restrict__ norm_w) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    v[i] = k0 + i < k_cols ? (v[i] * inv) * __half2float(__ushort_as_half(norm_w[k0 + i])) : 0.0f;
+}
+
 __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restrict__ a, int64_t lda, int64_t m_rows,
                                                             int64_t k_cols, int64_t kp, bool vec_rows,
+                                                            const uint16_t* __restrict__ norm_w, float eps,
                                                             uint8_t* __restrict__ at, float* __restrict__ row_inv) {
   // the GEMM may start its prologue and weight loads now; it waits for this
   // grid's completion before reading the tiles
@@ -154,23 +178,53 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
   const bool in_regs = nchunks <= (int64_t)kPrepThreads * kPrepChunks;
   __shared__ float red[kPrepThreads / 32];
   float v[kPrepChunks][8];
-  // max |a| over the row (NaN ignored here; it still reaches C)
-  float amax = 0.0f;
   if (in_regs) {
 #pragma unroll
     for (int j = 0; j < kPrepChunks; ++j) {
       const int64_t c = tid + (int64_t)j * kPrepThreads;
-      if (c < nchunks) {
-        prep_load8(row, c * 8, k_cols, vec, live, v[j]);
+      if (c < nchunks) prep_load8(row, c * 8, k_cols, vec, live, v[j]);
+    }
+  }
+  // RMSNorm factor of the row
+  float inv = 1.0f;
+  if (norm_w) {
+    float ss = 0.0f;
+    if (in_regs) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[j][i]));
+      for (int j = 0; j < kPrepChunks; ++j)
+        if (tid + (int64_t)j * kPrepThreads < nchunks)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) ss = fmaf(v[j][i], v[j][i], ss);
+    } else if (live) {
+      for (int64_t k = tid; k < k_cols; k += kPrepThreads) ss = fmaf(row[k], row[k], ss);
+    }
+    ss = prep_block_sum(ss, red);
+    inv = __fdiv_rn(1.0f, sqrtf(__fdiv_rn(ss, (float)k_cols) + eps));  // inference/math.rs:59
+    if (in_regs) {
+#pragma unroll
+      for (int j = 0; j < kPrepChunks; ++j) {
+        const int64_t c = tid + (int64_t)j * kPrepThreads;
+        if (c < nchunks) prep_norm8(v[j], c * 8, k_cols, inv, norm_w);
       }
     }
+  }
+  // max |a| over the row (NaN ignored here; it still reaches C)
+  float amax = 0.0f;
+  if (in_regs) {
+#pragma unroll
+    for (int j = 0; j < kPrepChunks; ++j)
+      if (tid + (int64_t)j * kPrepThreads < nchunks)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[j][i]));
   } else if (live) {
-    for (int64_t k = tid; k < k_cols; k += kPrepThreads) amax = fmaxf(amax, fabsf(row[k]));
+    for (int64_t k = tid; k < k_cols; k += kPrepThreads) {
+      const float x = norm_w ? (row[k] * inv) * __half2float(__ushort_as_half(norm_w[k])) : row[k];
+      amax = fmaxf(amax, fabsf(x));
+    }
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __syncthreads();  // red[] may still be read by the RMSNorm reduction
   if ((tid & 31) == 0) red[tid >> 5] = amax;
   __syncthreads();
   amax = red[0];
@@ -197,6 +251,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
     for (int64_t c = tid; c < nchunks; c += kPrepThreads) {
       float w[8];
       prep_load8(row, c * 8, k_cols, vec, live, w);
+      if (norm_w) prep_norm8(w, c * 8, k_cols, inv, norm_w);
       prep_store8(out_row, c, w, scale);
     }
   }
@@ -571,7 +626,7 @@ size_t gemm_workspace_bytes(const Q4Tiled& w, int64_t m) {
 }
 
 int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c, int64_t ldc, void* ws,
-             size_t ws_bytes, cudaStream_t st, int epi) {
+             size_t ws_bytes, cudaStream_t st, int epi, const uint16_t* norm_w, float eps) {
   AH_REQUIRE(m >= 0, "gemm: negative M");
   if (m == 0) return AH_OK;
   AH_REQUIRE(a != nullptr && c != nullptr && ws != nullptr, "gemm: null pointer");
@@ -586,7 +641,7 @@ int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c,
   uint8_t* at = static_cast<uint8_t*>(ws);
   float* row_inv = reinterpret_cast<float*>(at + align_up((size_t)mp * (size_t)w.kp * kBK * 2, 1024));
   const bool vec_rows = (lda % 4 == 0) && aligned16(a) && (w.cols % 8 == 0);
-  k_gemm_prep<<<(unsigned)mp, kPrepThreads, 0, st>>>(a, lda, m, w.cols, w.kp, vec_rows, at, row_inv);
+  k_gemm_prep<<<(unsigned)mp, kPrepThreads, 0, st>>>(a, lda, m, w.cols, w.kp, vec_rows, norm_w, eps, at, row_inv);
   AH_LAUNCH_CHECK();
   alignas(64) GemmArgs g{};
   g.w = w;

@@ -33,11 +33,13 @@ int gemv_prepare(const Q4Tiled& w, int batch, int prologue, int epilogue);
 // workspace it needs for m rows (1024-byte aligned).  Epilogues: store;
 // SwiGLU over an interleaved gate/up weight (16-row tiles of 8 gate rows,
 // then the 8 up rows of the same outputs; c gets rows/2 columns
-// silu(gate) * up); residual add (c += a . W^T).
+// silu(gate) * up); residual add (c += a . W^T).  With norm_w (f16, cols
+// entries) each row of a is RMS-normalised first (inference/math.rs:53-63).
 enum GemmEpilogue { kGemmEpiStore = 0, kGemmEpiSwiglu = 1, kGemmEpiAdd = 2 };
 size_t gemm_workspace_bytes(const Q4Tiled& w, int64_t m);
 int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c, int64_t ldc, void* ws,
-             size_t ws_bytes, cudaStream_t st, int epi = kGemmEpiStore);
+             size_t ws_bytes, cudaStream_t st, int epi = kGemmEpiStore, const uint16_t* norm_w = nullptr,
+             float eps = 0.0f);
 
 // The tcgen05 batched GEMV (ah_bgemv_tc.cu): the same products as
 // gemv_launch for 1..16 tokens, weights dequantised into tensor memory, work

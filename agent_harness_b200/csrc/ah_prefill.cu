@@ -24,28 +24,6 @@ __global__ void __launch_bounds__(256) k_embed_rows(const uint16_t* __restrict__
     hidden[r * d + c] = f16_bits_to_f32(emb[(size_t)tv * d + c]);
 }
 
-__global__ void __launch_bounds__(256) k_rmsnorm_rows(const float* __restrict__ x, const uint16_t* __restrict__ w,
-                                                      float eps, int d, float* __restrict__ out) {
-  const int64_t r = blockIdx.x;
-  const float* xr = x + r * d;
-  float ss = 0.0f;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) ss = fmaf(xr[c], xr[c], ss);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-  __shared__ float red[8];
-  __shared__ float inv;
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float s = 0.0f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
-    inv = __fdiv_rn(1.0f, sqrtf(__fdiv_rn(s, (float)d) + eps));  // inference/math.rs:59
-  }
-  __syncthreads();
-  for (int c = threadIdx.x; c < d; c += blockDim.x)
-    out[r * d + c] = (xr[c] * inv) * __half2float(__ushort_as_half(w[c]));
-}
-
 // grid (rows), block 128: RoPE on the nh local q heads (in place) and the nkv k
 // heads, then k and v rounded to f16 into the cache.
 __global__ void __launch_bounds__(128) k_rope_append_rows(float* __restrict__ qkv, int ld,
@@ -485,12 +463,6 @@ int prefill_embed(const uint16_t* emb, const int* prompt, const PrefillRows& pr,
   AH_REQUIRE(rows <= 65535 * 16, "prefill: too many rows per chunk");
   k_embed_rows<<<dim3((d + 255) / 256 < 8 ? (d + 255) / 256 : 8, (unsigned)rows), 256, 0, st>>>(emb, prompt, pr, d,
                                                                                                vocab, hidden);
-  AH_LAUNCH_CHECK();
-  return AH_OK;
-}
-
-int prefill_rmsnorm(const float* x, const uint16_t* w, float eps, int64_t rows, int d, float* out, cudaStream_t st) {
-  k_rmsnorm_rows<<<(unsigned)rows, 256, 0, st>>>(x, w, eps, d, out);
   AH_LAUNCH_CHECK();
   return AH_OK;
 }

@@ -19,8 +19,6 @@ struct PrefillRows {
 // hidden[r] = f16 -> f32 (token_embd[token of row r]) (inference/mod.rs:392-397)
 int prefill_embed(const uint16_t* emb, const int* prompt, const PrefillRows& pr, int d, int vocab, float* hidden,
                   cudaStream_t st);
-// out[r] = (x[r] * 1/rms(x[r])) * w, 1/rms = 1/sqrt(mean(x^2) + eps) (inference/math.rs:53-63)
-int prefill_rmsnorm(const float* x, const uint16_t* w, float eps, int64_t rows, int d, float* out, cudaStream_t st);
 // RoPE (per head, adjacent pairs) on q in place and on k; k and v rounded to
 // f16 into the cache at positions p0 + i: cache [B][L][nkv][max_seq][hd]
 int prefill_rope_append(float* qkv, int ld, const float2* rope, uint16_t* kc, uint16_t* vc, int layer, int n_layer,
