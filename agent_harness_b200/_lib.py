@@ -109,6 +109,7 @@ SIGNATURES = {
     "ah_model_position": (i32, [vp, C.POINTER(i32)]),
     "ah_model_set_prefill": (i32, [vp, i32]),
     "ah_model_set_batched_gemv": (i32, [vp, i32]),
+    "ah_q4w_gemm_ex": (i32, [vp, vp, i64, i64, vp, i64, i32, vp, f32, vp, sz, vp]),
     "ah_model_set_sampling": (i32, [vp, f32, i32, u64]),
     "ah_sample_workspace_bytes": (sz, [i32, i64]),
     "ah_sample_logits": (i32, [vp, i64, i32, i64, f32, i32, u64, i64, vp, vp, sz, vp]),

@@ -740,4 +740,12 @@ AH_API int ah_q4w_gemm(const AhQ4Weight* w, const float* a_dev, int64_t lda, int
                       ah::as_stream(stream));
 }
 
+AH_API int ah_q4w_gemm_ex(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev, int64_t ldc,
+                          int epilogue, const uint16_t* norm_w_dev, float eps, void* workspace_dev,
+                          size_t workspace_bytes, void* stream) {
+  AH_REQUIRE(w != nullptr, "ah_q4w_gemm_ex: null weight");
+  return ah::gemm_run(ah::q4w_tiled(w), a_dev, lda, m, c_dev, ldc, workspace_dev, workspace_bytes,
+                      ah::as_stream(stream), epilogue, norm_w_dev, eps);
+}
+
 }  // extern "C"

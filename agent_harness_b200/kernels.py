@@ -209,19 +209,31 @@ class Q4Weight:
         return int(n.value)
 
     def gemm(self, a: torch.Tensor, out: torch.Tensor | None = None,
-             workspace: torch.Tensor | None = None) -> torch.Tensor:
-        """C = A @ W^T on the tensor cores for A of shape [m, cols] f32 (prefill)."""
+             workspace: torch.Tensor | None = None, epilogue: str = "store", norm_w: torch.Tensor | None = None,
+             eps: float = 1e-5) -> torch.Tensor:
+        """C = A @ W^T on the tensor cores for A of shape [m, cols] f32 (prefill).
+        epilogue "swiglu" (an interleaved gate/up weight): C = silu(gate) * up,
+        [m, rows / 2]; "add": C += A @ W^T.  norm_w (f16 bits, cols): RMSNorm
+        each row of A first."""
         assert a.dtype == torch.float32 and a.dim() == 2 and a.shape[1] == self.cols and a.stride(1) == 1
         m = a.shape[0]
+        epi = {"store": 0, "swiglu": 1, "add": 2}[epilogue]
+        if out is not None and (not out.is_cuda or out.dtype != torch.float32 or out.stride(1) != 1):
+            raise AhError(-1, "expected a CUDA f32 output with unit-stride rows")
         if out is None:
-            out = torch.empty(m, self.rows, dtype=torch.float32, device=a.device)
+            assert epi != 2, "the add epilogue needs out"
+            out = torch.empty(m, self.rows // 2 if epi == 1 else self.rows, dtype=torch.float32, device=a.device)
         need = self.gemm_workspace_bytes(m)
         if workspace is None or workspace.numel() < need + 1024:
             workspace = torch.empty(need + 1024, dtype=torch.uint8, device=a.device)
         base = workspace.data_ptr()
         aligned = (base + 1023) // 1024 * 1024
-        call("ah_q4w_gemm", self._h, _ptr(a), a.stride(0), m, _ptr(out), out.stride(0),
-             C.c_void_p(aligned), need, _stream(a.device))
+        if epi == 0 and norm_w is None:
+            call("ah_q4w_gemm", self._h, _ptr(a), a.stride(0), m, C.c_void_p(out.data_ptr()), out.stride(0),
+                 C.c_void_p(aligned), need, _stream(a.device))
+        else:
+            call("ah_q4w_gemm_ex", self._h, _ptr(a), a.stride(0), m, C.c_void_p(out.data_ptr()), out.stride(0), epi,
+                 _ptr(norm_w) if norm_w is not None else None, eps, C.c_void_p(aligned), need, _stream(a.device))
         return out
 
     def gemv_tc_workspace_bytes(self) -> int:

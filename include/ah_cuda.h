@@ -198,6 +198,20 @@ AH_API int ah_q4w_gemv(const AhQ4Weight* w, const float* x_dev, float* y_dev, in
 AH_API int ah_q4w_gemm_workspace_bytes(const AhQ4Weight* w, int64_t m, size_t* bytes);
 AH_API int ah_q4w_gemm(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev, int64_t ldc,
                        void* workspace_dev, size_t workspace_bytes, void* stream);
+/* ah_q4w_gemm with the prefill step's fusions, for an engine that runs a
+ * block's projections over many tokens:
+ *   norm_w_dev (f16 bits, cols entries; may be null): each a row is first
+ *     RMS-normalised, inference/math.rs:53-63 rms_norm_into with `eps`;
+ *   epilogue 0: c = a . W^T;
+ *   epilogue 1: w is an interleaved gate/up weight (ah_q4w_from_*_gate_up,
+ *     2 * n_ff rows) and c [m][ldc >= n_ff] = silu(gate) * up, the
+ *     activation of inference/ffn.rs:155-174 swiglu_4bit_into for every row;
+ *   epilogue 2: c += a . W^T, the residual adds of inference/mod.rs:505-545
+ *     (an f32 add per element; subnormal sums flush to zero).
+ * Same precision and workspace as ah_q4w_gemm. */
+AH_API int ah_q4w_gemm_ex(const AhQ4Weight* w, const float* a_dev, int64_t lda, int64_t m, float* c_dev, int64_t ldc,
+                          int epilogue, const uint16_t* norm_w_dev, float eps, void* workspace_dev,
+                          size_t workspace_bytes, void* stream);
 /* No counterpart in the reference: ah_q4w_gemm without a caller workspace.  The
  * workspace lives in a fixed 8 MiB static device buffer per device (at 4096
  * columns: up to 768 tokens); larger requests return AH_EINVAL before any

@@ -135,3 +135,72 @@ def test_no_device_timeouts_recorded(cuda):
     from agent_harness_b200._lib import lib
     torch.cuda.synchronize()
     assert lib().ah_check_device_error(None) == 0
+
+
+def _silu(v):
+    return v / (1.0 + np.exp(-v))
+
+
+@pytest.mark.parametrize("m", [5, 130, 300])
+def test_fused_epilogues_and_norm(cuda, oracle, m):
+    # the prefill step's fusions through ah_q4w_gemm_ex against the oracle:
+    # SwiGLU over an interleaved gate/up weight (inference/ffn.rs:155-174 per
+    # token), the residual add (inference/mod.rs:505-545) and the RMSNorm
+    # prologue (inference/math.rs:53-63); aligned rows take the bulk-copy
+    # epilogue, rows of an odd stride the per-element stores
+    from agent_harness_b200 import kernels as K
+    n_embd, n_ff = 512, 384
+    gate = K.synth_q4_0(n_ff, n_embd, 0.05, 11, device=cuda)
+    up = K.synth_q4_0(n_ff, n_embd, 0.05, 12, device=cuda)
+    down = K.synth_q4_0(n_embd, n_ff, 0.05, 13, device=cuda)
+    blk = K.SwigluBlock.from_q4_0(gate, up, down, n_embd, n_ff)
+    x = K.fill_normal(m * n_embd, 0.0, 1.0, 14, device=cuda).reshape(m, n_embd)
+    xh = x.cpu().numpy()
+    g = oracle.gemm_q4_0(gate.cpu().numpy(), xh, n_ff).astype(np.float64)
+    u = oracle.gemm_q4_0(up.cpu().numpy(), xh, n_ff).astype(np.float64)
+    ref_act = _silu(g) * u
+    act = blk.gate_up.gemm(x, epilogue="swiglu")
+    assert act.shape == (m, n_ff)
+    assert relerr(act.cpu().numpy(), ref_act) <= TOL
+    wide = torch.full((m, n_ff + 1), 7.0, device=cuda)
+    blk.gate_up.gemm(x, out=wide[:, :n_ff], epilogue="swiglu")
+    assert relerr(wide[:, :n_ff].cpu().numpy(), ref_act) <= TOL
+    assert torch.all(wide[:, n_ff] == 7.0)
+    # residual add into hidden rows
+    h0 = K.fill_normal(m * n_embd, 0.0, 1.0, 15, device=cuda).reshape(m, n_embd)
+    ref_h = h0.cpu().numpy() + oracle.gemm_q4_0(down.cpu().numpy(), act.cpu().numpy(), n_embd)
+    h = h0.clone()
+    blk.down.gemm(act, out=h, epilogue="add")
+    assert relerr(h.cpu().numpy(), ref_h) <= TOL
+    hw = torch.zeros(m, n_embd + 3, device=cuda)
+    hw[:, :n_embd] = h0
+    blk.down.gemm(act, out=hw[:, :n_embd], epilogue="add")
+    assert relerr(hw[:, :n_embd].cpu().numpy(), ref_h) <= TOL
+    assert torch.all(hw[:, n_embd:] == 0)
+    # RMSNorm prologue (f16 norm weight), then SwiGLU
+    w16 = K.synth_f16(n_embd, 1.0, 0.1, 16, device=cuda)
+    wf = oracle.f16_to_f32(w16.cpu().numpy().view(np.uint16))
+    xn = np.stack([oracle.rms_norm(xh[i], wf, 1e-5) for i in range(m)])
+    gn = oracle.gemm_q4_0(gate.cpu().numpy(), xn, n_ff).astype(np.float64)
+    un = oracle.gemm_q4_0(up.cpu().numpy(), xn, n_ff).astype(np.float64)
+    act_n = blk.gate_up.gemm(x, epilogue="swiglu", norm_w=w16, eps=1e-5)
+    assert relerr(act_n.cpu().numpy(), _silu(gn) * un) <= TOL
+    y = K.Q4Weight.from_q4_0(down, n_embd, n_ff)
+    yn = y.gemm(act, norm_w=K.synth_f16(n_ff, 1.0, 0.1, 17, device=cuda), eps=1e-6)
+    wf2 = oracle.f16_to_f32(K.synth_f16(n_ff, 1.0, 0.1, 17, device=cuda).cpu().numpy().view(np.uint16))
+    an = np.stack([oracle.rms_norm(act.cpu().numpy()[i], wf2, 1e-6) for i in range(m)])
+    assert relerr(yn.cpu().numpy(), oracle.gemm_q4_0(down.cpu().numpy(), an, n_embd)) <= TOL
+    y.close()
+    blk.close()
+
+
+def test_fused_epilogue_arguments_refused(cuda):
+    from agent_harness_b200 import kernels as K
+    from agent_harness_b200._lib import AhError
+    W = K.Q4Weight.from_q4_0(K.synth_q4_0(24, 64, 0.05, 1, device=cuda), 24, 64)
+    a = torch.zeros(4, 64, device=cuda)
+    with pytest.raises(AhError):
+        W.gemm(a, epilogue="swiglu")  # 24 rows: not whole 16-row gate/up tiles
+    with pytest.raises(AhError):
+        W.gemm(a, out=torch.zeros(4, 24), epilogue="add")  # host output
+    W.close()
