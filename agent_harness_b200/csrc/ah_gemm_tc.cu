@@ -110,9 +110,8 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, in
 
 // ---- activation prep: f32 rows -> scaled row-major f16 -------------------------
 // One CTA per (padded) token row of kp*64 f16 (columns past K are zero).  The
-// row is read once
-// into registers (up to kPrepChunks 8-column chunks per thread, i.e. 16384
-// columns); longer rows take a second read.
+// row is read once into registers (kChunks <= kPrepChunks 8-column chunks per
+// thread, i.e. up to 16384 columns); longer rows take a second read.
 constexpr int kPrepThreads = 256;
 constexpr int kPrepChunks = 8;
 
@@ -162,6 +161,7 @@ __device__ __forceinline__ void prep_norm8(float (&v)[8], int64_t k0, int64_t k_
     v[i] = k0 + i < k_cols ? (v[i] * inv) * __half2float(__ushort_as_half(norm_w[k0 + i])) : 0.0f;
 }
 
+template <int kChunks>
 __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restrict__ a, int64_t lda, int64_t m_rows,
                                                             int64_t k_cols, int64_t kp, bool vec_rows,
                                                             const uint16_t* __restrict__ norm_w, float eps,
@@ -175,12 +175,12 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
   const float* row = a + (live ? m : 0) * lda;
   const bool vec = live && vec_rows;
   const int64_t nchunks = kp * 8;
-  const bool in_regs = nchunks <= (int64_t)kPrepThreads * kPrepChunks;
+  const bool in_regs = nchunks <= (int64_t)kPrepThreads * kChunks;
   __shared__ float red[kPrepThreads / 32];
-  float v[kPrepChunks][8];
+  float v[kChunks][8];
   if (in_regs) {
 #pragma unroll
-    for (int j = 0; j < kPrepChunks; ++j) {
+    for (int j = 0; j < kChunks; ++j) {
       const int64_t c = tid + (int64_t)j * kPrepThreads;
       if (c < nchunks) prep_load8(row, c * 8, k_cols, vec, live, v[j]);
     }
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
     float ss = 0.0f;
     if (in_regs) {
 #pragma unroll
-      for (int j = 0; j < kPrepChunks; ++j)
+      for (int j = 0; j < kChunks; ++j)
         if (tid + (int64_t)j * kPrepThreads < nchunks)
 #pragma unroll
           for (int i = 0; i < 8; ++i) ss = fmaf(v[j][i], v[j][i], ss);
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
     inv = __fdiv_rn(1.0f, sqrtf(__fdiv_rn(ss, (float)k_cols) + eps));  // inference/math.rs:59
     if (in_regs) {
 #pragma unroll
-      for (int j = 0; j < kPrepChunks; ++j) {
+      for (int j = 0; j < kChunks; ++j) {
         const int64_t c = tid + (int64_t)j * kPrepThreads;
         if (c < nchunks) prep_norm8(v[j], c * 8, k_cols, inv, norm_w);
       }
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
   float amax = 0.0f;
   if (in_regs) {
 #pragma unroll
-    for (int j = 0; j < kPrepChunks; ++j)
+    for (int j = 0; j < kChunks; ++j)
       if (tid + (int64_t)j * kPrepThreads < nchunks)
 #pragma unroll
         for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[j][i]));
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kPrepThreads) k_gemm_prep(const float* __restr
   uint8_t* out_row = at + (size_t)m * (size_t)kp * 128;
   if (in_regs) {
 #pragma unroll
-    for (int j = 0; j < kPrepChunks; ++j) {
+    for (int j = 0; j < kChunks; ++j) {
       const int64_t c = tid + (int64_t)j * kPrepThreads;
       if (c < nchunks) prep_store8(out_row, c, v[j], scale);
     }
@@ -641,7 +641,11 @@ int gemm_run(const Q4Tiled& w, const float* a, int64_t lda, int64_t m, float* c,
   uint8_t* at = static_cast<uint8_t*>(ws);
   float* row_inv = reinterpret_cast<float*>(at + align_up((size_t)mp * (size_t)w.kp * kBK * 2, 1024));
   const bool vec_rows = (lda % 4 == 0) && aligned16(a) && (w.cols % 8 == 0);
-  k_gemm_prep<<<(unsigned)mp, kPrepThreads, 0, st>>>(a, lda, m, w.cols, w.kp, vec_rows, norm_w, eps, at, row_inv);
+  // registers for as many chunks as a row needs (fewer registers: more CTAs
+  // per SM hide the load latency of short rows)
+  const int64_t per_thread = (w.kp * 8 + kPrepThreads - 1) / kPrepThreads;
+  auto prep = per_thread <= 2 ? k_gemm_prep<2> : per_thread <= 4 ? k_gemm_prep<4> : k_gemm_prep<kPrepChunks>;
+  prep<<<(unsigned)mp, kPrepThreads, 0, st>>>(a, lda, m, w.cols, w.kp, vec_rows, norm_w, eps, at, row_inv);
   AH_LAUNCH_CHECK();
   alignas(64) GemmArgs g{};
   g.w = w;
