@@ -3,7 +3,7 @@ dequantised into tensor memory, stream-K over persistent CTAs) against the
 oracle's per-token scalar GEMV (inference/math.rs:382-418 per token, as the
 reference's decode runs gemv_4bit_into for each sequence), plus a torch fp32
 matmul of the bit-exact dequantised weight at the 70B projection shapes.
-Tolerance (north star, f16 tensor-core operands with f32 accumulation, as the
+Tolerance (f16 tensor-core operands with f32 accumulation, as the
 prefill GEMM): normwise max|y - ref| / max|ref| <= 2e-3."""
 import numpy as np
 import pytest

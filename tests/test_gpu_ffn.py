@@ -1,7 +1,7 @@
 """GPU parity of the SwiGLU feed-forward block (inference/ffn.rs:155-174) and
 the row-range scalar worker (inference/math.rs:382-418) through the C-ABI,
 against the oracle's C restatements of the same functions.  Tolerance
-(north star): normwise max|y - ref| / max|ref| <= 1e-3."""
+(the f32-accumulate parity bar): normwise max|y - ref| / max|ref| <= 1e-3."""
 import numpy as np
 import pytest
 import torch

@@ -2,7 +2,7 @@
 oracle's per-token scalar GEMV (inference/math.rs:382-418 applied per token, as
 the reference's token-by-token prefill does, inference/mod.rs:550), plus a
 torch fp32 matmul of the bit-exact dequantised weight at full size.
-Tolerance (north star, prefill GEMM): normwise max|C - ref| / max|ref| <= 2e-3."""
+Tolerance (prefill GEMM, f16 operands with f32 accumulation): normwise max|C - ref| / max|ref| <= 2e-3."""
 import numpy as np
 import pytest
 import torch

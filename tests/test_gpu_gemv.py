@@ -1,5 +1,5 @@
 """GPU parity: the fused Q4 dequant+GEMV (inference/math.rs:255-418) against
-the oracle's scalar GEMV.  Tolerance (north star): normwise relative error
+the oracle's scalar GEMV.  Tolerance (the f32-accumulate parity bar): normwise relative error
 max|y - ref| / max|ref| <= 1e-3 with f32 accumulation."""
 import numpy as np
 import pytest
