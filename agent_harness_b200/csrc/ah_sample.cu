@@ -51,6 +51,7 @@ constexpr int kSampleThreads = 1024;  // whole-row CTAs
 constexpr int kPartThreads = 512;     // slice CTAs
 constexpr int kReduceThreads = 256;   // CTAs over a row's slice candidates
 constexpr int kSampleUnroll = 8;      // loads in flight per thread per sweep
+constexpr int kMergeParts = 64;       // slices per row the reduce merges as sorted lists
 
 // Larger float -> larger key; -0 and +0 share a key; NaN maps below every
 // number (never a candidate ahead of a number).
@@ -341,25 +342,88 @@ __global__ void __launch_bounds__(kPartThreads) k_sample_part(const float* __res
   }
 }
 
+// Warp 0: the top ke of the parts' sorted candidate lists (mv / mi [p][k],
+// each sorted by (value desc, index asc), parts <= 2 * 32) by a k-way merge:
+// lane l holds the heads of lists l and l + 32, and each step a butterfly
+// over the lanes picks the winner, which its list's lane replaces by the
+// list's next entry.  The result is sorted, as topk_row's.
+__device__ void merge_lists(const float* mv, const int* mi, int parts, int k, int ke, TopkSmem& sm) {
+  const int lane = threadIdx.x & 31;
+  int pos0 = 0, pos1 = 0;
+  uint32_t k0 = 0u, k1 = 0u;
+  int i0 = INT_MAX, i1 = INT_MAX;  // exhausted lists: (key 0, index INT_MAX) loses to every entry
+  const int p0 = lane, p1 = lane + 32;
+  if (p0 < parts) {
+    k0 = order_key(mv[p0 * k]);
+    i0 = mi[p0 * k];
+  }
+  if (p1 < parts) {
+    k1 = order_key(mv[p1 * k]);
+    i1 = mi[p1 * k];
+  }
+  for (int j = 0; j < ke; ++j) {
+    const bool second = cand_before(k1, i1, k0, i0);
+    uint32_t bk = second ? k1 : k0;
+    int bi = second ? i1 : i0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (cand_before(ok, oi, bk, bi)) {
+        bk = ok;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      sm.cv[j] = key_value(bk);
+      sm.ci[j] = bi;
+    }
+    // vocabulary indices are distinct: only the winner's list moves
+    if (bi != INT_MAX) {
+      if (!second && i0 == bi) {
+        ++pos0;
+        k0 = pos0 < k ? order_key(mv[p0 * k + pos0]) : 0u;
+        i0 = pos0 < k ? mi[p0 * k + pos0] : INT_MAX;
+      } else if (second && i1 == bi) {
+        ++pos1;
+        k1 = pos1 < k ? order_key(mv[p1 * k + pos1]) : 0u;
+        i1 = pos1 < k ? mi[p1 * k + pos1] : INT_MAX;
+      }
+    }
+  }
+}
+
 // Row b's parts * k slice candidates -> its top-k (position order among equal
 // values is index order: slices ascend, each sorted), then the sample or the
-// candidates as k_sample_topk.
+// candidates as k_sample_topk.  Up to kMergeParts slices: staged in shared
+// memory and merged by one warp; more: a radix select over them.
 __global__ void __launch_bounds__(kReduceThreads) k_sample_reduce(const float* __restrict__ part_v,
                                                                   const int* __restrict__ part_i, int parts, int k,
                                                                   int64_t n, float temperature, uint64_t seed,
                                                                   int64_t step, const int* step_dev, SampleCand* cand,
                                                                   int* tok, int* tok_log, int batch) {
   __shared__ TopkSmem sm;
+  __shared__ float mv[kMergeParts * kSampleMaxK];
+  __shared__ int mi[kMergeParts * kSampleMaxK];
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.x;
   const int64_t m = (int64_t)parts * k;
   const int ke = (int)(k < n ? k : n);
-  if (m <= 2 * kReduceThreads * kSampleUnroll)
-    topk_row<kReduceThreads, 2>(part_v + (size_t)b * m, m, ke, 0, sm);
-  else
-    topk_row<kReduceThreads, 0>(part_v + (size_t)b * m, m, ke, 0, sm);
-  if ((int)threadIdx.x < ke) sm.ci[threadIdx.x] = part_i[(size_t)b * m + sm.ci[threadIdx.x]];
+  if (parts <= kMergeParts) {
+    for (int i = threadIdx.x; i < (int)m; i += kReduceThreads) {
+      mv[i] = part_v[(size_t)b * m + i];
+      mi[i] = part_i[(size_t)b * m + i];
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) merge_lists(mv, mi, parts, k, ke, sm);
+  } else {
+    if (m <= 2 * kReduceThreads * kSampleUnroll)
+      topk_row<kReduceThreads, 2>(part_v + (size_t)b * m, m, ke, 0, sm);
+    else
+      topk_row<kReduceThreads, 0>(part_v + (size_t)b * m, m, ke, 0, sm);
+    if ((int)threadIdx.x < ke) sm.ci[threadIdx.x] = part_i[(size_t)b * m + sm.ci[threadIdx.x]];
+  }
   __syncthreads();
   sample_finish(sm, ke, k, b, temperature, seed, step, step_dev, cand, tok, tok_log, batch);
 }
